@@ -1,0 +1,170 @@
+// brew_common.cuh — shared device/host helpers of libbrew (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/brew.h"
+
+// ---------------------------------------------------------------------------
+// host-side error plumbing
+// ---------------------------------------------------------------------------
+namespace brew {
+
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+void count_launch(int n = 1);
+
+#define BREW_CUDA(call)                                                   \
+    do {                                                                  \
+        cudaError_t _e = (call);                                          \
+        if (_e != cudaSuccess) return ::brew::cuda_error(_e, #call);      \
+    } while (0)
+
+#define BREW_CHECK(cond, code, ...)                                       \
+    do {                                                                  \
+        if (!(cond)) return ::brew::set_error((code), __VA_ARGS__);       \
+    } while (0)
+
+// GGML block geometry
+struct TypeInfo {
+    int block_elems;
+    int block_bytes;
+};
+
+inline bool type_info(int type, TypeInfo* ti) {
+    switch (type) {
+        case BREW_TYPE_F32: *ti = {1, 4}; return true;
+        case BREW_TYPE_F16: *ti = {1, 2}; return true;
+        case BREW_TYPE_Q4_0: *ti = {32, 18}; return true;
+        case BREW_TYPE_Q8_0: *ti = {32, 34}; return true;
+        case BREW_TYPE_Q4_K: *ti = {256, 144}; return true;
+        case BREW_TYPE_Q6_K: *ti = {256, 210}; return true;
+        default: return false;
+    }
+}
+
+inline bool is_quant_matrix_type(int type) {
+    return type == BREW_TYPE_Q4_0 || type == BREW_TYPE_Q8_0 || type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K;
+}
+
+// device-side error flags (one word per device, written by bounded waits)
+#define BREW_DEVERR_TIMEOUT_FULL   1u
+#define BREW_DEVERR_TIMEOUT_EMPTY  2u
+#define BREW_DEVERR_BAD_INDEX      4u
+#define BREW_DEVERR_BAD_TOKEN      8u
+
+unsigned int* device_error_word();      // device pointer of this device's flag word
+int check_device_error(const char* where);  // reads + clears the flag (synchronising)
+
+}  // namespace brew
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+#ifdef __CUDACC__
+
+namespace brew {
+
+// Bounded spin limits: a wait that exceeds them records an error flag and
+// gives up instead of hanging the GPU.
+#define BREW_SPIN_LIMIT (1u << 24)
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for phase `parity` of `bar` for at most ~2 s (and at most
+// BREW_SPIN_LIMIT polls); on timeout records `err` in the device error word
+// and returns false, so a broken pipeline ends instead of hanging the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* err_word,
+                                                  unsigned int err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0; it < BREW_SPIN_LIMIT; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && global_ns() - t0 > 2000000000ull) break;
+    }
+    if (err_word) atomicOr(err_word, err);
+    return false;
+}
+
+// ---- bulk async copy global -> shared (TMA, non-tensor, no multicast) -----
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- programmatic dependent launch -------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---- misc ----------------------------------------------------------------
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace brew
+
+#endif  // __CUDACC__

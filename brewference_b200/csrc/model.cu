@@ -1,0 +1,679 @@
+// model.cu — device-resident model: TransformerGraph.forward for the llama,
+// qwen2, qwen3 and gemma3 graphs, captured into CUDA graphs, plus the greedy
+// generation loop of GenericModelSession (runtime/ModelRunner.java:100-217).
+//
+// Per layer the forward is five launches, chained with programmatic
+// dependent launch so each matvec streams its weights while the previous
+// kernel finishes:
+//   1. Q|K|V matvec (one launch over the three matrices, bias epilogue)
+//   2. attention: QK-norm, RoPE, KV append, split-context softmax.V, combine,
+//      prep records of xb
+//   3. wo matvec (+ residual, or Gemma3 post-norm) whose last CTA
+//      RMS-normalises x for the FFN and writes its prep records
+//   4. gate|up matvec with the SwiGLU/GeGLU epilogue and prep records of hb
+//   5. down matvec (+ residual / post-norm) whose last CTA normalises x for
+//      the next layer (or the final norm)
+// then the classifier matvec with a fused argmax.  The embedding lookup and
+// the first RMSNorm are one more kernel.
+#include "brew_internal.cuh"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <vector>
+
+namespace brew {
+
+namespace {
+
+enum { T_EMBED = 0, T_OUTPUT, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_COUNT };
+
+uint32_t tensor_id(int kind, int layer) { return ((uint32_t)kind << 16) | (uint32_t)layer; }
+
+__global__ void step_kernel(int32_t* tokens, int32_t* pos, const int32_t* tok_src, int32_t pos_val, int32_t* record,
+                            const int32_t* am) {
+    if (threadIdx.x == 0) {
+        if (record) *record = am[0];
+        tokens[0] = *tok_src;
+        pos[0] = pos_val;
+    }
+}
+
+}  // namespace
+
+}  // namespace brew
+
+using namespace brew;
+
+struct brew_model_s {
+    brew_config c;
+    int max_batch = 1;
+    brew_tensor t[T_COUNT] = {};
+    bool owns_tensors = false;
+    float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr, *post_att = nullptr, *post_ffn = nullptr;
+    float *rms_q = nullptr, *rms_k = nullptr, *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    int64_t cache_bstride = 0;
+    float *x = nullptr, *xb = nullptr, *xb2 = nullptr, *qkv = nullptr, *hb = nullptr, *logits = nullptr;
+    uint8_t *prep_x = nullptr, *prep_q = nullptr, *prep_h = nullptr;
+    float* part = nullptr;
+    int* counters = nullptr;   // [tile counters: sms][group counters][post][attn]
+    int n_counters = 0;
+    float* attn_part = nullptr;
+    float* am_val = nullptr;
+    int* am_idx = nullptr;
+    int32_t* am_out = nullptr;
+    int32_t *tokens_d = nullptr, *pos_d = nullptr;
+    int32_t* gen_d = nullptr;      // generated ids of brew_session_generate
+    int32_t* prompt_d = nullptr;   // prompt of brew_session_generate (+1 for bos)
+    int prompt_cap = 0;
+    int nchunk = 1;
+    int qkvw = 0;
+    std::vector<void*> allocs;
+    std::map<int, cudaGraphExec_t> graphs;   // key: batch*2 + with_classifier
+    int32_t* h_pin = nullptr;                // pinned staging (tokens, pos, argmax)
+    int h_pin_cap = 0;
+};
+
+namespace brew {
+namespace {
+
+template <class T>
+int dalloc(brew_model_s* m, T** p, size_t count) {
+    void* q = nullptr;
+    BREW_CUDA(cudaMalloc(&q, count * sizeof(T) + 256));
+    BREW_CUDA(cudaMemset(q, 0, count * sizeof(T) + 256));
+    m->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return BREW_OK;
+}
+
+int check_config(const brew_config& c, int max_batch) {
+    BREW_CHECK(c.arch >= BREW_ARCH_LLAMA && c.arch <= BREW_ARCH_GEMMA3, BREW_ERR_UNSUPPORTED, "arch %d", c.arch);
+    BREW_CHECK(c.dim > 0 && c.dim % 32 == 0, BREW_ERR_INVALID_ARG, "dim %d", c.dim);
+    BREW_CHECK(c.hidden_dim > 0 && c.hidden_dim % 32 == 0, BREW_ERR_INVALID_ARG, "hidden_dim %d", c.hidden_dim);
+    BREW_CHECK(c.n_layers > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0,
+               BREW_ERR_INVALID_ARG, "layers/heads %d/%d/%d", c.n_layers, c.n_heads, c.n_kv_heads);
+    BREW_CHECK(c.head_size > 0 && c.head_size % 32 == 0, BREW_ERR_INVALID_ARG, "head_size %d", c.head_size);
+    BREW_CHECK(c.vocab_size > 0 && c.seq_len > 0, BREW_ERR_INVALID_ARG, "vocab/seq_len");
+    BREW_CHECK(max_batch >= 1 && max_batch <= MV_MAX_BATCH, BREW_ERR_INVALID_ARG, "max_batch %d", max_batch);
+    const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down,
+                         c.tied_embeddings ? c.type_embed : c.type_output};
+    for (int t : types)
+        BREW_CHECK(t == BREW_TYPE_Q8_0 || t == BREW_TYPE_Q4_0, BREW_ERR_UNSUPPORTED,
+                   "the device forward streams Q8_0/Q4_0 matrices; GGML type %d is served by brew_matmul only", t);
+    BREW_CHECK(c.type_q == c.type_k && c.type_k == c.type_v, BREW_ERR_UNSUPPORTED, "Q/K/V of different types");
+    BREW_CHECK(c.type_gate == c.type_up, BREW_ERR_UNSUPPORTED, "gate/up of different types");
+    return BREW_OK;
+}
+
+void matrix_shape(const brew_config& c, int which, int64_t* rows, int64_t* cols, int* type, int* layers) {
+    const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
+    *layers = c.n_layers;
+    switch (which) {
+        case T_EMBED: *rows = c.vocab_size; *cols = c.dim; *type = c.type_embed; *layers = 1; break;
+        case T_OUTPUT: *rows = c.vocab_size; *cols = c.dim; *type = c.tied_embeddings ? c.type_embed : c.type_output; *layers = 1; break;
+        case T_Q: *rows = qw; *cols = c.dim; *type = c.type_q; break;
+        case T_K: *rows = kvd; *cols = c.dim; *type = c.type_k; break;
+        case T_V: *rows = kvd; *cols = c.dim; *type = c.type_v; break;
+        case T_O: *rows = c.dim; *cols = qw; *type = c.type_o; break;
+        case T_GATE: *rows = c.hidden_dim; *cols = c.dim; *type = c.type_gate; break;
+        case T_UP: *rows = c.hidden_dim; *cols = c.dim; *type = c.type_up; break;
+        default: *rows = c.dim; *cols = c.hidden_dim; *type = c.type_down; break;
+    }
+}
+
+int alloc_state(brew_model_s* m) {
+    const brew_config& c = m->c;
+    const int B = m->max_batch;
+    const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
+    m->qkvw = (int)(qw + 2 * kvd);
+    m->cache_bstride = (int64_t)c.n_layers * c.seq_len * kvd;
+    int rc;
+    if ((rc = dalloc(m, &m->kc, (size_t)B * m->cache_bstride))) return rc;
+    if ((rc = dalloc(m, &m->vc, (size_t)B * m->cache_bstride))) return rc;
+    if ((rc = dalloc(m, &m->x, (size_t)B * c.dim))) return rc;
+    if ((rc = dalloc(m, &m->xb, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
+    if ((rc = dalloc(m, &m->xb2, (size_t)B * c.dim))) return rc;
+    if ((rc = dalloc(m, &m->qkv, (size_t)B * m->qkvw))) return rc;
+    if ((rc = dalloc(m, &m->hb, (size_t)B * c.hidden_dim))) return rc;
+    if ((rc = dalloc(m, &m->logits, (size_t)B * c.vocab_size))) return rc;
+    const size_t rec = prep_rec_bytes(B);
+    if ((rc = dalloc(m, &m->prep_x, (size_t)(c.dim / 32) * rec))) return rc;
+    if ((rc = dalloc(m, &m->prep_q, (size_t)(qw / 32) * rec))) return rc;
+    if ((rc = dalloc(m, &m->prep_h, (size_t)(c.hidden_dim / 32) * rec))) return rc;
+    if ((rc = dalloc(m, &m->part, mv_part_floats(num_sms(), B)))) return rc;
+    m->n_counters = num_sms() + c.hidden_dim / 32 + 8 + B * c.n_kv_heads;
+    if ((rc = dalloc(m, &m->counters, (size_t)m->n_counters))) return rc;
+    m->nchunk = attn_pick_nchunk(c.n_kv_heads, B, c.seq_len);
+    if ((rc = dalloc(m, &m->attn_part, attn_part_floats(B, c.n_heads, m->nchunk, c.head_size)))) return rc;
+    if ((rc = dalloc(m, &m->am_val, (size_t)num_sms() * B))) return rc;
+    if ((rc = dalloc(m, &m->am_idx, (size_t)num_sms() * B))) return rc;
+    if ((rc = dalloc(m, &m->am_out, (size_t)B))) return rc;
+    if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
+    if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
+    if ((rc = dalloc(m, &m->gen_d, (size_t)c.seq_len + 1))) return rc;
+    m->h_pin_cap = std::max(4 * B, 64);
+    BREW_CUDA(cudaMallocHost(&m->h_pin, (size_t)m->h_pin_cap * sizeof(int32_t)));
+    return BREW_OK;
+}
+
+int upload_vec(brew_model_s* m, float** dst, const float* src, size_t n) {
+    if (!src) return BREW_OK;
+    int rc = dalloc(m, dst, n);
+    if (rc) return rc;
+    BREW_CUDA(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+    return BREW_OK;
+}
+
+int fill_vec(brew_model_s* m, float** dst, size_t n, float v) {
+    int rc = dalloc(m, dst, n);
+    if (rc) return rc;
+    return fill_f32_launch(*dst, (int64_t)n, v, ctx().stream);
+}
+
+const uint8_t* layer_ptr(brew_tensor t, int layer, int64_t rows, int64_t cols) {
+    TypeInfo ti;
+    type_info(t->type, &ti);
+    return t->d + (int64_t)layer * (rows * cols / ti.block_elems) * ti.block_bytes;
+}
+
+int64_t row_bytes_of(int type, int64_t cols) {
+    TypeInfo ti;
+    type_info(type, &ti);
+    return cols / ti.block_elems * ti.block_bytes;
+}
+
+// Enqueues one forward pass for `B` sequences reading tokens_d / pos_d.
+int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
+    const brew_config& c = m->c;
+    const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
+    const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
+    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    unsigned int* err = ctx().err_word;
+    int* tile_ctr = m->counters;
+    int* group_ctr = tile_ctr + num_sms();
+    int* post_ctr = group_ctr + hid / 32;
+    int* attn_ctr = post_ctr + 8;
+    int rc;
+
+    rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x, m->rms_att,
+                           c.eps, m->prep_x, err, s, true);
+    if (rc) return rc;
+
+    for (int l = 0; l < L; ++l) {
+        // 1. Q|K|V
+        {
+            MvParams p = {};
+            p.type = c.type_q;
+            p.K = dim;
+            p.row_bytes = row_bytes_of(c.type_q, dim);
+            p.batch = B;
+            p.ldy = m->qkvw;
+            p.epi = MV_EPI_STORE;
+            p.nseg = 3;
+            p.seg[0] = {layer_ptr(m->t[T_Q], l, qw, dim), m->qkv, m->q_bias ? m->q_bias + (int64_t)l * qw : nullptr,
+                        nullptr, qw, 0};
+            p.seg[1] = {layer_ptr(m->t[T_K], l, kvd, dim), m->qkv + qw, m->k_bias ? m->k_bias + (int64_t)l * kvd : nullptr,
+                        nullptr, kvd, 0};
+            p.seg[2] = {layer_ptr(m->t[T_V], l, kvd, dim), m->qkv + qw + kvd,
+                        m->v_bias ? m->v_bias + (int64_t)l * kvd : nullptr, nullptr, kvd, 0};
+            p.prep = m->prep_x;
+            p.part_buf = m->part;
+            p.tile_counters = tile_ctr;
+            p.err = err;
+            if ((rc = mv_launch(p, s, true))) return rc;
+        }
+        // 2. attention
+        {
+            AttnParams a = {};
+            a.batch = B;
+            a.n_heads = c.n_heads;
+            a.n_kv = c.n_kv_heads;
+            a.hd = hd;
+            a.seq_len = c.seq_len;
+            a.arch = c.arch;
+            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
+            a.window = (gemma && !global) ? c.sliding_window : 0;
+            a.eps = c.eps;
+            float base;
+            if (c.rope_base > 0.0f) base = c.rope_base;
+            else if (c.arch == BREW_ARCH_LLAMA) base = 10000.0f;
+            else if (gemma) base = global ? 1000000.0f : 10000.0f;
+            else base = 1000000.0f;
+            a.rope_base = base;
+            a.rope_scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
+            a.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
+            a.q = m->qkv;
+            a.k = m->qkv + qw;
+            a.v = m->qkv + qw + kvd;
+            a.ldq = a.ldkv = m->qkvw;
+            a.qnorm_w = qknorm ? m->rms_q + (int64_t)l * hd : nullptr;
+            a.knorm_w = qknorm ? m->rms_k + (int64_t)l * hd : nullptr;
+            a.kcache = m->kc + (int64_t)l * c.seq_len * kvd;
+            a.vcache = m->vc + (int64_t)l * c.seq_len * kvd;
+            a.cache_bstride = m->cache_bstride;
+            a.pos = m->pos_d;
+            a.xb = m->xb;
+            a.ldxb = qw;
+            a.part = m->attn_part;
+            a.counters = attn_ctr;
+            a.nchunk = m->nchunk;
+            a.prep_out = m->prep_q;
+            a.err = err;
+            if ((rc = attn_launch(a, s, true))) return rc;
+        }
+        // 3. wo (+ residual or Gemma3 post-attention norm), then FFN norm
+        {
+            MvParams p = {};
+            p.type = c.type_o;
+            p.K = qw;
+            p.row_bytes = row_bytes_of(c.type_o, qw);
+            p.batch = B;
+            p.ldy = dim;
+            p.epi = MV_EPI_STORE;
+            p.nseg = 1;
+            p.seg[0] = {layer_ptr(m->t[T_O], l, dim, qw), gemma ? m->xb2 : m->x, nullptr, gemma ? nullptr : m->x, dim, 0};
+            p.prep = m->prep_q;
+            p.part_buf = m->part;
+            p.tile_counters = tile_ctr;
+            p.post = MV_POST_PREP;
+            p.post_counter = post_ctr;
+            p.post_x = m->x;
+            p.post_ld = dim;
+            p.post_dim = dim;
+            p.post_add = gemma ? m->xb2 : nullptr;
+            p.post_add_w = gemma ? m->post_att + (int64_t)l * dim : nullptr;
+            p.post_norm_w = m->rms_ffn + (int64_t)l * dim;
+            p.eps = c.eps;
+            p.post_prep = m->prep_x;
+            p.err = err;
+            if ((rc = mv_launch(p, s, true))) return rc;
+        }
+        // 4. gate|up with the gated activation
+        {
+            MvParams p = {};
+            p.type = c.type_gate;
+            p.K = dim;
+            p.row_bytes = row_bytes_of(c.type_gate, dim);
+            p.batch = B;
+            p.ldy = hid;
+            p.epi = gemma ? MV_EPI_GLU_GELU : MV_EPI_GLU_SILU;
+            p.nseg = 2;
+            p.seg[0] = {layer_ptr(m->t[T_GATE], l, hid, dim), m->hb, nullptr, nullptr, hid, 0};
+            p.seg[1] = {layer_ptr(m->t[T_UP], l, hid, dim), nullptr, nullptr, nullptr, hid, 0};
+            p.prep = m->prep_x;
+            p.part_buf = m->part;
+            p.tile_counters = tile_ctr;
+            p.next_prep = m->prep_h;
+            p.group_counters = group_ctr;
+            p.err = err;
+            if ((rc = mv_launch(p, s, true))) return rc;
+        }
+        // 5. down (+ residual or Gemma3 post-FFN norm), then the next norm
+        {
+            MvParams p = {};
+            p.type = c.type_down;
+            p.K = hid;
+            p.row_bytes = row_bytes_of(c.type_down, hid);
+            p.batch = B;
+            p.ldy = dim;
+            p.epi = MV_EPI_STORE;
+            p.nseg = 1;
+            p.seg[0] = {layer_ptr(m->t[T_DOWN], l, dim, hid), gemma ? m->xb2 : m->x, nullptr, gemma ? nullptr : m->x, dim, 0};
+            p.prep = m->prep_h;
+            p.part_buf = m->part;
+            p.tile_counters = tile_ctr;
+            p.post = MV_POST_PREP;
+            p.post_counter = post_ctr;
+            p.post_x = m->x;
+            p.post_ld = dim;
+            p.post_dim = dim;
+            p.post_add = gemma ? m->xb2 : nullptr;
+            p.post_add_w = gemma ? m->post_ffn + (int64_t)l * dim : nullptr;
+            p.post_norm_w = l + 1 < L ? m->rms_att + (int64_t)(l + 1) * dim : m->rms_final;
+            p.eps = c.eps;
+            p.post_prep = m->prep_x;
+            p.err = err;
+            if ((rc = mv_launch(p, s, true))) return rc;
+        }
+    }
+    if (!with_classifier) return BREW_OK;
+    {
+        const int otype = c.tied_embeddings ? c.type_embed : c.type_output;
+        MvParams p = {};
+        p.type = otype;
+        p.K = dim;
+        p.row_bytes = row_bytes_of(otype, dim);
+        p.batch = B;
+        p.ldy = c.vocab_size;
+        p.epi = MV_EPI_STORE;
+        p.nseg = 1;
+        p.seg[0] = {m->t[T_OUTPUT]->d, m->logits, nullptr, nullptr, c.vocab_size, 0};
+        p.prep = m->prep_x;
+        p.part_buf = m->part;
+        p.tile_counters = tile_ctr;
+        const bool fused = B <= MV_ARGMAX_MAX_BATCH;
+        p.post = fused ? MV_POST_ARGMAX : MV_POST_NONE;
+        p.post_counter = post_ctr;
+        p.am_val = m->am_val;
+        p.am_idx = m->am_idx;
+        p.am_out = m->am_out;
+        p.err = err;
+        if ((rc = mv_launch(p, s, true))) return rc;
+        if (!fused && (rc = argmax_launch(m->logits, c.vocab_size, c.vocab_size, B, m->am_out, s, true))) return rc;
+    }
+    return BREW_OK;
+}
+
+int get_graph(brew_model_s* m, int B, bool with_classifier, cudaGraphExec_t* out) {
+    const int key = B * 2 + (with_classifier ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it != m->graphs.end()) {
+        *out = it->second;
+        return BREW_OK;
+    }
+    cudaStream_t s = ctx().stream;
+    cudaGraph_t g = nullptr;
+    BREW_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(m, B, with_classifier, s);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    BREW_CUDA(e);
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    BREW_CUDA(e);
+    m->graphs[key] = exec;
+    *out = exec;
+    return BREW_OK;
+}
+
+int model_finish_create(brew_model_s* m) {
+    int rc = alloc_state(m);
+    if (rc) return rc;
+    BREW_CUDA(cudaStreamSynchronize(ctx().stream));
+    BREW_CUDA(cudaDeviceSynchronize());
+    return BREW_OK;
+}
+
+void model_destroy(brew_model_s* m) {
+    if (!m) return;
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->h_pin) cudaFreeHost(m->h_pin);
+    if (m->owns_tensors)
+        for (int i = 0; i < T_COUNT; ++i)
+            if (m->t[i]) brew_tensor_free(m->t[i]);
+    delete m;
+}
+
+}  // namespace
+}  // namespace brew
+
+extern "C" {
+
+int brew_model_create(const brew_config* cfg, const brew_model_weights* w, int32_t max_batch, brew_model* out) {
+    BREW_CHECK(cfg && w && out, BREW_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    int rc = check_config(*cfg, max_batch);
+    if (rc) return rc;
+    if ((rc = ensure_init())) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    const brew_config& c = *cfg;
+    brew_tensor ts[T_COUNT] = {w->token_embd, c.tied_embeddings ? w->token_embd : w->output, w->wq, w->wk, w->wv, w->wo,
+                               w->w_gate, w->w_up, w->w_down};
+    for (int i = 0; i < T_COUNT; ++i) {
+        BREW_CHECK(ts[i], BREW_ERR_INVALID_ARG, "weight tensor %d is null", i);
+        int64_t rows, cols;
+        int type, layers;
+        matrix_shape(c, i, &rows, &cols, &type, &layers);
+        BREW_CHECK(ts[i]->type == type, BREW_ERR_INVALID_ARG, "tensor %d has type %d, config says %d", i, ts[i]->type, type);
+        BREW_CHECK(ts[i]->n == rows * cols * layers, BREW_ERR_INVALID_ARG, "tensor %d has %lld elements, expected %lld", i,
+                   (long long)ts[i]->n, (long long)(rows * cols * layers));
+    }
+    const bool gemma = c.arch == BREW_ARCH_GEMMA3, qk = c.arch == BREW_ARCH_QWEN3 || gemma, bias = c.arch == BREW_ARCH_QWEN2;
+    BREW_CHECK(w->rms_att && w->rms_ffn && w->rms_final, BREW_ERR_INVALID_ARG, "norm weights missing");
+    BREW_CHECK(!gemma || (w->post_att && w->post_ffn), BREW_ERR_INVALID_ARG, "Gemma3 post-norm weights missing");
+    BREW_CHECK(!qk || (w->rms_q && w->rms_k), BREW_ERR_INVALID_ARG, "QK-norm weights missing");
+    BREW_CHECK(!bias || (w->q_bias && w->k_bias && w->v_bias), BREW_ERR_INVALID_ARG, "QKV bias missing");
+    brew_model_s* m = new brew_model_s();
+    m->c = c;
+    m->max_batch = max_batch;
+    for (int i = 0; i < T_COUNT; ++i) m->t[i] = ts[i];
+    const size_t L = c.n_layers, dim = c.dim, hs = c.head_size;
+    const size_t qw = (size_t)c.n_heads * hs, kvd = (size_t)c.n_kv_heads * hs;
+    if ((rc = upload_vec(m, &m->rms_att, w->rms_att, L * dim)) || (rc = upload_vec(m, &m->rms_ffn, w->rms_ffn, L * dim)) ||
+        (rc = upload_vec(m, &m->rms_final, w->rms_final, dim)) ||
+        (gemma && ((rc = upload_vec(m, &m->post_att, w->post_att, L * dim)) || (rc = upload_vec(m, &m->post_ffn, w->post_ffn, L * dim)))) ||
+        (qk && ((rc = upload_vec(m, &m->rms_q, w->rms_q, L * hs)) || (rc = upload_vec(m, &m->rms_k, w->rms_k, L * hs)))) ||
+        (bias && ((rc = upload_vec(m, &m->q_bias, w->q_bias, L * qw)) || (rc = upload_vec(m, &m->k_bias, w->k_bias, L * kvd)) ||
+                  (rc = upload_vec(m, &m->v_bias, w->v_bias, L * kvd)))) ||
+        (rc = model_finish_create(m))) {
+        model_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return BREW_OK;
+}
+
+int brew_model_synthesize(const brew_config* cfg, uint64_t seed, int32_t max_batch, brew_model* out) {
+    BREW_CHECK(cfg && out, BREW_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    int rc = check_config(*cfg, max_batch);
+    if (rc) return rc;
+    if ((rc = ensure_init())) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    const brew_config& c = *cfg;
+    brew_model_s* m = new brew_model_s();
+    m->c = c;
+    m->max_batch = max_batch;
+    m->owns_tensors = true;
+    cudaStream_t s = ctx().stream;
+    for (int i = 0; i < T_COUNT && !rc; ++i) {
+        if (i == T_OUTPUT && c.tied_embeddings) continue;
+        int64_t rows, cols;
+        int type, layers;
+        matrix_shape(c, i, &rows, &cols, &type, &layers);
+        rc = brew_tensor_alloc(type, rows * cols * layers, &m->t[i]);
+        if (rc) break;
+        const int64_t per = brew_type_bytes(type, rows * cols);
+        for (int l = 0; l < layers && !rc; ++l)
+            rc = synth_launch(type, seed, tensor_id(i, l), rows * cols, 0.02f, m->t[i]->d + per * l, s);
+    }
+    if (!rc && c.tied_embeddings) {
+        brew_tensor v = new brew_tensor_s(*m->t[T_EMBED]);
+        v->owned = false;
+        m->t[T_OUTPUT] = v;
+    }
+    const size_t L = c.n_layers, dim = c.dim, hs = c.head_size;
+    const size_t qw = (size_t)c.n_heads * hs, kvd = (size_t)c.n_kv_heads * hs;
+    if (!rc) rc = fill_vec(m, &m->rms_att, L * dim, 1.0f);
+    if (!rc) rc = fill_vec(m, &m->rms_ffn, L * dim, 1.0f);
+    if (!rc) rc = fill_vec(m, &m->rms_final, dim, 1.0f);
+    if (!rc && c.arch == BREW_ARCH_GEMMA3) {
+        rc = fill_vec(m, &m->post_att, L * dim, 1.0f);
+        if (!rc) rc = fill_vec(m, &m->post_ffn, L * dim, 1.0f);
+    }
+    if (!rc && (c.arch == BREW_ARCH_QWEN3 || c.arch == BREW_ARCH_GEMMA3)) {
+        rc = fill_vec(m, &m->rms_q, L * hs, 1.0f);
+        if (!rc) rc = fill_vec(m, &m->rms_k, L * hs, 1.0f);
+    }
+    if (!rc && c.arch == BREW_ARCH_QWEN2) {
+        rc = dalloc(m, &m->q_bias, L * qw);
+        if (!rc) rc = dalloc(m, &m->k_bias, L * kvd);
+        if (!rc) rc = dalloc(m, &m->v_bias, L * kvd);
+        for (size_t l = 0; l < L && !rc; ++l) {
+            rc = synth_f32_launch(seed, tensor_id(9, (int)l), qw, 0.02f, m->q_bias + l * qw, s);
+            if (!rc) rc = synth_f32_launch(seed, tensor_id(10, (int)l), kvd, 0.02f, m->k_bias + l * kvd, s);
+            if (!rc) rc = synth_f32_launch(seed, tensor_id(11, (int)l), kvd, 0.02f, m->v_bias + l * kvd, s);
+        }
+    }
+    if (!rc) rc = model_finish_create(m);
+    if (rc) {
+        model_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return BREW_OK;
+}
+
+int brew_model_free(brew_model m) {
+    if (!m) return BREW_OK;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaDeviceSynchronize();
+    model_destroy(m);
+    return BREW_OK;
+}
+
+int brew_model_tensor(brew_model m, int which, brew_tensor* out) {
+    BREW_CHECK(m && out && which >= 0 && which < T_COUNT, BREW_ERR_INVALID_ARG, "bad argument");
+    *out = m->t[which];
+    return BREW_OK;
+}
+
+int brew_model_reset(brew_model m) {
+    BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null model");
+    std::lock_guard<std::mutex> lk(api_mutex());
+    BREW_CUDA(cudaMemsetAsync(m->kc, 0, (size_t)m->max_batch * m->cache_bstride * sizeof(float), ctx().stream));
+    BREW_CUDA(cudaMemsetAsync(m->vc, 0, (size_t)m->max_batch * m->cache_bstride * sizeof(float), ctx().stream));
+    BREW_CUDA(cudaStreamSynchronize(ctx().stream));
+    return BREW_OK;
+}
+
+int brew_model_forward_dev(brew_model m, const int32_t* tokens_dev, const int32_t* pos_dev, int32_t batch,
+                           float* logits_dev, int32_t* argmax_dev, void* stream) {
+    BREW_CHECK(m && tokens_dev && pos_dev, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(batch >= 1 && batch <= m->max_batch, BREW_ERR_INVALID_ARG, "batch %d (max %d)", batch, m->max_batch);
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaStream_t s = ctx().stream;
+    cudaStream_t us = static_cast<cudaStream_t>(stream);
+    cudaEvent_t ev;
+    if (us) {
+        BREW_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        BREW_CUDA(cudaEventRecord(ev, us));
+        BREW_CUDA(cudaStreamWaitEvent(s, ev));
+    }
+    BREW_CUDA(cudaMemcpyAsync(m->tokens_d, tokens_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    BREW_CUDA(cudaMemcpyAsync(m->pos_d, pos_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    cudaGraphExec_t g;
+    if ((rc = get_graph(m, batch, true, &g))) return rc;
+    BREW_CUDA(cudaGraphLaunch(g, s));
+    if (logits_dev)
+        BREW_CUDA(cudaMemcpyAsync(logits_dev, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, s));
+    if (argmax_dev) BREW_CUDA(cudaMemcpyAsync(argmax_dev, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    if (us) {
+        BREW_CUDA(cudaEventRecord(ev, s));
+        BREW_CUDA(cudaStreamWaitEvent(us, ev));
+        cudaEventDestroy(ev);
+    }
+    return BREW_OK;
+}
+
+int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos, int32_t batch, float* logits,
+                       int32_t* argmax) {
+    BREW_CHECK(m && tokens && pos, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(batch >= 1 && batch <= m->max_batch, BREW_ERR_INVALID_ARG, "batch %d (max %d)", batch, m->max_batch);
+    for (int b = 0; b < batch; ++b) {
+        BREW_CHECK(tokens[b] >= 0 && tokens[b] < m->c.vocab_size, BREW_ERR_INVALID_ARG, "token %d out of range", tokens[b]);
+        BREW_CHECK(pos[b] >= 0, BREW_ERR_INVALID_ARG, "position %d", pos[b]);
+        BREW_CHECK(pos[b] < m->c.seq_len, BREW_ERR_CONTEXT_FULL,
+                   "The session has reached its context limit of %d tokens.", m->c.seq_len);
+    }
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaStream_t s = ctx().stream;
+    int32_t* hp = m->h_pin;
+    memcpy(hp, tokens, batch * sizeof(int32_t));
+    memcpy(hp + batch, pos, batch * sizeof(int32_t));
+    BREW_CUDA(cudaMemcpyAsync(m->tokens_d, hp, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    BREW_CUDA(cudaMemcpyAsync(m->pos_d, hp + batch, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    cudaGraphExec_t g;
+    if ((rc = get_graph(m, batch, true, &g))) return rc;
+    BREW_CUDA(cudaGraphLaunch(g, s));
+    if (logits)
+        BREW_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
+    if (argmax) BREW_CUDA(cudaMemcpyAsync(hp + 2 * batch, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    BREW_CUDA(cudaStreamSynchronize(s));
+    if (argmax) memcpy(argmax, hp + 2 * batch, batch * sizeof(int32_t));
+    return check_device_error("brew_model_forward");
+}
+
+int brew_session_generate(brew_model m, const int32_t* prompt, int32_t n_prompt, int32_t max_new, int32_t* out,
+                          int32_t* n_out) {
+    BREW_CHECK(m && n_out && (prompt || n_prompt == 0), BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(n_prompt >= 0, BREW_ERR_INVALID_ARG, "n_prompt %d", n_prompt);
+    const brew_config& c = m->c;
+    // ensureContextAvailable (runtime/ModelRunner.java:208-216)
+    BREW_CHECK(n_prompt <= c.seq_len, BREW_ERR_CONTEXT_FULL,
+               "The session has reached its context limit of %d tokens.", c.seq_len);
+    for (int i = 0; i < n_prompt; ++i)
+        BREW_CHECK(prompt[i] >= 0 && prompt[i] < c.vocab_size, BREW_ERR_INVALID_ARG, "prompt token %d out of range", prompt[i]);
+    const int remaining = c.seq_len - n_prompt;
+    const int limit = max_new <= 0 ? remaining : std::min(max_new, remaining);
+    BREW_CHECK(limit == 0 || out, BREW_ERR_INVALID_ARG, "out is null");
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaStream_t s = ctx().stream;
+    // prompt (+ the pending token of reset(): BOS) to the device
+    if (m->prompt_cap < n_prompt + 1) {
+        if (m->prompt_d) cudaFree(m->prompt_d);
+        m->prompt_d = nullptr;
+        BREW_CUDA(cudaMalloc(&m->prompt_d, (size_t)(n_prompt + 1) * sizeof(int32_t)));
+        m->prompt_cap = n_prompt + 1;
+    }
+    std::vector<int32_t> staged(prompt, prompt + n_prompt);
+    staged.push_back(c.bos_token);
+    BREW_CUDA(cudaMemcpyAsync(m->prompt_d, staged.data(), staged.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    cudaGraphExec_t g_pre = nullptr, g_full = nullptr;
+    if (n_prompt > 0 && (rc = get_graph(m, 1, false, &g_pre))) return rc;
+    if ((rc = get_graph(m, 1, true, &g_full))) return rc;
+    // prefill (ModelRunner.java:196-206): forward(tok_i, i); the logits of
+    // the prompt positions are never read, so the classifier is skipped
+    for (int i = 0; i < n_prompt; ++i) {
+        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, m->prompt_d + i, i, nullptr, m->am_out);
+        count_launch();
+        BREW_CUDA(cudaGraphLaunch(g_pre, s));
+    }
+    // decode (:141-152): the pending token is the last prompt token (or BOS)
+    // forwarded at position n_prompt, then each argmax at the next position
+    const int32_t* pending0 = n_prompt > 0 ? m->prompt_d + n_prompt - 1 : m->prompt_d + n_prompt;
+    for (int k = 0; k < limit; ++k) {
+        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, k == 0 ? pending0 : m->am_out, n_prompt + k,
+                                     k == 0 ? nullptr : m->gen_d + k - 1, m->am_out);
+        count_launch();
+        BREW_CUDA(cudaGraphLaunch(g_full, s));
+    }
+    if (limit > 0) {
+        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, m->am_out, 0, m->gen_d + limit - 1, m->am_out);
+        count_launch();
+    }
+    BREW_CUDA(cudaGetLastError());
+    std::vector<int32_t> gen(limit);
+    if (limit > 0) BREW_CUDA(cudaMemcpyAsync(gen.data(), m->gen_d, limit * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    BREW_CUDA(cudaStreamSynchronize(s));
+    rc = check_device_error("brew_session_generate");
+    if (rc) return rc;
+    // stop at the first EOS, inclusive (:149-151)
+    int n = 0;
+    for (; n < limit; ++n) {
+        out[n] = gen[n];
+        if (gen[n] == c.eos_token) {
+            ++n;
+            break;
+        }
+    }
+    *n_out = n;
+    return BREW_OK;
+}
+
+}  // extern "C"

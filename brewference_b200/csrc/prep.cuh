@@ -1,0 +1,113 @@
+// prep.cuh — activation "prep records": the operand format the quantized
+// matvec consumes on the x side.
+//
+// A matvec against GGUF blocks needs, per 32-element block j of x, the dot
+// product sum_i q[r][32j+i] * x[32j+i].  x is fp32; the tensor cores only
+// multiply integers exactly.  So each 32-element block of x is rewritten as
+// a 24-bit block fixed-point number v_i = rint(x_i * 8290000 / max|x_block|)
+// and v_i is split into three balanced signed bytes
+//     v = hi * 2^16 + mid * 2^8 + lo,   hi, mid, lo in [-128, 127].
+// With those three "limb" columns as the B operand of an int8 MMA, the
+// per-block integer sums are exact; the fp32 epilogue multiplies them by the
+// block's fp16 weight scale and s_j * 2^16 / 2^8 / 1.  The x rounding error is
+// 2^-24 relative to the block maximum, i.e. at the level of fp32 itself.
+//
+// Record of block j (NCOL = 3*batch columns, column n = 3*b + l for batch
+// element b and limb l), padded to a multiple of 16 bytes:
+//     int8   limbs[NCOL][32]
+//     float  sw[NCOL]      s_b * {65536, 256, 1}[l]
+//     int32  lsum[NCOL]    sum_i limbs[n][i]   (zero-point correction, Q4_0)
+#pragma once
+
+#include "brew_common.cuh"
+
+namespace brew {
+
+constexpr float PREP_RANGE = 8290000.0f;   // |v| <= 8290001 keeps hi in [-127, 127]
+
+__host__ __device__ inline int prep_nt(int batch) { return (3 * batch + 7) / 8; }
+__host__ __device__ inline int prep_rec_bytes(int batch) { return (3 * batch * 40 + 15) & ~15; }
+
+#ifdef __CUDACC__
+
+// One warp writes the record columns of batch element b for one block:
+// lane i holds x[32j + i].
+__device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int ncol, int b, float x) {
+    const int lane = threadIdx.x & 31;
+    const float amax = warp_max(fabsf(x));
+    const float inv = amax > 0.0f ? PREP_RANGE / amax : 0.0f;
+    const float s = amax / PREP_RANGE;
+    const int v = __float2int_rn(x * inv);
+    const int lo = ((v + 128) & 255) - 128;
+    const int v1 = (v - lo) >> 8;
+    const int mid = ((v1 + 128) & 255) - 128;
+    const int hi = (v1 - mid) >> 8;
+    int8_t* limbs = reinterpret_cast<int8_t*>(rec);
+    limbs[(3 * b + 0) * 32 + lane] = (int8_t)hi;
+    limbs[(3 * b + 1) * 32 + lane] = (int8_t)mid;
+    limbs[(3 * b + 2) * 32 + lane] = (int8_t)lo;
+    const int shi = warp_sum_i(hi), smid = warp_sum_i(mid), slo = warp_sum_i(lo);
+    if (lane == 0) {
+        float* sw = reinterpret_cast<float*>(rec + ncol * 32);
+        int* ls = reinterpret_cast<int*>(rec + ncol * 36);
+        sw[3 * b + 0] = s * 65536.0f;
+        sw[3 * b + 1] = s * 256.0f;
+        sw[3 * b + 2] = s;
+        ls[3 * b + 0] = shi;
+        ls[3 * b + 1] = smid;
+        ls[3 * b + 2] = slo;
+    }
+}
+
+// Block-wide sum (all threads of the CTA call it; red has >= 32 floats).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    if (warp == 0) {
+        t = lane < nw ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[0] = t;
+    }
+    __syncthreads();
+    t = red[0];
+    __syncthreads();
+    return t;
+}
+
+// inverseRootMeanSquare (transformer/math/Kernels.java:77-88): the sum of
+// squares in fp32, meanSquare = ss / n in fp32, then 1/sqrt in double.
+__device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
+    const float meanSquare = ss / (float)n;
+    return (float)(1.0 / sqrt((double)(meanSquare + eps)));
+}
+
+// Whole-CTA prep of one vector x[K] (read through L2: it may have been
+// written by other CTAs of the same kernel) (optionally RMS-normalised with weight
+// nw: x * scale * nw, Kernels.java:47-58) into records[K/32].
+static __device__ void prep_vector_cta(const float* x, int K, const float* nw, float eps, uint8_t* recs, int rec_bytes,
+                                int ncol, int b, float* red) {
+    float scale = 1.0f;
+    if (nw) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float v = __ldcg(&x[i]);
+            ss += v * v;
+        }
+        ss = block_sum(ss, red);
+        scale = rms_scale(ss, K, eps);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw_ = blockDim.x >> 5;
+    for (int j = warp; j < K / 32; j += nw_) {
+        float v = __ldcg(&x[32 * j + lane]);
+        if (nw) v = v * scale * nw[32 * j + lane];
+        prep_emit_warp(recs + (size_t)j * rec_bytes, ncol, b, v);
+    }
+}
+
+#endif
+
+}  // namespace brew

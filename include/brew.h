@@ -1,0 +1,252 @@
+/*
+ * brew.h — C ABI of the B200 quantized-matmul path of brewference.
+ *
+ * Every entry point here replaces one piece of the reference's Java hot path
+ * (paths relative to src/main/java/com/epicmonstrosity/brewference/ of the
+ * reference).  The signatures use plain pointers, sizes and POD structs so a
+ * JNI glue file (Java 8 has no Panama), ctypes or C++ can bind them directly.
+ *
+ * Conventions
+ *   - Every function returns an int status: BREW_OK (0) or a negative
+ *     BREW_ERR_* code.  brew_last_error() returns the message of the last
+ *     failure on the calling thread.  The JNI glue maps
+ *       BREW_ERR_INVALID_ARG   -> IllegalArgumentException  (Linear.java:67-74)
+ *       BREW_ERR_OUT_OF_BOUNDS -> IllegalStateException     (Linear.java:46-50)
+ *       BREW_ERR_CONTEXT_FULL  -> IllegalStateException     (runtime/ModelRunner.java:208-216)
+ *       BREW_ERR_IO            -> IOException               (gguf/GgufWeightsLoader.java:76-78,251-253)
+ *     and everything else to IllegalStateException.
+ *   - Weight tensors are uploaded as the GGUF bytes, unchanged: 34-byte Q8_0,
+ *     18-byte Q4_0, 144-byte Q4_K and 210-byte Q6_K blocks, rows of `cols`
+ *     elements.  Element offsets (the reference's `weightsOffset`) are
+ *     converted to block offsets on the device side.
+ *   - Host pointers are plain host memory; functions with a _dev suffix take
+ *     device pointers and a cudaStream_t passed as void*.
+ */
+#ifndef BREW_H
+#define BREW_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BREW_API __attribute__((visibility("default")))
+#else
+#define BREW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define BREW_OK                 0
+#define BREW_ERR_INVALID_ARG   -1
+#define BREW_ERR_OUT_OF_BOUNDS -2
+#define BREW_ERR_CUDA          -3
+#define BREW_ERR_NCCL          -4
+#define BREW_ERR_TIMEOUT       -5
+#define BREW_ERR_CONTEXT_FULL  -6
+#define BREW_ERR_UNSUPPORTED   -7
+#define BREW_ERR_IO            -8
+#define BREW_ERR_NO_DEVICE     -9
+
+/* ---- GGML tensor type ids (gguf/Reader.java:67-81 reads them as `type`) -- */
+#define BREW_TYPE_F32   0
+#define BREW_TYPE_F16   1
+#define BREW_TYPE_Q4_0  2
+#define BREW_TYPE_Q8_0  8
+#define BREW_TYPE_Q4_K 12
+#define BREW_TYPE_Q6_K 14
+
+/* ---- architectures (model/ModelRunnerFactory.java:23-49) ---------------- */
+#define BREW_ARCH_LLAMA  0   /* model/llama2/Llama2Transformer.java:27-79   */
+#define BREW_ARCH_QWEN2  1   /* model/qwen2/Qwen2Transformer.java:27-84     */
+#define BREW_ARCH_QWEN3  2   /* model/qwen3/Qwen3Transformer.java:27-85     */
+#define BREW_ARCH_GEMMA3 3   /* model/gemma3/Gemma3Transformer.java:27-92   */
+
+/* Model hyper-parameters: the fields of gguf/Config.java that the forward
+ * pass reads (GgufConfigParser.java:9-59), plus the GGML type of each weight
+ * matrix.  `rope_base` <= 0 selects the architecture's fallback exactly as the
+ * reference's suppliers do (Llama2Transformer.java:45 -> 1e4,
+ * Qwen2/Qwen3 -> 1e6, Gemma3Transformer.java:51 -> 1e6 global / 1e4 local). */
+typedef struct brew_config {
+    int32_t arch;
+    int32_t dim;             /* {arch}.embedding_length                      */
+    int32_t hidden_dim;      /* {arch}.feed_forward_length                   */
+    int32_t n_layers;        /* {arch}.block_count                           */
+    int32_t n_heads;         /* {arch}.attention.head_count                  */
+    int32_t n_kv_heads;      /* {arch}.attention.head_count_kv               */
+    int32_t head_size;       /* Config.getHeadSize (Qwen3 128, Gemma3 256)   */
+    int32_t vocab_size;      /* size of tokenizer.ggml.tokens                */
+    int32_t seq_len;         /* {arch}.context_length                        */
+    int32_t sliding_window;  /* {arch}.attention.sliding_window (Gemma3)     */
+    float   eps;             /* {arch}.attention.layer_norm_rms_epsilon      */
+    float   rope_base;       /* {arch}.rope.freq_base (<= 0: arch fallback)  */
+    float   rope_scale;      /* Config.ropeFrequencyScale (<= 0: 1.0)        */
+    int32_t bos_token;
+    int32_t eos_token;
+    int32_t tied_embeddings; /* 1: classifier = token_embd (GgufWeightsLoader.java:159-162) */
+    /* GGML type of each weight matrix family */
+    int32_t type_embed, type_output;
+    int32_t type_q, type_k, type_v, type_o;
+    int32_t type_gate, type_up, type_down;
+} brew_config;
+
+/* ---- errors, devices ---------------------------------------------------- */
+
+/* Copies the calling thread's last error message into buf (NUL-terminated).
+ * Returns the message length. */
+BREW_API int brew_last_error(char* buf, size_t buf_size);
+
+/* Selects and initialises a CUDA device for the calling process.  Fails with
+ * BREW_ERR_NO_DEVICE when no device is visible: there is no CPU fallback. */
+BREW_API int brew_init(int device);
+
+/* Library version string and the number of kernels this library launched so
+ * far on this process (all kinds). */
+BREW_API const char* brew_version(void);
+BREW_API int64_t brew_kernel_launches(void);
+
+/* ---- weight tensors (gguf/GgufWeightsLoader.java:228-247 readQ8Block) ---- */
+
+typedef struct brew_tensor_s* brew_tensor;
+
+/* Bytes that `n_elements` of GGML type `type` occupy on disk (and in HBM). */
+BREW_API int64_t brew_type_bytes(int type, int64_t n_elements);
+BREW_API int brew_type_block(int type, int* block_elements, int* block_bytes);
+
+/* Uploads packed GGUF bytes unchanged to HBM.  Replaces readQ8Block +
+ * concatenateQ8Blocks (GgufWeightsLoader.java:167-185,228-247): per-layer
+ * tensors are uploaded one after another into one tensor so that the
+ * reference's element offsets `layer*in*out` stay valid.  n_elements must be
+ * a multiple of the type's block size (GgufWeightsLoader.java:229-231). */
+BREW_API int brew_tensor_upload(int type, const void* bytes, int64_t n_elements, brew_tensor* out);
+/* Appends more packed bytes at element offset `elem_offset` of an existing
+ * tensor created with brew_tensor_alloc (for layer-by-layer loading). */
+BREW_API int brew_tensor_alloc(int type, int64_t n_elements, brew_tensor* out);
+BREW_API int brew_tensor_write(brew_tensor t, int64_t elem_offset, const void* bytes, int64_t n_elements);
+BREW_API int brew_tensor_free(brew_tensor t);
+BREW_API int brew_tensor_info(brew_tensor t, int* type, int64_t* n_elements, int64_t* n_bytes);
+/* Copies the packed bytes of elements [elem_offset, elem_offset + n) back to
+ * host memory (whole blocks). */
+BREW_API int brew_tensor_read(brew_tensor t, int64_t elem_offset, int64_t n_elements, void* bytes);
+/* Device address of the packed bytes (for callers that launch their own work). */
+BREW_API int brew_tensor_device_ptr(brew_tensor t, void** dev_ptr);
+
+/* Dequantizes `n` elements starting at element `row_offset` into host fp32
+ * `out`.  Bit-exact with QuantizedWeights.dequantizeRow
+ * (gguf/QuantizedWeights.java:76-85) for Q8_0 and with the GGML definitions
+ * for Q4_0 / Q4_K / Q6_K. */
+BREW_API int brew_dequantize_row(brew_tensor t, int64_t row_offset, int64_t n, float* out);
+BREW_API int brew_dequantize_row_dev(brew_tensor t, int64_t row_offset, int64_t n, float* out_dev, void* stream);
+
+/* ---- the hot path: Linear.matmul (transformer/math/Linear.java:40-65) --- */
+
+/* output[row] = sum_k W[weights_offset + row*input_size + k] * input[k]
+ * for row < output_size, with host fp32 arrays — the drop-in for
+ * Linear.matmul(output, input, weights, weightsOffset, inputSize, outputSize).
+ * Errors: BREW_ERR_INVALID_ARG for null arrays/tensor (Linear.java:67-74) or
+ * an input_size that is not a whole number of blocks; BREW_ERR_OUT_OF_BOUNDS
+ * when the last block read lies past the tensor (Linear.java:46-50). */
+BREW_API int brew_matmul(float* output, const float* input, brew_tensor weights,
+                int64_t weights_offset, int32_t input_size, int32_t output_size);
+
+/* Batched form: `batch` input vectors [batch][input_size] -> outputs
+ * [batch][output_size], device pointers, on `stream` (0 = default). */
+BREW_API int brew_matmul_dev(float* output_dev, const float* input_dev, brew_tensor weights,
+                    int64_t weights_offset, int32_t input_size, int32_t output_size,
+                    int32_t batch, void* stream);
+
+/* Two-step form for callers that multiply one input by several matrices
+ * (Q, K and V share their input): brew_prepare_input_dev writes the
+ * quantized-activation records of x [batch][input_size] into `prep_dev`
+ * (brew_prep_bytes(input_size, batch) bytes, 16-byte aligned), and
+ * brew_matmul_prepared_dev multiplies a Q8_0 or Q4_0 tensor by them. */
+BREW_API int64_t brew_prep_bytes(int32_t input_size, int32_t batch);
+BREW_API int brew_prepare_input_dev(const float* input_dev, int32_t input_size, int32_t batch, void* prep_dev,
+                                    void* stream);
+BREW_API int brew_matmul_prepared_dev(float* output_dev, const void* prep_dev, brew_tensor weights,
+                                      int64_t weights_offset, int32_t input_size, int32_t output_size,
+                                      int32_t batch, void* stream);
+
+/* ---- device-resident model (TransformerGraph.forward, ModelRunner) ------ */
+
+typedef struct brew_model_s* brew_model;
+
+/* Per-layer weights of a model, as packed tensors whose layers are
+ * concatenated like QuantizedWeights (gguf/QuantizedWeights.java:37-60).
+ * Norm and bias vectors are host fp32 arrays concatenated over layers
+ * (GgufWeightsLoader.java:170-179); they are copied to the device.  Unused
+ * entries are NULL (e.g. biases outside Qwen2, post norms outside Gemma3). */
+typedef struct brew_model_weights {
+    brew_tensor token_embd, output;               /* output may be NULL when tied */
+    brew_tensor wq, wk, wv, wo, w_gate, w_up, w_down;
+    const float* rms_att;       /* [n_layers*dim]       */
+    const float* rms_ffn;       /* [n_layers*dim]       */
+    const float* rms_final;     /* [dim]                */
+    const float* post_att;      /* [n_layers*dim]  Gemma3 */
+    const float* post_ffn;      /* [n_layers*dim]  Gemma3 */
+    const float* rms_q;         /* [n_layers*head_size] Qwen3/Gemma3 */
+    const float* rms_k;         /* [n_layers*head_size] */
+    const float* q_bias;        /* [n_layers*n_heads*head_size] Qwen2 */
+    const float* k_bias;        /* [n_layers*kv_dim]    */
+    const float* v_bias;        /* [n_layers*kv_dim]    */
+} brew_model_weights;
+
+/* Creates a device-resident model with room for `max_batch` concurrent
+ * sequences (each with its own fp32 KV cache of n_layers*seq_len*kv_dim,
+ * RunStateAllocator.java:48-70). */
+BREW_API int brew_model_create(const brew_config* cfg, const brew_model_weights* w,
+                      int32_t max_batch, brew_model* out);
+
+/* Creates a model whose weights are generated on the device from `seed`
+ * (seeded N(0, 0.02) quantized to the configured GGML types, norms 1.0).
+ * The bytes equal those of the CPU generator used by the tests. */
+BREW_API int brew_model_synthesize(const brew_config* cfg, uint64_t seed, int32_t max_batch, brew_model* out);
+BREW_API int brew_model_free(brew_model m);
+/* Returns the model's tensors (borrowed handles) for inspection. */
+BREW_API int brew_model_tensor(brew_model m, int which, brew_tensor* out);
+
+/* One decode step of TransformerGraph.forward(token, pos, ...) for `batch`
+ * sequences (host arrays tokens[batch], pos[batch]).  Either output may be
+ * NULL: logits [batch][vocab] (host fp32) and/or argmax ids [batch] computed
+ * on the device with Kernels.argMax semantics (lowest index on ties,
+ * transformer/math/Kernels.java:150-162). */
+BREW_API int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos,
+                       int32_t batch, float* logits, int32_t* argmax);
+
+/* Device-pointer form for callers that keep tokens/positions/results resident. */
+BREW_API int brew_model_forward_dev(brew_model m, const int32_t* tokens_dev, const int32_t* pos_dev,
+                           int32_t batch, float* logits_dev, int32_t* argmax_dev, void* stream);
+
+/* Greedy generation for one sequence, with the token feeding order of
+ * GenericModelSession.generate/prefill (runtime/ModelRunner.java:122-206):
+ * each prompt token is forwarded at its position; then the last prompt token
+ * is forwarded again at position n_prompt, and each generated token is fed
+ * back at the next position; stops at eos or after
+ * min(max_new_tokens, seq_len - n_prompt) tokens.  `out_tokens` receives the
+ * generated ids; *n_out their count.  BREW_ERR_CONTEXT_FULL when the prompt
+ * does not fit (ModelRunner.java:208-216). */
+BREW_API int brew_session_generate(brew_model m, const int32_t* prompt, int32_t n_prompt,
+                          int32_t max_new_tokens, int32_t* out_tokens, int32_t* n_out);
+
+/* The two halves of brew_session_generate for callers that time or drive
+ * them separately.  brew_session_prefill resets the session and forwards
+ * prompt[i] at position i (the classifier is skipped: prompt logits are never
+ * read).  brew_session_decode then runs `n_steps` greedy steps from the
+ * session's pending token and position, enqueued on `stream` (NULL: the
+ * library stream) without host synchronisation; when `out_tokens` is not NULL
+ * it synchronises and copies the generated ids there. */
+BREW_API int brew_session_prefill(brew_model m, const int32_t* prompt, int32_t n_prompt, void* stream);
+BREW_API int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out_tokens, void* stream);
+/* Kernels in one decode step's CUDA graph (for launch accounting). */
+BREW_API int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n_kernels);
+
+/* Clears the sequence state (ModelSession.reset, ModelRunner.java:115-120). */
+BREW_API int brew_model_reset(brew_model m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BREW_H */
