@@ -105,6 +105,12 @@ def lib():
         "brew_model_forward_dev": (I, [V, V, V, ctypes.c_int32, V, V, V]),
         "brew_session_generate": (I, [V, c_i32p, ctypes.c_int32, ctypes.c_int32, c_i32p, c_i32p]),
         "brew_model_reset": (I, [V]),
+        "brew_session_prefill": (I, [V, c_i32p, ctypes.c_int32, V]),
+        "brew_session_decode": (I, [V, ctypes.c_int32, c_i32p, V]),
+        "brew_model_step_kernels": (I, [V, ctypes.c_int32, c_i32p]),
+        "brew_prep_bytes": (I64, [ctypes.c_int32, ctypes.c_int32]),
+        "brew_prepare_input_dev": (I, [V, ctypes.c_int32, ctypes.c_int32, V, V]),
+        "brew_matmul_prepared_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

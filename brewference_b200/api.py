@@ -112,6 +112,20 @@ class Linear:
                 "Linear.matmul")
 
     @staticmethod
+    def prep_bytes(input_size: int, batch: int = 1) -> int:
+        return int(N.lib().brew_prep_bytes(input_size, batch))
+
+    @staticmethod
+    def prepare_input_device(x_ptr: int, input_size: int, batch: int, prep_ptr: int, stream: int = 0) -> None:
+        N.check(N.lib().brew_prepare_input_dev(x_ptr, input_size, batch, prep_ptr, stream or None), "prepare_input")
+
+    @staticmethod
+    def matmul_prepared_device(y_ptr: int, prep_ptr: int, weights: PackedTensor, weights_offset: int, input_size: int,
+                               output_size: int, batch: int = 1, stream: int = 0) -> None:
+        N.check(N.lib().brew_matmul_prepared_dev(y_ptr, prep_ptr, weights.handle, weights_offset, input_size,
+                                                 output_size, batch, stream or None), "matmul_prepared")
+
+    @staticmethod
     def matmul_device(y_ptr: int, x_ptr: int, weights: PackedTensor, weights_offset: int, input_size: int,
                       output_size: int, batch: int = 1, stream: int = 0) -> None:
         """Device-pointer, batched form (x [batch][input_size] -> y [batch][output_size])."""
@@ -185,6 +199,24 @@ class DeviceModel:
         N.check(N.lib().brew_session_generate(self.handle, _i32(pr), pr.size, max_new_tokens, _i32(out),
                                               ctypes.byref(n)), "generate")
         return out[: n.value].tolist()
+
+    def prefill(self, prompt, stream: int = 0) -> None:
+        """GenericModelSession.prefill from a reset session."""
+        pr = np.ascontiguousarray(prompt, np.int32)
+        N.check(N.lib().brew_session_prefill(self.handle, _i32(pr), pr.size, stream or None), "prefill")
+
+    def decode(self, n_steps: int, stream: int = 0, want_tokens: bool = True):
+        """n greedy decode steps from the session state; returns the ids
+        (synchronising) or None (enqueue only, on `stream`)."""
+        out = np.empty(max(n_steps, 1), np.int32) if want_tokens else None
+        N.check(N.lib().brew_session_decode(self.handle, n_steps, _i32(out) if want_tokens else None, stream or None),
+                "decode")
+        return out[:n_steps].tolist() if want_tokens else None
+
+    def step_kernels(self, batch: int = 1) -> int:
+        n = ctypes.c_int32()
+        N.check(N.lib().brew_model_step_kernels(self.handle, batch, ctypes.byref(n)))
+        return n.value
 
     def reset(self):
         N.check(N.lib().brew_model_reset(self.handle), "reset")

@@ -138,13 +138,9 @@ int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const fl
     return BREW_OK;
 }
 
-constexpr size_t SCRATCH_COUNTER_BYTES = 4096;
-size_t scratch_fixed_bytes() {
-    return SCRATCH_COUNTER_BYTES + ((mv_part_floats(num_sms(), MV_MAX_BATCH) * sizeof(float) + 255) & ~size_t(255));
-}
-
 // Runs one matvec (any supported type) on device buffers: the shared core of
-// brew_matmul / brew_matmul_dev.
+// brew_matmul / brew_matmul_dev.  The prep records of x live in a growable
+// scratch buffer of the context.
 int run_matvec(brew_tensor t, int64_t weights_offset, const float* x_dev, int K, int N, float* y_dev, int batch,
                cudaStream_t stream) {
     TypeInfo ti;
@@ -156,46 +152,35 @@ int run_matvec(brew_tensor t, int64_t weights_offset, const float* x_dev, int K,
     Context& c = g_ctx;
     for (int b0 = 0; b0 < batch; b0 += MV_MAX_BATCH) {
         const int nb = std::min(MV_MAX_BATCH, batch - b0);
-        const int KB = K / 32;
-        // fixed layout [counters][stream-K parts][prep records]: the counters
-        // are zero between launches (each launch resets what it used), so
-        // they must not share bytes with anything whose size varies per call
-        const size_t prep_bytes = (size_t)KB * prep_rec_bytes(nb);
-        int rc = c.mv_scratch.reserve(scratch_fixed_bytes() + prep_bytes);
+        const size_t prep_bytes = (size_t)(K / 32) * prep_rec_bytes(nb);
+        int rc = c.mv_scratch.reserve(prep_bytes + 256);
         if (rc) return rc;
-        uint8_t* base = static_cast<uint8_t*>(c.mv_scratch.ptr);
-        int* ctr = reinterpret_cast<int*>(base);
-        float* part = reinterpret_cast<float*>(base + SCRATCH_COUNTER_BYTES);
-        uint8_t* prep = base + scratch_fixed_bytes();
+        uint8_t* prep = static_cast<uint8_t*>(c.mv_scratch.ptr);
         rc = prep_launch(x_dev + (int64_t)b0 * K, K, K, nb, nullptr, 0.0f, prep, stream, false);
         if (rc) return rc;
-        rc = launch_prepared(t, w, row_bytes, prep, part, ctr, K, N, y_dev + (int64_t)b0 * N, nb, stream);
+        rc = launch_prepared(t, w, row_bytes, prep, K, N, y_dev + (int64_t)b0 * N, nb, stream);
         if (rc) return rc;
     }
     return BREW_OK;
 }
 
-int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const uint8_t* prep, float* part, int* ctr,
-                    int K, int N, float* y, int nb, cudaStream_t stream) {
-    {
-        MvParams p = {};
-        p.nseg = 1;
-        p.seg[0].w = w;
-        p.seg[0].y = y;
-        p.seg[0].rows = N;
-        p.type = t->type;
-        p.K = K;
-        p.row_bytes = row_bytes;
-        p.batch = nb;
-        p.ldy = N;
-        p.epi = MV_EPI_STORE;
-        p.prep = prep;
-        p.part_buf = part;
-        p.tile_counters = ctr;
-        p.post = MV_POST_NONE;
-        p.err = g_ctx.err_word;
-        return mv_launch(p, stream, false);
-    }
+int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const uint8_t* prep, int K, int N, float* y,
+                    int nb, cudaStream_t stream) {
+    MvParams p = {};
+    p.nseg = 1;
+    p.seg[0].w = w;
+    p.seg[0].y = y;
+    p.seg[0].rows = N;
+    p.type = t->type;
+    p.K = K;
+    p.row_bytes = row_bytes;
+    p.batch = nb;
+    p.ldy = N;
+    p.epi = MV_EPI_STORE;
+    p.prep = prep;
+    p.post = MV_POST_NONE;
+    p.err = g_ctx.err_word;
+    return mv_launch(p, stream, false);
 }
 
 int run_matvec_prepared(brew_tensor t, int64_t weights_offset, const uint8_t* prep, int K, int N, float* y, int batch,
@@ -204,11 +189,7 @@ int run_matvec_prepared(brew_tensor t, int64_t weights_offset, const uint8_t* pr
     type_info(t->type, &ti);
     const int64_t row_bytes = (int64_t)K / ti.block_elems * ti.block_bytes;
     const uint8_t* w = t->d + weights_offset / ti.block_elems * ti.block_bytes;
-    int rc = g_ctx.pp_scratch.reserve(scratch_fixed_bytes());
-    if (rc) return rc;
-    int* ctr = static_cast<int*>(g_ctx.pp_scratch.ptr);
-    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(g_ctx.pp_scratch.ptr) + SCRATCH_COUNTER_BYTES);
-    return launch_prepared(t, w, row_bytes, prep, part, ctr, K, N, y, batch, stream);
+    return launch_prepared(t, w, row_bytes, prep, K, N, y, batch, stream);
 }
 
 }  // namespace brew

@@ -20,6 +20,8 @@ namespace brew {
 
 namespace {
 
+constexpr int ATTN_MIN_CHUNK = 64;
+
 __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnParams p, int cap) {
     extern __shared__ float sm[];
     const int hk = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
@@ -34,6 +36,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     float* sn = cs + half;           // [half]
     float* wc = sn + half;           // [G][nchunk]
     __shared__ int s_last;
+    __shared__ float s_m[16], s_l[16];
 
     pdl_launch_dependents();
     pdl_wait();
@@ -45,10 +48,18 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     }
     const int start = p.window > 0 ? max(0, pos - p.window + 1) : 0;
     const int len = pos - start + 1;
-    const int per = (len + p.nchunk - 1) / p.nchunk;
+    // at least ATTN_MIN_CHUNK positions per CTA: short contexts use few
+    // chunks (the others only check in), long ones spread over all
+    const int per = max(ATTN_MIN_CHUNK, (len + p.nchunk - 1) / p.nchunk);
+    const int used = (len + per - 1) / per;
     const int p0 = start + c * per;
     const int p1 = min(pos + 1, p0 + per);
-    const int n = max(0, p1 - p0);
+    const int n = min(cap, max(0, p1 - p0));   // per <= cap by construction
+    const int stride = hd + 2;
+    float* pbase = p.part + ((int64_t)b * p.n_heads + (int64_t)hk * G) * p.nchunk * stride;
+    int* ctr = &p.counters[b * p.n_kv + hk];
+    if (c >= used) goto arrive;
+    {
 
     // RoPE table for this position (RopeCache.precomputeAngles)
     const float posf = (float)pos * p.rope_scale;
@@ -112,7 +123,6 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     }
     __syncthreads();
     // chunk-local softmax numerators
-    __shared__ float s_m[16], s_l[16];
     for (int h = warp; h < G; h += 4) {
         float m = -INFINITY;
         for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[h * cap + t]);
@@ -127,8 +137,6 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
         if (lane == 0) { s_m[h] = m; s_l[h] = l; }
     }
     __syncthreads();
-    const int stride = hd + 2;
-    float* pbase = p.part + ((int64_t)b * p.n_heads + (int64_t)hk * G) * p.nchunk * stride;
     for (int idx = tid; idx < G * hd; idx += blockDim.x) {
         const int h = idx / hd, i = idx % hd;
         float acc = 0.0f;
@@ -139,21 +147,22 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
         __stcg(&pbase[((int64_t)tid * p.nchunk + c) * stride + 0], n > 0 ? s_m[tid] : -INFINITY);
         __stcg(&pbase[((int64_t)tid * p.nchunk + c) * stride + 1], n > 0 ? s_l[tid] : 0.0f);
     }
+    }
+arrive:
     __threadfence();
     __syncthreads();
-    int* ctr = &p.counters[b * p.n_kv + hk];
     if (tid == 0) s_last = (atomicAdd(ctr, 1) == p.nchunk - 1);
     __syncthreads();
     if (!s_last) return;
     __threadfence();
 
-    // combine chunks in order
+    // combine the used chunks in order
     for (int h = warp; h < G; h += 4) {
         float M = -INFINITY;
-        for (int k = lane; k < p.nchunk; k += 32) M = fmaxf(M, __ldcg(&pbase[((int64_t)h * p.nchunk + k) * stride]));
+        for (int k = lane; k < used; k += 32) M = fmaxf(M, __ldcg(&pbase[((int64_t)h * p.nchunk + k) * stride]));
         M = warp_max(M);
         float L = 0.0f;
-        for (int k = lane; k < p.nchunk; k += 32) {
+        for (int k = lane; k < used; k += 32) {
             const float mk = __ldcg(&pbase[((int64_t)h * p.nchunk + k) * stride]);
             const float w = mk == -INFINITY ? 0.0f : expf(mk - M);
             wc[h * p.nchunk + k] = w;
@@ -165,11 +174,19 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     __syncthreads();
     for (int idx = tid; idx < G * hd; idx += blockDim.x) {
         const int h = idx / hd, i = idx % hd;
+        const float* src = pbase + (int64_t)h * p.nchunk * stride + 2 + i;
+        const float* wh = wc + h * p.nchunk;
         float o = 0.0f;
-        for (int k = 0; k < p.nchunk; ++k) {
-            const float w = wc[h * p.nchunk + k];
-            if (w != 0.0f) o += w * __ldcg(&pbase[((int64_t)h * p.nchunk + k) * stride + 2 + i]);
+        int k = 0;
+        for (; k + 4 <= used; k += 4) {   // independent loads in flight
+            const float v0 = __ldcg(src + (int64_t)k * stride), v1 = __ldcg(src + (int64_t)(k + 1) * stride);
+            const float v2 = __ldcg(src + (int64_t)(k + 2) * stride), v3 = __ldcg(src + (int64_t)(k + 3) * stride);
+            o += wh[k] * v0;
+            o += wh[k + 1] * v1;
+            o += wh[k + 2] * v2;
+            o += wh[k + 3] * v3;
         }
+        for (; k < used; ++k) o += wh[k] * __ldcg(src + (int64_t)k * stride);
         o *= s_l[h];
         qs[idx] = o;
         p.xb[(int64_t)b * p.ldxb + (int64_t)hk * G * hd + idx] = o;
@@ -179,7 +196,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
         const int rec_bytes = prep_rec_bytes(p.batch);
         const int blk0 = hk * G * hd / 32;
         for (int kb = warp; kb < G * hd / 32; kb += 4)
-            prep_emit_warp(p.prep_out + (size_t)(blk0 + kb) * rec_bytes, 3 * p.batch, b, qs[kb * 32 + lane]);
+            prep_emit_warp(p.prep_out + (size_t)(blk0 + kb) * rec_bytes, p.batch, b, qs[kb * 32 + lane]);
     }
     if (tid == 0) *ctr = 0;
 }
@@ -202,7 +219,8 @@ int attn_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
     BREW_CHECK(p.hd % 32 == 0 && p.hd <= 512, BREW_ERR_INVALID_ARG, "attention: head size %d", p.hd);
     const int G = p.n_heads / p.n_kv;
     BREW_CHECK(G <= 16, BREW_ERR_INVALID_ARG, "attention: %d query heads per kv head", G);
-    const int cap = (p.seq_len + p.nchunk - 1) / p.nchunk;
+    // positions one CTA may hold: the kernel uses max(ATTN_MIN_CHUNK, ceil(len / nchunk))
+    const int cap = std::max(ATTN_MIN_CHUNK, (p.seq_len + p.nchunk - 1) / p.nchunk);
     const size_t smem = sizeof(float) * ((size_t)G * p.hd + p.hd + (size_t)G * cap + 32 + p.hd + (size_t)G * p.nchunk);
     BREW_CHECK(smem <= 200 * 1024, BREW_ERR_INVALID_ARG, "attention: %zu bytes of shared memory", smem);
     static bool attr_done = false;

@@ -31,9 +31,8 @@ struct Context {
     int device = -1;
     cudaStream_t stream = nullptr;
     unsigned int* err_word = nullptr;
-    Scratch mv_scratch;   // prep records, stream-K parts, counters of brew_matmul
+    Scratch mv_scratch;   // prep records of brew_matmul / brew_matmul_dev
     Scratch io_scratch;   // staging of brew_matmul / brew_dequantize_row
-    Scratch pp_scratch;   // stream-K parts and counters of brew_matmul_prepared_dev
 };
 
 Context& ctx();
@@ -44,8 +43,8 @@ int run_matvec(brew_tensor t, int64_t weights_offset, const float* x_dev, int K,
                cudaStream_t stream);
 int run_matvec_prepared(brew_tensor t, int64_t weights_offset, const uint8_t* prep, int K, int N, float* y, int batch,
                         cudaStream_t stream);
-int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const uint8_t* prep, float* part, int* ctr,
-                    int K, int N, float* y, int nb, cudaStream_t stream);
+int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const uint8_t* prep, int K, int N, float* y,
+                    int nb, cudaStream_t stream);
 int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K, int N, float* y,
                          int ldy, int batch, cudaStream_t stream, bool pdl);
 

@@ -24,6 +24,8 @@
 #include "matvec.cuh"
 #include "prep.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -86,10 +88,6 @@ __device__ __forceinline__ const uint8_t* tile_row_ptr(const MvParams& p, int ti
     return p.seg[s].w + (int64_t)local * p.row_bytes;
 }
 
-__device__ __forceinline__ int cta_of_unit(int64_t x, int units, int grid) {
-    return (int)(((x + 1) * (int64_t)grid - 1) / units);
-}
-
 __device__ __forceinline__ float act_glu(float g, int epi) {
     // FfnActivation.silu / geluPytorchTanh evaluated in double, cast to float
     // (transformer/ffn/FfnActivation.java:43-58).
@@ -104,64 +102,140 @@ __device__ __forceinline__ float act_glu(float g, int epi) {
     return (float)a;
 }
 
-struct ArgBest {
-    float v;
-    int i;
-};
-
-__device__ __forceinline__ void argbest_update(ArgBest& b, float v, int i) {
-    if (v > b.v || (v == b.v && i < b.i)) { b.v = v; b.i = i; }
+// Orderable 64-bit argmax key: larger value first, then smaller index
+// (Kernels.argMax keeps the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)idx);
 }
 
-// Writes the final values of one tile (vals[16][batch] in shared memory).
-__device__ void tile_epilogue(const MvParams& p, int tile, const float* vals, int ctid, ArgBest& best) {
+// One 16-row x 32-element block: the int8 MMA of the weight fragment against
+// the limb columns of every vector, then acc += C * (d_row * s_vector).  Lane
+// (g, t) holds accumulator columns 8n+2t and 8n+2t+1 of rows g and g+8; both
+// columns belong to vector (8n+2t)/4 (4 columns per vector, see prep.cuh).
+template <int TYPE, int NT>
+__device__ __forceinline__ void mma_block(float (&acc)[NT][4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          float d0, float d1, uint32_t rec, int batch, int g, int t) {
+    const uint32_t soff = prep_s_off(batch), loff = prep_lsum_off(batch);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        const int cB = n * 8 + g, bB = cB >> 2, lB = cB & 3;
+        const bool vB = lB < 3 && bB < batch;
+        const uint32_t ba = rec + (vB ? (3 * bB + lB) * 32 : 0) + 4 * t;
+        uint32_t b0 = lds32(ba), b1 = lds32(ba + 16);
+        if (!vB) b0 = b1 = 0u;
+        const int bC = (n * 8 + 2 * t) >> 2;
+        const int l0 = (2 * t) & 3;               // 0 or 2
+        const bool vC = bC < batch;
+        const int bCs = vC ? bC : 0;
+        int c[4];
+        if (TYPE == BREW_TYPE_Q8_0) {
+            mma_s8s8(c, a0, a1, a2, a3, b0, b1);
+        } else {
+            mma_u8s8(c, a0, a1, a2, a3, b0, b1);
+            // Q4_0 quants are stored as q+8: subtract 8 * sum(limbs)
+            const int ls0 = vC ? (int)lds32(rec + loff + 4 * (3 * bCs + l0)) : 0;
+            const int ls1 = (vC && l0 == 0) ? (int)lds32(rec + loff + 4 * (3 * bCs + 1)) : 0;
+            c[0] -= 8 * ls0;
+            c[1] -= 8 * ls1;
+            c[2] -= 8 * ls0;
+            c[3] -= 8 * ls1;
+        }
+        const float s = vC ? ldsf(rec + soff + 4 * bCs) : 0.0f;
+        const float ds0 = d0 * s, ds1 = d1 * s;
+        acc[n][0] = fmaf((float)c[0], ds0, acc[n][0]);
+        acc[n][1] = fmaf((float)c[1], ds0, acc[n][1]);
+        acc[n][2] = fmaf((float)c[2], ds1, acc[n][2]);
+        acc[n][3] = fmaf((float)c[3], ds1, acc[n][3]);
+    }
+}
+
+__device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xFFFFu))); }
+__device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
+
+// Rows per tile 16; a CTA owns whole tiles [t0, t1).  Group geometry: gs
+// tiles staged together, ws warps per tile (splitting the tile's blocks), nb
+// TMA boxes of `kcb` blocks per tile per stage.
+struct Geom {
+    int gs, ws, nb, KC, nchunks;
+};
+
+__device__ __forceinline__ Geom cta_geom(const MvParams& p, int nt) {
+    Geom g;
+    if (p.mode == MV_MODE_TMA) {
+        g.gs = min(MV_MAX_BOXES, nt);
+        g.ws = g.gs >= 3 ? 2 : (g.gs == 2 ? 4 : 8);
+        const int nbmax = min(p.nb_cap, max(1, MV_MAX_BOXES / g.gs));
+        const int nbox = p.KB / p.kcb;
+        g.nb = 1;
+        for (int d = nbmax; d >= 1; --d)
+            if (nbox % d == 0) { g.nb = d; break; }
+        g.KC = p.kcb * g.nb;
+    } else {
+        g.gs = 1;
+        g.ws = 8;
+        g.nb = 1;
+        g.KC = p.mode == MV_MODE_CONTIG ? p.KB : p.kcb;
+    }
+    g.nchunks = p.KB / g.KC;
+    return g;
+}
+
+// Writes one finished tile: vals are summed over the ws warps of the tile
+// (red slices warp0 .. warp0+ws-1, in order) and the three limb columns.
+template <int NTC>
+__device__ void tile_out(const MvParams& p, int tile, const float* red, int warp0, int ws, int lane,
+                         unsigned long long* s_best) {
+    auto V = [&](int r, int b) {
+        // limb columns hi, mid, lo of vector b carry weights 2^16, 2^8, 1
+        float v = 0.0f;
+        for (int s = 0; s < ws; ++s) {
+            const float* rr = red + ((warp0 + s) * 16 + r) * NTC + 4 * b;
+            v += (rr[2] + rr[1] * 256.0f) + rr[0] * 65536.0f;
+        }
+        return v;
+    };
     if (p.epi == MV_EPI_STORE) {
         int s = 0;
         if (p.nseg > 1 && tile >= p.seg[1].tile0) s = 1;
         if (p.nseg > 2 && tile >= p.seg[2].tile0) s = 2;
         const MvSeg& sg = p.seg[s];
         const int rb = (tile - sg.tile0) * MV_TILE_ROWS;
-        for (int idx = ctid; idx < MV_TILE_ROWS * p.batch; idx += 256) {
+        for (int idx = lane; idx < MV_TILE_ROWS * p.batch; idx += 32) {
             const int r = idx & 15, b = idx >> 4;
             const int row = rb + r;
             if (row >= sg.rows) continue;
-            float v = vals[idx];
+            float v = V(r, b);
             if (sg.bias) v = v + sg.bias[row];
             if (sg.resid) v = sg.resid[(int64_t)b * p.ldy + row] + v;
             sg.y[(int64_t)b * p.ldy + row] = v;
-            if (p.post == MV_POST_ARGMAX) argbest_update(best, v, row);
+            if (p.post == MV_POST_ARGMAX) atomicMax(&s_best[b], argmax_key(v, row));
         }
-    } else {
-        const int i0 = (tile - p.seg[0].tile0) * 8;
-        for (int idx = ctid; idx < 8 * p.batch; idx += 256) {
-            const int r = idx & 7, b = idx >> 3;
-            const int i = i0 + r;
-            if (i >= p.seg[0].rows) continue;
-            const float g = vals[b * 16 + r], u = vals[b * 16 + 8 + r];
-            p.seg[0].y[(int64_t)b * p.ldy + i] = act_glu(g, p.epi) * u;
-        }
-        if (p.next_prep) {
-            // when all four tiles of a 32-wide group are written, emit the
-            // group's prep record for the next matvec
-            __shared__ int s_last;
+        return;
+    }
+    const int i0 = (tile - p.seg[0].tile0) * 8;
+    for (int idx = lane; idx < 8 * p.batch; idx += 32) {
+        const int r = idx & 7, b = idx >> 3;
+        const int i = i0 + r;
+        if (i >= p.seg[0].rows) continue;
+        p.seg[0].y[(int64_t)b * p.ldy + i] = act_glu(V(r, b), p.epi) * V(r + 8, b);
+    }
+    if (p.next_prep) {
+        // the fourth tile of a 32-wide group to finish emits its prep record
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        const int group = i0 >> 5;
+        if (lane == 0) last = atomicAdd(&p.group_counters[group], 1) == 3;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
             __threadfence();
-            consumer_bar();
-            const int group = i0 >> 5;
-            if (ctid == 0) {
-                const int old = atomicAdd(&p.group_counters[group], 1);
-                s_last = (old == 3);
+            for (int b = 0; b < p.batch; ++b) {
+                const float v = __ldcg(&p.seg[0].y[(int64_t)b * p.ldy + group * 32 + lane]);
+                prep_emit_warp(p.next_prep + (size_t)group * p.rec_bytes, p.batch, b, v);
             }
-            consumer_bar();
-            if (s_last) {
-                __threadfence();
-                const int warp = ctid >> 5, lane = ctid & 31;
-                const int ncol = 3 * p.batch;
-                for (int b = warp; b < p.batch; b += MV_CONSUMER_WARPS) {
-                    const float v = __ldcg(&p.seg[0].y[(int64_t)b * p.ldy + group * 32 + lane]);
-                    prep_emit_warp(p.next_prep + (size_t)group * p.rec_bytes, ncol, b, v);
-                }
-                if (ctid == 0) p.group_counters[group] = 0;
-            }
+            if (lane == 0) p.group_counters[group] = 0;
         }
     }
 }
@@ -174,19 +248,23 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
     const int NS = p.nstages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + NS;
-    float* red = reinterpret_cast<float*>(smem + 256);               // [16][NTC]
-    float* vals = red + 16 * NTC;                                      // [16*batch]
-    uint8_t* stages = smem + 256 + (16 * NTC + 16 * MV_MAX_BATCH) * 4;
+    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(smem + 256);   // [16]
+    float* red = reinterpret_cast<float*>(smem + 384);                               // [8][16][NTC]
+    uint8_t* stages = smem + 384 + MV_CONSUMER_WARPS * 16 * NTC * 4;
     stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x;
-    const int u0 = (int)((int64_t)blockIdx.x * p.units / G);
-    const int u1 = (int)((int64_t)(blockIdx.x + 1) * p.units / G);
-    const int CB = p.KC * BB;
-    const int stage_w = MV_TILE_ROWS * p.slot_pitch;
-    const int prep_bytes = p.KC * p.rec_bytes;
+    const int t0 = (int)((int64_t)blockIdx.x * p.total_tiles / G);
+    const int t1 = (int)((int64_t)(blockIdx.x + 1) * p.total_tiles / G);
+    const int nt = t1 - t0;
+    const Geom geo = cta_geom(p, nt);
+    const int ngroups = (nt + geo.gs - 1) / geo.gs;
+    const int nq = ngroups * geo.nchunks;
+    const int BOXW = p.kcb * BB;                 // TMA box row bytes
+    const int prep_bytes = geo.KC * p.rec_bytes;
+    const bool glu = p.epi != MV_EPI_STORE;
 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -195,19 +273,67 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
         }
         fence_mbar_init();
     }
-    for (int i = tid; i < 16 * NTC; i += blockDim.x) red[i] = 0.0f;
+    if (tid < 16) s_best[tid] = 0ull;
     __syncthreads();
 
     if (warp == MV_CONSUMER_WARPS) {
         // ------------------------------ producer ------------------------------
         auto issue_weights = [&](int q) {
-            const int u = u0 + q;
             const int stage = q % NS;
-            const int tile = u / p.nchunks, chunk = u % p.nchunks;
+            const int grp = q / geo.nchunks, chunk = q % geo.nchunks;
+            const int tg0 = t0 + grp * geo.gs;
+            const int ng = min(geo.gs, t1 - tg0);
             uint8_t* sbase = stages + (size_t)stage * p.stage_bytes;
-            uint32_t len = 0;
+            if (p.mode == MV_MODE_TMA) {
+                const int nbox = ng * geo.nb * (glu ? 2 : 1);
+                if (lane == 0) mbar_arrive_expect_tx(&full[stage], ng * geo.nb * MV_TILE_ROWS * BOXW + prep_bytes);
+                __syncwarp();
+                for (int k = lane; k < nbox; k += 32) {
+                    const int half = glu ? (k & 1) : 0;
+                    const int kb = glu ? (k >> 1) : k;
+                    const int ts = kb / geo.nb, bi = kb % geo.nb;
+                    const int tile = tg0 + ts;
+                    const int x = (chunk * geo.KC + bi * p.kcb) * BB / 8;
+                    uint8_t* dst = sbase + ((ts * geo.nb + bi) * MV_TILE_ROWS + half * 8) * BOXW;
+                    if (glu) {
+                        tma_load_2d(dst, &p.tmap[half], x, (tile - p.seg[0].tile0) * 8, &full[stage]);
+                    } else {
+                        int s = 0;
+                        if (p.nseg > 1 && tile >= p.seg[1].tile0) s = 1;
+                        if (p.nseg > 2 && tile >= p.seg[2].tile0) s = 2;
+                        tma_load_2d(dst, &p.tmap[s], x, (tile - p.seg[s].tile0) * MV_TILE_ROWS, &full[stage]);
+                    }
+                }
+                return;
+            }
+            const int tile = tg0;   // gs == 1
+            if (p.mode == MV_MODE_CONTIG) {
+                // whole rows: region 0 = rows 0..15 (GLU: gate rows), region 1 = up rows
+                uint32_t len = 0, lead = 0;
+                const uint8_t* src = nullptr;
+                const int nreg = glu ? 2 : 1;
+                if (lane < nreg) {
+                    const int r0 = lane * 8;
+                    const uint8_t* rp = tile_row_ptr(p, tile, r0);
+                    if (rp) {
+                        int nv = 1;
+                        const int span = glu ? 8 : MV_TILE_ROWS;
+                        while (nv < span && tile_row_ptr(p, tile, r0 + nv)) ++nv;
+                        lead = (uint32_t)(reinterpret_cast<uintptr_t>(rp) & 15u);
+                        len = (lead + (uint32_t)(nv * p.row_bytes) + 15u) & ~15u;
+                        src = rp - lead;
+                    }
+                }
+                const uint32_t total = __shfl_sync(0xffffffffu, len, 0) + __shfl_sync(0xffffffffu, len, 1);
+                if (lane == 0) mbar_arrive_expect_tx(&full[stage], total + prep_bytes);
+                __syncwarp();
+                if (len) bulk_g2s(sbase + lane * p.region_stride, src, len, &full[stage]);
+                return;
+            }
+            // MV_MODE_ROW: one copy per row
+            uint32_t len = 0, lead = 0;
             const uint8_t* src = nullptr;
-            uint32_t lead = 0;
+            const int CB = geo.KC * BB;
             if (lane < MV_TILE_ROWS) {
                 const uint8_t* rp = tile_row_ptr(p, tile, lane);
                 if (rp) {
@@ -225,14 +351,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
         };
         auto issue_prep = [&](int q) {
             if (lane == 0) {
-                const int u = u0 + q;
-                const int chunk = u % p.nchunks;
+                const int chunk = q % geo.nchunks;
                 uint8_t* sbase = stages + (size_t)(q % NS) * p.stage_bytes;
-                bulk_g2s(sbase + stage_w, p.prep + (size_t)chunk * p.KC * p.rec_bytes, prep_bytes,
-                         &full[q % NS]);
+                bulk_g2s(sbase + p.stage_w, p.prep + (size_t)chunk * geo.KC * p.rec_bytes, prep_bytes, &full[q % NS]);
             }
         };
-        const int nq = u1 - u0;
         const int pre = nq < NS ? nq : NS;
         for (int q = 0; q < pre; ++q) issue_weights(q);
         pdl_launch_dependents();
@@ -250,166 +373,128 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
         pdl_launch_dependents();
         pdl_wait();
         const int g = lane >> 2, t = lane & 3;
-        const int ctid = tid;  // 0..255
-        const int ncol = 3 * p.batch;
+        const int tw = warp / geo.ws, sub = warp % geo.ws;   // tile slot, split index
         float acc[NT][4];
 #pragma unroll
         for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-        ArgBest best{-INFINITY, 0x7fffffff};
         bool aborted = false;
 
-        int q = 0;
-        for (int u = u0; u < u1; ++u, ++q) {
+        for (int q = 0; q < nq; ++q) {
             const int stage = q % NS;
             const uint32_t parity = (q / NS) & 1;
-            const int tile = u / p.nchunks, chunk = u % p.nchunks;
+            const int grp = q / geo.nchunks, chunk = q % geo.nchunks;
+            const int tg0 = t0 + grp * geo.gs;
+            const int ng = min(geo.gs, t1 - tg0);
             if (!aborted && !mbar_wait_bounded(&full[stage], parity, p.err, BREW_DEVERR_TIMEOUT_FULL)) aborted = true;
             const uint8_t* sbase = stages + (size_t)stage * p.stage_bytes;
-            const uint8_t* sprep = sbase + stage_w;
-            // rows g and g+8 of this tile: where their chunk starts in smem
-            const uint8_t* rp0 = tile_row_ptr(p, tile, g);
-            const uint8_t* rp1 = tile_row_ptr(p, tile, g + 8);
-            const uint32_t lead0 = rp0 ? (uint32_t)((reinterpret_cast<uintptr_t>(rp0) + (int64_t)chunk * CB) & 15u) : 0u;
-            const uint32_t lead1 = rp1 ? (uint32_t)((reinterpret_cast<uintptr_t>(rp1) + (int64_t)chunk * CB) & 15u) : 0u;
-            const uint32_t row0 = smem_u32(sbase) + g * p.slot_pitch + lead0;
-            const uint32_t row1 = smem_u32(sbase) + (g + 8) * p.slot_pitch + lead1;
-            const uint32_t prep0 = smem_u32(sprep);
-            if (!aborted) {
+            const uint32_t sb = smem_u32(sbase);
+            const uint32_t prep0 = sb + p.stage_w;
+            if (!aborted && tw < ng) {
+                const int tile = tg0 + tw;
+                if (p.mode == MV_MODE_TMA) {
+                    // boxes are [16 rows][8 blocks]; walk them in block pairs
+                    // (68 / 36 bytes: word aligned, only the even block's
+                    // quants need a byte permute)
+                    constexpr int BOXW = 8 * BB, PAIR = 2 * BB;
+                    const int npairs = geo.nb * 4;
 #pragma unroll 2
-                for (int j = warp; j < p.KC; j += MV_CONSUMER_WARPS) {
-                    const uint32_t b0p = row0 + j * BB;
-                    const uint32_t b1p = row1 + j * BB;
-                    uint32_t a0, a1, a2, a3;
-                    if (TYPE == BREW_TYPE_Q8_0) {
-                        a0 = lds32_a2(b0p + 2 + 4 * t);
-                        a1 = lds32_a2(b1p + 2 + 4 * t);
-                        a2 = lds32_a2(b0p + 18 + 4 * t);
-                        a3 = lds32_a2(b1p + 18 + 4 * t);
-                    } else {
-                        const uint32_t w0 = lds32_a2(b0p + 2 + 4 * t);
-                        const uint32_t w1 = lds32_a2(b1p + 2 + 4 * t);
-                        a0 = w0 & 0x0F0F0F0Fu;
-                        a1 = w1 & 0x0F0F0F0Fu;
-                        a2 = (w0 >> 4) & 0x0F0F0F0Fu;
-                        a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-                    }
-                    const float d0 = half_bits_to_float((uint16_t)lds16(b0p));
-                    const float d1 = half_bits_to_float((uint16_t)lds16(b1p));
-                    const uint32_t rec = prep0 + j * p.rec_bytes;
-                    const uint32_t sw = rec + ncol * 32;
-                    const uint32_t ls = rec + ncol * 36;
-#pragma unroll
-                    for (int n = 0; n < NT; ++n) {
-                        // columns past 3*batch are not stored: feed zeros
-                        // (indices are clamped so no load leaves the record)
-                        const int cb = n * 8 + g;
-                        const bool vb = cb < ncol;
-                        const int cbs = vb ? cb : 0;
-                        uint32_t bf0 = lds32(rec + cbs * 32 + 4 * t);
-                        uint32_t bf1 = lds32(rec + cbs * 32 + 16 + 4 * t);
-                        if (!vb) bf0 = bf1 = 0u;
-                        const int c0 = n * 8 + 2 * t, c1 = c0 + 1;
-                        const bool v0 = c0 < ncol, v1 = c1 < ncol;
-                        const int c0s = v0 ? c0 : 0, c1s = v1 ? c1 : 0;
-                        int c[4];
+                    for (int pp = sub; pp < npairs; pp += geo.ws) {
+                        const int bi = pp >> 2, pi = pp & 3;
+                        const uint32_t R0 = sb + ((tw * geo.nb + bi) * MV_TILE_ROWS + g) * BOXW + pi * PAIR;
+                        const uint32_t R1 = R0 + 8 * BOXW;
+                        const uint32_t recA = prep0 + (bi * 8 + pi * 2) * p.rec_bytes;
+                        const uint32_t recB = recA + p.rec_bytes;
                         if (TYPE == BREW_TYPE_Q8_0) {
-                            mma_s8s8(c, a0, a1, a2, a3, bf0, bf1);
+                            const uint32_t dA0 = lds32(R0), dA1 = lds32(R1);
+                            const uint32_t dB0 = lds32(R0 + 32), dB1 = lds32(R1 + 32);
+                            const uint32_t a0 = __byte_perm(lds32(R0 + 4 * t), lds32(R0 + 4 * t + 4), 0x5432);
+                            const uint32_t a1 = __byte_perm(lds32(R1 + 4 * t), lds32(R1 + 4 * t + 4), 0x5432);
+                            const uint32_t a2 = __byte_perm(lds32(R0 + 4 * t + 16), lds32(R0 + 4 * t + 20), 0x5432);
+                            const uint32_t a3 = __byte_perm(lds32(R1 + 4 * t + 16), lds32(R1 + 4 * t + 20), 0x5432);
+                            mma_block<TYPE, NT>(acc, a0, a1, a2, a3, h2f_lo(dA0), h2f_lo(dA1), recA, p.batch, g, t);
+                            mma_block<TYPE, NT>(acc, lds32(R0 + 36 + 4 * t), lds32(R1 + 36 + 4 * t),
+                                                lds32(R0 + 52 + 4 * t), lds32(R1 + 52 + 4 * t), h2f_hi(dB0),
+                                                h2f_hi(dB1), recB, p.batch, g, t);
                         } else {
-                            mma_u8s8(c, a0, a1, a2, a3, bf0, bf1);
-                            const int l0 = v0 ? (int)lds32(ls + 4 * c0s) : 0;
-                            const int l1 = v1 ? (int)lds32(ls + 4 * c1s) : 0;
-                            c[0] -= 8 * l0;
-                            c[1] -= 8 * l1;
-                            c[2] -= 8 * l0;
-                            c[3] -= 8 * l1;
+                            const uint32_t dA0 = lds32(R0), dA1 = lds32(R1);
+                            const uint32_t dB0 = lds32(R0 + 16), dB1 = lds32(R1 + 16);
+                            const uint32_t w0 = __byte_perm(lds32(R0 + 4 * t), lds32(R0 + 4 * t + 4), 0x5432);
+                            const uint32_t w1 = __byte_perm(lds32(R1 + 4 * t), lds32(R1 + 4 * t + 4), 0x5432);
+                            mma_block<TYPE, NT>(acc, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
+                                                (w1 >> 4) & 0x0F0F0F0Fu, h2f_lo(dA0), h2f_lo(dA1), recA, p.batch, g, t);
+                            const uint32_t v0 = lds32(R0 + 20 + 4 * t), v1 = lds32(R1 + 20 + 4 * t);
+                            mma_block<TYPE, NT>(acc, v0 & 0x0F0F0F0Fu, v1 & 0x0F0F0F0Fu, (v0 >> 4) & 0x0F0F0F0Fu,
+                                                (v1 >> 4) & 0x0F0F0F0Fu, h2f_hi(dB0), h2f_hi(dB1), recB, p.batch, g, t);
                         }
-                        const float s0 = v0 ? ldsf(sw + 4 * c0s) : 0.0f;
-                        const float s1 = v1 ? ldsf(sw + 4 * c1s) : 0.0f;
-                        acc[n][0] = fmaf((float)c[0], d0 * s0, acc[n][0]);
-                        acc[n][1] = fmaf((float)c[1], d0 * s1, acc[n][1]);
-                        acc[n][2] = fmaf((float)c[2], d1 * s0, acc[n][2]);
-                        acc[n][3] = fmaf((float)c[3], d1 * s1, acc[n][3]);
+                    }
+                } else {
+                    // CONTIG / ROW: rows at arbitrary 2-byte alignment, block by block
+                    uint32_t row0, row1;
+                    if (p.mode == MV_MODE_CONTIG) {
+                        const uint8_t* ra = tile_row_ptr(p, tile, 0);
+                        const uint32_t la = ra ? (uint32_t)(reinterpret_cast<uintptr_t>(ra) & 15u) : 0u;
+                        row0 = sb + la + g * (uint32_t)p.row_bytes;
+                        if (glu) {
+                            const uint8_t* rb = tile_row_ptr(p, tile, 8);
+                            const uint32_t lb = rb ? (uint32_t)(reinterpret_cast<uintptr_t>(rb) & 15u) : 0u;
+                            row1 = sb + p.region_stride + lb + g * (uint32_t)p.row_bytes;
+                        } else {
+                            row1 = sb + la + (g + 8) * (uint32_t)p.row_bytes;
+                        }
+                    } else {
+                        const int CB = geo.KC * BB;
+                        const uint8_t* rp0 = tile_row_ptr(p, tile, g);
+                        const uint8_t* rp1 = tile_row_ptr(p, tile, g + 8);
+                        const uint32_t l0 = rp0 ? (uint32_t)((reinterpret_cast<uintptr_t>(rp0) + (int64_t)chunk * CB) & 15u) : 0u;
+                        const uint32_t l1 = rp1 ? (uint32_t)((reinterpret_cast<uintptr_t>(rp1) + (int64_t)chunk * CB) & 15u) : 0u;
+                        row0 = sb + g * p.slot_pitch + l0;
+                        row1 = sb + (g + 8) * p.slot_pitch + l1;
+                    }
+                    for (int j = sub; j < geo.KC; j += geo.ws) {
+                        const uint32_t b0p = row0 + j * BB, b1p = row1 + j * BB;
+                        uint32_t a0, a1, a2, a3;
+                        if (TYPE == BREW_TYPE_Q8_0) {
+                            a0 = lds32_a2(b0p + 2 + 4 * t);
+                            a1 = lds32_a2(b1p + 2 + 4 * t);
+                            a2 = lds32_a2(b0p + 18 + 4 * t);
+                            a3 = lds32_a2(b1p + 18 + 4 * t);
+                        } else {
+                            const uint32_t w0 = lds32_a2(b0p + 2 + 4 * t);
+                            const uint32_t w1 = lds32_a2(b1p + 2 + 4 * t);
+                            a0 = w0 & 0x0F0F0F0Fu;
+                            a1 = w1 & 0x0F0F0F0Fu;
+                            a2 = (w0 >> 4) & 0x0F0F0F0Fu;
+                            a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+                        }
+                        mma_block<TYPE, NT>(acc, a0, a1, a2, a3, half_bits_to_float((uint16_t)lds16(b0p)),
+                                            half_bits_to_float((uint16_t)lds16(b1p)), prep0 + j * p.rec_bytes, p.batch,
+                                            g, t);
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
+            if (chunk != geo.nchunks - 1) continue;
 
-            const bool tile_end = (chunk == p.nchunks - 1) || (u == u1 - 1);
-            if (!tile_end) continue;
-
-            // ---- this CTA's share of the tile is done: reduce ----
+            // ---- group end: every tile of the group is complete in this CTA ----
+            float* myred = red + warp * 16 * NTC;
+            if (tw < ng) {
 #pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                atomicAdd(&red[g * NTC + n * 8 + 2 * t], acc[n][0]);
-                atomicAdd(&red[g * NTC + n * 8 + 2 * t + 1], acc[n][1]);
-                atomicAdd(&red[(g + 8) * NTC + n * 8 + 2 * t], acc[n][2]);
-                atomicAdd(&red[(g + 8) * NTC + n * 8 + 2 * t + 1], acc[n][3]);
-                acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-            }
-            consumer_bar();
-            for (int idx = ctid; idx < 16 * p.batch; idx += 256) {
-                const int r = idx & 15, b = idx >> 4;
-                float* rr = red + r * NTC + 3 * b;
-                vals[idx] = (rr[2] + rr[1]) + rr[0];
-                rr[0] = rr[1] = rr[2] = 0.0f;
-            }
-            const int64_t t0 = (int64_t)tile * p.nchunks;
-            const int first_cta = cta_of_unit(t0, p.units, G);
-            const int last_cta = cta_of_unit(t0 + p.nchunks - 1, p.units, G);
-            if (first_cta == last_cta) {
-                consumer_bar();
-                tile_epilogue(p, tile, vals, ctid, best);
-            } else {
-                // partial tile: publish, the last arriving CTA combines in order
-                __shared__ int s_last;
-                // a split tile is identified by its first CTA: CTA ranges are
-                // contiguous, so no two split tiles share a first CTA
-                const int part = blockIdx.x - first_cta;
-                const int nparts = last_cta - first_cta + 1;
-                if (nparts > MV_MAX_PARTS) {   // the host sizes the grid so this cannot happen
-                    if (ctid == 0) atomicOr(p.err, BREW_DEVERR_BAD_INDEX);
-                    consumer_bar();
-                    continue;
-                }
-                float* pb = p.part_buf + ((size_t)first_cta * MV_MAX_PARTS) * 16 * p.batch;
-                for (int idx = ctid; idx < 16 * p.batch; idx += 256) __stcg(&pb[part * 16 * p.batch + idx], vals[idx]);
-                __threadfence();
-                consumer_bar();
-                if (ctid == 0) {
-                    const int old = atomicAdd(&p.tile_counters[first_cta], 1);
-                    s_last = (old == nparts - 1);
-                }
-                consumer_bar();
-                if (s_last) {
-                    __threadfence();
-                    for (int idx = ctid; idx < 16 * p.batch; idx += 256) {
-                        float v = __ldcg(&pb[idx]);
-                        for (int k = 1; k < nparts; ++k) v += __ldcg(&pb[k * 16 * p.batch + idx]);
-                        vals[idx] = v;
-                    }
-                    consumer_bar();
-                    tile_epilogue(p, tile, vals, ctid, best);
-                    if (ctid == 0) p.tile_counters[first_cta] = 0;
+                for (int n = 0; n < NT; ++n) {
+                    myred[g * NTC + n * 8 + 2 * t] = acc[n][0];
+                    myred[g * NTC + n * 8 + 2 * t + 1] = acc[n][1];
+                    myred[(g + 8) * NTC + n * 8 + 2 * t] = acc[n][2];
+                    myred[(g + 8) * NTC + n * 8 + 2 * t + 1] = acc[n][3];
+                    acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
                 }
             }
-            consumer_bar();
+            if (geo.ws > 1) consumer_bar(); else __syncwarp();
+            if (tw < ng && sub == 0) tile_out<NTC>(p, tg0 + tw, red, warp, geo.ws, lane, s_best);
+            if (geo.ws > 1) consumer_bar(); else __syncwarp();
         }
-
         if (p.post == MV_POST_ARGMAX) {
-            // per-CTA best per batch element: threads 16b..16b+15 hold batch b
-            ArgBest bb = best;
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bb.v, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bb.i, o);
-                argbest_update(bb, ov, oi);
-            }
-            const int b = ctid >> 4;
-            if ((ctid & 15) == 0 && b < p.batch) {
-                p.am_val[blockIdx.x * p.batch + b] = bb.v;
-                p.am_idx[blockIdx.x * p.batch + b] = bb.i;
-            }
+            consumer_bar();
+            if (tid < p.batch) atomicMax(&p.am_key[tid], s_best[tid]);
         }
     }
 
@@ -427,21 +512,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
     if (!s_post_last) return;
     __threadfence();
     if (p.post == MV_POST_ARGMAX) {
-        if (tid < 32) {
-            for (int b = 0; b < p.batch; ++b) {
-                ArgBest bb{-INFINITY, 0x7fffffff};
-                for (int c = tid; c < G; c += 32) argbest_update(bb, __ldcg(&p.am_val[c * p.batch + b]), __ldcg(&p.am_idx[c * p.batch + b]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bb.v, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bb.i, o);
-                    argbest_update(bb, ov, oi);
-                }
-                if (tid == 0) p.am_out[b] = bb.i == 0x7fffffff ? 0 : bb.i;
-            }
+        if (tid < p.batch) {
+            const unsigned long long k = atomicExch(&p.am_key[tid], 0ull);
+            p.am_out[tid] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         }
     } else {
-        const int ncol = 3 * p.batch;
         for (int b = 0; b < p.batch; ++b) {
             float* x = p.post_x + (int64_t)b * p.post_ld;
             if (p.post_add) {
@@ -459,7 +534,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
                 __threadfence();
                 __syncthreads();
             }
-            prep_vector_cta(x, p.post_dim, p.post_norm_w, p.eps, p.post_prep, p.rec_bytes, ncol, b, s_red);
+            prep_vector_cta(x, p.post_dim, p.post_norm_w, p.eps, p.post_prep, p.rec_bytes, p.batch, b, s_red);
         }
     }
     __syncthreads();
@@ -472,7 +547,6 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* x, int ldx, int 
     pdl_launch_dependents();
     pdl_wait();
     const int b = blockIdx.y;
-    const int ncol = 3 * batch;
     const int rec_bytes = prep_rec_bytes(batch);
     const float* xb = x + (int64_t)b * ldx;
     float scale = 1.0f;
@@ -490,7 +564,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* x, int ldx, int 
     for (int j = blockIdx.x * nwarp + warp; j < K / 32; j += gridDim.x * nwarp) {
         float v = __ldcg(&xb[32 * j + lane]);
         if (nw) v = v * scale * nw[32 * j + lane];
-        prep_emit_warp(recs + (size_t)j * rec_bytes, ncol, b, v);
+        prep_emit_warp(recs + (size_t)j * rec_bytes, batch, b, v);
     }
 }
 
@@ -517,29 +591,45 @@ int launch_typed(const MvParams& p, cudaStream_t stream, bool pdl, int grid, siz
     return BREW_OK;
 }
 
+// The kernel is instantiated for NT in {1, 2, 3, 6, 12}: the n8 MMA tiles
+// (3 limb columns per batch element) rounded up.  Host-side shared-memory
+// sizing must use this same value.
+int nt_instance(int batch) {
+    const int nt = prep_nt(batch);
+    return nt <= 2 ? nt : (nt <= 4 ? 4 : 8);
+}
+
 template <int TYPE>
 int launch_nt(const MvParams& p, cudaStream_t stream, bool pdl, int grid, size_t smem) {
-    switch (prep_nt(p.batch)) {
+    switch (nt_instance(p.batch)) {
         case 1: return launch_typed<TYPE, 1>(p, stream, pdl, grid, smem);
         case 2: return launch_typed<TYPE, 2>(p, stream, pdl, grid, smem);
-        case 3: return launch_typed<TYPE, 3>(p, stream, pdl, grid, smem);
-        case 4: case 5: case 6: return launch_typed<TYPE, 6>(p, stream, pdl, grid, smem);
-        default: return launch_typed<TYPE, 12>(p, stream, pdl, grid, smem);
+        case 4: return launch_typed<TYPE, 4>(p, stream, pdl, grid, smem);
+        default: return launch_typed<TYPE, 8>(p, stream, pdl, grid, smem);
     }
 }
 
-// Largest number of CTAs that share one tile for a given grid (stream-K).
-int max_parts(int units, int nchunks, int grid) {
-    int worst = 1;
-    for (int c = 0; c < grid; ++c) {
-        // the tile containing this CTA's first unit, and the CTAs covering it
-        const int64_t u0 = (int64_t)c * units / grid;
-        const int64_t t0 = u0 / nchunks * nchunks;
-        const int64_t first = ((t0 + 1) * grid - 1) / units;
-        const int64_t last = ((t0 + nchunks) * grid - 1) / units;
-        worst = std::max(worst, (int)(last - first + 1));
+// Tensor map over `rows` rows of `pitch` bytes as 8-byte elements, box of
+// `box_bytes` x `box_rows`.  Rows past the end read as zeros.
+int encode_rows_map(CUtensorMap* map, const void* base, int rows, int pitch, int box_bytes, int box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        BREW_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        BREW_CHECK(fn && q == cudaDriverEntryPointSuccess, BREW_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
-    return worst;
+    const cuuint64_t dims[2] = {(cuuint64_t)(pitch / 8), (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 8), (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    BREW_CHECK(r == CUDA_SUCCESS, BREW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): rows %d pitch %d box %dx%d", (int)r,
+               rows, pitch, box_bytes, box_rows);
+    return BREW_OK;
 }
 
 }  // namespace
@@ -555,10 +645,6 @@ int num_sms() {
     return n;
 }
 
-size_t mv_part_floats(int grid, int batch) {
-    return (size_t)grid * MV_MAX_PARTS * 16 * (size_t)batch;
-}
-
 int mv_launch(MvParams p, cudaStream_t stream, bool pdl) {
     TypeInfo ti;
     BREW_CHECK(type_info(p.type, &ti), BREW_ERR_UNSUPPORTED, "matvec: unsupported type %d", p.type);
@@ -570,48 +656,74 @@ int mv_launch(MvParams p, cudaStream_t stream, bool pdl) {
                "matvec: fused argmax needs batch <= %d", MV_ARGMAX_MAX_BATCH);
     p.KB = p.K / 32;
     p.rec_bytes = prep_rec_bytes(p.batch);
-    // stage = 16 rows x KC blocks (+ their prep records); KC divides KB
     const int BB = ti.block_bytes;
-    int KC = 1;
-    for (int c = 1; c <= p.KB; ++c) {
-        if (p.KB % c) continue;
-        const int cb = c * BB;
-        const int slot = (cb + 47) & ~15;
-        const int st = MV_TILE_ROWS * slot + c * p.rec_bytes;
-        if (cb <= 1184 && st <= 40 * 1024) KC = c;
-    }
-    p.KC = KC;
-    p.nchunks = p.KB / KC;
-    p.slot_pitch = (KC * BB + 47) & ~15;
-    p.stage_bytes = MV_TILE_ROWS * p.slot_pitch + KC * p.rec_bytes;
-    const int NTC = prep_nt(p.batch) * 8;
-    const size_t fixed = 256 + (size_t)(16 * NTC + 16 * MV_MAX_BATCH) * 4 + 128;
-    const size_t budget = 112 * 1024;
-    int ns = (int)((budget - fixed) / p.stage_bytes);
-    ns = std::max(2, std::min(ns, 8));
-    p.nstages = ns;
-    const size_t smem = fixed + (size_t)ns * p.stage_bytes;
+    const int P = p.KB * BB;
+    const bool glu = p.epi != MV_EPI_STORE;
     // tiles per segment
     int tiles = 0;
     for (int s = 0; s < p.nseg; ++s) {
         p.seg[s].tile0 = tiles;
-        if (p.epi == MV_EPI_STORE) tiles += (p.seg[s].rows + MV_TILE_ROWS - 1) / MV_TILE_ROWS;
+        if (!glu) tiles += (p.seg[s].rows + MV_TILE_ROWS - 1) / MV_TILE_ROWS;
     }
-    if (p.epi != MV_EPI_STORE) {
+    if (glu) {
         BREW_CHECK(p.nseg == 2 && p.seg[0].rows == p.seg[1].rows, BREW_ERR_INVALID_ARG, "matvec: GLU needs 2 equal segments");
         p.seg[1].tile0 = 0;
         tiles = (p.seg[0].rows + 7) / 8;
         BREW_CHECK(!p.next_prep || p.seg[0].rows % 32 == 0, BREW_ERR_INVALID_ARG, "matvec: GLU prep needs rows %% 32 == 0");
     }
     p.total_tiles = tiles;
-    p.units = tiles * p.nchunks;
-    // grid: persistent, at most one CTA per SM, and no tile split more than
-    // MV_MAX_PARTS ways
-    int grid = std::min(num_sms(), p.units);
-    grid = std::min(grid, std::max(1, (MV_MAX_PARTS - 1) * p.units / p.nchunks));
-    grid = std::max(grid, 1);
-    while (grid > 1 && max_parts(p.units, p.nchunks, grid) > MV_MAX_PARTS) --grid;
-    if (p.post == MV_POST_ARGMAX) BREW_CHECK(p.am_val && p.am_idx && p.am_out, BREW_ERR_INVALID_ARG, "argmax buffers");
+    // staging mode (see MvMode)
+    bool aligned = (P % 16) == 0 && p.KB % 8 == 0;
+    for (int s = 0; s < p.nseg; ++s) aligned = aligned && ((reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) == 0);
+    const int contig_rs = (8 * P + 30) & ~15;
+    if (aligned) {
+        p.mode = MV_MODE_TMA;
+        p.kcb = 8;                                   // box: 16 rows x 8 blocks (272 or 144 bytes)
+        const int boxw = p.kcb * BB;
+        p.nb_cap = std::max(1, std::min(MV_MAX_BOXES, (8 * 1024) / (p.kcb * p.rec_bytes)));
+        p.stage_w = MV_MAX_BOXES * MV_TILE_ROWS * boxw;
+        p.stage_bytes = (p.stage_w + p.nb_cap * p.kcb * p.rec_bytes + 127) & ~127;
+    } else if (2 * contig_rs + p.KB * p.rec_bytes <= 56 * 1024) {
+        p.mode = MV_MODE_CONTIG;
+        p.kcb = p.KB;
+        p.nb_cap = 1;
+        p.region_stride = contig_rs;
+        p.stage_w = 2 * contig_rs;
+        p.stage_bytes = (p.stage_w + p.KB * p.rec_bytes + 127) & ~127;
+    } else {
+        p.mode = MV_MODE_ROW;
+        int KC = 1;
+        for (int c = 1; c <= p.KB; ++c) {
+            if (p.KB % c) continue;
+            const int cb = c * BB;
+            const int slot = (cb + 47) & ~15;
+            if (cb <= 1184 && MV_TILE_ROWS * slot + c * p.rec_bytes <= 40 * 1024) KC = c;
+        }
+        p.kcb = KC;
+        p.nb_cap = 1;
+        p.slot_pitch = (KC * BB + 47) & ~15;
+        p.stage_w = MV_TILE_ROWS * p.slot_pitch;
+        p.stage_bytes = (p.stage_w + KC * p.rec_bytes + 127) & ~127;
+    }
+    const int NTC = nt_instance(p.batch) * 8;     // as the kernel instance lays it out
+    const size_t fixed = 384 + (size_t)MV_CONSUMER_WARPS * 16 * NTC * 4 + 128;
+    const size_t budget = 112 * 1024;
+    int ns = budget > fixed ? (int)((budget - fixed) / p.stage_bytes) : 0;
+    ns = std::max(2, std::min(ns, 12));
+    p.nstages = ns;
+    const size_t smem = fixed + (size_t)ns * p.stage_bytes;
+    BREW_CHECK(smem <= 200 * 1024, BREW_ERR_INVALID_ARG, "matvec: %zu bytes of shared memory", smem);
+    if (p.mode == MV_MODE_TMA) {
+        const int box_rows = glu ? 8 : MV_TILE_ROWS;
+        for (int s = 0; s < p.nseg; ++s) {
+            const int rc = encode_rows_map(&p.tmap[s], p.seg[s].w, p.seg[s].rows, P, p.kcb * BB, box_rows);
+            if (rc) return rc;
+        }
+    }
+    // grid: persistent, at most one CTA per SM, each owning whole tiles
+    const int grid = std::max(1, std::min(num_sms(), tiles));
+    if (p.post == MV_POST_ARGMAX)
+        BREW_CHECK(p.am_key && p.am_out && p.batch <= MV_ARGMAX_MAX_BATCH, BREW_ERR_INVALID_ARG, "argmax buffers");
     if (p.type == BREW_TYPE_Q8_0) return launch_nt<BREW_TYPE_Q8_0>(p, stream, pdl, grid, smem);
     return launch_nt<BREW_TYPE_Q4_0>(p, stream, pdl, grid, smem);
 }

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) embed_prep_kernel(int type, const uint8_t
     }
     __threadfence();
     __syncthreads();
-    prep_vector_cta(xb, dim, nw, eps, prep, prep_rec_bytes(batch), 3 * batch, b, red);
+    prep_vector_cta(xb, dim, nw, eps, prep, prep_rec_bytes(batch), batch, b, red);
 }
 
 __global__ void dequant_kernel(int type, const uint8_t* w, int64_t off, int64_t n, float* out) {

@@ -56,12 +56,10 @@ struct brew_model_s {
     int64_t cache_bstride = 0;
     float *x = nullptr, *xb = nullptr, *xb2 = nullptr, *qkv = nullptr, *hb = nullptr, *logits = nullptr;
     uint8_t *prep_x = nullptr, *prep_q = nullptr, *prep_h = nullptr;
-    float* part = nullptr;
-    int* counters = nullptr;   // [tile counters: sms][group counters][post][attn]
+    int* counters = nullptr;   // [group counters][post][attn]
     int n_counters = 0;
     float* attn_part = nullptr;
-    float* am_val = nullptr;
-    int* am_idx = nullptr;
+    unsigned long long* am_key = nullptr;
     int32_t* am_out = nullptr;
     int32_t *tokens_d = nullptr, *pos_d = nullptr;
     int32_t* gen_d = nullptr;      // generated ids of brew_session_generate
@@ -71,6 +69,11 @@ struct brew_model_s {
     int qkvw = 0;
     std::vector<void*> allocs;
     std::map<int, cudaGraphExec_t> graphs;   // key: batch*2 + with_classifier
+    std::map<int, int> graph_kernels;        // kernels captured in each graph
+    // greedy session (GenericModelSession state: position, pendingToken)
+    int sess_pos = 0;
+    const int32_t* sess_pending = nullptr;   // device address of the pending token
+    int sess_generated = 0;                  // ids recorded in gen_d since prefill
     int32_t* h_pin = nullptr;                // pinned staging (tokens, pos, argmax)
     int h_pin_cap = 0;
 };
@@ -142,13 +145,11 @@ int alloc_state(brew_model_s* m) {
     if ((rc = dalloc(m, &m->prep_x, (size_t)(c.dim / 32) * rec))) return rc;
     if ((rc = dalloc(m, &m->prep_q, (size_t)(qw / 32) * rec))) return rc;
     if ((rc = dalloc(m, &m->prep_h, (size_t)(c.hidden_dim / 32) * rec))) return rc;
-    if ((rc = dalloc(m, &m->part, mv_part_floats(num_sms(), B)))) return rc;
-    m->n_counters = num_sms() + c.hidden_dim / 32 + 8 + B * c.n_kv_heads;
+    m->n_counters = c.hidden_dim / 32 + 8 + B * c.n_kv_heads;
     if ((rc = dalloc(m, &m->counters, (size_t)m->n_counters))) return rc;
     m->nchunk = attn_pick_nchunk(c.n_kv_heads, B, c.seq_len);
     if ((rc = dalloc(m, &m->attn_part, attn_part_floats(B, c.n_heads, m->nchunk, c.head_size)))) return rc;
-    if ((rc = dalloc(m, &m->am_val, (size_t)num_sms() * B))) return rc;
-    if ((rc = dalloc(m, &m->am_idx, (size_t)num_sms() * B))) return rc;
+    if ((rc = dalloc(m, &m->am_key, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->am_out, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
@@ -192,8 +193,7 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
     const bool gemma = c.arch == BREW_ARCH_GEMMA3;
     const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
     unsigned int* err = ctx().err_word;
-    int* tile_ctr = m->counters;
-    int* group_ctr = tile_ctr + num_sms();
+    int* group_ctr = m->counters;
     int* post_ctr = group_ctr + hid / 32;
     int* attn_ctr = post_ctr + 8;
     int rc;
@@ -220,8 +220,6 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
             p.seg[2] = {layer_ptr(m->t[T_V], l, kvd, dim), m->qkv + qw + kvd,
                         m->v_bias ? m->v_bias + (int64_t)l * kvd : nullptr, nullptr, kvd, 0};
             p.prep = m->prep_x;
-            p.part_buf = m->part;
-            p.tile_counters = tile_ctr;
             p.err = err;
             if ((rc = mv_launch(p, s, true))) return rc;
         }
@@ -276,8 +274,6 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
             p.nseg = 1;
             p.seg[0] = {layer_ptr(m->t[T_O], l, dim, qw), gemma ? m->xb2 : m->x, nullptr, gemma ? nullptr : m->x, dim, 0};
             p.prep = m->prep_q;
-            p.part_buf = m->part;
-            p.tile_counters = tile_ctr;
             p.post = MV_POST_PREP;
             p.post_counter = post_ctr;
             p.post_x = m->x;
@@ -304,8 +300,6 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
             p.seg[0] = {layer_ptr(m->t[T_GATE], l, hid, dim), m->hb, nullptr, nullptr, hid, 0};
             p.seg[1] = {layer_ptr(m->t[T_UP], l, hid, dim), nullptr, nullptr, nullptr, hid, 0};
             p.prep = m->prep_x;
-            p.part_buf = m->part;
-            p.tile_counters = tile_ctr;
             p.next_prep = m->prep_h;
             p.group_counters = group_ctr;
             p.err = err;
@@ -323,8 +317,6 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
             p.nseg = 1;
             p.seg[0] = {layer_ptr(m->t[T_DOWN], l, dim, hid), gemma ? m->xb2 : m->x, nullptr, gemma ? nullptr : m->x, dim, 0};
             p.prep = m->prep_h;
-            p.part_buf = m->part;
-            p.tile_counters = tile_ctr;
             p.post = MV_POST_PREP;
             p.post_counter = post_ctr;
             p.post_x = m->x;
@@ -352,13 +344,10 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
         p.nseg = 1;
         p.seg[0] = {m->t[T_OUTPUT]->d, m->logits, nullptr, nullptr, c.vocab_size, 0};
         p.prep = m->prep_x;
-        p.part_buf = m->part;
-        p.tile_counters = tile_ctr;
         const bool fused = B <= MV_ARGMAX_MAX_BATCH;
         p.post = fused ? MV_POST_ARGMAX : MV_POST_NONE;
         p.post_counter = post_ctr;
-        p.am_val = m->am_val;
-        p.am_idx = m->am_idx;
+        p.am_key = m->am_key;
         p.am_out = m->am_out;
         p.err = err;
         if ((rc = mv_launch(p, s, true))) return rc;
@@ -376,9 +365,14 @@ int get_graph(brew_model_s* m, int B, bool with_classifier, cudaGraphExec_t* out
     }
     cudaStream_t s = ctx().stream;
     cudaGraph_t g = nullptr;
+    const int64_t before = brew_kernel_launches();
     BREW_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     int rc = enqueue_forward(m, B, with_classifier, s);
     cudaError_t e = cudaStreamEndCapture(s, &g);
+    // captured kernels do not run yet: count them per replay instead
+    const int nk = (int)(brew_kernel_launches() - before);
+    count_launch(-nk);
+    m->graph_kernels[key] = nk;
     if (rc) {
         if (g) cudaGraphDestroy(g);
         return rc;
@@ -390,6 +384,77 @@ int get_graph(brew_model_s* m, int B, bool with_classifier, cudaGraphExec_t* out
     BREW_CUDA(e);
     m->graphs[key] = exec;
     *out = exec;
+    return BREW_OK;
+}
+
+int launch_graph(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
+    cudaGraphExec_t g;
+    int rc = get_graph(m, B, with_classifier, &g);
+    if (rc) return rc;
+    BREW_CUDA(cudaGraphLaunch(g, s));
+    count_launch(m->graph_kernels[B * 2 + (with_classifier ? 1 : 0)]);
+    return BREW_OK;
+}
+
+int launch_step(brew_model_s* m, const int32_t* tok_src, int pos, int32_t* record, cudaStream_t s) {
+    step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, tok_src, pos, record, m->am_out);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+// GenericModelSession.prefill (runtime/ModelRunner.java:196-206) from a reset
+// session: forward(prompt[i], i) for each prompt token.
+int session_prefill(brew_model_s* m, const int32_t* prompt, int n_prompt, cudaStream_t s) {
+    const brew_config& c = m->c;
+    BREW_CHECK(n_prompt >= 0 && (prompt || n_prompt == 0), BREW_ERR_INVALID_ARG, "bad prompt");
+    BREW_CHECK(n_prompt <= c.seq_len, BREW_ERR_CONTEXT_FULL, "The session has reached its context limit of %d tokens.",
+               c.seq_len);
+    for (int i = 0; i < n_prompt; ++i)
+        BREW_CHECK(prompt[i] >= 0 && prompt[i] < c.vocab_size, BREW_ERR_INVALID_ARG, "prompt token %d out of range",
+                   prompt[i]);
+    if (m->prompt_cap < n_prompt + 1) {
+        if (m->prompt_d) cudaFree(m->prompt_d);
+        m->prompt_d = nullptr;
+        BREW_CUDA(cudaMalloc(&m->prompt_d, (size_t)(n_prompt + 1) * sizeof(int32_t)));
+        m->prompt_cap = n_prompt + 1;
+    }
+    // the prompt plus reset()'s pending token (BOS, ModelRunner.java:119)
+    std::vector<int32_t> staged(prompt, prompt + n_prompt);
+    staged.push_back(c.bos_token);
+    BREW_CUDA(cudaMemcpyAsync(m->prompt_d, staged.data(), staged.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    BREW_CUDA(cudaStreamSynchronize(s));
+    int rc;
+    for (int i = 0; i < n_prompt; ++i) {
+        if ((rc = launch_step(m, m->prompt_d + i, i, nullptr, s))) return rc;
+        if ((rc = launch_graph(m, 1, false, s))) return rc;
+    }
+    m->sess_pos = n_prompt;
+    m->sess_pending = n_prompt > 0 ? m->prompt_d + n_prompt - 1 : m->prompt_d + n_prompt;
+    m->sess_generated = 0;
+    return BREW_OK;
+}
+
+// The decode loop of GenericModelSession.generate (:141-152): forward the
+// pending token at the current position, take the argmax as the next
+// pending token.  Each step's id is recorded in gen_d on the device.
+int session_decode(brew_model_s* m, int n_steps, cudaStream_t s) {
+    const brew_config& c = m->c;
+    BREW_CHECK(m->sess_pending, BREW_ERR_INVALID_ARG, "no session: call brew_session_prefill first");
+    BREW_CHECK(n_steps >= 0, BREW_ERR_INVALID_ARG, "n_steps %d", n_steps);
+    BREW_CHECK(m->sess_pos + n_steps <= c.seq_len, BREW_ERR_CONTEXT_FULL,
+               "The session has reached its context limit of %d tokens.", c.seq_len);
+    int rc;
+    for (int k = 0; k < n_steps; ++k) {
+        const int g = m->sess_generated;
+        if ((rc = launch_step(m, m->sess_pending, m->sess_pos, g > 0 ? m->gen_d + g - 1 : nullptr, s))) return rc;
+        if ((rc = launch_graph(m, 1, true, s))) return rc;
+        m->sess_pending = m->am_out;
+        m->sess_pos++;
+        m->sess_generated++;
+    }
+    // record the last step's id
+    if (n_steps > 0 && (rc = launch_step(m, m->am_out, m->sess_pos, m->gen_d + m->sess_generated - 1, s))) return rc;
     return BREW_OK;
 }
 
@@ -562,9 +627,7 @@ int brew_model_forward_dev(brew_model m, const int32_t* tokens_dev, const int32_
     }
     BREW_CUDA(cudaMemcpyAsync(m->tokens_d, tokens_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     BREW_CUDA(cudaMemcpyAsync(m->pos_d, pos_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
-    cudaGraphExec_t g;
-    if ((rc = get_graph(m, batch, true, &g))) return rc;
-    BREW_CUDA(cudaGraphLaunch(g, s));
+    if ((rc = launch_graph(m, batch, true, s))) return rc;
     if (logits_dev)
         BREW_CUDA(cudaMemcpyAsync(logits_dev, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float),
                                   cudaMemcpyDeviceToDevice, s));
@@ -596,15 +659,49 @@ int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos, 
     memcpy(hp + batch, pos, batch * sizeof(int32_t));
     BREW_CUDA(cudaMemcpyAsync(m->tokens_d, hp, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     BREW_CUDA(cudaMemcpyAsync(m->pos_d, hp + batch, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    cudaGraphExec_t g;
-    if ((rc = get_graph(m, batch, true, &g))) return rc;
-    BREW_CUDA(cudaGraphLaunch(g, s));
+    if ((rc = launch_graph(m, batch, true, s))) return rc;
     if (logits)
         BREW_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
     if (argmax) BREW_CUDA(cudaMemcpyAsync(hp + 2 * batch, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));
     if (argmax) memcpy(argmax, hp + 2 * batch, batch * sizeof(int32_t));
     return check_device_error("brew_model_forward");
+}
+
+int brew_session_prefill(brew_model m, const int32_t* prompt, int32_t n_prompt, void* stream) {
+    BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null model");
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx().stream;
+    return session_prefill(m, prompt, n_prompt, s);
+}
+
+int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out, void* stream) {
+    BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null model");
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx().stream;
+    const int first = m->sess_generated;
+    if ((rc = session_decode(m, n_steps, s))) return rc;
+    if (!out) return BREW_OK;
+    if (n_steps > 0)
+        BREW_CUDA(cudaMemcpyAsync(out, m->gen_d + first, (size_t)n_steps * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    BREW_CUDA(cudaStreamSynchronize(s));
+    return check_device_error("brew_session_decode");
+}
+
+int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n) {
+    BREW_CHECK(m && n, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(batch >= 1 && batch <= m->max_batch, BREW_ERR_INVALID_ARG, "batch %d", batch);
+    int rc = ensure_init();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    cudaGraphExec_t g;
+    if ((rc = get_graph(m, batch, true, &g))) return rc;
+    *n = m->graph_kernels[batch * 2 + 1];
+    return BREW_OK;
 }
 
 int brew_session_generate(brew_model m, const int32_t* prompt, int32_t n_prompt, int32_t max_new, int32_t* out,
@@ -615,49 +712,15 @@ int brew_session_generate(brew_model m, const int32_t* prompt, int32_t n_prompt,
     // ensureContextAvailable (runtime/ModelRunner.java:208-216)
     BREW_CHECK(n_prompt <= c.seq_len, BREW_ERR_CONTEXT_FULL,
                "The session has reached its context limit of %d tokens.", c.seq_len);
-    for (int i = 0; i < n_prompt; ++i)
-        BREW_CHECK(prompt[i] >= 0 && prompt[i] < c.vocab_size, BREW_ERR_INVALID_ARG, "prompt token %d out of range", prompt[i]);
-    const int remaining = c.seq_len - n_prompt;
+    const int remaining = c.seq_len - n_prompt;              // :132-135
     const int limit = max_new <= 0 ? remaining : std::min(max_new, remaining);
     BREW_CHECK(limit == 0 || out, BREW_ERR_INVALID_ARG, "out is null");
     int rc = ensure_init();
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(api_mutex());
     cudaStream_t s = ctx().stream;
-    // prompt (+ the pending token of reset(): BOS) to the device
-    if (m->prompt_cap < n_prompt + 1) {
-        if (m->prompt_d) cudaFree(m->prompt_d);
-        m->prompt_d = nullptr;
-        BREW_CUDA(cudaMalloc(&m->prompt_d, (size_t)(n_prompt + 1) * sizeof(int32_t)));
-        m->prompt_cap = n_prompt + 1;
-    }
-    std::vector<int32_t> staged(prompt, prompt + n_prompt);
-    staged.push_back(c.bos_token);
-    BREW_CUDA(cudaMemcpyAsync(m->prompt_d, staged.data(), staged.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    cudaGraphExec_t g_pre = nullptr, g_full = nullptr;
-    if (n_prompt > 0 && (rc = get_graph(m, 1, false, &g_pre))) return rc;
-    if ((rc = get_graph(m, 1, true, &g_full))) return rc;
-    // prefill (ModelRunner.java:196-206): forward(tok_i, i); the logits of
-    // the prompt positions are never read, so the classifier is skipped
-    for (int i = 0; i < n_prompt; ++i) {
-        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, m->prompt_d + i, i, nullptr, m->am_out);
-        count_launch();
-        BREW_CUDA(cudaGraphLaunch(g_pre, s));
-    }
-    // decode (:141-152): the pending token is the last prompt token (or BOS)
-    // forwarded at position n_prompt, then each argmax at the next position
-    const int32_t* pending0 = n_prompt > 0 ? m->prompt_d + n_prompt - 1 : m->prompt_d + n_prompt;
-    for (int k = 0; k < limit; ++k) {
-        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, k == 0 ? pending0 : m->am_out, n_prompt + k,
-                                     k == 0 ? nullptr : m->gen_d + k - 1, m->am_out);
-        count_launch();
-        BREW_CUDA(cudaGraphLaunch(g_full, s));
-    }
-    if (limit > 0) {
-        step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, m->am_out, 0, m->gen_d + limit - 1, m->am_out);
-        count_launch();
-    }
-    BREW_CUDA(cudaGetLastError());
+    if ((rc = session_prefill(m, prompt, n_prompt, s))) return rc;
+    if ((rc = session_decode(m, limit, s))) return rc;
     std::vector<int32_t> gen(limit);
     if (limit > 0) BREW_CUDA(cudaMemcpyAsync(gen.data(), m->gen_d, limit * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));

@@ -9,14 +9,17 @@
 //     v = hi * 2^16 + mid * 2^8 + lo,   hi, mid, lo in [-128, 127].
 // With those three "limb" columns as the B operand of an int8 MMA, the
 // per-block integer sums are exact; the fp32 epilogue multiplies them by the
-// block's fp16 weight scale and s_j * 2^16 / 2^8 / 1.  The x rounding error is
+// block's fp16 weight scale and s_j, and the limb weights 2^16 / 2^8 / 1 are
+// applied (exactly) when the columns are combined.  The x rounding error is
 // 2^-24 relative to the block maximum, i.e. at the level of fp32 itself.
 //
-// Record of block j (NCOL = 3*batch columns, column n = 3*b + l for batch
-// element b and limb l), padded to a multiple of 16 bytes:
-//     int8   limbs[NCOL][32]
-//     float  sw[NCOL]      s_b * {65536, 256, 1}[l]
-//     int32  lsum[NCOL]    sum_i limbs[n][i]   (zero-point correction, Q4_0)
+// Record of block j for `batch` vectors, padded to a multiple of 16 bytes:
+//     int8   limbs[3*batch][32]   limb l of vector b at row 3*b + l
+//     float  s[batch]             block scale of vector b
+//     int32  lsum[3*batch]        sum_i limbs[3*b+l][i]  (zero-point correction, Q4_0)
+// In the MMA, vector b occupies the four B columns 4*b .. 4*b+3 (limbs
+// hi, mid, lo and a zero column), so each thread's pair of accumulator
+// columns belongs to one vector.
 #pragma once
 
 #include "brew_common.cuh"
@@ -25,14 +28,17 @@ namespace brew {
 
 constexpr float PREP_RANGE = 8290000.0f;   // |v| <= 8290001 keeps hi in [-127, 127]
 
-__host__ __device__ inline int prep_nt(int batch) { return (3 * batch + 7) / 8; }
-__host__ __device__ inline int prep_rec_bytes(int batch) { return (3 * batch * 40 + 15) & ~15; }
+// n8 MMA column tiles for `batch` vectors (4 columns per vector)
+__host__ __device__ inline int prep_nt(int batch) { return (batch + 1) / 2; }
+__host__ __device__ inline int prep_rec_bytes(int batch) { return (batch * (3 * 32 + 4 + 3 * 4) + 15) & ~15; }
+__host__ __device__ inline int prep_s_off(int batch) { return 3 * batch * 32; }
+__host__ __device__ inline int prep_lsum_off(int batch) { return 3 * batch * 32 + 4 * batch; }
 
 #ifdef __CUDACC__
 
-// One warp writes the record columns of batch element b for one block:
-// lane i holds x[32j + i].
-__device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int ncol, int b, float x) {
+// One warp writes the record entries of vector b for one block: lane i
+// holds x[32j + i].
+__device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int batch, int b, float x) {
     const int lane = threadIdx.x & 31;
     const float amax = warp_max(fabsf(x));
     const float inv = amax > 0.0f ? PREP_RANGE / amax : 0.0f;
@@ -48,11 +54,8 @@ __device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int ncol, int b, fl
     limbs[(3 * b + 2) * 32 + lane] = (int8_t)lo;
     const int shi = warp_sum_i(hi), smid = warp_sum_i(mid), slo = warp_sum_i(lo);
     if (lane == 0) {
-        float* sw = reinterpret_cast<float*>(rec + ncol * 32);
-        int* ls = reinterpret_cast<int*>(rec + ncol * 36);
-        sw[3 * b + 0] = s * 65536.0f;
-        sw[3 * b + 1] = s * 256.0f;
-        sw[3 * b + 2] = s;
+        reinterpret_cast<float*>(rec + prep_s_off(batch))[b] = s;
+        int* ls = reinterpret_cast<int*>(rec + prep_lsum_off(batch));
         ls[3 * b + 0] = shi;
         ls[3 * b + 1] = smid;
         ls[3 * b + 2] = slo;
@@ -89,7 +92,7 @@ __device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
 // written by other CTAs of the same kernel) (optionally RMS-normalised with weight
 // nw: x * scale * nw, Kernels.java:47-58) into records[K/32].
 static __device__ void prep_vector_cta(const float* x, int K, const float* nw, float eps, uint8_t* recs, int rec_bytes,
-                                int ncol, int b, float* red) {
+                                int batch, int b, float* red) {
     float scale = 1.0f;
     if (nw) {
         float ss = 0.0f;
@@ -104,7 +107,7 @@ static __device__ void prep_vector_cta(const float* x, int K, const float* nw, f
     for (int j = warp; j < K / 32; j += nw_) {
         float v = __ldcg(&x[32 * j + lane]);
         if (nw) v = v * scale * nw[32 * j + lane];
-        prep_emit_warp(recs + (size_t)j * rec_bytes, ncol, b, v);
+        prep_emit_warp(recs + (size_t)j * rec_bytes, batch, b, v);
     }
 }
 
