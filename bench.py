@@ -258,6 +258,16 @@ def run_gpu(args):
     t0 = time.perf_counter()
     dm = DeviceModel.synthesize(cfg, SEED)
     synth_s = time.perf_counter() - t0
+    if args.profile_decode:
+        # a short prompt, then a few decode steps (profiling entry: the decode
+        # kernel of the steps after the prompt)
+        rng = np.random.default_rng(SEED)
+        prompt = rng.integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+        dm.prefill(prompt)
+        toks = dm.decode(args.steps)
+        print(json.dumps({"profile_decode": True, "prompt": args.prompt_len, "steps": args.steps, "tokens": toks[:4]}))
+        dm.close()
+        return 0
     if args.kernel_only:
         # the decode matvec alone (profiling entry: a few launches, no decode)
         alg, kms, _ = kernel_roofline(dm, cfg, iters=args.steps)
@@ -358,6 +368,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
+    ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

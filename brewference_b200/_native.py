@@ -108,6 +108,8 @@ def lib():
         "brew_session_prefill": (I, [V, c_i32p, ctypes.c_int32, V]),
         "brew_session_decode": (I, [V, ctypes.c_int32, c_i32p, V]),
         "brew_model_step_kernels": (I, [V, ctypes.c_int32, c_i32p]),
+        "brew_model_set_trace": (I, [V, ctypes.c_int32]),
+        "brew_model_trace": (I, [V, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32, c_i32p]),
         "brew_prep_bytes": (I64, [ctypes.c_int32, ctypes.c_int32]),
         "brew_prepare_input_dev": (I, [V, ctypes.c_int32, ctypes.c_int32, V, V]),
         "brew_matmul_prepared_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),

@@ -213,6 +213,17 @@ class DeviceModel:
                 "decode")
         return out[:n_steps].tolist() if want_tokens else None
 
+    def set_trace(self, on: bool = True) -> None:
+        N.check(N.lib().brew_model_set_trace(self.handle, int(on)))
+
+    def trace(self) -> list:
+        """%globaltimer stamps (ns) of the last decode step, per CTA: start,
+        then per phase prep-done, work-done, barrier-passed."""
+        buf = (ctypes.c_int64 * (1 << 18))()
+        n = ctypes.c_int32()
+        N.check(N.lib().brew_model_trace(self.handle, buf, 1 << 18, ctypes.byref(n)))
+        return list(buf[: n.value])
+
     def step_kernels(self, batch: int = 1) -> int:
         n = ctypes.c_int32()
         N.check(N.lib().brew_model_step_kernels(self.handle, batch, ctypes.byref(n)))

@@ -129,6 +129,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     const uint64_t t0 = global_ns();
     for (uint32_t it = 0; it < BREW_SPIN_LIMIT; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(64);   // leave issue slots to the warps that compute
         if ((it & 255u) == 255u && global_ns() - t0 > 2000000000ull) break;
     }
     if (err_word) atomicOr(err_word, err);

@@ -2,26 +2,25 @@
 //
 // Replaces Linear.matmul (transformer/math/Linear.java:40-99).  Design:
 //   * Weights stay in their 34-byte (Q8_0) / 18-byte (Q4_0) blocks.  One
-//     producer warp streams 16-row tiles, KC blocks at a time, from HBM into
-//     a ring of shared-memory stages with cp.async.bulk (the TMA bulk-copy
-//     engine; no multicast), each row copy rounded out to 16-byte bounds.
-//   * The x side arrives as prep records (prep.cuh): per 32-block three
-//     int8 limb columns per batch element.  One mma.sync m16n8k32 int8 MMA
-//     then produces the exact integer block dot products of 16 rows x 8
-//     columns; the fp32 epilogue multiplies by the block's fp16 weight scale
-//     and the limb's scale and accumulates.  That is ~0.06 instructions per
-//     weight byte, so the kernel is bound by HBM, not by issue.
-//   * Work is split "stream-K": the grid is persistent (<= #SMs CTAs) and
-//     each CTA takes an equal contiguous share of (tile, stage) units; tiles
-//     cut between CTAs combine their partial sums in a fixed order, so the
-//     result is deterministic.
+//     producer warp streams them into a ring of shared-memory stages with TMA:
+//     cp.async.bulk.tensor.2d boxes of 16 rows x 8 blocks through a tensor map
+//     (row pitch a multiple of 16 bytes; no multicast), or bulk copies of whole
+//     rows otherwise.
+//   * The x side arrives as prep records (prep.cuh): per 32-block three int8
+//     limb columns per vector.  One mma.sync m16n8k32 int8 MMA gives the exact
+//     integer block dot products of 16 rows; the fp32 epilogue multiplies by
+//     the block's fp16 weight scale and the vector's block scale.
+//   * Each CTA owns whole 16-row tiles (no cross-CTA reduction).  With many
+//     tiles a warp owns a tile; with few, 2/4/8 warps split a tile's blocks and
+//     combine through shared memory in a fixed order: the result is
+//     deterministic.
 //   * Fused epilogues: bias, residual add, SwiGLU/GeGLU (gate and up rows in
-//     one tile), the next matvec's prep records, and a "last CTA" pass that
-//     RMS-normalises the finished vector for the next layer or reduces the
-//     classifier argmax.
+//     one tile) with the next matvec's prep records, a last-CTA pass that
+//     RMS-normalises the finished vector, and the classifier argmax.
 //   * Programmatic dependent launch: weight copies are issued before
 //     griddepcontrol.wait, so they overlap the previous kernel's tail.
 #include "matvec.cuh"
+#include "mv_device.cuh"
 #include "prep.cuh"
 
 #include <cudaTypedefs.h>
@@ -32,46 +31,6 @@
 namespace brew {
 
 namespace {
-
-// shared-memory loads by 32-bit shared-window address
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
-
-// 4 bytes at a 2-byte aligned shared-memory address: two aligned words and a
-// funnel shift (shift 0 or 16).
-__device__ __forceinline__ uint32_t lds32_a2(uint32_t a) {
-    const uint32_t b = a & ~3u;
-    return __funnelshift_r(lds32(b), lds32(b + 4), (a & 3u) * 8u);
-}
-
-__device__ __forceinline__ void mma_s8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // Global address of row r (0..15) of `tile`, or null past the matrix end.
 __device__ __forceinline__ const uint8_t* tile_row_ptr(const MvParams& p, int tile, int r) {
@@ -88,96 +47,13 @@ __device__ __forceinline__ const uint8_t* tile_row_ptr(const MvParams& p, int ti
     return p.seg[s].w + (int64_t)local * p.row_bytes;
 }
 
-__device__ __forceinline__ float act_glu(float g, int epi) {
-    // FfnActivation.silu / geluPytorchTanh evaluated in double, cast to float
-    // (transformer/ffn/FfnActivation.java:43-58).
-    const double v = (double)g;
-    double a;
-    if (epi == MV_EPI_GLU_GELU) {
-        const double inner = (double)0.7978845608028654f * (v + (double)0.044715f * v * v * v);
-        a = 0.5 * v * (1.0 + tanh(inner));
-    } else {
-        a = v / (1.0 + exp(-v));
-    }
-    return (float)a;
-}
-
-// Orderable 64-bit argmax key: larger value first, then smaller index
-// (Kernels.argMax keeps the first maximum).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-    uint32_t u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)idx);
-}
-
-// One 16-row x 32-element block: the int8 MMA of the weight fragment against
-// the limb columns of every vector, then acc += C * (d_row * s_vector).  Lane
-// (g, t) holds accumulator columns 8n+2t and 8n+2t+1 of rows g and g+8; both
-// columns belong to vector (8n+2t)/4 (4 columns per vector, see prep.cuh).
-template <int TYPE, int NT>
-__device__ __forceinline__ void mma_block(float (&acc)[NT][4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          float d0, float d1, uint32_t rec, int batch, int g, int t) {
-    const uint32_t soff = prep_s_off(batch), loff = prep_lsum_off(batch);
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        const int cB = n * 8 + g, bB = cB >> 2, lB = cB & 3;
-        const bool vB = lB < 3 && bB < batch;
-        const uint32_t ba = rec + (vB ? (3 * bB + lB) * 32 : 0) + 4 * t;
-        uint32_t b0 = lds32(ba), b1 = lds32(ba + 16);
-        if (!vB) b0 = b1 = 0u;
-        const int bC = (n * 8 + 2 * t) >> 2;
-        const int l0 = (2 * t) & 3;               // 0 or 2
-        const bool vC = bC < batch;
-        const int bCs = vC ? bC : 0;
-        int c[4];
-        if (TYPE == BREW_TYPE_Q8_0) {
-            mma_s8s8(c, a0, a1, a2, a3, b0, b1);
-        } else {
-            mma_u8s8(c, a0, a1, a2, a3, b0, b1);
-            // Q4_0 quants are stored as q+8: subtract 8 * sum(limbs)
-            const int ls0 = vC ? (int)lds32(rec + loff + 4 * (3 * bCs + l0)) : 0;
-            const int ls1 = (vC && l0 == 0) ? (int)lds32(rec + loff + 4 * (3 * bCs + 1)) : 0;
-            c[0] -= 8 * ls0;
-            c[1] -= 8 * ls1;
-            c[2] -= 8 * ls0;
-            c[3] -= 8 * ls1;
-        }
-        const float s = vC ? ldsf(rec + soff + 4 * bCs) : 0.0f;
-        const float ds0 = d0 * s, ds1 = d1 * s;
-        acc[n][0] = fmaf((float)c[0], ds0, acc[n][0]);
-        acc[n][1] = fmaf((float)c[1], ds0, acc[n][1]);
-        acc[n][2] = fmaf((float)c[2], ds1, acc[n][2]);
-        acc[n][3] = fmaf((float)c[3], ds1, acc[n][3]);
-    }
-}
-
-__device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xFFFFu))); }
-__device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
-
-// Rows per tile 16; a CTA owns whole tiles [t0, t1).  Group geometry: gs
-// tiles staged together, ws warps per tile (splitting the tile's blocks), nb
-// TMA boxes of `kcb` blocks per tile per stage.
-struct Geom {
-    int gs, ws, nb, KC, nchunks;
-};
-
 __device__ __forceinline__ Geom cta_geom(const MvParams& p, int nt) {
+    if (p.mode == MV_MODE_TMA) return tma_geom(nt, p.KB, p.nb_cap);
     Geom g;
-    if (p.mode == MV_MODE_TMA) {
-        g.gs = min(MV_MAX_BOXES, nt);
-        g.ws = g.gs >= 3 ? 2 : (g.gs == 2 ? 4 : 8);
-        const int nbmax = min(p.nb_cap, max(1, MV_MAX_BOXES / g.gs));
-        const int nbox = p.KB / p.kcb;
-        g.nb = 1;
-        for (int d = nbmax; d >= 1; --d)
-            if (nbox % d == 0) { g.nb = d; break; }
-        g.KC = p.kcb * g.nb;
-    } else {
-        g.gs = 1;
-        g.ws = 8;
-        g.nb = 1;
-        g.KC = p.mode == MV_MODE_CONTIG ? p.KB : p.kcb;
-    }
+    g.gs = 1;
+    g.ws = 8;
+    g.nb = 1;
+    g.KC = p.mode == MV_MODE_CONTIG ? p.KB : p.kcb;
     g.nchunks = p.KB / g.KC;
     return g;
 }
@@ -392,41 +268,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(const __grid_constant
             if (!aborted && tw < ng) {
                 const int tile = tg0 + tw;
                 if (p.mode == MV_MODE_TMA) {
-                    // boxes are [16 rows][8 blocks]; walk them in block pairs
-                    // (68 / 36 bytes: word aligned, only the even block's
-                    // quants need a byte permute)
-                    constexpr int BOXW = 8 * BB, PAIR = 2 * BB;
-                    const int npairs = geo.nb * 4;
-#pragma unroll 2
-                    for (int pp = sub; pp < npairs; pp += geo.ws) {
-                        const int bi = pp >> 2, pi = pp & 3;
-                        const uint32_t R0 = sb + ((tw * geo.nb + bi) * MV_TILE_ROWS + g) * BOXW + pi * PAIR;
-                        const uint32_t R1 = R0 + 8 * BOXW;
-                        const uint32_t recA = prep0 + (bi * 8 + pi * 2) * p.rec_bytes;
-                        const uint32_t recB = recA + p.rec_bytes;
-                        if (TYPE == BREW_TYPE_Q8_0) {
-                            const uint32_t dA0 = lds32(R0), dA1 = lds32(R1);
-                            const uint32_t dB0 = lds32(R0 + 32), dB1 = lds32(R1 + 32);
-                            const uint32_t a0 = __byte_perm(lds32(R0 + 4 * t), lds32(R0 + 4 * t + 4), 0x5432);
-                            const uint32_t a1 = __byte_perm(lds32(R1 + 4 * t), lds32(R1 + 4 * t + 4), 0x5432);
-                            const uint32_t a2 = __byte_perm(lds32(R0 + 4 * t + 16), lds32(R0 + 4 * t + 20), 0x5432);
-                            const uint32_t a3 = __byte_perm(lds32(R1 + 4 * t + 16), lds32(R1 + 4 * t + 20), 0x5432);
-                            mma_block<TYPE, NT>(acc, a0, a1, a2, a3, h2f_lo(dA0), h2f_lo(dA1), recA, p.batch, g, t);
-                            mma_block<TYPE, NT>(acc, lds32(R0 + 36 + 4 * t), lds32(R1 + 36 + 4 * t),
-                                                lds32(R0 + 52 + 4 * t), lds32(R1 + 52 + 4 * t), h2f_hi(dB0),
-                                                h2f_hi(dB1), recB, p.batch, g, t);
-                        } else {
-                            const uint32_t dA0 = lds32(R0), dA1 = lds32(R1);
-                            const uint32_t dB0 = lds32(R0 + 16), dB1 = lds32(R1 + 16);
-                            const uint32_t w0 = __byte_perm(lds32(R0 + 4 * t), lds32(R0 + 4 * t + 4), 0x5432);
-                            const uint32_t w1 = __byte_perm(lds32(R1 + 4 * t), lds32(R1 + 4 * t + 4), 0x5432);
-                            mma_block<TYPE, NT>(acc, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
-                                                (w1 >> 4) & 0x0F0F0F0Fu, h2f_lo(dA0), h2f_lo(dA1), recA, p.batch, g, t);
-                            const uint32_t v0 = lds32(R0 + 20 + 4 * t), v1 = lds32(R1 + 20 + 4 * t);
-                            mma_block<TYPE, NT>(acc, v0 & 0x0F0F0F0Fu, v1 & 0x0F0F0F0Fu, (v0 >> 4) & 0x0F0F0F0Fu,
-                                                (v1 >> 4) & 0x0F0F0F0Fu, h2f_hi(dB0), h2f_hi(dB1), recB, p.batch, g, t);
-                        }
-                    }
+                    tma_tile_stage<TYPE, NT>(acc, sb, prep0, p.rec_bytes, tw, geo.nb, sub, geo.ws, g, t, p.batch);
                 } else {
                     // CONTIG / ROW: rows at arbitrary 2-byte alignment, block by block
                     uint32_t row0, row1;
@@ -591,9 +433,9 @@ int launch_typed(const MvParams& p, cudaStream_t stream, bool pdl, int grid, siz
     return BREW_OK;
 }
 
-// The kernel is instantiated for NT in {1, 2, 3, 6, 12}: the n8 MMA tiles
-// (3 limb columns per batch element) rounded up.  Host-side shared-memory
-// sizing must use this same value.
+// The kernel is instantiated for NT in {1, 2, 4, 8}: the n8 MMA tiles (4
+// columns per vector) rounded up.  Host-side shared-memory sizing must use
+// this same value.
 int nt_instance(int batch) {
     const int nt = prep_nt(batch);
     return nt <= 2 ? nt : (nt <= 4 ? 4 : 8);
@@ -608,6 +450,8 @@ int launch_nt(const MvParams& p, cudaStream_t stream, bool pdl, int grid, size_t
         default: return launch_typed<TYPE, 8>(p, stream, pdl, grid, smem);
     }
 }
+
+}  // namespace
 
 // Tensor map over `rows` rows of `pitch` bytes as 8-byte elements, box of
 // `box_bytes` x `box_rows`.  Rows past the end read as zeros.
@@ -631,8 +475,6 @@ int encode_rows_map(CUtensorMap* map, const void* base, int rows, int pitch, int
                rows, pitch, box_bytes, box_rows);
     return BREW_OK;
 }
-
-}  // namespace
 
 int num_sms() {
     static int n = 0;

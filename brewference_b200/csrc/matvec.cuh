@@ -10,7 +10,7 @@ namespace brew {
 constexpr int MV_TILE_ROWS = 16;        // rows per tile (one m16 MMA row block)
 constexpr int MV_CONSUMER_WARPS = 8;
 constexpr int MV_THREADS = (MV_CONSUMER_WARPS + 1) * 32;
-constexpr int MV_MAX_BOXES = 4;         // TMA boxes (16 rows x kcb blocks) per stage
+constexpr int MV_MAX_BOXES = 8;         // TMA boxes (16 rows x kcb blocks) per stage
 constexpr int MV_MAX_BATCH = 16;        // per launch; larger batches loop on the host
 constexpr int MV_ARGMAX_MAX_BATCH = 16;
 
@@ -79,5 +79,9 @@ int prep_launch(const float* x, int ldx, int K, int batch, const float* norm_w, 
                 cudaStream_t stream, bool pdl);
 
 int num_sms();
+
+// Tensor map over `rows` rows of `pitch` bytes viewed as 8-byte elements,
+// with a box of `box_bytes` x `box_rows` (rows past the end read as zeros).
+int encode_rows_map(CUtensorMap* map, const void* base, int rows, int pitch, int box_bytes, int box_rows);
 
 }  // namespace brew

@@ -16,8 +16,10 @@
 // then the classifier matvec with a fused argmax.  The embedding lookup and
 // the first RMSNorm are one more kernel.
 #include "brew_internal.cuh"
+#include "decode.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -76,6 +78,14 @@ struct brew_model_s {
     int sess_generated = 0;                  // ids recorded in gen_d since prefill
     int32_t* h_pin = nullptr;                // pinned staging (tokens, pos, argmax)
     int h_pin_cap = 0;
+    // persistent decode kernel (batch <= DK_MAX_BATCH)
+    bool use_decode = false;
+    DecodeParams dp;
+    float *x1 = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
+    unsigned long long* bar = nullptr;
+    int* abort_flag = nullptr;
+    unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
+    int trace_n = 0;
 };
 
 namespace brew {
@@ -396,6 +406,15 @@ int launch_graph(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
     return BREW_OK;
 }
 
+int launch_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
+    if (m->use_decode && B == 1) {
+        // the decode kernel always runs the classifier (prefill logits are
+        // simply not read)
+        return decode_launch(m->dp, s);
+    }
+    return launch_graph(m, B, with_classifier, s);
+}
+
 int launch_step(brew_model_s* m, const int32_t* tok_src, int pos, int32_t* record, cudaStream_t s) {
     step_kernel<<<1, 32, 0, s>>>(m->tokens_d, m->pos_d, tok_src, pos, record, m->am_out);
     BREW_CUDA(cudaGetLastError());
@@ -427,7 +446,7 @@ int session_prefill(brew_model_s* m, const int32_t* prompt, int n_prompt, cudaSt
     int rc;
     for (int i = 0; i < n_prompt; ++i) {
         if ((rc = launch_step(m, m->prompt_d + i, i, nullptr, s))) return rc;
-        if ((rc = launch_graph(m, 1, false, s))) return rc;
+        if ((rc = launch_forward(m, 1, false, s))) return rc;
     }
     m->sess_pos = n_prompt;
     m->sess_pending = n_prompt > 0 ? m->prompt_d + n_prompt - 1 : m->prompt_d + n_prompt;
@@ -448,7 +467,7 @@ int session_decode(brew_model_s* m, int n_steps, cudaStream_t s) {
     for (int k = 0; k < n_steps; ++k) {
         const int g = m->sess_generated;
         if ((rc = launch_step(m, m->sess_pending, m->sess_pos, g > 0 ? m->gen_d + g - 1 : nullptr, s))) return rc;
-        if ((rc = launch_graph(m, 1, true, s))) return rc;
+        if ((rc = launch_forward(m, 1, true, s))) return rc;
         m->sess_pending = m->am_out;
         m->sess_pos++;
         m->sess_generated++;
@@ -458,9 +477,110 @@ int session_decode(brew_model_s* m, int n_steps, cudaStream_t s) {
     return BREW_OK;
 }
 
+// Sets up the persistent decode kernel when the shapes allow it.
+int setup_decode(brew_model_s* m) {
+    const brew_config& c = m->c;
+    if (!decode_supported(c, 1) || getenv("BREW_NO_DECODE_KERNEL")) return BREW_OK;
+    const int B = std::min(m->max_batch, DK_MAX_BATCH);
+    const int hd = c.head_size, half = hd / 2;
+    int rc;
+    if ((rc = dalloc(m, &m->x1, (size_t)B * c.dim))) return rc;
+    if ((rc = dalloc(m, &m->rope_cos, (size_t)2 * c.seq_len * half))) return rc;
+    if ((rc = dalloc(m, &m->rope_sin, (size_t)2 * c.seq_len * half))) return rc;
+    if ((rc = dalloc(m, &m->bar, 2))) return rc;
+    if ((rc = dalloc(m, &m->abort_flag, 1))) return rc;
+    const bool gem = c.arch == BREW_ARCH_GEMMA3;
+    const float base0 = c.rope_base > 0.0f ? c.rope_base : (c.arch == BREW_ARCH_LLAMA ? 10000.0f : 1000000.0f);
+    const float base1 = c.rope_base > 0.0f ? c.rope_base : (gem ? 10000.0f : base0);
+    const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
+    if ((rc = rope_tables_launch(m->rope_cos, m->rope_sin, c.seq_len, hd, base0, base1, scale, ctx().stream))) return rc;
+    DecodeParams& p = m->dp;
+    p = DecodeParams{};
+    p.arch = c.arch;
+    p.dim = c.dim;
+    p.hidden = c.hidden_dim;
+    p.n_layers = c.n_layers;
+    p.n_heads = c.n_heads;
+    p.n_kv = c.n_kv_heads;
+    p.hd = hd;
+    p.vocab = c.vocab_size;
+    p.seq_len = c.seq_len;
+    p.window = c.sliding_window;
+    p.batch = 1;
+    p.type_layer = c.type_q;
+    p.type_out = c.tied_embeddings ? c.type_embed : c.type_output;
+    p.eps = c.eps;
+    p.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
+    p.embed = m->t[T_EMBED]->d;
+    p.type_embed = c.type_embed;
+    p.rms_att = m->rms_att;
+    p.rms_ffn = m->rms_ffn;
+    p.rms_final = m->rms_final;
+    p.post_att = m->post_att;
+    p.post_ffn = m->post_ffn;
+    p.rms_q = m->rms_q;
+    p.rms_k = m->rms_k;
+    p.q_bias = m->q_bias;
+    p.k_bias = m->k_bias;
+    p.v_bias = m->v_bias;
+    p.kc = m->kc;
+    p.vc = m->vc;
+    p.cache_bstride = m->cache_bstride;
+    p.rope_cos = m->rope_cos;
+    p.rope_sin = m->rope_sin;
+    p.x0 = m->x;
+    p.x1 = m->x1;
+    p.xb = m->xb;
+    p.xb2 = m->xb2;
+    p.qkv = m->qkv;
+    p.hb = m->hb;
+    p.logits = m->logits;
+    p.nchunk = std::max(1, std::min(64, num_sms() / (B * c.n_kv_heads)));
+    if ((rc = dalloc(m, &m->dk_part, attn_part_floats(B, c.n_heads, p.nchunk, hd)))) return rc;
+    p.attn_part = m->dk_part;
+    p.attn_ctr = m->counters + c.hidden_dim / 32 + 8;
+    p.am_key = m->am_key;
+    p.am_out = m->am_out;
+    p.tokens = m->tokens_d;
+    p.pos = m->pos_d;
+    p.bar = m->bar;
+    p.abort = m->abort_flag;
+    p.err = ctx().err_word;
+    p.trace_slots = 1 + 3 * (5 * c.n_layers + 1);
+    m->trace_n = num_sms() * p.trace_slots;
+    if ((rc = dalloc(m, &m->trace, (size_t)m->trace_n))) return rc;
+    p.trace = getenv("BREW_TRACE") ? m->trace : nullptr;
+    const int64_t qw = (int64_t)c.n_heads * hd;
+    (void)qw;
+    rc = decode_prepare(&p, m->t[T_Q]->d, m->t[T_K]->d, m->t[T_V]->d, m->t[T_O]->d, m->t[T_GATE]->d, m->t[T_UP]->d,
+                        m->t[T_DOWN]->d, m->t[T_OUTPUT]->d);
+    if (rc == BREW_ERR_UNSUPPORTED) return BREW_OK;   // fall back to the kernel graph
+    if (rc) return rc;
+    m->use_decode = true;
+    return BREW_OK;
+}
+
+// One forward of `B` sequences reading tokens_d / pos_d: the persistent
+// decode kernel when available, else the captured kernel graph.
+int launch_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s);
+
+// After a device-side error the decode kernel's barrier words may be
+// inconsistent: clear them (and the abort flag) so the next step starts clean.
+int after_step_check(brew_model_s* m, const char* where) {
+    const int rc = check_device_error(where);
+    if (rc && m->use_decode) {
+        cudaMemset(m->bar, 0, 2 * sizeof(unsigned long long));
+        cudaMemset(m->abort_flag, 0, sizeof(int));
+        cudaMemset(m->am_key, 0, (size_t)m->max_batch * sizeof(unsigned long long));
+        cudaDeviceSynchronize();
+    }
+    return rc;
+}
+
 int model_finish_create(brew_model_s* m) {
     int rc = alloc_state(m);
     if (rc) return rc;
+    if ((rc = setup_decode(m))) return rc;
     BREW_CUDA(cudaStreamSynchronize(ctx().stream));
     BREW_CUDA(cudaDeviceSynchronize());
     return BREW_OK;
@@ -471,6 +591,7 @@ void model_destroy(brew_model_s* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_pin) cudaFreeHost(m->h_pin);
+    if (m->prompt_d) cudaFree(m->prompt_d);
     if (m->owns_tensors)
         for (int i = 0; i < T_COUNT; ++i)
             if (m->t[i]) brew_tensor_free(m->t[i]);
@@ -601,6 +722,24 @@ int brew_model_tensor(brew_model m, int which, brew_tensor* out) {
     return BREW_OK;
 }
 
+int brew_model_trace(brew_model m, int64_t* ns, int32_t max_n, int32_t* n) {
+    BREW_CHECK(m && ns && n, BREW_ERR_INVALID_ARG, "null argument");
+    *n = 0;
+    if (!m->use_decode || !m->dp.trace) return BREW_OK;
+    std::lock_guard<std::mutex> lk(api_mutex());
+    const int k = std::min(max_n, m->trace_n);
+    BREW_CUDA(cudaStreamSynchronize(ctx().stream));
+    BREW_CUDA(cudaMemcpy(ns, m->trace, (size_t)k * sizeof(int64_t), cudaMemcpyDeviceToHost));
+    *n = k;
+    return BREW_OK;
+}
+
+int brew_model_set_trace(brew_model m, int32_t on) {
+    BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null model");
+    if (m->use_decode) m->dp.trace = on ? m->trace : nullptr;
+    return BREW_OK;
+}
+
 int brew_model_reset(brew_model m) {
     BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null model");
     std::lock_guard<std::mutex> lk(api_mutex());
@@ -627,7 +766,7 @@ int brew_model_forward_dev(brew_model m, const int32_t* tokens_dev, const int32_
     }
     BREW_CUDA(cudaMemcpyAsync(m->tokens_d, tokens_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     BREW_CUDA(cudaMemcpyAsync(m->pos_d, pos_dev, batch * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
-    if ((rc = launch_graph(m, batch, true, s))) return rc;
+    if ((rc = launch_forward(m, batch, true, s))) return rc;
     if (logits_dev)
         BREW_CUDA(cudaMemcpyAsync(logits_dev, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float),
                                   cudaMemcpyDeviceToDevice, s));
@@ -659,13 +798,13 @@ int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos, 
     memcpy(hp + batch, pos, batch * sizeof(int32_t));
     BREW_CUDA(cudaMemcpyAsync(m->tokens_d, hp, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     BREW_CUDA(cudaMemcpyAsync(m->pos_d, hp + batch, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    if ((rc = launch_graph(m, batch, true, s))) return rc;
+    if ((rc = launch_forward(m, batch, true, s))) return rc;
     if (logits)
         BREW_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
     if (argmax) BREW_CUDA(cudaMemcpyAsync(hp + 2 * batch, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));
     if (argmax) memcpy(argmax, hp + 2 * batch, batch * sizeof(int32_t));
-    return check_device_error("brew_model_forward");
+    return after_step_check(m, "brew_model_forward");
 }
 
 int brew_session_prefill(brew_model m, const int32_t* prompt, int32_t n_prompt, void* stream) {
@@ -689,7 +828,7 @@ int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out, void* strea
     if (n_steps > 0)
         BREW_CUDA(cudaMemcpyAsync(out, m->gen_d + first, (size_t)n_steps * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));
-    return check_device_error("brew_session_decode");
+    return after_step_check(m, "brew_session_decode");
 }
 
 int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n) {
@@ -698,6 +837,10 @@ int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n) {
     int rc = ensure_init();
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(api_mutex());
+    if (m->use_decode && batch == 1) {
+        *n = 1;
+        return BREW_OK;
+    }
     cudaGraphExec_t g;
     if ((rc = get_graph(m, batch, true, &g))) return rc;
     *n = m->graph_kernels[batch * 2 + 1];
@@ -724,7 +867,7 @@ int brew_session_generate(brew_model m, const int32_t* prompt, int32_t n_prompt,
     std::vector<int32_t> gen(limit);
     if (limit > 0) BREW_CUDA(cudaMemcpyAsync(gen.data(), m->gen_d, limit * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));
-    rc = check_device_error("brew_session_generate");
+    rc = after_step_check(m, "brew_session_generate");
     if (rc) return rc;
     // stop at the first EOS, inclusive (:149-151)
     int n = 0;

@@ -242,6 +242,16 @@ BREW_API int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out_tok
 /* Kernels in one decode step's CUDA graph (for launch accounting). */
 BREW_API int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n_kernels);
 
+/* Phase tracing of the persistent decode kernel: when on, every CTA of every
+ * decode step records %globaltimer (ns) at its start and, per phase (5 per
+ * layer: QKV, attention, wo, gate|up, down; then the classifier), when its
+ * input preparation is done, when its work is done and when it leaves the
+ * grid barrier: [n_ctas][1 + 3 * (5 * n_layers + 1)] values.  brew_model_trace
+ * copies the last step's stamps (n = 0 when the model runs the kernel-graph
+ * path). */
+BREW_API int brew_model_set_trace(brew_model m, int32_t on);
+BREW_API int brew_model_trace(brew_model m, int64_t* ns, int32_t max_n, int32_t* n);
+
 /* Clears the sequence state (ModelSession.reset, ModelRunner.java:115-120). */
 BREW_API int brew_model_reset(brew_model m);
 
