@@ -39,18 +39,20 @@ namespace {
 enum { PH_QKV = 0, PH_O, PH_GU, PH_DOWN, PH_CLS };
 
 constexpr int ATTN_MIN_POS = 32;   // positions per attention CTA at least
+constexpr size_t DK_SMEM_BUDGET = 224 * 1024;   // dynamic shared memory of the decode kernel, at most
+constexpr int DK_RED_BYTES = 8 * 8 * 16 * 2 * 4;   // cross-warp partial sums of a tile group
+constexpr int DK_STAGE_BYTES = 64 * 544;           // one pipeline stage: 64 Q8_0 block-tiles
 
-struct DSeg {
-    int rows, tile0, map, yoff;
-    float* y;
-    const float* bias;
-    const float* resid;
-};
-
+// One matvec phase over fragment-packed tiles (packed.cuh): y = W x for the
+// tiles of this layer's family, split over the CTAs by whole tiles.
 struct DPhase {
-    int K, KB, tiles, nseg, epi, ldy, tt;
+    const uint8_t* w;        // this layer's packed tiles
+    int KB, tiles, rows, epi, ldy, tt;
     bool argmax;
-    DSeg s[3];
+    float* y;
+    const float* resid;      // STORE: y = resid + (W x + bias)
+    const float* bias[3];    // bias of rows [r0[k], r0[k + 1]) is bias[k][row - r0[k]]
+    int r0[4];
 };
 
 __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int ph, float* xcur) {
@@ -61,57 +63,80 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
     f.tt = P.type_layer;
     switch (ph) {
         case PH_QKV:
-            f.K = P.dim;
-            f.nseg = 3;
-            f.ldy = qw + 2 * kvd;
-            f.s[0] = {qw, 0, DK_MAP_Q, l * qw, P.qkv, P.q_bias ? P.q_bias + (int64_t)l * qw : nullptr, nullptr};
-            f.s[1] = {kvd, qw / 16, DK_MAP_K, l * kvd, P.qkv + qw, P.k_bias ? P.k_bias + (int64_t)l * kvd : nullptr, nullptr};
-            f.s[2] = {kvd, qw / 16 + kvd / 16, DK_MAP_V, l * kvd, P.qkv + qw + kvd,
-                      P.v_bias ? P.v_bias + (int64_t)l * kvd : nullptr, nullptr};
-            f.tiles = qw / 16 + 2 * (kvd / 16);
+            f.w = P.pk[PK_QKV] + (int64_t)l * P.pk_lb[PK_QKV];
+            f.KB = P.dim / 32;
+            f.rows = qw + 2 * kvd;
+            f.y = P.qkv;
+            f.ldy = f.rows;
+            f.bias[0] = P.q_bias ? P.q_bias + (int64_t)l * qw : nullptr;
+            f.bias[1] = P.k_bias ? P.k_bias + (int64_t)l * kvd : nullptr;
+            f.bias[2] = P.v_bias ? P.v_bias + (int64_t)l * kvd : nullptr;
+            f.r0[0] = 0;
+            f.r0[1] = qw;
+            f.r0[2] = qw + kvd;
+            f.r0[3] = qw + 2 * kvd;
+            f.tiles = f.rows / 16;
             break;
         case PH_O:
-            f.K = qw;
-            f.nseg = 1;
+            f.w = P.pk[PK_O] + (int64_t)l * P.pk_lb[PK_O];
+            f.KB = qw / 32;
+            f.rows = P.dim;
+            f.y = gem ? P.xb2 : xcur;
+            f.resid = gem ? nullptr : xcur;
             f.ldy = P.dim;
-            f.s[0] = {P.dim, 0, DK_MAP_O, l * P.dim, gem ? P.xb2 : xcur, nullptr, gem ? nullptr : xcur};
             f.tiles = P.dim / 16;
             break;
         case PH_GU:
-            f.K = P.dim;
-            f.nseg = 2;
+            f.w = P.pk[PK_GU] + (int64_t)l * P.pk_lb[PK_GU];
+            f.KB = P.dim / 32;
+            f.rows = P.hidden;
             f.epi = gem ? MV_EPI_GLU_GELU : MV_EPI_GLU_SILU;
+            f.y = P.hb;
             f.ldy = P.hidden;
-            f.s[0] = {P.hidden, 0, DK_MAP_GATE, l * P.hidden, P.hb, nullptr, nullptr};
-            f.s[1] = {P.hidden, 0, DK_MAP_UP, l * P.hidden, nullptr, nullptr, nullptr};
             f.tiles = P.hidden / 8;
             break;
         case PH_DOWN:
-            f.K = P.hidden;
-            f.nseg = 1;
+            f.w = P.pk[PK_DOWN] + (int64_t)l * P.pk_lb[PK_DOWN];
+            f.KB = P.hidden / 32;
+            f.rows = P.dim;
+            f.y = gem ? P.xb2 : xcur;
+            f.resid = gem ? nullptr : xcur;
             f.ldy = P.dim;
-            f.s[0] = {P.dim, 0, DK_MAP_DOWN, l * P.dim, gem ? P.xb2 : xcur, nullptr, gem ? nullptr : xcur};
             f.tiles = P.dim / 16;
             break;
         default:  // PH_CLS
-            f.K = P.dim;
-            f.nseg = 1;
-            f.ldy = P.vocab;
+            f.w = P.pk[PK_OUT];
+            f.KB = P.dim / 32;
+            f.rows = P.vocab;
             f.tt = P.type_out;
             f.argmax = true;
-            f.s[0] = {P.vocab, 0, DK_MAP_OUT, 0, P.logits, nullptr, nullptr};
+            f.y = P.logits;
+            f.ldy = P.vocab;
             f.tiles = (P.vocab + 15) / 16;
             break;
     }
-    f.KB = f.K / 32;
     return f;
 }
 
-__device__ __forceinline__ int seg_of(const DPhase& f, int tile) {
-    int s = 0;
-    if (f.nseg > 1 && f.epi == MV_EPI_STORE && tile >= f.s[1].tile0) s = 1;
-    if (f.nseg > 2 && tile >= f.s[2].tile0) s = 2;
-    return s;
+// Stage geometry of a CTA that owns `nt` tiles: gs tiles per group (their
+// accumulators live in registers together), KC block columns of each per
+// stage (a multiple of 8 dividing KB: warp w takes columns w, w + 8, ...).
+struct PGeom {
+    int gs, KC, nchunks;
+};
+
+__device__ __forceinline__ PGeom pk_geom(int nt, int KB, int bs, int stage_bytes) {
+    PGeom g;
+    g.gs = min(8, nt);
+    const int cap = min(KB, stage_bytes / (g.gs * bs));
+    g.KC = 8;
+    for (int kc = (cap / 8) * 8; kc >= 8; kc -= 8)
+        if (KB % kc == 0) {
+            g.KC = kc;
+            break;
+        }
+    g.nchunks = KB / g.KC;
+    return g;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -162,29 +187,47 @@ __device__ __forceinline__ float consumer_sum(float v, float* red) {
 
 enum { SRC_EMBED = 0, SRC_PLAIN = 1, SRC_GEMMA_ADD = 2 };
 
-// Loads K floats (K % 4 == 0, 16-byte aligned) into shared memory with every
-// load in flight at once (through L2: the data was written by other CTAs).
-__device__ __forceinline__ void stage_vec(float* dst, const float* src, int K) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    const int n4 = K / 4;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < n4; i += 256) d4[i] = __ldcg(&s4[i]);
+// Copies n4 float4 from global memory (through L2: the data may have been
+// written by other CTAs of this kernel) to shared memory, and optionally a
+// second array beside it, as asynchronous copies that are all in flight at
+// once (completed by cp_async_wait_all).
+__device__ __forceinline__ void stage_async(float4* d0, const float4* s0, float4* d1, const float4* s1, int n4) {
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        if (s0) cp_async16(d0 + i, s0 + i);
+        if (s1) cp_async16(d1 + i, s1 + i);
+    }
+}
+
+// This thread's sum of squares over the float4 it staged (i = tid + 256 k).
+__device__ __forceinline__ float sumsq4(const float4* v, int n4) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        const float4 a = v[i];
+        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    }
+    return ss;
 }
 
 // Builds the prep records of one phase's input vector(s) in shared memory.
 //   SRC_EMBED      v = dequant(token row) (* sqrt(dim), Gemma3); written to xout
 //   SRC_PLAIN      v = src
 //   SRC_GEMMA_ADD  v = src + rmsnorm(t, tw)   (Gemma3 post-norm residual); written to xout
-// then records of rmsnorm(v, nw) (nw != null) or of v.  The vector is first
-// staged in shared memory (`vec`, K floats).  xout writes are split over the
-// CTAs by block (block j by CTA j % G), so each element has one writer.
+// then records of rmsnorm(v, nw) (nw != null) or of v.  The vector is staged
+// in shared memory (`vec`, K floats) and the norm weight beside it (K more
+// floats).  xout writes are split over the CTAs by block (block j by CTA
+// j % G), so each element has one writer.  `lsum`: the consumer multiplies
+// Q4_0 blocks (needs the limb sums).
 __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, int ld, int K, const float* nw,
-                           const float* t, const float* tw, float* xout, uint8_t* prep, float* vec, float* red) {
+                           const float* t, const float* tw, float* xout, uint8_t* prep, float* vec, float* red,
+                           bool lsum) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int KB = K / 32;
+    const int KB = K / 32, K4 = K / 4;
     const int G = gridDim.x;
+    float4* v4 = reinterpret_cast<float4*>(vec);
+    float4* w4 = v4 + K4;
+    const float4* nw4 = reinterpret_cast<const float4*>(nw);
     for (int b = 0; b < P.batch; ++b) {
+        float ss = 0.0f;
         if (mode == SRC_EMBED) {
             int tok = P.tokens[b];
             if (tok < 0 || tok >= P.vocab) {
@@ -196,68 +239,59 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
                 float v = dequant_elem(P.type_embed, P.embed, (int64_t)tok * K + i);
                 vec[i] = P.arch == BREW_ARCH_GEMMA3 ? __fmul_rn(v, es) : v;
             }
+            if (nw) stage_async(w4, nullptr, w4, nw4, K4);
+            cp_async_wait_all();
             consumer_bar();
+            for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
         } else if (mode == SRC_GEMMA_ADD) {
-            stage_vec(vec, t + (int64_t)b * ld, K);
+            stage_async(v4, reinterpret_cast<const float4*>(t + (int64_t)b * ld), w4,
+                        reinterpret_cast<const float4*>(tw), K4);
+            cp_async_wait_all();
             consumer_bar();
-            float ss = 0.0f;
-            for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
-            const float tsc = rms_scale(consumer_sum(ss, red), K, P.eps);
+            const float tsc = rms_scale(consumer_sum(sumsq4(v4, K4), red), K, P.eps);
             const float* sb = src + (int64_t)b * ld;
-            for (int i = threadIdx.x; i < K; i += 256) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * tw[i];
+            for (int i = threadIdx.x; i < K; i += 256) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * vec[K + i];
             consumer_bar();
-        } else {
-            stage_vec(vec, src + (int64_t)b * ld, K);
-            consumer_bar();
-        }
-        float scale = 1.0f;
-        if (nw) {
-            float ss = 0.0f;
+            if (nw) stage_async(w4, nullptr, w4, nw4, K4);
+            cp_async_wait_all();
             for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
-            scale = rms_scale(consumer_sum(ss, red), K, P.eps);
+        } else {
+            stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4, nw ? nw4 : nullptr, K4);
+            cp_async_wait_all();
+            // each thread reads back only the float4 it copied itself
+            if (nw) ss = sumsq4(v4, K4);
         }
-        for (int j = warp; j < KB; j += 8) {
-            const float v = vec[32 * j + lane];
-            if (xout && (j % G) == (int)blockIdx.x) __stcg(&xout[(int64_t)b * ld + 32 * j + lane], v);
-            const float r = nw ? v * scale * nw[32 * j + lane] : v;
-            prep_emit_warp(prep + (size_t)j * P.rec_bytes, P.batch, b, r);
+        // one barrier publishes the staged vector and the partial sums
+        if (nw) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
         }
         consumer_bar();
-    }
-}
-
-// Writes one finished tile of a phase (values summed over the tile's ws warps
-// and the three limb columns).
-template <int NTC>
-__device__ void phase_tile_out(const DecodeParams& P, const DPhase& f, int tile, const float* red, int warp0, int ws,
-                               int lane, unsigned long long* s_best) {
-    auto V = [&](int r, int b) {
-        float v = 0.0f;
-        for (int s = 0; s < ws; ++s) {
-            const float* rr = red + ((warp0 + s) * 16 + r) * NTC + 4 * b;
-            v += (rr[2] + rr[1] * 256.0f) + rr[0] * 65536.0f;
+        float scale = 1.0f;
+        if (nw) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) tot += red[w];
+            scale = rms_scale(tot, K, P.eps);
         }
-        return v;
-    };
-    if (f.epi == MV_EPI_STORE) {
-        const DSeg& sg = f.s[seg_of(f, tile)];
-        const int rb = (tile - sg.tile0) * 16;
-        for (int idx = lane; idx < 16 * P.batch; idx += 32) {
-            const int r = idx & 15, b = idx >> 4;
-            const int row = rb + r;
-            if (row >= sg.rows) continue;
-            float v = V(r, b);
-            if (sg.bias) v = v + sg.bias[row];
-            if (sg.resid) v = __ldcg(&sg.resid[(int64_t)b * f.ldy + row]) + v;
-            sg.y[(int64_t)b * f.ldy + row] = v;
-            if (f.argmax) atomicMax(&s_best[b], argmax_key(v, row));
+        const int gq = lane >> 3, e = (lane & 7) * 4;
+        for (int j0 = warp * 4; j0 < KB; j0 += 32) {
+            const int j = j0 + gq;
+            const bool ok = j < KB;
+            const int jj = ok ? j : KB - 1;
+            float4 v = v4[(32 * jj + e) >> 2];
+            if (xout && ok && (j % G) == (int)blockIdx.x)
+                __stcg(reinterpret_cast<float4*>(xout + (int64_t)b * ld + 32 * j + e), v);
+            if (nw) {
+                const float4 w = w4[(32 * jj + e) >> 2];
+                v.x = v.x * scale * w.x;
+                v.y = v.y * scale * w.y;
+                v.z = v.z * scale * w.z;
+                v.w = v.w * scale * w.w;
+            }
+            prep_emit_quad(prep + (size_t)jj * P.rec_bytes, P.batch, b, v, ok, lsum);
         }
-        return;
-    }
-    const int i0 = tile * 8;
-    for (int idx = lane; idx < 8 * P.batch; idx += 32) {
-        const int r = idx & 7, b = idx >> 3;
-        f.s[0].y[(int64_t)b * f.ldy + i0 + r] = act_glu(V(r, b), f.epi) * V(r + 8, b);
+        consumer_bar();
     }
 }
 
@@ -268,70 +302,172 @@ struct Ring {
     int ns, stage_bytes;
 };
 
-// Consumer side of one matvec phase: this CTA's tiles, stage by stage.
+__device__ __forceinline__ uint4 lds128(uint32_t a) { return *reinterpret_cast<const uint4*>(sptr(a)); }
+__device__ __forceinline__ uint2 lds64(uint32_t a) { return *reinterpret_cast<const uint2*>(sptr(a)); }
+
+// Consumer side of one matvec phase: this CTA's tiles in groups of up to 8,
+// stage by stage.  Warp w multiplies block columns w, w + 8, ... of the stage
+// for every tile of the group (the x operand of a column is loaded once and
+// used for all tiles).  At the end of a group the warps' partial sums meet
+// in shared memory (`red`, [8 warps][8 tiles][16 rows][2 vectors]) and each
+// of the 256 threads finishes one output.
 template <int TT, int NT>
 __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q, uint32_t prep_s,
-                         float* red, unsigned long long* s_best, bool& aborted) {
-    constexpr int NTC = NT * 8;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+                         float* red, unsigned long long* s_best, bool& aborted, unsigned long long* t_full) {
+    static_assert(NT == 1, "decode batch <= 2: one n8 column tile");
+    constexpr int BS = pk_block_bytes(TT), SO = pk_scale_off(TT);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
     const int t0 = (int)((int64_t)blockIdx.x * f.tiles / G);
     const int t1 = (int)((int64_t)(blockIdx.x + 1) * f.tiles / G);
     const int nt = t1 - t0;
     if (nt <= 0) return;
-    const Geom geo = tma_geom(nt, f.KB, P.nb_cap);
+    const int batch = P.batch;
+    const PGeom geo = pk_geom(nt, f.KB, BS, ring.stage_bytes);
     const int ngroups = (nt + geo.gs - 1) / geo.gs;
-    const int tw = warp / geo.ws, sub = warp % geo.ws;
-    float acc[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+    const bool glu = f.epi != MV_EPI_STORE;
+    const int per_tile = (glu ? 8 : 16) * batch;
+    // x-operand offsets inside a prep record for this lane (prep.cuh):
+    // B column g = limb (g & 3) of vector g >> 2; accumulator columns 2t, 2t+1
+    // belong to vector t >> 1 (limbs (2t) & 3 and (2t + 1) & 3)
+    const int bB = g >> 2, lB = g & 3;
+    const bool vB = lB < 3 && bB < batch;
+    const uint32_t boff = (vB ? (3 * bB + lB) * 32 : 0) + 4 * t;
+    const int bC = t >> 1;
+    const bool vC = bC < batch;
+    const int bCs = vC ? bC : 0;
+    const int l0 = (2 * t) & 3;
+    const uint32_t soff = prep_s_off(batch) + 4 * bCs;
+    const uint32_t loff0 = prep_lsum_off(batch) + 4 * (3 * bCs + l0);
+    const uint32_t loff1 = prep_lsum_off(batch) + 4 * (3 * bCs + 1);
     for (int grp = 0; grp < ngroups; ++grp) {
         const int tg0 = t0 + grp * geo.gs;
         const int ng = min(geo.gs, t1 - tg0);
+        // this thread's output of the group: its bias and residual are read
+        // now, so that their latency overlaps the MMA loop
+        const int ok = tid / per_tile, orem = tid % per_tile;
+        const int orow = orem / batch, ob = orem % batch;
+        float pr = 0.0f, pb = 0.0f;
+        if (!glu && ok < ng) {
+            const int row = (tg0 + ok) * 16 + orow;
+            if (row < f.rows) {
+                for (int k = 0; k < 3; ++k)
+                    if (f.bias[k] && row >= f.r0[k] && row < f.r0[k + 1]) pb = __ldg(&f.bias[k][row - f.r0[k]]);
+                if (f.resid) pr = __ldcg(&f.resid[(int64_t)ob * f.ldy + row]);
+            }
+        }
+        float acc[8][4];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
         for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
             const int stage = q % ring.ns;
             if (!aborted && !mbar_wait_bounded(&ring.full[stage], (q / ring.ns) & 1, P.err, BREW_DEVERR_TIMEOUT_FULL))
                 aborted = true;
-            if (!aborted && tw < ng) {
+            if (t_full && warp == 0) *t_full = global_ns();
+            if (!aborted) {
                 const uint32_t sb = smem_u32(ring.stages + (size_t)stage * ring.stage_bytes);
-                tma_tile_stage<TT, NT>(acc, sb, prep_s + chunk * geo.KC * P.rec_bytes, P.rec_bytes, tw, geo.nb, sub,
-                                       geo.ws, g, t, P.batch);
+                for (int kb = warp; kb < geo.KC; kb += 8) {
+                    const uint32_t rec = prep_s + (chunk * geo.KC + kb) * P.rec_bytes;
+                    uint32_t b0 = lds32(rec + boff), b1 = lds32(rec + boff + 16);
+                    if (!vB) b0 = b1 = 0u;
+                    const float s = vC ? ldsf(rec + soff) : 0.0f;
+                    int ls0 = 0, ls1 = 0;
+                    if (TT == BREW_TYPE_Q4_0) {   // Q4_0 quants are stored as q + 8
+                        ls0 = vC ? 8 * (int)lds32(rec + loff0) : 0;
+                        ls1 = (vC && l0 == 0) ? 8 * (int)lds32(rec + loff1) : 0;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        if (k < ng) {
+                            const uint32_t blk = sb + (k * geo.KC + kb) * BS;
+                            uint32_t a0, a1, a2, a3;
+                            int c[4];
+                            if (TT == BREW_TYPE_Q8_0) {
+                                const uint4 A = lds128(blk + lane * 16);
+                                a0 = A.x;
+                                a1 = A.y;
+                                a2 = A.z;
+                                a3 = A.w;
+                                mma_s8s8(c, a0, a1, a2, a3, b0, b1);
+                            } else {
+                                const uint2 W = lds64(blk + lane * 8);
+                                a0 = W.x & 0x0F0F0F0Fu;
+                                a1 = W.y & 0x0F0F0F0Fu;
+                                a2 = (W.x >> 4) & 0x0F0F0F0Fu;
+                                a3 = (W.y >> 4) & 0x0F0F0F0Fu;
+                                mma_u8s8(c, a0, a1, a2, a3, b0, b1);
+                                c[0] -= ls0;
+                                c[1] -= ls1;
+                                c[2] -= ls0;
+                                c[3] -= ls1;
+                            }
+                            const uint32_t dd = lds32(blk + SO + 4 * g);
+                            const float ds0 = h2f_lo(dd) * s, ds1 = h2f_hi(dd) * s;
+                            acc[k][0] = fmaf((float)c[0], ds0, acc[k][0]);
+                            acc[k][1] = fmaf((float)c[1], ds0, acc[k][1]);
+                            acc[k][2] = fmaf((float)c[2], ds1, acc[k][2]);
+                            acc[k][3] = fmaf((float)c[3], ds1, acc[k][3]);
+                        }
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&ring.empty[stage]);
         }
-        float* myred = red + warp * 16 * NTC;
-        if (tw < ng) {
+        // limbs hi / mid (lane t even) and lo (lane t + 1) -> one value per
+        // row and vector: v = (lo + mid * 2^8) + hi * 2^16
 #pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                myred[g * NTC + n * 8 + 2 * t] = acc[n][0];
-                myred[g * NTC + n * 8 + 2 * t + 1] = acc[n][1];
-                myred[(g + 8) * NTC + n * 8 + 2 * t] = acc[n][2];
-                myred[(g + 8) * NTC + n * 8 + 2 * t + 1] = acc[n][3];
-                acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+        for (int k = 0; k < 8; ++k) {
+            const float lo0 = __shfl_down_sync(0xffffffffu, acc[k][0], 1);
+            const float lo1 = __shfl_down_sync(0xffffffffu, acc[k][2], 1);
+            if (k < ng && (t & 1) == 0 && bC < batch) {
+                red[((warp * 8 + k) * 16 + g) * 2 + bC] = (lo0 + acc[k][1] * 256.0f) + acc[k][0] * 65536.0f;
+                red[((warp * 8 + k) * 16 + g + 8) * 2 + bC] = (lo1 + acc[k][3] * 256.0f) + acc[k][2] * 65536.0f;
             }
         }
         consumer_bar();
-        if (tw < ng && sub == 0) phase_tile_out<NTC>(P, f, tg0 + tw, red, warp, geo.ws, lane, s_best);
+        if (ok < ng) {
+            auto V = [&](int r) {
+                float v = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) v += red[((w * 8 + ok) * 16 + r) * 2 + ob];
+                return v;
+            };
+            if (!glu) {
+                const int row = (tg0 + ok) * 16 + orow;
+                if (row < f.rows) {
+                    float v = V(orow);
+                    bool hb = false;
+                    for (int k = 0; k < 3; ++k) hb |= f.bias[k] && row >= f.r0[k] && row < f.r0[k + 1];
+                    if (hb) v = v + pb;
+                    if (f.resid) v = pr + v;
+                    f.y[(int64_t)ob * f.ldy + row] = v;
+                    if (f.argmax) atomicMax(&s_best[ob], argmax_key(v, row));
+                }
+            } else {
+                const int i = (tg0 + ok) * 8 + orow;
+                f.y[(int64_t)ob * f.ldy + i] = act_glu(V(orow), f.epi) * V(orow + 8);
+            }
+        }
         consumer_bar();
     }
 }
 
-// Producer side of one matvec phase: the same tiles and stages, in order.
+// Producer side of one matvec phase: the same tiles and stages, in order;
+// one bulk copy per tile per stage (the tile's KC block-tiles are contiguous).
 template <int TT>
 __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q) {
-    constexpr int BB = TT == BREW_TYPE_Q8_0 ? 34 : 18;
-    constexpr int BOXW = 8 * BB;
+    constexpr int BS = pk_block_bytes(TT);
     const int lane = threadIdx.x & 31;
     const int G = gridDim.x;
     const int t0 = (int)((int64_t)blockIdx.x * f.tiles / G);
     const int t1 = (int)((int64_t)(blockIdx.x + 1) * f.tiles / G);
     const int nt = t1 - t0;
     if (nt <= 0) return;
-    const Geom geo = tma_geom(nt, f.KB, P.nb_cap);
+    const PGeom geo = pk_geom(nt, f.KB, BS, ring.stage_bytes);
     const int ngroups = (nt + geo.gs - 1) / geo.gs;
-    const bool glu = f.epi != MV_EPI_STORE;
+    const uint32_t cbytes = (uint32_t)geo.KC * BS;
     for (int grp = 0; grp < ngroups; ++grp) {
         const int tg0 = t0 + grp * geo.gs;
         const int ng = min(geo.gs, t1 - tg0);
@@ -355,53 +491,54 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
                 }
             }
             uint8_t* sbase = ring.stages + (size_t)stage * ring.stage_bytes;
-            const int nbox = ng * geo.nb * (glu ? 2 : 1);
-            if (lane == 0) mbar_arrive_expect_tx(&ring.full[stage], ng * geo.nb * 16 * BOXW);
+            if (lane == 0) mbar_arrive_expect_tx(&ring.full[stage], (uint32_t)ng * cbytes);
             __syncwarp();
-            for (int k = lane; k < nbox; k += 32) {
-                const int half = glu ? (k & 1) : 0;
-                const int kb = glu ? (k >> 1) : k;
-                const int ts = kb / geo.nb, bi = kb % geo.nb;
-                const int tile = tg0 + ts;
-                const int x = (chunk * geo.KC + bi * 8) * BB / 8;
-                uint8_t* dst = sbase + ((ts * geo.nb + bi) * 16 + half * 8) * BOXW;
-                if (glu) {
-                    const DSeg& sg = f.s[half];
-                    tma_load_2d(dst, &P.maps[sg.map], x, sg.yoff + tile * 8, &ring.full[stage]);
-                } else {
-                    const DSeg& sg = f.s[seg_of(f, tile)];
-                    tma_load_2d(dst, &P.maps[sg.map], x, sg.yoff + (tile - sg.tile0) * 16, &ring.full[stage]);
-                }
-            }
+            if (lane < ng)
+                bulk_g2s(sbase + (size_t)lane * cbytes,
+                         f.w + ((int64_t)(tg0 + lane) * f.KB + (int64_t)chunk * geo.KC) * BS, cbytes, &ring.full[stage]);
             __syncwarp();
         }
     }
 }
 
-// Positions of K / V staged in shared memory at a time.
-__device__ __forceinline__ int attn_sub(int hd) { return hd <= 128 ? 64 : 32; }
-
 // Attention for the items of this CTA (AttentionEngine.attend), then the
-// last CTA of each (sequence, kv head) combines the chunks into xb.  K and V
-// rows of a chunk are staged in shared memory (`kv`, attn_sub(hd) positions
-// at a time) with every load in flight.
-__device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
-    const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2;
+// last CTA of each (sequence, kv head) combines the chunks into xb.
+//
+// An item is (sequence, kv head, chunk of positions).  Everything it reads
+// (its q heads, the new k and v, the head-norm weights, the RoPE row and the
+// K / V rows of the chunk) is fetched with asynchronous global->shared copies
+// issued together, so the item waits for one memory round trip instead of
+// one per dependent load.  Chunks longer than attn_sub(hd) positions are
+// walked in rounds with a running (online) softmax.  `sm` is the attention
+// area of shared memory (P.attn_floats floats):
+//   K rows [SUB][hd] | V rows [SUB][hd] | q [G][hd] | k [hd] | v [hd] |
+//   q-norm w [hd] | k-norm w [hd] | cos [hd/2] | sin [hd/2] |
+//   scores [G][SUB] | per head: running max, running sum, round rescale, -
+// and, for the combine, the partials [heads][nchunk][hd + 4].
+__device__ void attn_phase(const DecodeParams& P, int l, float* sm) {
+    const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool gem = P.arch == BREW_ARCH_GEMMA3;
     const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
     const int window = (gem && !global) ? P.window : 0;
     const int table = (gem && !global) ? 1 : 0;
+    const bool inter = P.arch == BREW_ARCH_LLAMA;
     const int nch = P.nchunk;
-    const int cap = max(ATTN_MIN_POS, (P.seq_len + nch - 1) / nch);
     const int SUB = attn_sub(hd);
-    float* qs = sm;                // [G][hd]
-    float* ks = qs + G * hd;       // [hd]
-    float* sc = ks + hd;           // [G][cap]
-    float* wc = sc + G * cap;      // [G][nch]
-    float* sml = wc + G * nch;     // [2][16]: m, l / 1/L
-    int* s_last = reinterpret_cast<int*>(sml + 32);
+    const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
+    float* kb = sm;
+    float* vb = kb + SUB * hd;
+    float* qs = vb + SUB * hd;
+    float* ks = qs + G * hd;
+    float* vs = ks + hd;
+    float* wq = vs + hd;
+    float* wk = wq + hd;
+    float* cs = wk + hd;
+    float* sn = cs + half;
+    float* sc = sn + half;
+    float* st = sc + G * SUB;
+    __shared__ int s_last;
     const int items = P.batch * P.n_kv * nch;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int c = item % nch, hk = (item / nch) % P.n_kv, b = item / (nch * P.n_kv);
@@ -415,21 +552,53 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
         const int per = max(ATTN_MIN_POS, (len + nch - 1) / nch);
         const int used = (len + per - 1) / per;
         const int p0 = start + c * per;
-        const int n = min(cap, max(0, min(pos + 1, p0 + per) - p0));
-        const int stride = hd + 2;
+        const int n = max(0, min(pos + 1, p0 + per) - p0);
         float* pbase = P.attn_part + ((int64_t)b * P.n_heads + (int64_t)hk * G) * nch * stride;
         float* kc = P.kc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
         float* vc = P.vc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
         if (c < used) {
             const float* qsrc = P.qkv + (int64_t)b * ldq + (int64_t)hk * G * hd;
-            for (int i = tid; i < G * hd; i += 256) qs[i] = __ldcg(&qsrc[i]);
             const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
-            for (int i = tid; i < hd; i += 256) ks[i] = __ldcg(&ksrc[i]);
+            const float* vsrc = ksrc + kvd;
+            const float* csrc = P.rope_cos + ((int64_t)table * P.seq_len + pos) * half;
+            const float* ssrc = P.rope_sin + ((int64_t)table * P.seq_len + pos) * half;
+            // K / V rows of positions r0 .. r0 + SUB - 1 of the chunk; the row
+            // of this step's position comes from k / v instead (not yet cached)
+            auto issue_round = [&](int r0) {
+                const int ns = min(SUB, n - r0);
+                for (int i = tid; i < ns * hd4; i += 256) {
+                    const int r = i / hd4, ci = i % hd4;
+                    const int p = p0 + r0 + r;
+                    if (p == pos) continue;
+                    const int64_t off = (int64_t)p * kvd + (int64_t)hk * hd + 4 * ci;
+                    cp_async16(kb + r * hd + 4 * ci, kc + off);
+                    cp_async16(vb + r * hd + 4 * ci, vc + off);
+                }
+            };
+            for (int i = tid; i < G * hd4; i += 256) cp_async16(qs + 4 * i, qsrc + 4 * i);
+            for (int i = tid; i < hd4; i += 256) {
+                cp_async16(ks + 4 * i, ksrc + 4 * i);
+                cp_async16(vs + 4 * i, vsrc + 4 * i);
+                if (P.rms_q) {
+                    cp_async16(wq + 4 * i, P.rms_q + (int64_t)l * hd + 4 * i);
+                    cp_async16(wk + 4 * i, P.rms_k + (int64_t)l * hd + 4 * i);
+                }
+            }
+            for (int i = tid; i < half / 4; i += 256) {
+                cp_async16(cs + 4 * i, csrc + 4 * i);
+                cp_async16(sn + 4 * i, ssrc + 4 * i);
+            }
+            issue_round(0);
+            if (tid < G) {
+                st[4 * tid + 0] = -INFINITY;
+                st[4 * tid + 1] = 0.0f;
+            }
+            cp_async_wait_all();
             consumer_bar();
             if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
                 for (int hh = warp; hh <= G; hh += 8) {
                     float* vecp = hh < G ? qs + hh * hd : ks;
-                    const float* w = (hh < G ? P.rms_q : P.rms_k) + (int64_t)l * hd;
+                    const float* w = hh < G ? wq : wk;
                     float ss = 0.0f;
                     for (int i = lane; i < hd; i += 32) ss += vecp[i] * vecp[i];
                     const float scale = rms_scale(warp_sum(ss), hd, P.eps);
@@ -438,10 +607,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
                 }
                 consumer_bar();
             }
-            const float* cs = P.rope_cos + ((int64_t)table * P.seq_len + pos) * half;
-            const float* sn = P.rope_sin + ((int64_t)table * P.seq_len + pos) * half;
-            const bool inter = P.arch == BREW_ARCH_LLAMA;
-            for (int idx = tid; idx < (G + 1) * half; idx += 256) {
+            for (int idx = tid; idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
                 const int hh = idx / half, d = idx % half;
                 float* vecp = hh < G ? qs + hh * hd : ks;
                 const int i0 = inter ? 2 * d : d;
@@ -451,60 +617,59 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
                 vecp[i1] = __fadd_rn(__fmul_rn(a, ss), __fmul_rn(bb, cc));
             }
             consumer_bar();
-            if (pos >= p0 && pos < p0 + n) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
-                const float* vsrc = P.qkv + (int64_t)b * ldq + qw + kvd + (int64_t)hk * hd;
+            const bool has_pos = pos >= p0 && pos < p0 + n;
+            if (has_pos) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
                 for (int i = tid; i < hd; i += 256) {
                     kc[(int64_t)pos * kvd + hk * hd + i] = ks[i];
-                    vc[(int64_t)pos * kvd + hk * hd + i] = __ldcg(&vsrc[i]);
+                    vc[(int64_t)pos * kvd + hk * hd + i] = vs[i];
                 }
             }
-            consumer_bar();
-            const int hd4 = hd / 4;
-            // scores q.k / sqrt(hd), K staged SUB positions at a time
-            for (int s0 = 0; s0 < n; s0 += SUB) {
-                const int ns = min(SUB, n - s0);
-                for (int i = tid; i < ns * hd4; i += 256) {
-                    const int r = i / hd4, cidx = i % hd4;
-                    reinterpret_cast<float4*>(kv)[i] =
-                        __ldcg(reinterpret_cast<const float4*>(kc + (int64_t)(p0 + s0 + r) * kvd + hk * hd) + cidx);
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // outputs tid + 256 k of [G][hd] (G * hd <= 1024)
+            for (int r0 = 0; r0 < n; r0 += SUB) {
+                const int ns = min(SUB, n - r0);
+                if (r0 > 0) {
+                    issue_round(r0);
+                    cp_async_wait_all();
+                }
+                if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
+                    const int r = pos - p0 - r0;
+                    for (int i = tid; i < hd; i += 256) {
+                        kb[r * hd + i] = ks[i];
+                        vb[r * hd + i] = vs[i];
+                    }
                 }
                 consumer_bar();
+                // scores q.k / sqrt(hd)
                 for (int tt = warp; tt < ns; tt += 8) {
-                    const float* kr = kv + tt * hd;
+                    const float* kr = kb + tt * hd;
                     for (int h = 0; h < G; ++h) {
                         float s = 0.0f;
                         for (int i = lane; i < hd; i += 32) s += qs[h * hd + i] * kr[i];
                         s = warp_sum(s);
-                        if (lane == 0) sc[h * cap + s0 + tt] = s * P.inv_scale;
+                        if (lane == 0) sc[h * SUB + tt] = s * P.inv_scale;
                     }
                 }
                 consumer_bar();
-            }
-            for (int h = warp; h < G; h += 8) {
-                float m = -INFINITY;
-                for (int tt = lane; tt < n; tt += 32) m = fmaxf(m, sc[h * cap + tt]);
-                m = warp_max(m);
-                float lsum = 0.0f;
-                for (int tt = lane; tt < n; tt += 32) {
-                    const float e = expf(sc[h * cap + tt] - m);
-                    sc[h * cap + tt] = e;
-                    lsum += e;
-                }
-                lsum = warp_sum(lsum);
-                if (lane == 0) {
-                    sml[h] = m;
-                    sml[16 + h] = lsum;
-                }
-            }
-            consumer_bar();
-            // P.V with V staged SUB positions at a time; thread owns outputs idx
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // G*hd <= 1024 outputs over 256 threads
-            for (int s0 = 0; s0 < n; s0 += SUB) {
-                const int ns = min(SUB, n - s0);
-                for (int i = tid; i < ns * hd4; i += 256) {
-                    const int r = i / hd4, cidx = i % hd4;
-                    reinterpret_cast<float4*>(kv)[i] =
-                        __ldcg(reinterpret_cast<const float4*>(vc + (int64_t)(p0 + s0 + r) * kvd + hk * hd) + cidx);
+                // running softmax: weights of this round relative to the new maximum
+                for (int h = warp; h < G; h += 8) {
+                    float m = -INFINITY;
+                    for (int tt = lane; tt < ns; tt += 32) m = fmaxf(m, sc[h * SUB + tt]);
+                    m = warp_max(m);
+                    const float mo = st[4 * h], mn = fmaxf(mo, m);
+                    float ls = 0.0f;
+                    for (int tt = lane; tt < ns; tt += 32) {
+                        const float e = expf(sc[h * SUB + tt] - mn);
+                        sc[h * SUB + tt] = e;
+                        ls += e;
+                    }
+                    ls = warp_sum(ls);
+                    __syncwarp();
+                    if (lane == 0) {
+                        const float corr = expf(mo - mn);
+                        st[4 * h + 2] = corr;
+                        st[4 * h + 0] = mn;
+                        st[4 * h + 1] = st[4 * h + 1] * corr + ls;
+                    }
                 }
                 consumer_bar();
 #pragma unroll
@@ -512,8 +677,8 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
                     const int idx = tid + 256 * k;
                     if (idx < G * hd) {
                         const int h = idx / hd, i = idx % hd;
-                        float a = acc[k];
-                        for (int tt = 0; tt < ns; ++tt) a += sc[h * cap + s0 + tt] * kv[tt * hd + i];
+                        float a = acc[k] * st[4 * h + 2];
+                        for (int tt = 0; tt < ns; ++tt) a += sc[h * SUB + tt] * vb[tt * hd + i];
                         acc[k] = a;
                     }
                 }
@@ -524,51 +689,53 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
                 const int idx = tid + 256 * k;
                 if (idx < G * hd) {
                     const int h = idx / hd, i = idx % hd;
-                    __stcg(&pbase[((int64_t)h * nch + c) * stride + 2 + i], acc[k]);
+                    __stcg(&pbase[((int64_t)h * nch + c) * stride + 4 + i], acc[k]);
                 }
             }
             if (tid < G) {
-                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 0], sml[tid]);
-                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 1], sml[16 + tid]);
+                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 0], st[4 * tid + 0]);
+                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 1], st[4 * tid + 1]);
             }
         }
         // arrival; the last CTA of (b, hk) combines the used chunks in order
         __threadfence();
         consumer_bar();
         int* ctr = &P.attn_ctr[b * P.n_kv + hk];
-        if (tid == 0) *s_last = (atomicAdd(ctr, 1) == nch - 1);
+        if (tid == 0) s_last = (atomicAdd(ctr, 1) == nch - 1);
         consumer_bar();
-        if (*s_last) {
+        if (s_last) {
             __threadfence();
-            for (int h = warp; h < G; h += 8) {
-                float M = -INFINITY;
-                for (int k = lane; k < used; k += 32) M = fmaxf(M, __ldcg(&pbase[((int64_t)h * nch + k) * stride]));
-                M = warp_max(M);
-                float L = 0.0f;
-                for (int k = lane; k < used; k += 32) {
-                    const float w = expf(__ldcg(&pbase[((int64_t)h * nch + k) * stride]) - M);
-                    wc[h * nch + k] = w;
-                    L += w * __ldcg(&pbase[((int64_t)h * nch + k) * stride + 1]);
+            const int hpw = max(1, min(G, P.attn_floats / (nch * stride)));
+            for (int h0 = 0; h0 < G; h0 += hpw) {
+                const int nh = min(hpw, G - h0);
+                const float* src = pbase + (int64_t)h0 * nch * stride;
+                const int n4 = nh * nch * stride / 4;
+                for (int i = tid; i < n4; i += 256) cp_async16(sm + 4 * i, src + 4 * i);
+                cp_async_wait_all();
+                consumer_bar();
+                for (int hl = warp; hl < nh; hl += 8) {
+                    float* ph = sm + hl * nch * stride;
+                    float M = -INFINITY;
+                    for (int k = lane; k < used; k += 32) M = fmaxf(M, ph[k * stride]);
+                    M = warp_max(M);
+                    float Ls = 0.0f;
+                    for (int k = lane; k < used; k += 32) {
+                        const float w = expf(ph[k * stride] - M);
+                        ph[k * stride + 2] = w;
+                        Ls += w * ph[k * stride + 1];
+                    }
+                    Ls = warp_sum(Ls);
+                    if (lane == 0) ph[3] = 1.0f / Ls;
                 }
-                L = warp_sum(L);
-                if (lane == 0) sml[16 + h] = 1.0f / L;
-            }
-            consumer_bar();
-            for (int idx = tid; idx < G * hd; idx += 256) {
-                const int h = idx / hd, i = idx % hd;
-                const float* src = pbase + (int64_t)h * nch * stride + 2 + i;
-                float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
-                int k = 0;
-                for (; k + 4 <= used; k += 4) {   // independent loads in flight
-                    const float v0 = __ldcg(src + (int64_t)k * stride), v1 = __ldcg(src + (int64_t)(k + 1) * stride);
-                    const float v2 = __ldcg(src + (int64_t)(k + 2) * stride), v3 = __ldcg(src + (int64_t)(k + 3) * stride);
-                    o0 += wc[h * nch + k] * v0;
-                    o1 += wc[h * nch + k + 1] * v1;
-                    o2 += wc[h * nch + k + 2] * v2;
-                    o3 += wc[h * nch + k + 3] * v3;
+                consumer_bar();
+                for (int idx = tid; idx < nh * hd; idx += 256) {
+                    const int hl = idx / hd, i = idx % hd;
+                    const float* ph = sm + hl * nch * stride;
+                    float o = 0.0f;
+                    for (int k = 0; k < used; ++k) o += ph[k * stride + 2] * ph[k * stride + 4 + i];
+                    P.xb[(int64_t)b * qw + (int64_t)(hk * G + h0 + hl) * hd + i] = o * ph[3];
                 }
-                for (; k < used; ++k) o0 += wc[h * nch + k] * __ldcg(src + (int64_t)k * stride);
-                P.xb[(int64_t)b * qw + (int64_t)hk * G * hd + idx] = ((o0 + o1) + (o2 + o3)) * sml[16 + h];
+                consumer_bar();
             }
             if (tid == 0) *ctr = 0;
         }
@@ -579,7 +746,6 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, float* kv) {
 template <int TYPE, int CTYPE, int NT>
 __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int NTC = NT * 8;
     const int NS = P.nstages;
     Ring ring;
     ring.full = reinterpret_cast<uint64_t*>(smem);
@@ -590,8 +756,8 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     __shared__ unsigned long long s_base;
     __shared__ int s_ok;
     float* s_red = reinterpret_cast<float*>(smem + 640);                               // [32]
-    float* red = reinterpret_cast<float*>(smem + 768);                                 // [8][16][NTC]
-    float* vec = reinterpret_cast<float*>(smem + 768 + 8 * 16 * NTC * 4);
+    float* red = reinterpret_cast<float*>(smem + 768);                                 // [8][8][16][2]
+    float* vec = reinterpret_cast<float*>(smem + 768 + DK_RED_BYTES);
     vec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(vec) + 127) & ~uintptr_t(127));
     uint8_t* prep = reinterpret_cast<uint8_t*>(vec) + P.vec_bytes;
     ring.stages = prep + P.prep_bytes;
@@ -633,15 +799,22 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     int q = 0;
     bool aborted = false;
     const bool gem = P.arch == BREW_ARCH_GEMMA3;
+    constexpr bool lsum_l = TYPE == BREW_TYPE_Q4_0, lsum_c = CTYPE == BREW_TYPE_Q4_0;
     float* xcur = P.x0;
     float* xalt = P.x1;
-    // trace: per CTA, slot 0 = start, then per phase (prep done, work done,
+    // trace: per CTA, slot 0 = start, then per phase (prep done, last weight stage in, work done,
     // barrier passed)
     int nev = 0;
     unsigned long long* tr = P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots : nullptr;
     auto mark = [&]() {
         if (tr && tid == 0 && nev < P.trace_slots) tr[nev] = global_ns();
         ++nev;
+    };
+    unsigned long long tfull = 0;
+    auto markv = [&](unsigned long long v) {
+        if (tr && tid == 0 && nev < P.trace_slots) tr[nev] = v;
+        ++nev;
+        tfull = 0;
     };
     mark();
     auto barrier = [&]() {
@@ -653,59 +826,64 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     for (int l = 0; l < L && !aborted; ++l) {
         // ---- RMSNorm (attention) + Q|K|V ----
         if (l == 0) {
-            prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red);
+            prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red, lsum_l);
         } else if (gem) {
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, P.xb2,
-                       P.post_ffn + (int64_t)(l - 1) * P.dim, xalt, prep, vec, s_red);
+                       P.post_ffn + (int64_t)(l - 1) * P.dim, xalt, prep, vec, s_red, lsum_l);
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red);
+                       vec, s_red, lsum_l);
         }
         mark();
         {
             const DPhase f = make_phase(P, l, PH_QKV, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            markv(tfull);
         }
         barrier();
         if (aborted) break;
         // ---- attention ----
         mark();
-        attn_phase(P, l, reinterpret_cast<float*>(prep), vec);
+        attn_phase(P, l, vec);
+        markv(0);
         barrier();
         if (aborted) break;
         // ---- wo (+ residual) ----
         prep_phase(P, SRC_PLAIN, P.xb, P.n_heads * P.hd, P.n_heads * P.hd, nullptr, nullptr, nullptr, nullptr, prep,
-                   vec, s_red);
+                   vec, s_red, lsum_l);
         mark();
         {
             const DPhase f = make_phase(P, l, PH_O, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            markv(tfull);
         }
         barrier();
         if (aborted) break;
         // ---- RMSNorm (FFN) + gate|up ----
         if (gem) {
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, P.xb2,
-                       P.post_att + (int64_t)l * P.dim, xalt, prep, vec, s_red);
+                       P.post_att + (int64_t)l * P.dim, xalt, prep, vec, s_red, lsum_l);
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red);
+                       vec, s_red, lsum_l);
         }
         mark();
         {
             const DPhase f = make_phase(P, l, PH_GU, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            markv(tfull);
         }
         barrier();
         if (aborted) break;
         // ---- down (+ residual) ----
-        prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red);
+        prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l);
         mark();
         {
             const DPhase f = make_phase(P, l, PH_DOWN, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            markv(tfull);
         }
         barrier();
     }
@@ -713,12 +891,13 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         // ---- final RMSNorm + classifier + argmax ----
         if (gem)
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_final, P.xb2, P.post_ffn + (int64_t)(L - 1) * P.dim,
-                       nullptr, prep, vec, s_red);
+                       nullptr, prep, vec, s_red, lsum_c);
         else
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red);
+            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c);
         mark();
         const DPhase f = make_phase(P, 0, PH_CLS, xcur);
-        mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted);
+        mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+        markv(tfull);
         consumer_bar();
         if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);
         barrier();
@@ -751,11 +930,15 @@ __global__ void rope_table_kernel(float* cos_t, float* sin_t, int seq_len, int h
 
 template <int TYPE, int CTYPE, int NT>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
-    static bool attr = false;
-    if (!attr) {
+    // the attribute is per device; it is set to the whole budget, so every
+    // model's size (p.smem <= DK_SMEM_BUDGET) is covered
+    static unsigned long long attr_set = 0;   // one bit per device
+    int dev = 0;
+    BREW_CUDA(cudaGetDevice(&dev));
+    if (dev >= 64 || !(attr_set >> dev & 1ull)) {
         BREW_CUDA(cudaFuncSetAttribute(decode_kernel<TYPE, CTYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)p.smem));
-        attr = true;
+                                       (int)DK_SMEM_BUDGET));
+        if (dev < 64) attr_set |= 1ull << dev;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
@@ -785,7 +968,9 @@ bool decode_supported(const brew_config& c, int batch) {
     // TMA boxes of 8 blocks over 16-byte row pitches: K multiple of 256
     if (c.dim % 256 || qw % 256 || c.hidden_dim % 256) return false;
     if ((c.n_kv_heads * c.head_size) % 16) return false;
-    if (c.n_heads / c.n_kv_heads > 16 || c.head_size > 512) return false;
+    // attention: a CTA holds the G * hd outputs of a kv head's queries in
+    // four registers per thread; 16-byte copies of half rows
+    if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
     return true;
 }
 
@@ -798,38 +983,26 @@ int rope_tables_launch(float* cos_t, float* sin_t, int seq_len, int hd, float ba
     return BREW_OK;
 }
 
-int decode_prepare(DecodeParams* p, const uint8_t* wq, const uint8_t* wk, const uint8_t* wv, const uint8_t* wo,
-                   const uint8_t* wgate, const uint8_t* wup, const uint8_t* wdown, const uint8_t* wout) {
-    TypeInfo tl, to;
-    type_info(p->type_layer, &tl);
-    type_info(p->type_out, &to);
-    const int qw = p->n_heads * p->hd, kvd = p->n_kv * p->hd, L = p->n_layers;
-    const int Pd = p->dim / 32 * tl.block_bytes, Pq = qw / 32 * tl.block_bytes, Ph = p->hidden / 32 * tl.block_bytes;
-    const int Po = p->dim / 32 * to.block_bytes;
-    int rc;
-    if ((rc = encode_rows_map(&p->maps[DK_MAP_Q], wq, L * qw, Pd, 8 * tl.block_bytes, 16)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_K], wk, L * kvd, Pd, 8 * tl.block_bytes, 16)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_V], wv, L * kvd, Pd, 8 * tl.block_bytes, 16)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_O], wo, L * p->dim, Pq, 8 * tl.block_bytes, 16)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_GATE], wgate, L * p->hidden, Pd, 8 * tl.block_bytes, 8)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_UP], wup, L * p->hidden, Pd, 8 * tl.block_bytes, 8)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_DOWN], wdown, L * p->dim, Ph, 8 * tl.block_bytes, 16)) ||
-        (rc = encode_rows_map(&p->maps[DK_MAP_OUT], wout, p->vocab, Po, 8 * to.block_bytes, 16)))
-        return rc;
+int decode_prepare(DecodeParams* p) {
+    const int qw = p->n_heads * p->hd;
     p->rec_bytes = prep_rec_bytes(p->batch);
-    p->nb_cap = std::max(1, std::min(MV_MAX_BOXES, (8 * 1024) / (8 * p->rec_bytes)));
     const int kmax = std::max(std::max(p->dim, qw), p->hidden);
     const int G = p->n_heads / p->n_kv;
-    const int cap = std::max(ATTN_MIN_POS, (p->seq_len + p->nchunk - 1) / p->nchunk);
-    const size_t attn_floats = (size_t)G * p->hd + p->hd + (size_t)G * cap + (size_t)G * p->nchunk + 64;
-    p->prep_bytes = (int)((std::max((size_t)(kmax / 32) * p->rec_bytes, attn_floats * 4) + 127) & ~size_t(127));
-    // staged input vector, or K / V rows of an attention sub-chunk
-    p->vec_bytes = (int)((std::max((size_t)kmax * 4, (size_t)(p->hd <= 128 ? 64 : 32) * p->hd * 4) + 127) & ~size_t(127));
-    const int boxw = 8 * std::max(tl.block_bytes, to.block_bytes);
-    p->stage_bytes = MV_MAX_BOXES * 16 * boxw;
-    const int NT = 1;   // DK_MAX_BATCH <= 2
-    const size_t fixed = 768 + (size_t)8 * 16 * NT * 8 * 4 + 128 + p->vec_bytes + p->prep_bytes + 128;
-    const size_t budget = 224 * 1024;
+    // attention area (vec and prep are contiguous): the item layout of
+    // attn_phase, or one head's partials of all chunks for the combine
+    const int SUB = attn_sub(p->hd);
+    const size_t attn_fl = std::max((size_t)2 * SUB * p->hd + (size_t)G * p->hd + 5 * (size_t)p->hd +
+                                        (size_t)G * SUB + 4 * (size_t)G + 64,
+                                    (size_t)p->nchunk * (p->hd + 4));
+    // staged input vector and the norm weight beside it
+    p->vec_bytes = (int)(((size_t)std::max(kmax, 2 * p->dim) * 4 + 127) & ~size_t(127));
+    const size_t prep_need = (size_t)(kmax / 32) * p->rec_bytes;
+    const size_t attn_need = attn_fl * 4 > (size_t)p->vec_bytes ? attn_fl * 4 - p->vec_bytes : 0;
+    p->prep_bytes = (int)((std::max(prep_need, attn_need) + 127) & ~size_t(127));
+    p->attn_floats = (p->vec_bytes + p->prep_bytes) / 4;
+    p->stage_bytes = DK_STAGE_BYTES;
+    const size_t fixed = 768 + (size_t)DK_RED_BYTES + 128 + p->vec_bytes + p->prep_bytes + 128;
+    const size_t budget = DK_SMEM_BUDGET;
     BREW_CHECK(fixed + 2 * (size_t)p->stage_bytes <= budget, BREW_ERR_UNSUPPORTED, "decode kernel: shapes too large");
     p->nstages = (int)std::min<size_t>(32, (budget - fixed) / p->stage_bytes);
     p->smem = fixed + (size_t)p->nstages * p->stage_bytes;

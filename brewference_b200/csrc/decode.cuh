@@ -4,16 +4,23 @@
 #include <cuda.h>
 
 #include "brew_common.cuh"
+#include "packed.cuh"
 
 namespace brew {
 
-// tensor maps of the weight families (all layers concatenated)
-enum { DK_MAP_Q = 0, DK_MAP_K, DK_MAP_V, DK_MAP_O, DK_MAP_GATE, DK_MAP_UP, DK_MAP_DOWN, DK_MAP_OUT, DK_NMAPS };
+// weight families of the decode kernel, each a fragment-packed copy
+// (packed.cuh) of all layers: Q|K|V rows, wo, gate/up interleaved, down, and
+// the classifier
+enum { PK_QKV = 0, PK_O, PK_GU, PK_DOWN, PK_OUT, PK_NFAM };
 
 constexpr int DK_MAX_BATCH = 2;
 
+// K / V positions an attention item stages in shared memory per round.
+__host__ __device__ inline int attn_sub(int hd) { return hd <= 128 ? 32 : 16; }
+
 struct alignas(64) DecodeParams {
-    CUtensorMap maps[DK_NMAPS];
+    const uint8_t* pk[PK_NFAM];         // packed weights
+    int64_t pk_lb[PK_NFAM];             // bytes per layer of each family
     // dimensions
     int arch, dim, hidden, n_layers, n_heads, n_kv, hd, vocab, seq_len, window, batch;
     int type_layer, type_out;
@@ -29,9 +36,9 @@ struct alignas(64) DecodeParams {
     const float *rope_cos, *rope_sin;   // [2][seq_len][hd/2]: 0 = global/default base, 1 = Gemma3 local
     float *x0, *x1;                     // residual stream (Gemma3 alternates between the two)
     float *xb, *xb2, *qkv, *hb, *logits;
-    float* attn_part;
+    float* attn_part;                   // [batch][n_heads][nchunk][hd + 4]: m, l, -, -, o[hd]
     int* attn_ctr;
-    int nchunk;
+    int nchunk, attn_floats;            // attn_floats: shared-memory floats of the attention area
     unsigned long long* am_key;
     int32_t* am_out;
     const int32_t *tokens, *pos;
@@ -39,17 +46,16 @@ struct alignas(64) DecodeParams {
     int* abort;
     unsigned int* err;
     unsigned long long* trace;          // optional [grid][trace_slots]: %globaltimer per CTA
-    int trace_slots;                    // 1 + 3 per phase (prep done, work done, barrier passed)
+    int trace_slots;                    // 1 + 4 per phase (prep done, last weight stage in, work done, barrier passed)
     // launch geometry
-    int nstages, stage_bytes, vec_bytes, prep_bytes, rec_bytes, nb_cap, grid;
+    int nstages, stage_bytes, vec_bytes, prep_bytes, rec_bytes, grid;
     size_t smem;
 };
 
 // True when the model can run on the persistent decode kernel.
 bool decode_supported(const brew_config& c, int batch);
-// Fills the geometry fields and the tensor maps (maps need `w` pointers).
-int decode_prepare(DecodeParams* p, const uint8_t* wq, const uint8_t* wk, const uint8_t* wv, const uint8_t* wo,
-                   const uint8_t* wgate, const uint8_t* wup, const uint8_t* wdown, const uint8_t* wout);
+// Fills the shared-memory geometry fields (needs the dimensions, batch and nchunk).
+int decode_prepare(DecodeParams* p);
 int decode_launch(const DecodeParams& p, cudaStream_t stream);
 // RoPE cos/sin tables [2][seq_len][hd/2] (RopeCache.precomputeAngles per position).
 int rope_tables_launch(float* cos_t, float* sin_t, int seq_len, int hd, float base0, float base1, float scale,

@@ -82,6 +82,7 @@ struct brew_model_s {
     bool use_decode = false;
     DecodeParams dp;
     float *x1 = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
+    uint8_t* pk[PK_NFAM] = {};              // fragment-packed weight copies of the decode kernel
     unsigned long long* bar = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
@@ -536,7 +537,7 @@ int setup_decode(brew_model_s* m) {
     p.hb = m->hb;
     p.logits = m->logits;
     p.nchunk = std::max(1, std::min(64, num_sms() / (B * c.n_kv_heads)));
-    if ((rc = dalloc(m, &m->dk_part, attn_part_floats(B, c.n_heads, p.nchunk, hd)))) return rc;
+    if ((rc = dalloc(m, &m->dk_part, (size_t)B * c.n_heads * p.nchunk * (hd + 4)))) return rc;
     p.attn_part = m->dk_part;
     p.attn_ctr = m->counters + c.hidden_dim / 32 + 8;
     p.am_key = m->am_key;
@@ -546,16 +547,30 @@ int setup_decode(brew_model_s* m) {
     p.bar = m->bar;
     p.abort = m->abort_flag;
     p.err = ctx().err_word;
-    p.trace_slots = 1 + 3 * (5 * c.n_layers + 1);
+    p.trace_slots = 1 + 4 * (5 * c.n_layers + 1);
     m->trace_n = num_sms() * p.trace_slots;
     if ((rc = dalloc(m, &m->trace, (size_t)m->trace_n))) return rc;
     p.trace = getenv("BREW_TRACE") ? m->trace : nullptr;
-    const int64_t qw = (int64_t)c.n_heads * hd;
-    (void)qw;
-    rc = decode_prepare(&p, m->t[T_Q]->d, m->t[T_K]->d, m->t[T_V]->d, m->t[T_O]->d, m->t[T_GATE]->d, m->t[T_UP]->d,
-                        m->t[T_DOWN]->d, m->t[T_OUTPUT]->d);
+    rc = decode_prepare(&p);
     if (rc == BREW_ERR_UNSUPPORTED) return BREW_OK;   // fall back to the kernel graph
     if (rc) return rc;
+    // fragment-packed copies of the weights (the GGUF-layout tensors stay for
+    // the kernel-graph path and for read-back)
+    const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+    PackSpec spec[PK_NFAM] = {};
+    spec[PK_QKV] = {{m->t[T_Q]->d, m->t[T_K]->d, m->t[T_V]->d}, {qw, kvd, kvd}, PK_ROWS, c.type_q, c.dim, c.n_layers};
+    spec[PK_O] = {{m->t[T_O]->d, nullptr, nullptr}, {c.dim, 0, 0}, PK_ROWS, c.type_o, qw, c.n_layers};
+    spec[PK_GU] = {{m->t[T_GATE]->d, m->t[T_UP]->d, nullptr}, {c.hidden_dim, 0, 0}, PK_GLU, c.type_gate, c.dim,
+                   c.n_layers};
+    spec[PK_DOWN] = {{m->t[T_DOWN]->d, nullptr, nullptr}, {c.dim, 0, 0}, PK_ROWS, c.type_down, c.hidden_dim,
+                     c.n_layers};
+    spec[PK_OUT] = {{m->t[T_OUTPUT]->d, nullptr, nullptr}, {c.vocab_size, 0, 0}, PK_ROWS, p.type_out, c.dim, 1};
+    for (int f = 0; f < PK_NFAM; ++f) {
+        p.pk_lb[f] = (int64_t)pk_layer_bytes(spec[f]);
+        if ((rc = dalloc(m, &m->pk[f], (size_t)spec[f].layers * pk_layer_bytes(spec[f])))) return rc;
+        if ((rc = pack_tiles_launch(m->pk[f], spec[f], ctx().stream))) return rc;
+        p.pk[f] = m->pk[f];
+    }
     m->use_decode = true;
     return BREW_OK;
 }

@@ -62,6 +62,61 @@ __device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int batch, int b, f
     }
 }
 
+// The same record entries as prep_emit_warp, written by eight lanes per
+// block: lane group (lane >> 3) of the warp holds one block, lane (lane & 7)
+// its elements 4*(lane & 7) .. +3 in x.  Every lane of the warp calls it (the
+// group max is a shuffle); `ok` masks the shared-memory stores.  `lsum`
+// selects whether the limb sums (used only by the Q4_0 zero-point
+// correction) are produced.
+__device__ __forceinline__ void prep_emit_quad(uint8_t* rec, int batch, int b, float4 x, bool ok, bool lsum) {
+    const int lane = threadIdx.x & 31, e = (lane & 7) * 4;
+    float am = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+    const float inv = am > 0.0f ? PREP_RANGE / am : 0.0f;
+    const float s = am / PREP_RANGE;
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+    uint32_t phi = 0u, pmid = 0u, plo = 0u;
+    int shi = 0, smid = 0, slo = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int v = __float2int_rn(xs[k] * inv);
+        const int lo = ((v + 128) & 255) - 128;
+        const int v1 = (v - lo) >> 8;
+        const int mid = ((v1 + 128) & 255) - 128;
+        const int hi = (v1 - mid) >> 8;
+        phi |= (uint32_t)(hi & 255) << (8 * k);
+        pmid |= (uint32_t)(mid & 255) << (8 * k);
+        plo |= (uint32_t)(lo & 255) << (8 * k);
+        shi += hi;
+        smid += mid;
+        slo += lo;
+    }
+    if (ok) {
+        *reinterpret_cast<uint32_t*>(rec + (3 * b + 0) * 32 + e) = phi;
+        *reinterpret_cast<uint32_t*>(rec + (3 * b + 1) * 32 + e) = pmid;
+        *reinterpret_cast<uint32_t*>(rec + (3 * b + 2) * 32 + e) = plo;
+    }
+    if (lsum) {
+        // four limbs per lane: each lane sum is in [-512, 508]; hi and mid
+        // share one word with a bias of 512 per lane (eight lanes < 2^16)
+        int hm = (shi + 512) | ((smid + 512) << 16);
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            hm += __shfl_xor_sync(0xffffffffu, hm, o);
+            slo += __shfl_xor_sync(0xffffffffu, slo, o);
+        }
+        if (ok && (lane & 7) == 0) {
+            int* ls = reinterpret_cast<int*>(rec + prep_lsum_off(batch));
+            ls[3 * b + 0] = (hm & 0xFFFF) - 8 * 512;
+            ls[3 * b + 1] = (hm >> 16) - 8 * 512;
+            ls[3 * b + 2] = slo;
+        }
+    }
+    if (ok && (lane & 7) == 0) reinterpret_cast<float*>(rec + prep_s_off(batch))[b] = s;
+}
+
 // Block-wide sum (all threads of the CTA call it; red has >= 32 floats).
 __device__ __forceinline__ float block_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
