@@ -67,7 +67,11 @@ int Scratch::reserve(size_t need_bytes) {
     ptr = nullptr;
     bytes = 0;
     BREW_CUDA(cudaMalloc(&ptr, need_bytes));
+    // cudaMemset runs on the legacy default stream, which does not order
+    // against the library's non-blocking streams: wait for it, or it could
+    // land after the kernels that use the buffer next
     BREW_CUDA(cudaMemset(ptr, 0, need_bytes));
+    BREW_CUDA(cudaStreamSynchronize(0));
     bytes = need_bytes;
     return BREW_OK;
 }
@@ -277,6 +281,7 @@ int brew_tensor_alloc(int type, int64_t n, brew_tensor* out) {
         return cuda_error(e, "cudaMalloc(tensor)");
     }
     cudaMemset(t->d + t->bytes, 0, 256);
+    cudaStreamSynchronize(0);   // legacy-stream memset: finish it before any non-blocking stream uses t
     *out = t;
     return BREW_OK;
 }
@@ -290,8 +295,12 @@ int brew_tensor_write(brew_tensor t, int64_t off, const void* bytes, int64_t n) 
     BREW_CHECK(off + n <= t->n, BREW_ERR_OUT_OF_BOUNDS, "write past the tensor end");
     int rc = ensure_init();
     if (rc) return rc;
+    // a pageable host->device cudaMemcpy may return before its DMA has
+    // landed, and it runs on the legacy stream, which the library's
+    // non-blocking streams do not wait for: wait for it here
     BREW_CUDA(cudaMemcpy(t->d + off / ti.block_elems * ti.block_bytes, bytes, (size_t)(n / ti.block_elems * ti.block_bytes),
                          cudaMemcpyHostToDevice));
+    BREW_CUDA(cudaStreamSynchronize(0));
     return BREW_OK;
 }
 
@@ -331,6 +340,9 @@ int brew_tensor_read(brew_tensor t, int64_t off, int64_t n, void* bytes) {
     BREW_CHECK(off + n <= t->n, BREW_ERR_OUT_OF_BOUNDS, "read past the tensor end");
     int rc = ensure_init();
     if (rc) return rc;
+    // kernels on non-blocking streams may still be writing t: the legacy
+    // stream's copy does not wait for them
+    BREW_CUDA(cudaDeviceSynchronize());
     BREW_CUDA(cudaMemcpy(bytes, t->d + off / ti.block_elems * ti.block_bytes, (size_t)(n / ti.block_elems * ti.block_bytes),
                          cudaMemcpyDeviceToHost));
     return BREW_OK;

@@ -219,7 +219,7 @@ __device__ __forceinline__ float sumsq4(const float4* v, int n4) {
 // Q4_0 blocks (needs the limb sums).
 __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, int ld, int K, const float* nw,
                            const float* t, const float* tw, float* xout, uint8_t* prep, float* vec, float* red,
-                           bool lsum) {
+                           bool lsum, unsigned long long* t_wave) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int KB = K / 32, K4 = K / 4;
     const int G = gridDim.x;
@@ -267,6 +267,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             if (lane == 0) red[warp] = ss;
         }
         consumer_bar();
+        if (t_wave && b == 0) *t_wave = global_ns();
         float scale = 1.0f;
         if (nw) {
             float tot = 0.0f;
@@ -313,7 +314,9 @@ __device__ __forceinline__ uint2 lds64(uint32_t a) { return *reinterpret_cast<co
 // of the 256 threads finishes one output.
 template <int TT, int NT>
 __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q, uint32_t prep_s,
-                         float* red, unsigned long long* s_best, bool& aborted, unsigned long long* t_full) {
+                         float* red, unsigned long long* s_best, bool& aborted, unsigned long long* t_full,
+                         unsigned long long* detail) {
+    int dch = 0;
     static_assert(NT == 1, "decode batch <= 2: one n8 column tile");
     constexpr int BS = pk_block_bytes(TT), SO = pk_scale_off(TT);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -365,6 +368,7 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
             if (!aborted && !mbar_wait_bounded(&ring.full[stage], (q / ring.ns) & 1, P.err, BREW_DEVERR_TIMEOUT_FULL))
                 aborted = true;
             if (t_full && warp == 0) *t_full = global_ns();
+            if (detail && tid == 0 && dch < DK_DETAIL) detail[DK_DETAIL + dch] = global_ns();
             if (!aborted) {
                 const uint32_t sb = smem_u32(ring.stages + (size_t)stage * ring.stage_bytes);
                 for (int kb = warp; kb < geo.KC; kb += 8) {
@@ -414,6 +418,8 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&ring.empty[stage]);
+            if (detail && tid == 0 && dch < DK_DETAIL) detail[2 * DK_DETAIL + dch] = global_ns();
+            ++dch;
         }
         // limbs hi / mid (lane t even) and lo (lane t + 1) -> one value per
         // row and vector: v = (lo + mid * 2^8) + hi * 2^16
@@ -457,7 +463,9 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
 // Producer side of one matvec phase: the same tiles and stages, in order;
 // one bulk copy per tile per stage (the tile's KC block-tiles are contiguous).
 template <int TT>
-__device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q) {
+__device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q,
+                                           unsigned long long* detail) {
+    int dch = 0;
     constexpr int BS = pk_block_bytes(TT);
     const int lane = threadIdx.x & 31;
     const int G = gridDim.x;
@@ -491,6 +499,8 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
                 }
             }
             uint8_t* sbase = ring.stages + (size_t)stage * ring.stage_bytes;
+            if (detail && lane == 0 && dch < DK_DETAIL) detail[dch] = global_ns();
+            ++dch;
             if (lane == 0) mbar_arrive_expect_tx(&ring.full[stage], (uint32_t)ng * cbytes);
             __syncwarp();
             if (lane < ng)
@@ -515,7 +525,7 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
 //   q-norm w [hd] | k-norm w [hd] | cos [hd/2] | sin [hd/2] |
 //   scores [G][SUB] | per head: running max, running sum, round rescale, -
 // and, for the combine, the partials [heads][nchunk][hd + 4].
-__device__ void attn_phase(const DecodeParams& P, int l, float* sm) {
+__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -595,6 +605,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm) {
             }
             cp_async_wait_all();
             consumer_bar();
+            if (t_wave) *t_wave = global_ns();
             if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
                 for (int hh = warp; hh <= G; hh += 8) {
                     float* vecp = hh < G ? qs + hh * hd : ks;
@@ -779,15 +790,17 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     if (warp == 8) {
         // ------------------------------- producer -------------------------------
         int q = 0;
+        unsigned long long* dtr =
+            P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots + P.trace_slots - 3 * DK_DETAIL : nullptr;
         for (int l = 0; l < L && q < (1 << 29); ++l) {
             for (int ph = PH_QKV; ph <= PH_DOWN && q < (1 << 29); ++ph) {
                 const DPhase f = make_phase(P, l, ph, P.x0);
-                produce_phase<TYPE>(P, f, ring, q);
+                produce_phase<TYPE>(P, f, ring, q, (l == P.detail_l && ph == P.detail_ph) ? dtr : nullptr);
             }
         }
         if (q < (1 << 29)) {
             const DPhase f = make_phase(P, 0, PH_CLS, P.x0);
-            produce_phase<CTYPE>(P, f, ring, q);
+            produce_phase<CTYPE>(P, f, ring, q, (L == P.detail_l && PH_CLS == P.detail_ph) ? dtr : nullptr);
         }
         return;
     }
@@ -802,7 +815,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     constexpr bool lsum_l = TYPE == BREW_TYPE_Q4_0, lsum_c = CTYPE == BREW_TYPE_Q4_0;
     float* xcur = P.x0;
     float* xalt = P.x1;
-    // trace: per CTA, slot 0 = start, then per phase (prep done, last weight stage in, work done,
+    // trace: per CTA, slot 0 = start, then per phase (load wave landed, prep done, last weight stage in, work done,
     // barrier passed)
     int nev = 0;
     unsigned long long* tr = P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots : nullptr;
@@ -811,11 +824,19 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         ++nev;
     };
     unsigned long long tfull = 0;
+    unsigned long long twave = 0;
     auto markv = [&](unsigned long long v) {
         if (tr && tid == 0 && nev < P.trace_slots) tr[nev] = v;
         ++nev;
         tfull = 0;
     };
+    auto mark_prep = [&]() {   // the prep's load wave landed, then the prep is done
+        markv(twave);
+        twave = 0;
+        mark();
+    };
+    unsigned long long* dtr = tr ? tr + P.trace_slots - 3 * DK_DETAIL : nullptr;
+    auto det = [&](int l, int ph) { return (dtr && l == P.detail_l && ph == P.detail_ph) ? dtr : nullptr; };
     mark();
     auto barrier = [&]() {
         mark();
@@ -826,36 +847,38 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     for (int l = 0; l < L && !aborted; ++l) {
         // ---- RMSNorm (attention) + Q|K|V ----
         if (l == 0) {
-            prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red, lsum_l);
+            prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
         } else if (gem) {
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, P.xb2,
-                       P.post_ffn + (int64_t)(l - 1) * P.dim, xalt, prep, vec, s_red, lsum_l);
+                       P.post_ffn + (int64_t)(l - 1) * P.dim, xalt, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l);
+                       vec, s_red, lsum_l, tr ? &twave : nullptr);
         }
-        mark();
+        mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_QKV, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_QKV));
             markv(tfull);
         }
         barrier();
         if (aborted) break;
         // ---- attention ----
-        mark();
-        attn_phase(P, l, vec);
+        attn_phase(P, l, vec, tr ? &twave : nullptr);
+        markv(twave);   // the first load wave landed
+        twave = 0;
+        markv(0);
         markv(0);
         barrier();
         if (aborted) break;
         // ---- wo (+ residual) ----
         prep_phase(P, SRC_PLAIN, P.xb, P.n_heads * P.hd, P.n_heads * P.hd, nullptr, nullptr, nullptr, nullptr, prep,
-                   vec, s_red, lsum_l);
-        mark();
+                   vec, s_red, lsum_l, tr ? &twave : nullptr);
+        mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_O, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_O));
             markv(tfull);
         }
         barrier();
@@ -863,26 +886,26 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         // ---- RMSNorm (FFN) + gate|up ----
         if (gem) {
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, P.xb2,
-                       P.post_att + (int64_t)l * P.dim, xalt, prep, vec, s_red, lsum_l);
+                       P.post_att + (int64_t)l * P.dim, xalt, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l);
+                       vec, s_red, lsum_l, tr ? &twave : nullptr);
         }
-        mark();
+        mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_GU, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_GU));
             markv(tfull);
         }
         barrier();
         if (aborted) break;
         // ---- down (+ residual) ----
-        prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l);
-        mark();
+        prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
+        mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_DOWN, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_DOWN));
             markv(tfull);
         }
         barrier();
@@ -891,12 +914,12 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         // ---- final RMSNorm + classifier + argmax ----
         if (gem)
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_final, P.xb2, P.post_ffn + (int64_t)(L - 1) * P.dim,
-                       nullptr, prep, vec, s_red, lsum_c);
+                       nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr);
         else
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c);
-        mark();
+            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr);
+        mark_prep();
         const DPhase f = make_phase(P, 0, PH_CLS, xcur);
-        mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr);
+        mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(L, PH_CLS));
         markv(tfull);
         consumer_bar();
         if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);

@@ -14,6 +14,7 @@ namespace brew {
 enum { PK_QKV = 0, PK_O, PK_GU, PK_DOWN, PK_OUT, PK_NFAM };
 
 constexpr int DK_MAX_BATCH = 2;
+constexpr int DK_DETAIL = 32;   // chunks of the detailed phase traced
 
 // K / V positions an attention item stages in shared memory per round.
 __host__ __device__ inline int attn_sub(int hd) { return hd <= 128 ? 32 : 16; }
@@ -46,7 +47,8 @@ struct alignas(64) DecodeParams {
     int* abort;
     unsigned int* err;
     unsigned long long* trace;          // optional [grid][trace_slots]: %globaltimer per CTA
-    int trace_slots;                    // 1 + 4 per phase (prep done, last weight stage in, work done, barrier passed)
+    int trace_slots;                    // 1 + 5 per phase (load wave landed, prep done, last weight stage in, work done, barrier passed)
+    int detail_l, detail_ph;            // optional per-chunk trace of one (layer, phase): 3 x DK_DETAIL more slots
     // launch geometry
     int nstages, stage_bytes, vec_bytes, prep_bytes, rec_bytes, grid;
     size_t smem;

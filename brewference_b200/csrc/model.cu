@@ -97,6 +97,7 @@ int dalloc(brew_model_s* m, T** p, size_t count) {
     void* q = nullptr;
     BREW_CUDA(cudaMalloc(&q, count * sizeof(T) + 256));
     BREW_CUDA(cudaMemset(q, 0, count * sizeof(T) + 256));
+    BREW_CUDA(cudaStreamSynchronize(0));   // legacy-stream memset: done before the non-blocking stream's kernels
     m->allocs.push_back(q);
     *p = static_cast<T*>(q);
     return BREW_OK;
@@ -175,6 +176,7 @@ int upload_vec(brew_model_s* m, float** dst, const float* src, size_t n) {
     int rc = dalloc(m, dst, n);
     if (rc) return rc;
     BREW_CUDA(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+    BREW_CUDA(cudaStreamSynchronize(0));   // pageable copy on the legacy stream: landed before the model's kernels
     return BREW_OK;
 }
 
@@ -547,7 +549,10 @@ int setup_decode(brew_model_s* m) {
     p.bar = m->bar;
     p.abort = m->abort_flag;
     p.err = ctx().err_word;
-    p.trace_slots = 1 + 4 * (5 * c.n_layers + 1);
+    p.trace_slots = 1 + 5 * (5 * c.n_layers + 1) + 3 * DK_DETAIL;
+    p.detail_l = -1;
+    p.detail_ph = -1;
+    if (const char* e = getenv("BREW_TRACE_DETAIL")) sscanf(e, "%d,%d", &p.detail_l, &p.detail_ph);
     m->trace_n = num_sms() * p.trace_slots;
     if ((rc = dalloc(m, &m->trace, (size_t)m->trace_n))) return rc;
     p.trace = getenv("BREW_TRACE") ? m->trace : nullptr;

@@ -244,10 +244,11 @@ BREW_API int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n_ker
 
 /* Phase tracing of the persistent decode kernel: when on, every CTA of every
  * decode step records %globaltimer (ns) at its start and, per phase (5 per
- * layer: QKV, attention, wo, gate|up, down; then the classifier), when its
- * input preparation is done, when its last weight stage arrived (0: none),
- * when its work is done and when it leaves the grid barrier:
- * [n_ctas][1 + 4 * (5 * n_layers + 1)] values.  brew_model_trace
+ * layer: QKV, attention, wo, gate|up, down; then the classifier), when the
+ * first load wave of its input landed, when its input preparation is done,
+ * when its last weight stage arrived (0: none), when its work is done and
+ * when it leaves the grid barrier: [n_ctas][1 + 5 * (5 * n_layers + 1)]
+ * values.  brew_model_trace
  * copies the last step's stamps (n = 0 when the model runs the kernel-graph
  * path). */
 BREW_API int brew_model_set_trace(brew_model m, int32_t on);
