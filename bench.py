@@ -14,8 +14,12 @@ Printed JSON line (rank 0):
   value      decode tok/s, device-resident, CUDA events on the launching stream
   e2e        the same metric through the C ABI call a host caller makes per
              token (brew_model_forward: token+position H2D, argmax D2H)
-  roofline   the decode matvec kernel timed alone (gate matrices of all 28
-             layers in rotation, 375 MB) against the measured HBM copy peak
+  roofline   the dominant kernel, the persistent decode kernel (one launch
+             per token): weight + KV bytes per step over its time, against
+             the measured HBM copy peak; `traffic` is the DRAM bytes per
+             launch from the committed ncu summary of the same kernel
+  matvec_sweep  the packed-block matvec kernel alone on the decode shapes,
+             Q8_0 and Q4_0, batch 1 and 8, layers rotated (inputs > L2)
   cpu_baseline  the oracle (CPU restatement of the reference's Java path,
              row-parallel over all host cores) on a bounded sample
 
@@ -52,6 +56,17 @@ def workload_cfg():
     return C.qwen3_1_7b()
 
 
+def q4_cfg(cfg):
+    """The same shapes with Q4_0 layer matrices and a Q4_0 classifier (the
+    Q4_0 half of the matvec sweep)."""
+    q4 = C.TYPE_Q4_0
+    return cfg.replace(type_embed=q4, type_output=q4, type_q=q4, type_k=q4, type_v=q4, type_o=q4, type_gate=q4,
+                       type_up=q4, type_down=q4)
+
+
+TRAFFIC_PROFILE = "decode_kernel_qwen3-1.7b_q8_0.md"
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -62,56 +77,79 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled every 20 ms during the timed
+    region, through NVML (nvidia-smi as the fallback).  Reads only."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, torch_device: int):
+        self.dev = torch_device
+        self.samples, self.reasons, self.smax = [], set(), None
+        self.stop_ev = threading.Event()
+        self.thread = None
+        self.nvml = None
+        self.handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        prop = torch.cuda.get_device_properties(self.dev)
+        bus = "%08x:%02x:%02x.0" % (getattr(prop, "pci_domain_id", 0), prop.pci_bus_id, prop.pci_device_id)
+        self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+
+    def _reasons(self):
+        n = self.nvml
+        f = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(f(self.handle))
+
+    def _run(self):
+        n = self.nvml
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)))
+                r = self._reasons()
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:   # noqa: BLE001 - sampling must not break the benchmark
+                pass
+            self.stop_ev.wait(0.02)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
-
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            self._open()
+        except Exception as e:   # noqa: BLE001
+            self.nvml = None
+            self.err = str(e)
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        if self.nvml is None:
+            return _nvidia_smi_clocks(self.dev)
+        self.stop_ev.set()
         self.thread.join(timeout=2)
-        sm, smax, reasons = [], None, set()
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.smax,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml, 20 ms"}
+
+
+def _nvidia_smi_clocks(dev: int):
+    fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        out = subprocess.run(["nvidia-smi", "-i", str(dev), f"--query-gpu={fields}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=10).stdout.strip().split(",")
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": float(out[0]), "sm_max_mhz": float(out[1]),
+                "reasons": [n for n, v in zip(names, out[2:6]) if v.strip().lower() == "active"],
+                "samples": 1, "source": "nvidia-smi after the timed region"}
+    except Exception:   # noqa: BLE001
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
 
 
 def dist_init(n_gpus):
@@ -205,31 +243,30 @@ def run_reference(args):
 # --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
-def kernel_roofline(dm, cfg, iters: int):
-    """Times the decode matvec kernel alone: the gate matrices of all layers
-    in rotation (inputs far larger than L2), batch 1, CUDA events on the
-    launching stream.  Returns per-launch algorithmic bytes and mean ms."""
+def time_matvec(w, K, Nr, layers, batch, iters):
+    """Times the packed-block matvec kernel alone on tensor `w` ([layers][Nr][K]),
+    rotating over the layers so the inputs exceed L2 (a single matrix larger
+    than L2 needs no rotation).  The x records are prepared once; the timed
+    launches run from a CUDA graph on a dedicated stream, CUDA events on that
+    stream.  Returns (algorithmic bytes per launch, ms per launch)."""
     import torch
     from brewference_b200.api import Linear
-    K, Nr = cfg.dim, cfg.hidden_dim
-    w = dm.tensor(C.W_GATE)
-    x = torch.randn(K, device="cuda", dtype=torch.float32)
-    y = torch.empty(Nr, device="cuda", dtype=torch.float32)
-    prep = torch.empty(Linear.prep_bytes(K, 1) + 256, dtype=torch.uint8, device="cuda")
+    x = torch.randn(batch, K, device="cuda", dtype=torch.float32)
+    y = torch.empty(batch, Nr, device="cuda", dtype=torch.float32)
+    prep = torch.empty(Linear.prep_bytes(K, batch) + 256, dtype=torch.uint8, device="cuda")
     pp = (prep.data_ptr() + 15) // 16 * 16
     st = torch.cuda.Stream()
+    prev = torch.cuda.current_stream()
     torch.cuda.set_stream(st)
     s = st.cuda_stream
-    Linear.prepare_input_device(x.data_ptr(), K, 1, pp, s)
-    for l in range(4):
-        Linear.matmul_prepared_device(y.data_ptr(), pp, w, l * K * Nr, K, Nr, 1, s)
+    Linear.prepare_input_device(x.data_ptr(), K, batch, pp, s)
+    for l in range(min(layers, 4)):
+        Linear.matmul_prepared_device(y.data_ptr(), pp, w, l * K * Nr, K, Nr, batch, s)
     torch.cuda.synchronize()
-    # the launches are captured in a CUDA graph so host launch cost does not
-    # enter the kernel time
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=st):
         for i in range(iters):
-            Linear.matmul_prepared_device(y.data_ptr(), pp, w, (i % cfg.n_layers) * K * Nr, K, Nr, 1,
+            Linear.matmul_prepared_device(y.data_ptr(), pp, w, (i % layers) * K * Nr, K, Nr, batch,
                                           torch.cuda.current_stream().cuda_stream)
     g.replay()
     torch.cuda.synchronize()
@@ -240,9 +277,60 @@ def kernel_roofline(dm, cfg, iters: int):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / iters
     del g
-    wbytes = Nr * K // 32 * 34
-    alg = wbytes + 4 * K + 4 * Nr
-    return alg, ms, wbytes
+    torch.cuda.set_stream(prev)
+    qt = w.type
+    eb, bb = C.TYPE_BLOCK[qt]
+    wbytes = Nr * K // eb * bb
+    alg = wbytes + 4 * K * batch + 4 * Nr * batch
+    return alg, ms
+
+
+def matvec_sweep(models, cfg, peak):
+    """The quant-matvec half of the metric: HBM GB/s of the matvec kernel on
+    the decode shapes (W = N x K) for each weight type and batch 1 / 8."""
+    shapes = [("2048x2048 (wq)", C.W_Q, cfg.n_heads * cfg.head_size, cfg.dim, cfg.n_layers),
+              ("6144x2048 (gate)", C.W_GATE, cfg.hidden_dim, cfg.dim, cfg.n_layers),
+              ("2048x6144 (down)", C.W_DOWN, cfg.dim, cfg.hidden_dim, cfg.n_layers),
+              ("151936x2048 (classifier)", C.W_OUTPUT, cfg.vocab_size, cfg.dim, 1)]
+    out = []
+    for tname, dm in models:
+        for name, which, Nr, K, layers in shapes:
+            w = dm.tensor(which)
+            if which == C.W_OUTPUT and tname != C.TYPE_NAMES[w.type]:
+                continue   # the tied classifier keeps the embedding's type
+            for batch in (1, 8):
+                alg, ms = time_matvec(w, K, Nr, layers, batch, iters=56 if layers > 1 else 16)
+                gbs = alg / (ms / 1000.0) / 1e9
+                out.append({"type": tname, "shape": name, "batch": batch, "GBps": round(gbs, 1),
+                            "frac": round(gbs / peak, 4), "us": round(ms * 1000.0, 2)})
+    return out
+
+
+def kv_bytes_per_step(cfg, positions):
+    """fp32 K/V cache bytes one decode step moves at each position: the rows
+    of every earlier position read (K and V, all layers) plus the new row
+    written.  Mean over the timed positions."""
+    kvd = cfg.n_kv_heads * cfg.head_size
+    row = 2 * kvd * 4 * cfg.n_layers
+    tot = []
+    for p in positions:
+        seen = min(p, cfg.sliding_window - 1) if cfg.sliding_window else p
+        tot.append(seen * row + row)
+    return float(np.mean(tot))
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch recorded in a committed ncu summary
+    (line `dram_bytes_per_launch: <n>`), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(path) as f:
+            for ln in f:
+                if ln.strip().startswith("dram_bytes_per_launch:"):
+                    return float(ln.split(":", 1)[1].split()[0])
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
 
 
 def run_gpu(args):
@@ -269,8 +357,8 @@ def run_gpu(args):
         dm.close()
         return 0
     if args.kernel_only:
-        # the decode matvec alone (profiling entry: a few launches, no decode)
-        alg, kms, _ = kernel_roofline(dm, cfg, iters=args.steps)
+        # the matvec kernel alone (profiling entry: a few launches, no decode)
+        alg, kms = time_matvec(dm.tensor(C.W_GATE), cfg.dim, cfg.hidden_dim, cfg.n_layers, 1, iters=args.steps)
         peak, peak_kind = measured_peaks()
         print(json.dumps({"kernel": "mv_kernel Q8_0 batch 1, 6144x2048", "ms_per_launch": kms,
                           "GBps": alg / (kms / 1000.0) / 1e9, "peak": peak, "peak_kind": peak_kind}), flush=True)
@@ -316,15 +404,25 @@ def run_gpu(args):
     e2e_s = max_over_ranks(dist, e2e_s)
     e2e = world * e2e_steps / e2e_s
 
-    # roofline of the dominant kernel (decode matvec) timed alone
-    alg, kms, wbytes = kernel_roofline(dm, cfg, iters=112)
+    # roofline of the dominant kernel: the persistent decode kernel is one
+    # launch per token and carries the whole forward; its algorithmic bytes
+    # are the packed weights plus the KV rows of the timed positions
     peak, peak_kind = measured_peaks()
-    achieved = alg / (kms / 1000.0) / 1e9
+    positions = list(range(args.prompt_len + args.warmup, args.prompt_len + args.warmup + args.steps))
+    kvb = kv_bytes_per_step(cfg, positions)
+    wbytes = cfg.decode_weight_bytes()
+    alg = wbytes + kvb
+    achieved = alg / (ms_max / args.steps / 1000.0) / 1e9
+    sweep = []
+    if not args.no_sweep:
+        dm4 = DeviceModel.synthesize(q4_cfg(cfg), SEED)
+        sweep = matvec_sweep([("Q8_0", dm), ("Q4_0", dm4)], cfg, peak)
+        dm4.close()
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32",
+        "vs_baseline": None, "dtype": "s8 MMA, f32 accumulate",
         "data": "synthetic (seeded random-init N(0,0.02) weights quantized to Q8_0 on the device, seeded prompt ids)",
         "config": {"workload": f"{cfg.name} Q8_0 greedy decode at batch 1 after a {args.prompt_len}-token prompt",
                    "model": cfg.name, "global_batch": world, "seq_len": cfg.seq_len,
@@ -335,11 +433,12 @@ def run_gpu(args):
                 "call": "brew_model_forward per token, host token/position in, host argmax out"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "mv_kernel Q8_0 batch 1, gate matrix 6144x2048 (13.37 MB), layers rotated",
-                     "bytes_per_launch": alg, "ms_per_launch": kms},
-        "weight_stream": {"bytes_per_step": cfg.decode_weight_bytes(),
-                          "GBps": cfg.decode_weight_bytes() / (ms_max / args.steps / 1000.0) / 1e9},
+                     "traffic": profiled_traffic(TRAFFIC_PROFILE), "peak_kind": peak_kind,
+                     "kernel": "decode_kernel (persistent; one launch = one decode step, timed with the step's "
+                               "1-launch token update)",
+                     "bytes_per_launch": alg, "weight_bytes": wbytes, "kv_bytes": kvb,
+                     "ms_per_launch": ms_max / args.steps},
+        "matvec_sweep": sweep,
         "clocks": clk,
         "setup_s": {"synthesize": round(synth_s, 2)},
     }
@@ -367,6 +466,7 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the matvec sweep")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     args = ap.parse_args()
