@@ -157,6 +157,23 @@ BREW_API int brew_matmul_dev(float* output_dev, const float* input_dev, brew_ten
                     int64_t weights_offset, int32_t input_size, int32_t output_size,
                     int32_t batch, void* stream);
 
+/* brew_matmul_dev without any allocation in the call: the quantized records
+ * of the input live in a 256 KiB array that is part of the loaded module
+ * (one per device), not in a buffer grown on demand.  No counterpart in the
+ * reference (its Java matmul allocates nothing on a device).  For callers
+ * that must not allocate device memory mid-call (a JNI critical region, a
+ * server whose memory is reserved up front).  Same arguments, results and
+ * errors as brew_matmul_dev, plus: brew_init must have been called
+ * (BREW_ERR_INVALID_ARG otherwise); (input_size / 32) * record bytes of
+ * min(batch, 16) vectors must fit in 256 KiB (input_size <= 74880 at batch
+ * 1, <= 4672 at batch 16), else BREW_ERR_INVALID_ARG.  The first call on a
+ * device looks up the array's address; make it before any stream capture
+ * starts.  Calls whose device work may overlap (different unordered streams)
+ * race on the one array. */
+BREW_API int brew_matmul_dev_static(float* output_dev, const float* input_dev, brew_tensor weights,
+                    int64_t weights_offset, int32_t input_size, int32_t output_size,
+                    int32_t batch, void* stream);
+
 /* Two-step form for callers that multiply one input by several matrices
  * (Q, K and V share their input): brew_prepare_input_dev writes the
  * quantized-activation records of x [batch][input_size] into `prep_dev`
