@@ -1,0 +1,24 @@
+// eltwise.cuh — the per-row vector steps of the forward pass as separate
+// kernels, for layers whose matrices are not fused with them (the K-quant
+// forward): RMSNorm, bias, residual, gated activation.
+#pragma once
+
+#include "brew_common.cuh"
+
+namespace brew {
+
+// out[b][i] = x[b][i] * scale_b * w[i], scale_b = inverseRootMeanSquare
+// (Kernels.rmsNorm, transformer/math/Kernels.java:47-58,77-88).
+int rmsnorm_launch(const float* x, int ldx, const float* w, float eps, int K, int B, float* out, int ldo,
+                   cudaStream_t s);
+// y[b][i] = y[b][i] + bias[i] for i < N (Kernels.addBias, Kernels.java:171-197).
+int add_bias_launch(float* y, int ldy, const float* bias, int N, int B, cudaStream_t s);
+// x[b][i] = x[b][i] + t[b][i] (Kernels.accum), or with norm_w (Gemma3's
+// post-norm): x[b][i] = x[b][i] + rmsnorm(t[b], norm_w)[i].
+int residual_launch(float* x, int ldx, const float* t, int ldt, const float* norm_w, float eps, int K, int B,
+                    cudaStream_t s);
+// hb[b][i] = (float)act((double)g[b][i]) * u[b][i] (FfnActivation.swiGlu /
+// geGlu, transformer/ffn/FfnActivation.java:23-58).
+int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s);
+
+}  // namespace brew

@@ -17,6 +17,7 @@
 // the first RMSNorm are one more kernel.
 #include "brew_internal.cuh"
 #include "decode.cuh"
+#include "eltwise.cuh"
 
 #include <cmath>
 #include <cstdlib>
@@ -83,6 +84,10 @@ struct brew_model_s {
     DecodeParams dp;
     float *x1 = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
     uint8_t* pk[PK_NFAM] = {};              // fragment-packed weight copies of the decode kernel
+    // unfused forward (models with K-quant matrices)
+    bool unfused = false;
+    float *xn = nullptr, *hb2 = nullptr;    // normed input of a matvec; the up projection
+    uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
     unsigned long long* bar = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
@@ -103,6 +108,16 @@ int dalloc(brew_model_s* m, T** p, size_t count) {
     return BREW_OK;
 }
 
+// Any Q4_K / Q6_K matrix: the model runs the unfused forward (separate
+// norm / bias / residual / activation kernels around each matvec).
+bool uses_kquants(const brew_config& c) {
+    const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down,
+                         c.tied_embeddings ? c.type_embed : c.type_output};
+    for (int t : types)
+        if (t == BREW_TYPE_Q4_K || t == BREW_TYPE_Q6_K) return true;
+    return false;
+}
+
 int check_config(const brew_config& c, int max_batch) {
     BREW_CHECK(c.arch >= BREW_ARCH_LLAMA && c.arch <= BREW_ARCH_GEMMA3, BREW_ERR_UNSUPPORTED, "arch %d", c.arch);
     BREW_CHECK(c.dim > 0 && c.dim % 32 == 0, BREW_ERR_INVALID_ARG, "dim %d", c.dim);
@@ -113,12 +128,25 @@ int check_config(const brew_config& c, int max_batch) {
     BREW_CHECK(c.vocab_size > 0 && c.seq_len > 0, BREW_ERR_INVALID_ARG, "vocab/seq_len");
     BREW_CHECK(max_batch >= 1 && max_batch <= MV_MAX_BATCH, BREW_ERR_INVALID_ARG, "max_batch %d", max_batch);
     const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down,
-                         c.tied_embeddings ? c.type_embed : c.type_output};
+                         c.tied_embeddings ? c.type_embed : c.type_output, c.type_embed};
     for (int t : types)
-        BREW_CHECK(t == BREW_TYPE_Q8_0 || t == BREW_TYPE_Q4_0, BREW_ERR_UNSUPPORTED,
-                   "the device forward streams Q8_0/Q4_0 matrices; GGML type %d is served by brew_matmul only", t);
-    BREW_CHECK(c.type_q == c.type_k && c.type_k == c.type_v, BREW_ERR_UNSUPPORTED, "Q/K/V of different types");
-    BREW_CHECK(c.type_gate == c.type_up, BREW_ERR_UNSUPPORTED, "gate/up of different types");
+        BREW_CHECK(is_quant_matrix_type(t), BREW_ERR_UNSUPPORTED, "GGML type %d is not a supported weight type", t);
+    if (!uses_kquants(c)) {
+        // the fused forward: one type for Q/K/V and one for gate/up
+        BREW_CHECK(c.type_q == c.type_k && c.type_k == c.type_v, BREW_ERR_UNSUPPORTED, "Q/K/V of different types");
+        BREW_CHECK(c.type_gate == c.type_up, BREW_ERR_UNSUPPORTED, "gate/up of different types");
+    } else {
+        // K-quant rows are whole 256-element super-blocks
+        const int qw = c.n_heads * c.head_size;
+        auto kq = [](int t) { return t == BREW_TYPE_Q4_K || t == BREW_TYPE_Q6_K; };
+        const int in_dim[] = {c.type_q, c.type_k, c.type_v, c.type_gate, c.type_up,
+                              c.tied_embeddings ? c.type_embed : c.type_output, c.type_embed};
+        for (int t : in_dim)
+            BREW_CHECK(!kq(t) || c.dim % 256 == 0, BREW_ERR_UNSUPPORTED, "K-quant matrix with dim %d %% 256", c.dim);
+        BREW_CHECK(!kq(c.type_o) || qw % 256 == 0, BREW_ERR_UNSUPPORTED, "K-quant wo with %d inputs", qw);
+        BREW_CHECK(!kq(c.type_down) || c.hidden_dim % 256 == 0, BREW_ERR_UNSUPPORTED, "K-quant down with %d inputs",
+                   c.hidden_dim);
+    }
     return BREW_OK;
 }
 
@@ -166,6 +194,13 @@ int alloc_state(brew_model_s* m) {
     if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->gen_d, (size_t)c.seq_len + 1))) return rc;
+    if (uses_kquants(c)) {
+        m->unfused = true;
+        const int64_t kmax = std::max<int64_t>(std::max<int64_t>(c.dim, qw), c.hidden_dim);
+        if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
+        if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
+        if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * rec))) return rc;
+    }
     m->h_pin_cap = std::max(4 * B, 64);
     BREW_CUDA(cudaMallocHost(&m->h_pin, (size_t)m->h_pin_cap * sizeof(int32_t)));
     return BREW_OK;
@@ -199,7 +234,122 @@ int64_t row_bytes_of(int type, int64_t cols) {
 }
 
 // Enqueues one forward pass for `B` sequences reading tokens_d / pos_d.
+// y[b][0:N] = W x[b] for any supported type: the K-quant kernel, or the
+// int8-MMA matvec after preparing x's records.
+int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx, int K, int N, float* y, int ldy, int B,
+           cudaStream_t s) {
+    const int64_t rb = row_bytes_of(type, K);
+    if (type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K)
+        return kquant_matvec_launch(type, w, rb, x, ldx, K, N, y, ldy, B, s, false);
+    int rc = prep_launch(x, ldx, K, B, nullptr, 0.0f, m->prep_any, s, false);
+    if (rc) return rc;
+    MvParams p = {};
+    p.type = type;
+    p.K = K;
+    p.row_bytes = rb;
+    p.batch = B;
+    p.ldy = ldy;
+    p.epi = MV_EPI_STORE;
+    p.nseg = 1;
+    p.seg[0] = {w, y, nullptr, nullptr, N, 0};
+    p.prep = m->prep_any;
+    p.err = ctx().err_word;
+    return mv_launch(p, s, false);
+}
+
+// The forward of a model with K-quant matrices (the Qwen2.5-7B Q4_K/Q6_K
+// config): each matvec reads fp32 activations, and RMSNorm, bias, residual
+// and the gated activation are separate kernels.  Op order of the
+// reference's forward methods (model/*/...Transformer.java).
+int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
+    const brew_config& c = m->c;
+    const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
+    const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
+    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    unsigned int* err = ctx().err_word;
+    int* attn_ctr = m->counters + hid / 32 + 8;
+    int rc;
+    // embedding row (scaled for Gemma3); its records are not used here
+    if ((rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x,
+                                m->rms_att, c.eps, m->prep_x, err, s, false)))
+        return rc;
+    for (int l = 0; l < L; ++l) {
+        if ((rc = rmsnorm_launch(m->x, dim, m->rms_att + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s))) return rc;
+        float* q = m->qkv;
+        float* k = m->qkv + qw;
+        float* v = m->qkv + qw + kvd;
+        if ((rc = mv_any(m, c.type_q, layer_ptr(m->t[T_Q], l, qw, dim), m->xn, dim, dim, qw, q, m->qkvw, B, s)) ||
+            (rc = mv_any(m, c.type_k, layer_ptr(m->t[T_K], l, kvd, dim), m->xn, dim, dim, kvd, k, m->qkvw, B, s)) ||
+            (rc = mv_any(m, c.type_v, layer_ptr(m->t[T_V], l, kvd, dim), m->xn, dim, dim, kvd, v, m->qkvw, B, s)))
+            return rc;
+        if (m->q_bias &&
+            ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
+             (rc = add_bias_launch(k, m->qkvw, m->k_bias + (int64_t)l * kvd, kvd, B, s)) ||
+             (rc = add_bias_launch(v, m->qkvw, m->v_bias + (int64_t)l * kvd, kvd, B, s))))
+            return rc;
+        {
+            AttnParams a = {};
+            a.batch = B;
+            a.n_heads = c.n_heads;
+            a.n_kv = c.n_kv_heads;
+            a.hd = hd;
+            a.seq_len = c.seq_len;
+            a.arch = c.arch;
+            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
+            a.window = (gemma && !global) ? c.sliding_window : 0;
+            a.eps = c.eps;
+            float base;
+            if (c.rope_base > 0.0f) base = c.rope_base;
+            else if (c.arch == BREW_ARCH_LLAMA) base = 10000.0f;
+            else if (gemma) base = global ? 1000000.0f : 10000.0f;
+            else base = 1000000.0f;
+            a.rope_base = base;
+            a.rope_scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
+            a.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
+            a.q = q;
+            a.k = k;
+            a.v = v;
+            a.ldq = a.ldkv = m->qkvw;
+            a.qnorm_w = qknorm ? m->rms_q + (int64_t)l * hd : nullptr;
+            a.knorm_w = qknorm ? m->rms_k + (int64_t)l * hd : nullptr;
+            a.kcache = m->kc + (int64_t)l * c.seq_len * kvd;
+            a.vcache = m->vc + (int64_t)l * c.seq_len * kvd;
+            a.cache_bstride = m->cache_bstride;
+            a.pos = m->pos_d;
+            a.xb = m->xb;
+            a.ldxb = qw;
+            a.part = m->attn_part;
+            a.counters = attn_ctr;
+            a.nchunk = m->nchunk;
+            a.prep_out = m->prep_q;
+            a.err = err;
+            if ((rc = attn_launch(a, s, false))) return rc;
+        }
+        if ((rc = mv_any(m, c.type_o, layer_ptr(m->t[T_O], l, dim, qw), m->xb, qw, qw, dim, m->xb2, dim, B, s)) ||
+            (rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr, c.eps,
+                                  dim, B, s)) ||
+            (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)) ||
+            (rc = mv_any(m, c.type_gate, layer_ptr(m->t[T_GATE], l, hid, dim), m->xn, dim, dim, hid, m->hb, hid, B,
+                         s)) ||
+            (rc = mv_any(m, c.type_up, layer_ptr(m->t[T_UP], l, hid, dim), m->xn, dim, dim, hid, m->hb2, hid, B, s)) ||
+            (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
+            (rc = mv_any(m, c.type_down, layer_ptr(m->t[T_DOWN], l, dim, hid), m->hb, hid, hid, dim, m->xb2, dim, B,
+                         s)) ||
+            (rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_ffn + (int64_t)l * dim : nullptr, c.eps,
+                                  dim, B, s)))
+            return rc;
+    }
+    if (!with_classifier) return BREW_OK;
+    const int otype = c.tied_embeddings ? c.type_embed : c.type_output;
+    if ((rc = rmsnorm_launch(m->x, dim, m->rms_final, c.eps, dim, B, m->xn, dim, s)) ||
+        (rc = mv_any(m, otype, m->t[T_OUTPUT]->d, m->xn, dim, dim, c.vocab_size, m->logits, c.vocab_size, B, s)))
+        return rc;
+    return argmax_launch(m->logits, c.vocab_size, c.vocab_size, B, m->am_out, s, false);
+}
+
 int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
+    if (m->unfused) return enqueue_forward_unfused(m, B, with_classifier, s);
     const brew_config& c = m->c;
     const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
     const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
