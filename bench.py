@@ -333,6 +333,100 @@ def profiled_traffic(name: str):
     return None
 
 
+def run_tp(args):
+    """Tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config
+    (Q4_K attention/FFN, Q6_K down and classifier, QKV bias): every matrix
+    row-sharded over the N ranks with one NCCL all-gather per projection;
+    B concurrent sequences prefilled with seeded prompts (untimed), then
+    decode steps fed back on the device.  value = tokens of all B sequences
+    per second (the ranks cooperate on the same tokens: strong scaling)."""
+    import ctypes
+    import torch
+    from brewference_b200 import _native as N
+    from brewference_b200.api import Communicator, DeviceModel, comm_unique_id
+
+    rank, world, dist = dist_init(args.gpus)
+    dev = torch.cuda.current_device() if world > 1 else 0
+    torch.cuda.set_device(dev)
+    N.init(dev)
+    cfg = C.qwen25_7b()
+    B = args.batch
+    box = [comm_unique_id() if rank == 0 else None]
+    if dist is not None:
+        dist.broadcast_object_list(box, src=0)
+    comm = Communicator(box[0], world, rank)
+    t0 = time.perf_counter()
+    dm = DeviceModel.synthesize(cfg, SEED, max_batch=B)
+    dm.set_tp(comm)
+    synth_s = time.perf_counter() - t0
+    rng = np.random.default_rng(SEED)
+    plen = args.prompt_len
+    prompts = rng.integers(0, cfg.vocab_size, (B, plen)).astype(np.int32)
+    t0 = time.perf_counter()
+    for i in range(plen):
+        dm.forward(prompts[:, i], np.full(B, i, np.int32), want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    s = stream.cuda_stream
+    tok = torch.from_numpy(prompts[:, -1].copy()).cuda()
+    n_pos = args.warmup + args.steps
+    pos = torch.arange(plen, plen + n_pos, dtype=torch.int32, device="cuda").repeat_interleave(B).view(n_pos, B)
+    lib = N.lib()
+
+    def step(k):
+        N.check(lib.brew_model_forward_dev(dm.handle, ctypes.c_void_p(tok.data_ptr()),
+                                           ctypes.c_void_p(pos[k].data_ptr()), B, None,
+                                           ctypes.c_void_p(tok.data_ptr()), ctypes.c_void_p(s)), "forward_dev")
+
+    for k in range(args.warmup):
+        step(k)
+    barrier(dist)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    k0 = N.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    e0.record(stream)
+    for k in range(args.warmup, n_pos):
+        step(k)
+    e1.record(stream)
+    barrier(dist)
+    launches = N.kernel_launches() - k0
+    clk = clocks.stop()
+    ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    value = B * args.steps / (ms / 1000.0)
+    peak, peak_kind = measured_peaks()
+    wbytes = cfg.decode_weight_bytes()
+    per_gpu = wbytes / world / (ms / args.steps / 1000.0) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (K-quant dequant in registers)",
+        "data": "synthetic (seeded random-init N(0,0.02) weights quantized to Q4_K/Q6_K on the device, seeded prompts)",
+        "config": {"workload": f"{cfg.name} Q4_K/Q6_K decode, {B} concurrent sequences after {plen}-token prompts, "
+                               f"tensor-parallel over {world} GPU(s)",
+                   "model": cfg.name, "global_batch": B, "seq_len": cfg.seq_len,
+                   "parallelism": f"tp{world} (row-sharded matrices, NCCL all-gather per projection)",
+                   "l2": "inputs larger than L2 (4.6 GB of weights per step)"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "per-GPU weight stream of the forward (weight bytes / P per step)"},
+        "clocks": clk,
+        "setup_s": {"synthesize": round(synth_s, 2), "prefill": round(prefill_s, 2)},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    dm.close()
+    comm.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_gpu(args):
     import torch
     from brewference_b200 import _native as N
@@ -463,17 +557,26 @@ def main():
     ap.add_argument("--steps", type=int, default=240)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
+    ap.add_argument("--prompt-len", type=int, default=None,
+                    help=f"prompt tokens (default {PROMPT_LEN}; 256 with --tp)")
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the matvec sweep")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config over --gpus ranks")
+    ap.add_argument("--batch", type=int, default=16, help="concurrent sequences of the --tp workload")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        args.prompt_len = args.prompt_len or PROMPT_LEN
         return run_reference(args)
+    if args.tp:
+        args.prompt_len = args.prompt_len or 256
+        return run_tp(args)
+    args.prompt_len = args.prompt_len or PROMPT_LEN
     return run_gpu(args)
 
 

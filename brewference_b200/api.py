@@ -133,6 +133,37 @@ class Linear:
                                         stream), "Linear.matmul_device")
 
 
+def tp_rows(rows: int, nranks: int, rank: int):
+    """Rows [r0, r1) of an N-row matrix that `rank` of `nranks` owns in the
+    tensor-parallel forward."""
+    r0, r1 = ctypes.c_int64(), ctypes.c_int64()
+    N.check(N.lib().brew_tp_rows(rows, nranks, rank, ctypes.byref(r0), ctypes.byref(r1)), "tp_rows")
+    return r0.value, r1.value
+
+
+def comm_unique_id() -> bytes:
+    """The 128-byte NCCL id rank 0 creates and shares (e.g. through
+    torch.distributed's object broadcast)."""
+    buf = ctypes.create_string_buffer(128)
+    N.check(N.lib().brew_comm_unique_id(buf), "comm_unique_id")
+    return buf.raw
+
+
+class Communicator:
+    """A NCCL communicator over the GPUs of one box (one process per GPU)."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        assert len(uid) == 128
+        h = ctypes.c_void_p()
+        N.check(N.lib().brew_comm_init(uid, nranks, rank, ctypes.byref(h)), "comm_init")
+        self.handle, self.nranks, self.rank = h.value, nranks, rank
+
+    def close(self):
+        if self.handle:
+            N.lib().brew_comm_free(self.handle)
+            self.handle = None
+
+
 class DeviceModel:
     """A device-resident model: weights, fp32 KV caches and the CUDA graphs of
     its forward pass."""
@@ -231,6 +262,12 @@ class DeviceModel:
 
     def reset(self):
         N.check(N.lib().brew_model_reset(self.handle), "reset")
+
+    def set_tp(self, comm: "Communicator") -> None:
+        """Shards this model's matrices by rows over `comm` (every rank holds
+        the same model); the forward then all-gathers each projection."""
+        N.check(N.lib().brew_model_set_tp(self.handle, comm.handle), "set_tp")
+        self.comm = comm
 
     def close(self):
         if self.handle:

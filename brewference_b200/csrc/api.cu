@@ -82,21 +82,28 @@ int Scratch::reserve(size_t need_bytes) {
 namespace {
 __device__ __forceinline__ float ldh(const uint8_t* p) { return half_bits_to_float((uint16_t)(p[0] | (p[1] << 8))); }
 
+// One warp per output row for up to MAXB vectors: each weight is dequantized
+// once and multiplied into every vector's sum (the per-vector summation
+// order is the same for any batch).
+template <int MAXB>
 __global__ void kquant_matvec_kernel(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K,
-                                     int N, float* y, int ldy) {
+                                     int N, float* y, int ldy, int batch) {
     pdl_launch_dependents();
     pdl_wait();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    const int b = blockIdx.y;
+    const int b0 = blockIdx.y * MAXB;
     if (row >= N) return;
     const uint8_t* wr = w + (int64_t)row * row_bytes;
-    const float* xb = x + (int64_t)b * ldx;
-    float acc = 0.0f;
+    float acc[MAXB];
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) acc[b] = 0.0f;
     for (int k0 = 0; k0 < K; k0 += 256) {
         const int s = lane >> 2;  // 8 sub-blocks of 32 per super-block, 4 lanes each
         const uint8_t* blk = wr + (int64_t)(k0 / 256) * (type == BREW_TYPE_Q4_K ? 144 : 210);
-        float part = 0.0f;
+        float part[MAXB];
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) part[b] = 0.0f;
         for (int i = (lane & 3) * 8; i < (lane & 3) * 8 + 8; ++i) {
             const int r = s * 32 + i;
             float wv;
@@ -116,20 +123,27 @@ __global__ void kquant_matvec_kernel(int type, const uint8_t* w, int64_t row_byt
                 const int q = (low | (high << 4)) - 32;
                 wv = __fmul_rn(__fmul_rn(ldh(blk + 208), (float)(int8_t)blk[192 + r / 16]), (float)q);
             }
-            part += wv * xb[k0 + r];
+#pragma unroll
+            for (int b = 0; b < MAXB; ++b)
+                if (b0 + b < batch) part[b] += wv * x[(int64_t)(b0 + b) * ldx + k0 + r];
         }
-        acc += part;
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) acc[b] += part[b];
     }
-    acc = warp_sum(acc);
-    if (lane == 0) y[(int64_t)b * ldy + row] = acc;
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+        const float v = warp_sum(acc[b]);
+        if (lane == 0 && b0 + b < batch) y[(int64_t)(b0 + b) * ldy + row] = v;
+    }
 }
 }  // namespace
 
 int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K, int N, float* y,
                          int ldy, int batch, cudaStream_t stream, bool pdl) {
     BREW_CHECK(K % 256 == 0, BREW_ERR_INVALID_ARG, "K-quant matvec: K=%d not a multiple of 256", K);
+    const int maxb = batch <= 1 ? 1 : (batch <= 4 ? 4 : 16);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + 7) / 8, batch);
+    cfg.gridDim = dim3((N + 7) / 8, (batch + maxb - 1) / maxb);
     cfg.blockDim = dim3(256);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -137,7 +151,12 @@ int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const fl
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel, type, w, row_bytes, x, ldx, K, N, y, ldy));
+    if (maxb == 1)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<1>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    else if (maxb == 4)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<4>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    else
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<16>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
     count_launch();
     return BREW_OK;
 }

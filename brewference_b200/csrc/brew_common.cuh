@@ -148,7 +148,7 @@ __device__ __forceinline__ void prefetch_l2(const void* src_gmem, uint32_t bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");
 }
 
-// ---- bulk async copy global -> shared (TMA, non-tensor, no multicast) -----
+// ---- bulk async copy global -> this CTA's shared memory (TMA, non-tensor) ----
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -157,7 +157,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
-// 2-D tiled TMA load through a tensor map (no multicast): box at element
+// 2-D tiled TMA load through a tensor map into this CTA's shared memory: box at element
 // coordinates (x, y) into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, int x, int y, uint64_t* bar) {
     asm volatile(

@@ -6,13 +6,16 @@
 // attention -> wo -> norm -> gate/up -> down) is long.  As separate kernels
 // each link pays a launch/ramp/drain gap and the HBM idles in between.  Here:
 //   * one CTA per SM (cooperative launch); warp 8 of every CTA is a producer
-//     that streams the CTA's share of EVERY phase's weight tiles (TMA boxes of
-//     16 rows x 8 blocks through per-family tensor maps, no multicast) into a
-//     ring of shared-memory stages, running ahead across phase boundaries;
+//     that streams the CTA's share of EVERY phase's weight tiles into a ring
+//     of shared-memory stages, running ahead across phase boundaries.  The
+//     weights are a fragment-packed copy (packed.cuh): a tile's block columns
+//     are contiguous, so a stage is one 1-D bulk copy per tile into this
+//     CTA's own shared memory;
 //   * warps 0-7 consume: each phase starts by building its own prep records
 //     (RMSNorm + limb split of the input vector, prep.cuh) in shared memory,
-//     then multiplies the staged tiles (int8 MMA, mv_device.cuh) and writes
-//     its output rows;
+//     then multiplies the staged tiles (int8 MMA, warp w taking block columns
+//     w, w+8, ... of every tile) and writes its output rows after a
+//     cross-warp sum;
 //   * phases are separated by a grid barrier among the consumer warps
 //     (acquire/release counter in global memory, bounded wait);
 //   * attention (QK-norm, RoPE from precomputed tables, KV append, chunked

@@ -4,7 +4,7 @@
 //   * Weights stay in their 34-byte (Q8_0) / 18-byte (Q4_0) blocks.  One
 //     producer warp streams them into a ring of shared-memory stages with TMA:
 //     cp.async.bulk.tensor.2d boxes of 16 rows x 8 blocks through a tensor map
-//     (row pitch a multiple of 16 bytes; no multicast), or bulk copies of whole
+//     (row pitch a multiple of 16 bytes; each CTA loads only for itself), or bulk copies of whole
 //     rows otherwise.
 //   * The x side arrives as prep records (prep.cuh): per 32-block three int8
 //     limb columns per vector.  One mma.sync m16n8k32 int8 MMA gives the exact

@@ -18,6 +18,7 @@
 #include "brew_internal.cuh"
 #include "decode.cuh"
 #include "eltwise.cuh"
+#include "tp.cuh"
 
 #include <cmath>
 #include <cstdlib>
@@ -88,6 +89,10 @@ struct brew_model_s {
     bool unfused = false;
     float *xn = nullptr, *hb2 = nullptr;    // normed input of a matvec; the up projection
     uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
+    // tensor parallelism (brew_model_set_tp): this rank's row slices
+    brew_comm comm = nullptr;
+    float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
+    unsigned long long *tp_keys = nullptr, *tp_keys_all = nullptr;
     unsigned long long* bar = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
@@ -166,6 +171,21 @@ void matrix_shape(const brew_config& c, int which, int64_t* rows, int64_t* cols,
     }
 }
 
+// Buffers of the unfused forward (K-quant models, tensor parallelism).
+int alloc_unfused(brew_model_s* m) {
+    if (m->unfused) return BREW_OK;
+    const brew_config& c = m->c;
+    const int B = m->max_batch;
+    const int64_t qw = (int64_t)c.n_heads * c.head_size;
+    const int64_t kmax = std::max<int64_t>(std::max<int64_t>(c.dim, qw), c.hidden_dim);
+    int rc;
+    if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
+    if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
+    if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * prep_rec_bytes(B)))) return rc;
+    m->unfused = true;
+    return BREW_OK;
+}
+
 int alloc_state(brew_model_s* m) {
     const brew_config& c = m->c;
     const int B = m->max_batch;
@@ -194,13 +214,7 @@ int alloc_state(brew_model_s* m) {
     if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->gen_d, (size_t)c.seq_len + 1))) return rc;
-    if (uses_kquants(c)) {
-        m->unfused = true;
-        const int64_t kmax = std::max<int64_t>(std::max<int64_t>(c.dim, qw), c.hidden_dim);
-        if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
-        if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
-        if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * rec))) return rc;
-    }
+    if (uses_kquants(c) && (rc = alloc_unfused(m))) return rc;
     m->h_pin_cap = std::max(4 * B, 64);
     BREW_CUDA(cudaMallocHost(&m->h_pin, (size_t)m->h_pin_cap * sizeof(int32_t)));
     return BREW_OK;
@@ -270,6 +284,17 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
     unsigned int* err = ctx().err_word;
     int* attn_ctr = m->counters + hid / 32 + 8;
     int rc;
+    // tensor parallelism: this rank multiplies rows [R*N/P, (R+1)*N/P) of
+    // every matrix and the slices are all-gathered
+    const int P = m->comm ? m->comm->nranks : 1, R = m->comm ? m->comm->rank : 0;
+    auto shard = [&](brew_tensor t, int type, int l, int N, int K) {
+        return layer_ptr(t, l, N, K) + (int64_t)(N / P) * R * row_bytes_of(type, K);
+    };
+    auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd) {
+        int r = tp_allgather(m->comm, m->tp_send, m->tp_recv, (size_t)B * slice, s);
+        if (!r) r = tp_unshard_launch(m->tp_recv, P, B, slice, segs, nseg, dst, ldd, s);
+        return r;
+    };
     // embedding row (scaled for Gemma3); its records are not used here
     if ((rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x,
                                 m->rms_att, c.eps, m->prep_x, err, s, false)))
@@ -279,15 +304,34 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         float* q = m->qkv;
         float* k = m->qkv + qw;
         float* v = m->qkv + qw + kvd;
-        if ((rc = mv_any(m, c.type_q, layer_ptr(m->t[T_Q], l, qw, dim), m->xn, dim, dim, qw, q, m->qkvw, B, s)) ||
-            (rc = mv_any(m, c.type_k, layer_ptr(m->t[T_K], l, kvd, dim), m->xn, dim, dim, kvd, k, m->qkvw, B, s)) ||
-            (rc = mv_any(m, c.type_v, layer_ptr(m->t[T_V], l, kvd, dim), m->xn, dim, dim, kvd, v, m->qkvw, B, s)))
-            return rc;
-        if (m->q_bias &&
-            ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
-             (rc = add_bias_launch(k, m->qkvw, m->k_bias + (int64_t)l * kvd, kvd, B, s)) ||
-             (rc = add_bias_launch(v, m->qkvw, m->v_bias + (int64_t)l * kvd, kvd, B, s))))
-            return rc;
+        if (P == 1) {
+            if ((rc = mv_any(m, c.type_q, layer_ptr(m->t[T_Q], l, qw, dim), m->xn, dim, dim, qw, q, m->qkvw, B, s)) ||
+                (rc = mv_any(m, c.type_k, layer_ptr(m->t[T_K], l, kvd, dim), m->xn, dim, dim, kvd, k, m->qkvw, B, s)) ||
+                (rc = mv_any(m, c.type_v, layer_ptr(m->t[T_V], l, kvd, dim), m->xn, dim, dim, kvd, v, m->qkvw, B, s)))
+                return rc;
+            if (m->q_bias &&
+                ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
+                 (rc = add_bias_launch(k, m->qkvw, m->k_bias + (int64_t)l * kvd, kvd, B, s)) ||
+                 (rc = add_bias_launch(v, m->qkvw, m->v_bias + (int64_t)l * kvd, kvd, B, s))))
+                return rc;
+        } else {
+            // slices [q_R | k_R | v_R] per rank, gathered into q | k | v
+            const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
+            float* sq = m->tp_send;
+            if ((rc = mv_any(m, c.type_q, shard(m->t[T_Q], c.type_q, l, qw, dim), m->xn, dim, dim, qs, sq, sl, B, s)) ||
+                (rc = mv_any(m, c.type_k, shard(m->t[T_K], c.type_k, l, kvd, dim), m->xn, dim, dim, ks, sq + qs, sl, B,
+                             s)) ||
+                (rc = mv_any(m, c.type_v, shard(m->t[T_V], c.type_v, l, kvd, dim), m->xn, dim, dim, ks, sq + qs + ks,
+                             sl, B, s)))
+                return rc;
+            if (m->q_bias &&
+                ((rc = add_bias_launch(sq, sl, m->q_bias + (int64_t)l * qw + (int64_t)R * qs, qs, B, s)) ||
+                 (rc = add_bias_launch(sq + qs, sl, m->k_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s)) ||
+                 (rc = add_bias_launch(sq + qs + ks, sl, m->v_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s))))
+                return rc;
+            const TpSeg segs[3] = {{qs, 0, 0}, {ks, qs, qw}, {ks, qs + ks, qw + kvd}};
+            if ((rc = gather(sl, segs, 3, m->qkv, m->qkvw))) return rc;
+        }
         {
             AttnParams a = {};
             a.batch = B;
@@ -326,26 +370,66 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             a.err = err;
             if ((rc = attn_launch(a, s, false))) return rc;
         }
-        if ((rc = mv_any(m, c.type_o, layer_ptr(m->t[T_O], l, dim, qw), m->xb, qw, qw, dim, m->xb2, dim, B, s)) ||
-            (rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr, c.eps,
+        if (P == 1) {
+            if ((rc = mv_any(m, c.type_o, layer_ptr(m->t[T_O], l, dim, qw), m->xb, qw, qw, dim, m->xb2, dim, B, s)))
+                return rc;
+        } else {
+            const TpSeg seg = {dim / P, 0, 0};
+            if ((rc = mv_any(m, c.type_o, shard(m->t[T_O], c.type_o, l, dim, qw), m->xb, qw, qw, dim / P, m->tp_send,
+                             dim / P, B, s)) ||
+                (rc = gather(dim / P, &seg, 1, m->xb2, dim)))
+                return rc;
+        }
+        if ((rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr, c.eps,
                                   dim, B, s)) ||
-            (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)) ||
-            (rc = mv_any(m, c.type_gate, layer_ptr(m->t[T_GATE], l, hid, dim), m->xn, dim, dim, hid, m->hb, hid, B,
-                         s)) ||
-            (rc = mv_any(m, c.type_up, layer_ptr(m->t[T_UP], l, hid, dim), m->xn, dim, dim, hid, m->hb2, hid, B, s)) ||
-            (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
-            (rc = mv_any(m, c.type_down, layer_ptr(m->t[T_DOWN], l, dim, hid), m->hb, hid, hid, dim, m->xb2, dim, B,
-                         s)) ||
-            (rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_ffn + (int64_t)l * dim : nullptr, c.eps,
+            (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)))
+            return rc;
+        if (P == 1) {
+            if ((rc = mv_any(m, c.type_gate, layer_ptr(m->t[T_GATE], l, hid, dim), m->xn, dim, dim, hid, m->hb, hid, B,
+                             s)) ||
+                (rc = mv_any(m, c.type_up, layer_ptr(m->t[T_UP], l, hid, dim), m->xn, dim, dim, hid, m->hb2, hid, B,
+                             s)) ||
+                (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
+                (rc = mv_any(m, c.type_down, layer_ptr(m->t[T_DOWN], l, dim, hid), m->hb, hid, hid, dim, m->xb2, dim,
+                             B, s)))
+                return rc;
+        } else {
+            const int hs = hid / P;
+            const TpSeg hseg = {hs, 0, 0}, dseg = {dim / P, 0, 0};
+            if ((rc = mv_any(m, c.type_gate, shard(m->t[T_GATE], c.type_gate, l, hid, dim), m->xn, dim, dim, hs, m->tp_g,
+                             hs, B, s)) ||
+                (rc = mv_any(m, c.type_up, shard(m->t[T_UP], c.type_up, l, hid, dim), m->xn, dim, dim, hs, m->tp_u, hs,
+                             B, s)) ||
+                (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s)) ||
+                (rc = gather(hs, &hseg, 1, m->hb, hid)) ||
+                (rc = mv_any(m, c.type_down, shard(m->t[T_DOWN], c.type_down, l, dim, hid), m->hb, hid, hid, dim / P,
+                             m->tp_send, dim / P, B, s)) ||
+                (rc = gather(dim / P, &dseg, 1, m->xb2, dim)))
+                return rc;
+        }
+        if ((rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_ffn + (int64_t)l * dim : nullptr, c.eps,
                                   dim, B, s)))
             return rc;
     }
     if (!with_classifier) return BREW_OK;
     const int otype = c.tied_embeddings ? c.type_embed : c.type_output;
-    if ((rc = rmsnorm_launch(m->x, dim, m->rms_final, c.eps, dim, B, m->xn, dim, s)) ||
-        (rc = mv_any(m, otype, m->t[T_OUTPUT]->d, m->xn, dim, dim, c.vocab_size, m->logits, c.vocab_size, B, s)))
+    const int V = c.vocab_size;
+    if ((rc = rmsnorm_launch(m->x, dim, m->rms_final, c.eps, dim, B, m->xn, dim, s))) return rc;
+    if (P == 1) {
+        if ((rc = mv_any(m, otype, m->t[T_OUTPUT]->d, m->xn, dim, dim, V, m->logits, V, B, s))) return rc;
+        return argmax_launch(m->logits, V, V, B, m->am_out, s, false);
+    }
+    // sharded classifier: per-rank argmax keys, gathered and reduced; the
+    // logits slices are gathered too (brew_model_forward returns them)
+    const int vs = V / P;
+    const TpSeg vseg = {vs, 0, 0};
+    if ((rc = mv_any(m, otype, shard(m->t[T_OUTPUT], otype, 0, V, dim), m->xn, dim, dim, vs, m->tp_send, vs, B, s)) ||
+        (rc = tp_argmax_keys_launch(m->tp_send, vs, vs, B, R * vs, m->tp_keys, s)) ||
+        (rc = tp_allgather_u64(m->comm, m->tp_keys, m->tp_keys_all, (size_t)B, s)) ||
+        (rc = tp_argmax_reduce_launch(m->tp_keys_all, P, B, m->am_out, s)) ||
+        (rc = gather(vs, &vseg, 1, m->logits, V)))
         return rc;
-    return argmax_launch(m->logits, c.vocab_size, c.vocab_size, B, m->am_out, s, false);
+    return BREW_OK;
 }
 
 int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
@@ -883,6 +967,38 @@ int brew_model_free(brew_model m) {
     std::lock_guard<std::mutex> lk(api_mutex());
     cudaDeviceSynchronize();
     model_destroy(m);
+    return BREW_OK;
+}
+
+int brew_model_set_tp(brew_model m, brew_comm comm) {
+    BREW_CHECK(m && comm, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(!m->comm, BREW_ERR_INVALID_ARG, "the model is already sharded");
+    const brew_config& c = m->c;
+    const int P = comm->nranks;
+    const int qw = c.n_heads * c.head_size, kvd = c.n_kv_heads * c.head_size;
+    const int rows[] = {qw, kvd, c.dim, c.hidden_dim, c.vocab_size};
+    for (int n : rows)
+        BREW_CHECK(n % P == 0, BREW_ERR_UNSUPPORTED, "%d rows do not split over %d ranks", n, P);
+    std::lock_guard<std::mutex> lk(api_mutex());
+    int rc = ensure_init();
+    if (rc) return rc;
+    BREW_CHECK(comm->device == ctx().device, BREW_ERR_INVALID_ARG, "communicator on device %d, model on %d",
+               comm->device, ctx().device);
+    BREW_CUDA(cudaDeviceSynchronize());
+    // the forward changes: drop captured graphs and the one-GPU decode kernel
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    m->graphs.clear();
+    m->graph_kernels.clear();
+    m->use_decode = false;
+    if ((rc = alloc_unfused(m))) return rc;
+    const int B = m->max_batch;
+    const int slice = std::max(std::max((qw + 2 * kvd) / P, c.dim / P), std::max(c.hidden_dim / P, c.vocab_size / P));
+    if ((rc = dalloc(m, &m->tp_send, (size_t)B * slice)) || (rc = dalloc(m, &m->tp_recv, (size_t)P * B * slice)) ||
+        (rc = dalloc(m, &m->tp_g, (size_t)B * (c.hidden_dim / P))) ||
+        (rc = dalloc(m, &m->tp_u, (size_t)B * (c.hidden_dim / P))) || (rc = dalloc(m, &m->tp_keys, (size_t)B)) ||
+        (rc = dalloc(m, &m->tp_keys_all, (size_t)P * B)))
+        return rc;
+    m->comm = comm;
     return BREW_OK;
 }
 

@@ -1,0 +1,192 @@
+// tp.cu — NCCL communicator, row-shard plan and the gather helpers of the
+// tensor-parallel forward.  NCCL is loaded with dlopen when a communicator
+// is first created, so one-GPU use has no NCCL dependency.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "brew_internal.cuh"
+#include "mv_device.cuh"
+#include "tp.cuh"
+
+namespace brew {
+namespace {
+
+struct NcclApi {
+    void* lib = nullptr;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+int nccl_load() {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.lib) return BREW_OK;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return set_error(BREW_ERR_NCCL, "cannot load libnccl.so.2: %s", dlerror());
+    NcclApi a;
+    a.lib = h;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_gather || !a.error_string)
+        return set_error(BREW_ERR_NCCL, "libnccl.so.2 lacks an entry point this library uses");
+    g_nccl = a;
+    return BREW_OK;
+}
+
+int nccl_check(ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return BREW_OK;
+    return set_error(BREW_ERR_NCCL, "%s: %s", what, g_nccl.error_string ? g_nccl.error_string(r) : "nccl error");
+}
+
+__global__ void unshard_kernel(const float* recv, int P, int B, int slice, TpSeg s0, TpSeg s1, TpSeg s2, int nseg,
+                               float* dst, int ldd) {
+    // one thread per (segment value, rank, row)
+    const TpSeg segs[3] = {s0, s1, s2};
+    const int b = blockIdx.y, r = blockIdx.z;
+    for (int k = 0; k < nseg; ++k) {
+        const TpSeg s = segs[k];
+        const float* src = recv + ((int64_t)r * B + b) * slice + s.src_off;
+        float* d = dst + (int64_t)b * ldd + s.dst_off + (int64_t)r * s.n;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < s.n; i += gridDim.x * blockDim.x) d[i] = src[i];
+    }
+}
+
+__global__ void argmax_keys_kernel(const float* logits, int ld, int n, int row0, unsigned long long* keys) {
+    const int b = blockIdx.x;
+    const float* lr = logits + (int64_t)b * ld;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long k = argmax_key(lr[i], row0 + i);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
+    __shared__ unsigned long long red[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long t = 0ull;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = red[w] > t ? red[w] : t;
+        keys[b] = t;
+    }
+}
+
+__global__ void argmax_reduce_kernel(const unsigned long long* keys, int P, int B, int32_t* out) {
+    const int b = threadIdx.x;
+    if (b >= B) return;
+    unsigned long long t = 0ull;
+    for (int r = 0; r < P; ++r) t = keys[(int64_t)r * B + b] > t ? keys[(int64_t)r * B + b] : t;
+    out[b] = (int32_t)(0xFFFFFFFFu - (uint32_t)(t & 0xFFFFFFFFull));
+}
+
+}  // namespace
+
+int tp_allgather(brew_comm_s* c, const float* send, float* recv, size_t count, cudaStream_t stream) {
+    return nccl_check(g_nccl.all_gather(send, recv, count, ncclFloat32, static_cast<ncclComm_t>(c->nccl), stream),
+                      "ncclAllGather");
+}
+
+int tp_allgather_u64(brew_comm_s* c, const unsigned long long* send, unsigned long long* recv, size_t count,
+                     cudaStream_t stream) {
+    return nccl_check(g_nccl.all_gather(send, recv, count, ncclUint64, static_cast<ncclComm_t>(c->nccl), stream),
+                      "ncclAllGather");
+}
+
+int tp_unshard_launch(const float* recv, int P, int B, int slice, const TpSeg* segs, int nseg, float* dst, int ldd,
+                      cudaStream_t stream) {
+    BREW_CHECK(nseg >= 1 && nseg <= 3, BREW_ERR_INVALID_ARG, "unshard: %d segments", nseg);
+    int nmax = 0;
+    for (int k = 0; k < nseg; ++k) nmax = std::max(nmax, segs[k].n);
+    const TpSeg z = {0, 0, 0};
+    const dim3 grid(std::max(1, std::min(64, (nmax + 255) / 256)), B, P);
+    unshard_kernel<<<grid, 256, 0, stream>>>(recv, P, B, slice, segs[0], nseg > 1 ? segs[1] : z,
+                                             nseg > 2 ? segs[2] : z, nseg, dst, ldd);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+int tp_argmax_keys_launch(const float* logits, int ld, int n, int B, int row0, unsigned long long* keys,
+                          cudaStream_t stream) {
+    argmax_keys_kernel<<<B, 1024, 0, stream>>>(logits, ld, n, row0, keys);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+int tp_argmax_reduce_launch(const unsigned long long* keys, int P, int B, int32_t* out, cudaStream_t stream) {
+    argmax_reduce_kernel<<<1, 32, 0, stream>>>(keys, P, B, out);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+}  // namespace brew
+
+using namespace brew;
+
+extern "C" {
+
+int brew_tp_rows(int64_t rows, int32_t nranks, int32_t rank, int64_t* r0, int64_t* r1) {
+    BREW_CHECK(r0 && r1, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(nranks >= 1 && rank >= 0 && rank < nranks, BREW_ERR_INVALID_ARG, "rank %d of %d", rank, nranks);
+    BREW_CHECK(rows >= 0 && rows % nranks == 0, BREW_ERR_UNSUPPORTED, "%lld rows do not split over %d ranks",
+               (long long)rows, nranks);
+    *r0 = rows / nranks * rank;
+    *r1 = rows / nranks * (rank + 1);
+    return BREW_OK;
+}
+
+int brew_comm_unique_id(uint8_t* out) {
+    BREW_CHECK(out, BREW_ERR_INVALID_ARG, "null argument");
+    int rc = nccl_load();
+    if (rc) return rc;
+    ncclUniqueId id;
+    if ((rc = nccl_check(g_nccl.get_unique_id(&id), "ncclGetUniqueId"))) return rc;
+    memcpy(out, id.internal, NCCL_UNIQUE_ID_BYTES);
+    return BREW_OK;
+}
+
+int brew_comm_init(const uint8_t* id_bytes, int32_t nranks, int32_t rank, brew_comm* out) {
+    BREW_CHECK(id_bytes && out, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(nranks >= 1 && rank >= 0 && rank < nranks, BREW_ERR_INVALID_ARG, "rank %d of %d", rank, nranks);
+    *out = nullptr;
+    int rc = ensure_init();
+    if (rc) return rc;
+    if ((rc = nccl_load())) return rc;
+    ncclUniqueId id;
+    memcpy(id.internal, id_bytes, NCCL_UNIQUE_ID_BYTES);
+    ncclComm_t comm = nullptr;
+    if ((rc = nccl_check(g_nccl.comm_init_rank(&comm, nranks, id, rank), "ncclCommInitRank"))) return rc;
+    brew_comm c = new brew_comm_s();
+    c->nccl = comm;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->device = ctx().device;
+    *out = c;
+    return BREW_OK;
+}
+
+int brew_comm_free(brew_comm c) {
+    if (!c) return BREW_OK;
+    if (c->nccl && g_nccl.comm_destroy) g_nccl.comm_destroy(static_cast<ncclComm_t>(c->nccl));
+    delete c;
+    return BREW_OK;
+}
+
+}  // extern "C"

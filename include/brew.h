@@ -221,6 +221,29 @@ BREW_API int brew_model_create(const brew_config* cfg, const brew_model_weights*
  * The bytes equal those of the CPU generator used by the tests. */
 BREW_API int brew_model_synthesize(const brew_config* cfg, uint64_t seed, int32_t max_batch, brew_model* out);
 BREW_API int brew_model_free(brew_model m);
+/* ---- tensor parallelism (one process per GPU of a box) --------------------
+ * Every matrix is split by rows over the ranks of a communicator: rank r of P
+ * multiplies rows [r*N/P, (r+1)*N/P) of each N-row matrix and the slices are
+ * all-gathered with NCCL after each projection (q|k|v, wo, gate|up, down,
+ * classifier; the argmax is reduced over the ranks' (value, index) keys).
+ * Attention, norms and residuals are replicated, so every rank ends a step
+ * with the full activations, and each output row is the one-GPU row: the
+ * sharded forward returns the one-GPU logits bit for bit.  N must be a
+ * multiple of P for every matrix.  The row split is the one the reference's
+ * matvec parallelises over (Linear.java:51-64, rows of `out`). */
+typedef struct brew_comm_s* brew_comm;
+/* Rows [r0, r1) of an N-row matrix that rank `rank` of `nranks` owns. */
+BREW_API int brew_tp_rows(int64_t rows, int32_t nranks, int32_t rank, int64_t* r0, int64_t* r1);
+/* Rank 0 creates the 128-byte NCCL unique id and shares it with the others. */
+BREW_API int brew_comm_unique_id(uint8_t* id_out);
+/* Collective: every rank calls it with the same id (device = brew_init's). */
+BREW_API int brew_comm_init(const uint8_t* id, int32_t nranks, int32_t rank, brew_comm* out);
+/* Free the models that use a communicator before the communicator. */
+BREW_API int brew_comm_free(brew_comm c);
+/* Shards model `m` over `comm` (same model on every rank, same seed or same
+ * tensors).  The model then runs the unfused forward with the gathers. */
+BREW_API int brew_model_set_tp(brew_model m, brew_comm comm);
+
 /* Returns the model's tensors (borrowed handles) for inspection. */
 BREW_API int brew_model_tensor(brew_model m, int which, brew_tensor* out);
 
