@@ -13,7 +13,7 @@ import re
 from .config import BrewConfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbrew.so")
+LIB_PATH = os.environ.get("BREW_LIB") or os.path.join(HERE, "libbrew.so")   # BREW_LIB: another build of the library
 HEADER = os.path.join(os.path.dirname(HERE), "include", "brew.h")
 
 OK, ERR_INVALID_ARG, ERR_OUT_OF_BOUNDS, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_CONTEXT_FULL, ERR_UNSUPPORTED, \

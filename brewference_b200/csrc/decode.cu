@@ -278,22 +278,31 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             for (int w = 0; w < 8; ++w) tot += red[w];
             scale = rms_scale(tot, K, P.eps);
         }
+        // two independent block quads per iteration (their shuffle and
+        // divide chains overlap)
         const int gq = lane >> 3, e = (lane & 7) * 4;
-        for (int j0 = warp * 4; j0 < KB; j0 += 32) {
-            const int j = j0 + gq;
-            const bool ok = j < KB;
-            const int jj = ok ? j : KB - 1;
-            float4 v = v4[(32 * jj + e) >> 2];
-            if (xout && ok && (j % G) == (int)blockIdx.x)
-                __stcg(reinterpret_cast<float4*>(xout + (int64_t)b * ld + 32 * j + e), v);
-            if (nw) {
-                const float4 w = w4[(32 * jj + e) >> 2];
-                v.x = v.x * scale * w.x;
-                v.y = v.y * scale * w.y;
-                v.z = v.z * scale * w.z;
-                v.w = v.w * scale * w.w;
+        for (int j0 = warp * 4; j0 < KB; j0 += 64) {
+            int jj[2];
+            bool ok[2];
+            float4 v[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int j = j0 + 32 * u + gq;
+                ok[u] = j < KB;
+                jj[u] = ok[u] ? j : KB - 1;
+                v[u] = v4[(32 * jj[u] + e) >> 2];
+                if (xout && ok[u] && (j % G) == (int)blockIdx.x)
+                    __stcg(reinterpret_cast<float4*>(xout + (int64_t)b * ld + 32 * j + e), v[u]);
+                if (nw) {
+                    const float4 w = w4[(32 * jj[u] + e) >> 2];
+                    v[u].x = v[u].x * scale * w.x;
+                    v[u].y = v[u].y * scale * w.y;
+                    v[u].z = v[u].z * scale * w.z;
+                    v[u].w = v[u].w * scale * w.w;
+                }
             }
-            prep_emit_quad(prep + (size_t)jj * P.rec_bytes, P.batch, b, v, ok, lsum);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) prep_emit_quad(prep + (size_t)jj[u] * P.rec_bytes, P.batch, b, v[u], ok[u], lsum);
         }
         consumer_bar();
     }
@@ -306,8 +315,6 @@ struct Ring {
     int ns, stage_bytes;
 };
 
-__device__ __forceinline__ uint4 lds128(uint32_t a) { return *reinterpret_cast<const uint4*>(sptr(a)); }
-__device__ __forceinline__ uint2 lds64(uint32_t a) { return *reinterpret_cast<const uint2*>(sptr(a)); }
 
 // Consumer side of one matvec phase: this CTA's tiles in groups of up to 8,
 // stage by stage.  Warp w multiplies block columns w, w + 8, ... of the stage
@@ -391,14 +398,14 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
                             uint32_t a0, a1, a2, a3;
                             int c[4];
                             if (TT == BREW_TYPE_Q8_0) {
-                                const uint4 A = lds128(blk + lane * 16);
+                                const uint4 A = *reinterpret_cast<const uint4*>(sptr(blk + lane * 16));
                                 a0 = A.x;
                                 a1 = A.y;
                                 a2 = A.z;
                                 a3 = A.w;
                                 mma_s8s8(c, a0, a1, a2, a3, b0, b1);
                             } else {
-                                const uint2 W = lds64(blk + lane * 8);
+                                const uint2 W = *reinterpret_cast<const uint2*>(sptr(blk + lane * 8));
                                 a0 = W.x & 0x0F0F0F0Fu;
                                 a1 = W.y & 0x0F0F0F0Fu;
                                 a2 = (W.x >> 4) & 0x0F0F0F0Fu;
@@ -469,6 +476,7 @@ template <int TT>
 __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q,
                                            unsigned long long* detail) {
     int dch = 0;
+    const uint64_t pol = l2_evict_first_policy();
     constexpr int BS = pk_block_bytes(TT);
     const int lane = threadIdx.x & 31;
     const int G = gridDim.x;
@@ -507,8 +515,8 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
             if (lane == 0) mbar_arrive_expect_tx(&ring.full[stage], (uint32_t)ng * cbytes);
             __syncwarp();
             if (lane < ng)
-                bulk_g2s(sbase + (size_t)lane * cbytes,
-                         f.w + ((int64_t)(tg0 + lane) * f.KB + (int64_t)chunk * geo.KC) * BS, cbytes, &ring.full[stage]);
+                bulk_g2s_hint(sbase + (size_t)lane * cbytes,
+                         f.w + ((int64_t)(tg0 + lane) * f.KB + (int64_t)chunk * geo.KC) * BS, cbytes, &ring.full[stage], pol);
             __syncwarp();
         }
     }
@@ -528,7 +536,37 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
 //   q-norm w [hd] | k-norm w [hd] | cos [hd/2] | sin [hd/2] |
 //   scores [G][SUB] | per head: running max, running sum, round rescale, -
 // and, for the combine, the partials [heads][nchunk][hd + 4].
-__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave) {
+// The RoPE cos/sin of this step's positions: thread t always rotates pair
+// d = t % (hd/2) (hd/2 divides 256), so each thread keeps its column for both
+// sequences and both tables (global / Gemma3 local) in registers for the
+// whole step.
+struct RopeRegs {
+    float c00, c01, c10, c11, s00, s01, s10, s11;   // [sequence][table]
+    __device__ __forceinline__ float cosv(int b, int t) const { return b ? (t ? c11 : c10) : (t ? c01 : c00); }
+    __device__ __forceinline__ float sinv(int b, int t) const { return b ? (t ? s11 : s10) : (t ? s01 : s00); }
+};
+
+__device__ __forceinline__ RopeRegs load_rope(const DecodeParams& P) {
+    RopeRegs r = {};
+    const int half = P.hd / 2, d = threadIdx.x % half;
+    const bool two = P.arch == BREW_ARCH_GEMMA3;
+    float* cv[2][2] = {{&r.c00, &r.c01}, {&r.c10, &r.c11}};
+    float* sv[2][2] = {{&r.s00, &r.s01}, {&r.s10, &r.s11}};
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            if (b >= P.batch || (t == 1 && !two)) continue;
+            const int pos = P.pos[b];
+            if (pos < 0 || pos >= P.seq_len) continue;
+            const int64_t o = ((int64_t)t * P.seq_len + pos) * half + d;
+            *cv[b][t] = __ldg(P.rope_cos + o);
+            *sv[b][t] = __ldg(P.rope_sin + o);
+        }
+    return r;
+}
+
+__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave, const RopeRegs& rope) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -547,9 +585,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     float* vs = ks + hd;
     float* wq = vs + hd;
     float* wk = wq + hd;
-    float* cs = wk + hd;
-    float* sn = cs + half;
-    float* sc = sn + half;
+    float* sc = wk + hd;
     float* st = sc + G * SUB;
     __shared__ int s_last;
     const int items = P.batch * P.n_kv * nch;
@@ -573,8 +609,6 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             const float* qsrc = P.qkv + (int64_t)b * ldq + (int64_t)hk * G * hd;
             const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
             const float* vsrc = ksrc + kvd;
-            const float* csrc = P.rope_cos + ((int64_t)table * P.seq_len + pos) * half;
-            const float* ssrc = P.rope_sin + ((int64_t)table * P.seq_len + pos) * half;
             // K / V rows of positions r0 .. r0 + SUB - 1 of the chunk; the row
             // of this step's position comes from k / v instead (not yet cached)
             auto issue_round = [&](int r0) {
@@ -596,10 +630,6 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     cp_async16(wq + 4 * i, P.rms_q + (int64_t)l * hd + 4 * i);
                     cp_async16(wk + 4 * i, P.rms_k + (int64_t)l * hd + 4 * i);
                 }
-            }
-            for (int i = tid; i < half / 4; i += 256) {
-                cp_async16(cs + 4 * i, csrc + 4 * i);
-                cp_async16(sn + 4 * i, ssrc + 4 * i);
             }
             issue_round(0);
             if (tid < G) {
@@ -626,7 +656,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 float* vecp = hh < G ? qs + hh * hd : ks;
                 const int i0 = inter ? 2 * d : d;
                 const int i1 = inter ? 2 * d + 1 : d + half;
-                const float a = vecp[i0], bb = vecp[i1], cc = cs[d], ss = sn[d];
+                const float a = vecp[i0], bb = vecp[i1], cc = rope.cosv(b, table), ss = rope.sinv(b, table);
                 vecp[i0] = __fsub_rn(__fmul_rn(a, cc), __fmul_rn(bb, ss));
                 vecp[i1] = __fadd_rn(__fmul_rn(a, ss), __fmul_rn(bb, cc));
             }
@@ -711,11 +741,15 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 __stcg(&pbase[((int64_t)tid * nch + c) * stride + 1], st[4 * tid + 1]);
             }
         }
-        // arrival; the last CTA of (b, hk) combines the used chunks in order
-        __threadfence();
+        // arrival; the last CTA of (b, hk) combines the used chunks in order.
+        // The barrier orders every thread's partial stores before thread 0's
+        // fence, which makes them visible before its arrival is counted.
         consumer_bar();
         int* ctr = &P.attn_ctr[b * P.n_kv + hk];
-        if (tid == 0) s_last = (atomicAdd(ctr, 1) == nch - 1);
+        if (tid == 0) {
+            __threadfence();
+            s_last = (atomicAdd(ctr, 1) == nch - 1);
+        }
         consumer_bar();
         if (s_last) {
             __threadfence();
@@ -776,6 +810,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     uint8_t* prep = reinterpret_cast<uint8_t*>(vec) + P.vec_bytes;
     ring.stages = prep + P.prep_bytes;
     ring.stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ring.stages) + 127) & ~uintptr_t(127));
+    const uint32_t prep_s = smem_u32(prep);
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int L = P.n_layers;
@@ -809,7 +844,6 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     }
 
     // --------------------------------- consumers ---------------------------------
-    const uint32_t prep_s = smem_u32(prep);
     const int Gc = gridDim.x;
     unsigned long long target = s_base;
     int q = 0;
@@ -847,7 +881,16 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         if (!grid_sync(P, target, &s_ok)) aborted = true;
         mark();
     };
+    const RopeRegs rope = load_rope(P);
     for (int l = 0; l < L && !aborted; ++l) {
+        // the small vectors of the next phase go to L2 one phase ahead (HBM
+        // misses otherwise; fetched earlier they would be evicted again by
+        // the weight stream)
+        auto pf = [&](const float* v, int n) {
+            if (v && blockIdx.x == 0 && tid == 0) prefetch_l2(v, (uint32_t)n * 4u);
+        };
+        pf(P.rms_q ? P.rms_q + (int64_t)l * P.hd : nullptr, P.hd);
+        pf(P.rms_k ? P.rms_k + (int64_t)l * P.hd : nullptr, P.hd);
         // ---- RMSNorm (attention) + Q|K|V ----
         if (l == 0) {
             prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
@@ -868,7 +911,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- attention ----
-        attn_phase(P, l, vec, tr ? &twave : nullptr);
+        attn_phase(P, l, vec, tr ? &twave : nullptr, rope);
         markv(twave);   // the first load wave landed
         twave = 0;
         markv(0);
@@ -876,6 +919,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- wo (+ residual) ----
+        pf(P.rms_ffn + (int64_t)l * P.dim, P.dim);
         prep_phase(P, SRC_PLAIN, P.xb, P.n_heads * P.hd, P.n_heads * P.hd, nullptr, nullptr, nullptr, nullptr, prep,
                    vec, s_red, lsum_l, tr ? &twave : nullptr);
         mark_prep();
@@ -904,6 +948,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- down (+ residual) ----
+        pf(l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final, P.dim);
         prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
         mark_prep();
         {
@@ -997,6 +1042,7 @@ bool decode_supported(const brew_config& c, int batch) {
     // attention: a CTA holds the G * hd outputs of a kv head's queries in
     // four registers per thread; 16-byte copies of half rows
     if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
+    if (256 % (c.head_size / 2)) return false;   // each thread's RoPE column is fixed
     return true;
 }
 
