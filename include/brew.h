@@ -174,6 +174,16 @@ BREW_API int brew_matmul_dev_static(float* output_dev, const float* input_dev, b
                     int64_t weights_offset, int32_t input_size, int32_t output_size,
                     int32_t batch, void* stream);
 
+/* Prefill GEMM on the tcgen05 tensor cores: output_dev [T][N] = W x for T
+ * token vectors input_dev [T][K] at once (the prompt of ModelRunner.prefill,
+ * runtime/ModelRunner.java:196-206, instead of T matvecs).  Q8_0 weights;
+ * N a multiple of 128, T of 32.  Each 32-element block's integer dot product
+ * is exact (24-bit limb split of x) and scaled by d_row * s_block in fp32,
+ * as brew_matmul does per token. */
+BREW_API int brew_gemm_q8_dev(float* output_dev, const float* input_dev, brew_tensor weights,
+                              int64_t weights_offset, int32_t input_size, int32_t output_size,
+                              int32_t tokens, void* stream);
+
 /* Two-step form for callers that multiply one input by several matrices
  * (Q, K and V share their input): brew_prepare_input_dev writes the
  * quantized-activation records of x [batch][input_size] into `prep_dev`
