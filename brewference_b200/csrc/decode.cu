@@ -42,7 +42,9 @@ namespace {
 enum { PH_QKV = 0, PH_O, PH_GU, PH_DOWN, PH_CLS };
 
 constexpr int ATTN_MIN_POS = 32;   // positions per attention CTA at least
-constexpr size_t DK_SMEM_BUDGET = 224 * 1024;   // dynamic shared memory of the decode kernel, at most
+// dynamic shared memory of the decode kernel, at most: 226 KB of the 227 KB a
+// block may opt in to (the kernel's static shared variables take the rest)
+constexpr size_t DK_SMEM_BUDGET = 226 * 1024;
 constexpr int DK_RED_BYTES = 8 * 8 * 16 * 2 * 4;   // cross-warp partial sums of a tile group
 constexpr int DK_STAGE_BYTES = 64 * 544;           // one pipeline stage: 64 Q8_0 block-tiles
 
@@ -50,7 +52,7 @@ constexpr int DK_STAGE_BYTES = 64 * 544;           // one pipeline stage: 64 Q8_
 // tiles of this layer's family, split over the CTAs by whole tiles.
 struct DPhase {
     const uint8_t* w;        // this layer's packed tiles
-    int KB, tiles, rows, epi, ldy, tt;
+    int KB, tiles, rows, epi, ldy, tt, ph;
     bool argmax;
     float* y;
     const float* resid;      // STORE: y = resid + (W x + bias)
@@ -64,6 +66,7 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
     const bool gem = P.arch == BREW_ARCH_GEMMA3;
     f.epi = MV_EPI_STORE;
     f.tt = P.type_layer;
+    f.ph = ph;
     switch (ph) {
         case PH_QKV:
             f.w = P.pk[PK_QKV] + (int64_t)l * P.pk_lb[PK_QKV];
@@ -121,23 +124,19 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
     return f;
 }
 
-// Stage geometry of a CTA that owns `nt` tiles: gs tiles per group (their
-// accumulators live in registers together), KC block columns of each per
+// Stage geometry of a group of tiles: KC block columns of each tile per
 // stage (a multiple of 8 dividing KB: warp w takes columns w, w + 8, ...).
+// The group sizes and KC come from tables that decode_prepare fills (they
+// maximise the bytes a stage carries).
 struct PGeom {
-    int gs, KC, nchunks;
+    int KC, nchunks;
 };
 
-__device__ __forceinline__ PGeom pk_geom(int nt, int KB, int bs, int stage_bytes) {
+__device__ __forceinline__ int pk_gs(const DecodeParams& P, int ph, int nt) { return P.geo_gs[ph][min(nt, 9)]; }
+
+__device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, int KB) {
     PGeom g;
-    g.gs = min(8, nt);
-    const int cap = min(KB, stage_bytes / (g.gs * bs));
-    g.KC = 8;
-    for (int kc = (cap / 8) * 8; kc >= 8; kc -= 8)
-        if (KB % kc == 0) {
-            g.KC = kc;
-            break;
-        }
+    g.KC = P.geo_kc[ph][ng];
     g.nchunks = KB / g.KC;
     return g;
 }
@@ -316,6 +315,91 @@ struct Ring {
 };
 
 
+// This lane's operand offsets inside a prep record (prep.cuh): B column g =
+// limb (g & 3) of vector g >> 2; accumulator columns 2t, 2t+1 belong to
+// vector t >> 1 (limbs (2t) & 3 and (2t + 1) & 3).
+struct LaneOps {
+    uint32_t boff, soff, loff0, loff1;
+    bool vB, vC;
+    int l0, bC;
+};
+
+// The stages of one tile group of NG tiles, then the limb combine of each
+// warp's partial sums into `red`.  NG is a compile-time count: the tile loop
+// is straight-line code, so the compiler schedules every tile's loads ahead
+// of the MMAs (with a run-time count and predicated tile slots, the loop
+// measured 2.5-3x slower per block column for one and two tiles).
+template <int TT, int NG>
+__device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo, const Ring& ring, int& q,
+                                         uint32_t prep_s, const LaneOps& o, float* red, bool& aborted,
+                                         unsigned long long* t_full, unsigned long long* detail, int& dch) {
+    constexpr int BS = pk_block_bytes(TT), SO = pk_scale_off(TT);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    float acc[NG][4];
+#pragma unroll
+    for (int k = 0; k < NG; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
+    for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
+        const int stage = q % ring.ns;
+        if (!aborted && !mbar_wait_bounded(&ring.full[stage], (q / ring.ns) & 1, P.err, BREW_DEVERR_TIMEOUT_FULL))
+            aborted = true;
+        if (t_full && warp == 0) *t_full = global_ns();
+        if (detail && tid == 0 && dch < DK_DETAIL) detail[DK_DETAIL + dch] = global_ns();
+        if (!aborted) {
+            const uint32_t sb = smem_u32(ring.stages + (size_t)stage * ring.stage_bytes);
+            for (int kb = warp; kb < geo.KC; kb += 8) {
+                const uint32_t rec = prep_s + (chunk * geo.KC + kb) * P.rec_bytes;
+                uint32_t b0 = lds32(rec + o.boff), b1 = lds32(rec + o.boff + 16);
+                if (!o.vB) b0 = b1 = 0u;
+                const float s = o.vC ? ldsf(rec + o.soff) : 0.0f;
+                int ls0 = 0, ls1 = 0;
+                if (TT == BREW_TYPE_Q4_0) {   // Q4_0 quants are stored as q + 8
+                    ls0 = o.vC ? 8 * (int)lds32(rec + o.loff0) : 0;
+                    ls1 = (o.vC && o.l0 == 0) ? 8 * (int)lds32(rec + o.loff1) : 0;
+                }
+#pragma unroll
+                for (int k = 0; k < NG; ++k) {
+                    const uint32_t blk = sb + (k * geo.KC + kb) * BS;
+                    int c[4];
+                    if (TT == BREW_TYPE_Q8_0) {
+                        const uint4 A = *reinterpret_cast<const uint4*>(sptr(blk + lane * 16));
+                        mma_s8s8(c, A.x, A.y, A.z, A.w, b0, b1);
+                    } else {
+                        const uint2 W = *reinterpret_cast<const uint2*>(sptr(blk + lane * 8));
+                        mma_u8s8(c, W.x & 0x0F0F0F0Fu, W.y & 0x0F0F0F0Fu, (W.x >> 4) & 0x0F0F0F0Fu,
+                                 (W.y >> 4) & 0x0F0F0F0Fu, b0, b1);
+                        c[0] -= ls0;
+                        c[1] -= ls1;
+                        c[2] -= ls0;
+                        c[3] -= ls1;
+                    }
+                    const uint32_t dd = lds32(blk + SO + 4 * g);
+                    const float ds0 = h2f_lo(dd) * s, ds1 = h2f_hi(dd) * s;
+                    acc[k][0] = fmaf((float)c[0], ds0, acc[k][0]);
+                    acc[k][1] = fmaf((float)c[1], ds0, acc[k][1]);
+                    acc[k][2] = fmaf((float)c[2], ds1, acc[k][2]);
+                    acc[k][3] = fmaf((float)c[3], ds1, acc[k][3]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ring.empty[stage]);
+        if (detail && tid == 0 && dch < DK_DETAIL) detail[2 * DK_DETAIL + dch] = global_ns();
+        ++dch;
+    }
+    // limbs hi / mid (lane t even) and lo (lane t + 1) -> one value per row
+    // and vector: v = (lo + mid * 2^8) + hi * 2^16
+#pragma unroll
+    for (int k = 0; k < NG; ++k) {
+        const float lo0 = __shfl_down_sync(0xffffffffu, acc[k][0], 1);
+        const float lo1 = __shfl_down_sync(0xffffffffu, acc[k][2], 1);
+        if ((t & 1) == 0 && o.vC) {
+            red[((warp * 8 + k) * 16 + g) * 2 + o.bC] = (lo0 + acc[k][1] * 256.0f) + acc[k][0] * 65536.0f;
+            red[((warp * 8 + k) * 16 + g + 8) * 2 + o.bC] = (lo1 + acc[k][3] * 256.0f) + acc[k][2] * 65536.0f;
+        }
+    }
+}
+
 // Consumer side of one matvec phase: this CTA's tiles in groups of up to 8,
 // stage by stage.  Warp w multiplies block columns w, w + 8, ... of the stage
 // for every tile of the group (the x operand of a column is loaded once and
@@ -328,8 +412,8 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
                          unsigned long long* detail) {
     int dch = 0;
     static_assert(NT == 1, "decode batch <= 2: one n8 column tile");
-    constexpr int BS = pk_block_bytes(TT), SO = pk_scale_off(TT);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int BS = pk_block_bytes(TT);
+    const int tid = threadIdx.x, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
     const int t0 = (int)((int64_t)blockIdx.x * f.tiles / G);
@@ -337,26 +421,27 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
     const int nt = t1 - t0;
     if (nt <= 0) return;
     const int batch = P.batch;
-    const PGeom geo = pk_geom(nt, f.KB, BS, ring.stage_bytes);
-    const int ngroups = (nt + geo.gs - 1) / geo.gs;
+    const int gs = pk_gs(P, f.ph, nt);
+    const int ngroups = (nt + gs - 1) / gs;
     const bool glu = f.epi != MV_EPI_STORE;
     const int per_tile = (glu ? 8 : 16) * batch;
-    // x-operand offsets inside a prep record for this lane (prep.cuh):
-    // B column g = limb (g & 3) of vector g >> 2; accumulator columns 2t, 2t+1
-    // belong to vector t >> 1 (limbs (2t) & 3 and (2t + 1) & 3)
-    const int bB = g >> 2, lB = g & 3;
-    const bool vB = lB < 3 && bB < batch;
-    const uint32_t boff = (vB ? (3 * bB + lB) * 32 : 0) + 4 * t;
-    const int bC = t >> 1;
-    const bool vC = bC < batch;
-    const int bCs = vC ? bC : 0;
-    const int l0 = (2 * t) & 3;
-    const uint32_t soff = prep_s_off(batch) + 4 * bCs;
-    const uint32_t loff0 = prep_lsum_off(batch) + 4 * (3 * bCs + l0);
-    const uint32_t loff1 = prep_lsum_off(batch) + 4 * (3 * bCs + 1);
+    LaneOps o;
+    {
+        const int bB = g >> 2, lB = g & 3;
+        o.vB = lB < 3 && bB < batch;
+        o.boff = (o.vB ? (3 * bB + lB) * 32 : 0) + 4 * t;
+        o.bC = t >> 1;
+        o.vC = o.bC < batch;
+        const int bCs = o.vC ? o.bC : 0;
+        o.l0 = (2 * t) & 3;
+        o.soff = prep_s_off(batch) + 4 * bCs;
+        o.loff0 = prep_lsum_off(batch) + 4 * (3 * bCs + o.l0);
+        o.loff1 = prep_lsum_off(batch) + 4 * (3 * bCs + 1);
+    }
     for (int grp = 0; grp < ngroups; ++grp) {
-        const int tg0 = t0 + grp * geo.gs;
-        const int ng = min(geo.gs, t1 - tg0);
+        const int tg0 = t0 + grp * gs;
+        const int ng = min(gs, t1 - tg0);
+        const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
         // this thread's output of the group: its bias and residual are read
         // now, so that their latency overlaps the MMA loop
         const int ok = tid / per_tile, orem = tid % per_tile;
@@ -370,77 +455,15 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
                 if (f.resid) pr = __ldcg(&f.resid[(int64_t)ob * f.ldy + row]);
             }
         }
-        float acc[8][4];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
-        for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
-            const int stage = q % ring.ns;
-            if (!aborted && !mbar_wait_bounded(&ring.full[stage], (q / ring.ns) & 1, P.err, BREW_DEVERR_TIMEOUT_FULL))
-                aborted = true;
-            if (t_full && warp == 0) *t_full = global_ns();
-            if (detail && tid == 0 && dch < DK_DETAIL) detail[DK_DETAIL + dch] = global_ns();
-            if (!aborted) {
-                const uint32_t sb = smem_u32(ring.stages + (size_t)stage * ring.stage_bytes);
-                for (int kb = warp; kb < geo.KC; kb += 8) {
-                    const uint32_t rec = prep_s + (chunk * geo.KC + kb) * P.rec_bytes;
-                    uint32_t b0 = lds32(rec + boff), b1 = lds32(rec + boff + 16);
-                    if (!vB) b0 = b1 = 0u;
-                    const float s = vC ? ldsf(rec + soff) : 0.0f;
-                    int ls0 = 0, ls1 = 0;
-                    if (TT == BREW_TYPE_Q4_0) {   // Q4_0 quants are stored as q + 8
-                        ls0 = vC ? 8 * (int)lds32(rec + loff0) : 0;
-                        ls1 = (vC && l0 == 0) ? 8 * (int)lds32(rec + loff1) : 0;
-                    }
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        if (k < ng) {
-                            const uint32_t blk = sb + (k * geo.KC + kb) * BS;
-                            uint32_t a0, a1, a2, a3;
-                            int c[4];
-                            if (TT == BREW_TYPE_Q8_0) {
-                                const uint4 A = *reinterpret_cast<const uint4*>(sptr(blk + lane * 16));
-                                a0 = A.x;
-                                a1 = A.y;
-                                a2 = A.z;
-                                a3 = A.w;
-                                mma_s8s8(c, a0, a1, a2, a3, b0, b1);
-                            } else {
-                                const uint2 W = *reinterpret_cast<const uint2*>(sptr(blk + lane * 8));
-                                a0 = W.x & 0x0F0F0F0Fu;
-                                a1 = W.y & 0x0F0F0F0Fu;
-                                a2 = (W.x >> 4) & 0x0F0F0F0Fu;
-                                a3 = (W.y >> 4) & 0x0F0F0F0Fu;
-                                mma_u8s8(c, a0, a1, a2, a3, b0, b1);
-                                c[0] -= ls0;
-                                c[1] -= ls1;
-                                c[2] -= ls0;
-                                c[3] -= ls1;
-                            }
-                            const uint32_t dd = lds32(blk + SO + 4 * g);
-                            const float ds0 = h2f_lo(dd) * s, ds1 = h2f_hi(dd) * s;
-                            acc[k][0] = fmaf((float)c[0], ds0, acc[k][0]);
-                            acc[k][1] = fmaf((float)c[1], ds0, acc[k][1]);
-                            acc[k][2] = fmaf((float)c[2], ds1, acc[k][2]);
-                            acc[k][3] = fmaf((float)c[3], ds1, acc[k][3]);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ring.empty[stage]);
-            if (detail && tid == 0 && dch < DK_DETAIL) detail[2 * DK_DETAIL + dch] = global_ns();
-            ++dch;
-        }
-        // limbs hi / mid (lane t even) and lo (lane t + 1) -> one value per
-        // row and vector: v = (lo + mid * 2^8) + hi * 2^16
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float lo0 = __shfl_down_sync(0xffffffffu, acc[k][0], 1);
-            const float lo1 = __shfl_down_sync(0xffffffffu, acc[k][2], 1);
-            if (k < ng && (t & 1) == 0 && bC < batch) {
-                red[((warp * 8 + k) * 16 + g) * 2 + bC] = (lo0 + acc[k][1] * 256.0f) + acc[k][0] * 65536.0f;
-                red[((warp * 8 + k) * 16 + g + 8) * 2 + bC] = (lo1 + acc[k][3] * 256.0f) + acc[k][2] * 65536.0f;
-            }
+        switch (ng) {
+            case 1: mv_group<TT, 1>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 2: mv_group<TT, 2>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 3: mv_group<TT, 3>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 4: mv_group<TT, 4>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 5: mv_group<TT, 5>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 6: mv_group<TT, 6>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 7: mv_group<TT, 7>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            default: mv_group<TT, 8>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
         }
         consumer_bar();
         if (ok < ng) {
@@ -484,12 +507,13 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
     const int t1 = (int)((int64_t)(blockIdx.x + 1) * f.tiles / G);
     const int nt = t1 - t0;
     if (nt <= 0) return;
-    const PGeom geo = pk_geom(nt, f.KB, BS, ring.stage_bytes);
-    const int ngroups = (nt + geo.gs - 1) / geo.gs;
-    const uint32_t cbytes = (uint32_t)geo.KC * BS;
+    const int gs = pk_gs(P, f.ph, nt);
+    const int ngroups = (nt + gs - 1) / gs;
     for (int grp = 0; grp < ngroups; ++grp) {
-        const int tg0 = t0 + grp * geo.gs;
-        const int ng = min(geo.gs, t1 - tg0);
+        const int tg0 = t0 + grp * gs;
+        const int ng = min(gs, t1 - tg0);
+        const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
+        const uint32_t cbytes = (uint32_t)geo.KC * BS;
         for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
             const int stage = q % ring.ns;
             if (q >= ring.ns) {
@@ -1078,6 +1102,40 @@ int decode_prepare(DecodeParams* p) {
     BREW_CHECK(fixed + 2 * (size_t)p->stage_bytes <= budget, BREW_ERR_UNSUPPORTED, "decode kernel: shapes too large");
     p->nstages = (int)std::min<size_t>(32, (budget - fixed) / p->stage_bytes);
     p->smem = fixed + (size_t)p->nstages * p->stage_bytes;
+    // stage geometry per phase: for a group of ng tiles the widest KC (a
+    // multiple of 8 dividing KB) whose ng * KC blocks fit a stage; for a CTA
+    // of nt tiles the group size (<= 8) whose stages carry the most bytes
+    // (ties: the larger group, whose x operand is loaded once for more tiles)
+    const int phase_kb[5] = {p->dim / 32, qw / 32, p->dim / 32, p->hidden / 32, p->dim / 32};
+    for (int ph = 0; ph < 5; ++ph) {
+        const int KB = phase_kb[ph];
+        const int bs = pk_block_bytes(ph == PH_CLS ? p->type_out : p->type_layer);
+        BREW_CHECK(KB % 8 == 0, BREW_ERR_UNSUPPORTED, "decode kernel: %d block columns", KB);
+        int kc[9] = {0};
+        for (int ng = 1; ng <= 8; ++ng) {
+            const int cap = std::min(KB, p->stage_bytes / (ng * bs));
+            kc[ng] = 8;
+            for (int c = (cap / 8) * 8; c >= 8; c -= 8)
+                if (KB % c == 0) {
+                    kc[ng] = c;
+                    break;
+                }
+            BREW_CHECK(ng * kc[ng] * bs <= p->stage_bytes && kc[ng] < 32768, BREW_ERR_UNSUPPORTED,
+                       "decode kernel: stage geometry");
+            p->geo_kc[ph][ng] = (int16_t)kc[ng];
+        }
+        p->geo_kc[ph][0] = 8;
+        p->geo_gs[ph][0] = 1;
+        for (int nt = 1; nt <= 9; ++nt) {
+            int best = 1, fill = 0;
+            for (int gs = std::min(8, nt); gs >= 1; --gs)
+                if (gs * kc[gs] * bs > fill) {
+                    fill = gs * kc[gs] * bs;
+                    best = gs;
+                }
+            p->geo_gs[ph][nt] = (int8_t)best;
+        }
+    }
     int dev = 0, coop = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);

@@ -52,6 +52,11 @@ struct alignas(64) DecodeParams {
     // launch geometry
     int nstages, stage_bytes, vec_bytes, prep_bytes, rec_bytes, grid;
     size_t smem;
+    // stage geometry per matvec phase (PH_QKV .. PH_CLS): tiles per group
+    // for a CTA owning nt tiles (index min(nt, 9)), and block columns per
+    // stage for a group of ng tiles (index ng <= 8)
+    int8_t geo_gs[5][10];
+    int16_t geo_kc[5][9];
 };
 
 // True when the model can run on the persistent decode kernel.
