@@ -39,7 +39,7 @@ namespace brew {
 
 namespace {
 
-enum { PH_QKV = 0, PH_O, PH_GU, PH_DOWN, PH_CLS };
+enum { PH_QKV = 0, PH_O, PH_GU, PH_DOWN, PH_CLS, PH_ATTN };
 
 constexpr int ATTN_MIN_POS = 32;   // positions per attention CTA at least
 // dynamic shared memory of the decode kernel, at most: 226 KB of the 227 KB a
@@ -218,10 +218,11 @@ __device__ __forceinline__ float sumsq4(const float4* v, int n4) {
 // in shared memory (`vec`, K floats) and the norm weight beside it (K more
 // floats).  xout writes are split over the CTAs by block (block j by CTA
 // j % G), so each element has one writer.  `lsum`: the consumer multiplies
-// Q4_0 blocks (needs the limb sums).
+// Q4_0 blocks (needs the limb sums).  `nw_staged` (SRC_PLAIN): this thread
+// already issued the copy of nw into the weight half of `vec` (stage_norm).
 __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, int ld, int K, const float* nw,
                            const float* t, const float* tw, float* xout, uint8_t* prep, float* vec, float* red,
-                           bool lsum, unsigned long long* t_wave) {
+                           bool lsum, unsigned long long* t_wave, bool nw_staged = false) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int KB = K / 32, K4 = K / 4;
     const int G = gridDim.x;
@@ -258,7 +259,8 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             cp_async_wait_all();
             for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
         } else {
-            stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4, nw ? nw4 : nullptr, K4);
+            stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4,
+                        (nw && !(nw_staged && b == 0)) ? nw4 : nullptr, K4);
             cp_async_wait_all();
             // each thread reads back only the float4 it copied itself
             if (nw) ss = sumsq4(v4, K4);
@@ -590,18 +592,67 @@ __device__ __forceinline__ RopeRegs load_rope(const DecodeParams& P) {
     return r;
 }
 
-__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave, const RopeRegs& rope) {
+// One attention item: sequence b, kv head hk, chunk c of the positions
+// start .. pos (Gemma3's local layers: the last `window` positions), split
+// into chunks of `per` positions; `used` chunks are non-empty.
+struct AttnItem {
+    int c, hk, b, pos, p0, n, used;
+};
+
+// This step's position of each sequence, read from P.pos once at kernel start.
+__shared__ int s_pos[DK_MAX_BATCH];
+
+__device__ __forceinline__ bool attn_item(const DecodeParams& P, int l, int item, AttnItem& it) {
+    const int nch = P.nchunk;
+    const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
+    const int window = (P.arch == BREW_ARCH_GEMMA3 && !global) ? P.window : 0;
+    it.c = item % nch;
+    it.hk = (item / nch) % P.n_kv;
+    it.b = item / (nch * P.n_kv);
+    it.pos = s_pos[it.b];
+    if (it.pos < 0 || it.pos >= P.seq_len) return false;
+    const int start = window > 0 ? max(0, it.pos - window + 1) : 0;
+    const int len = it.pos - start + 1;
+    const int per = max(ATTN_MIN_POS, (len + nch - 1) / nch);
+    it.used = (len + per - 1) / per;
+    it.p0 = start + it.c * per;
+    it.n = max(0, min(it.pos + 1, it.p0 + per) - it.p0);
+    return true;
+}
+
+// Asynchronous copies of the cached K / V rows of positions p0 + r0 ..
+// p0 + r0 + SUB - 1 of an item into shared memory (kb, vb: [SUB][hd]); the
+// row of this step's position is skipped (it comes from this step's k / v).
+__device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, const AttnItem& it, int r0, float* kb,
+                                              float* vb) {
+    const int hd = P.hd, hd4 = hd / 4, kvd = P.n_kv * hd;
+    const int ns = min(attn_sub(hd), it.n - r0);
+    const float* kc = P.kc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
+    const float* vc = P.vc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
+    for (int i = threadIdx.x; i < ns * hd4; i += 256) {
+        const int r = i / hd4, ci = i % hd4;
+        const int p = it.p0 + r0 + r;
+        if (p == it.pos) continue;
+        const int64_t off = (int64_t)p * kvd + (int64_t)it.hk * hd + 4 * ci;
+        cp_async16(kb + r * hd + 4 * ci, kc + off);
+        cp_async16(vb + r * hd + 4 * ci, vc + off);
+    }
+}
+
+__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave, const RopeRegs& rope,
+                           unsigned long long* detail) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool gem = P.arch == BREW_ARCH_GEMMA3;
     const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
-    const int window = (gem && !global) ? P.window : 0;
     const int table = (gem && !global) ? 1 : 0;
     const bool inter = P.arch == BREW_ARCH_LLAMA;
     const int nch = P.nchunk;
     const int SUB = attn_sub(hd);
     const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
+    int tpp = 1;                 // lanes per (position, head) score (power of two <= 8)
+    while (tpp < 8 && 2 * tpp * G * SUB <= 256) tpp *= 2;
     float* kb = sm;
     float* vb = kb + SUB * hd;
     float* qs = vb + SUB * hd;
@@ -612,20 +663,22 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     float* sc = wk + hd;
     float* st = sc + G * SUB;
     __shared__ int s_last;
+    // detail trace (first item of the CTA): 0 start, 1 wave landed, 2 head
+    // norm, 3 RoPE, 4 rounds done, 5 arrival counted, 6 partials landed
+    // (combining CTA), 7 combine done, 8 phase end
+    unsigned long long* const det0 = detail;
+    auto stamp = [&](int k) {
+        if (detail && tid == 0) detail[k] = global_ns();
+    };
+    stamp(0);
     const int items = P.batch * P.n_kv * nch;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int c = item % nch, hk = (item / nch) % P.n_kv, b = item / (nch * P.n_kv);
-        const int pos = P.pos[b];
-        if (pos < 0 || pos >= P.seq_len) {
+        AttnItem it;
+        if (!attn_item(P, l, item, it)) {
             if (tid == 0) atomicOr(P.err, BREW_DEVERR_BAD_INDEX);
             continue;
         }
-        const int start = window > 0 ? max(0, pos - window + 1) : 0;
-        const int len = pos - start + 1;
-        const int per = max(ATTN_MIN_POS, (len + nch - 1) / nch);
-        const int used = (len + per - 1) / per;
-        const int p0 = start + c * per;
-        const int n = max(0, min(pos + 1, p0 + per) - p0);
+        const int c = it.c, hk = it.hk, b = it.b, pos = it.pos, used = it.used, p0 = it.p0, n = it.n;
         float* pbase = P.attn_part + ((int64_t)b * P.n_heads + (int64_t)hk * G) * nch * stride;
         float* kc = P.kc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
         float* vc = P.vc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
@@ -633,19 +686,6 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             const float* qsrc = P.qkv + (int64_t)b * ldq + (int64_t)hk * G * hd;
             const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
             const float* vsrc = ksrc + kvd;
-            // K / V rows of positions r0 .. r0 + SUB - 1 of the chunk; the row
-            // of this step's position comes from k / v instead (not yet cached)
-            auto issue_round = [&](int r0) {
-                const int ns = min(SUB, n - r0);
-                for (int i = tid; i < ns * hd4; i += 256) {
-                    const int r = i / hd4, ci = i % hd4;
-                    const int p = p0 + r0 + r;
-                    if (p == pos) continue;
-                    const int64_t off = (int64_t)p * kvd + (int64_t)hk * hd + 4 * ci;
-                    cp_async16(kb + r * hd + 4 * ci, kc + off);
-                    cp_async16(vb + r * hd + 4 * ci, vc + off);
-                }
-            };
             for (int i = tid; i < G * hd4; i += 256) cp_async16(qs + 4 * i, qsrc + 4 * i);
             for (int i = tid; i < hd4; i += 256) {
                 cp_async16(ks + 4 * i, ksrc + 4 * i);
@@ -655,7 +695,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     cp_async16(wk + 4 * i, P.rms_k + (int64_t)l * hd + 4 * i);
                 }
             }
-            issue_round(0);
+            attn_issue_kv(P, l, it, 0, kb, vb);
             if (tid < G) {
                 st[4 * tid + 0] = -INFINITY;
                 st[4 * tid + 1] = 0.0f;
@@ -663,6 +703,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             cp_async_wait_all();
             consumer_bar();
             if (t_wave) *t_wave = global_ns();
+            stamp(1);
             if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
                 for (int hh = warp; hh <= G; hh += 8) {
                     float* vecp = hh < G ? qs + hh * hd : ks;
@@ -675,6 +716,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 }
                 consumer_bar();
             }
+            stamp(2);
             for (int idx = tid; idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
                 const int hh = idx / half, d = idx % half;
                 float* vecp = hh < G ? qs + hh * hd : ks;
@@ -685,6 +727,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 vecp[i1] = __fadd_rn(__fmul_rn(a, ss), __fmul_rn(bb, cc));
             }
             consumer_bar();
+            stamp(3);
             const bool has_pos = pos >= p0 && pos < p0 + n;
             if (has_pos) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
                 for (int i = tid; i < hd; i += 256) {
@@ -696,7 +739,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             for (int r0 = 0; r0 < n; r0 += SUB) {
                 const int ns = min(SUB, n - r0);
                 if (r0 > 0) {
-                    issue_round(r0);
+                    attn_issue_kv(P, l, it, r0, kb, vb);
                     cp_async_wait_all();
                 }
                 if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
@@ -707,17 +750,42 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     }
                 }
                 consumer_bar();
-                // scores q.k / sqrt(hd)
-                for (int tt = warp; tt < ns; tt += 8) {
-                    const float* kr = kb + tt * hd;
-                    for (int h = 0; h < G; ++h) {
-                        float s = 0.0f;
-                        for (int i = lane; i < hd; i += 32) s += qs[h * hd + i] * kr[i];
-                        s = warp_sum(s);
-                        if (lane == 0) sc[h * SUB + tt] = s * P.inv_scale;
+                if (r0 == 0) stamp(9);
+                // scores q.k / sqrt(hd): tpp lanes per (position, head) pair,
+                // each summing every tpp-th float4 of the row, then a shuffle
+                // sum over the pair's lanes.  Every lane runs the same number
+                // of iterations (the shuffles need the whole warp).
+                {
+                    const int npair = G * ns, ppi = 256 / tpp;
+                    const int j = tid & (tpp - 1);
+                    for (int p00 = 0; p00 < npair; p00 += ppi) {
+                        const int pr = p00 + tid / tpp;
+                        const int pc = pr < npair ? pr : npair - 1;
+                        const int tt = pc / G, h = pc % G;
+                        const float4* q4 = reinterpret_cast<const float4*>(qs + h * hd);
+                        const float4* k4 = reinterpret_cast<const float4*>(kb + tt * hd);
+                        float s0 = 0.0f, s1 = 0.0f;
+                        for (int m = j; m < hd4; m += 2 * tpp) {
+                            const float4 a = q4[m], kk = k4[m];
+                            s0 = fmaf(a.x, kk.x, s0);
+                            s0 = fmaf(a.y, kk.y, s0);
+                            s0 = fmaf(a.z, kk.z, s0);
+                            s0 = fmaf(a.w, kk.w, s0);
+                            if (m + tpp < hd4) {
+                                const float4 a1 = q4[m + tpp], k1 = k4[m + tpp];
+                                s1 = fmaf(a1.x, k1.x, s1);
+                                s1 = fmaf(a1.y, k1.y, s1);
+                                s1 = fmaf(a1.z, k1.z, s1);
+                                s1 = fmaf(a1.w, k1.w, s1);
+                            }
+                        }
+                        float sv = s0 + s1;
+                        for (int o = tpp >> 1; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+                        if (j == 0 && pr < npair) sc[h * SUB + tt] = sv * P.inv_scale;
                     }
                 }
                 consumer_bar();
+                if (r0 == 0) stamp(10);
                 // running softmax: weights of this round relative to the new maximum
                 for (int h = warp; h < G; h += 8) {
                     float m = -INFINITY;
@@ -740,18 +808,30 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     }
                 }
                 consumer_bar();
+                if (r0 == 0) stamp(11);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int idx = tid + 256 * k;
                     if (idx < G * hd) {
                         const int h = idx / hd, i = idx % hd;
-                        float a = acc[k] * st[4 * h + 2];
-                        for (int tt = 0; tt < ns; ++tt) a += sc[h * SUB + tt] * vb[tt * hd + i];
-                        acc[k] = a;
+                        const float* sh = sc + h * SUB;
+                        const float* vcol = vb + i;
+                        float a0 = acc[k] * st[4 * h + 2], a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                        int tt = 0;
+                        for (; tt + 4 <= ns; tt += 4) {
+                            a0 = fmaf(sh[tt], vcol[tt * hd], a0);
+                            a1 = fmaf(sh[tt + 1], vcol[(tt + 1) * hd], a1);
+                            a2 = fmaf(sh[tt + 2], vcol[(tt + 2) * hd], a2);
+                            a3 = fmaf(sh[tt + 3], vcol[(tt + 3) * hd], a3);
+                        }
+                        for (; tt < ns; ++tt) a0 = fmaf(sh[tt], vcol[tt * hd], a0);
+                        acc[k] = (a0 + a1) + (a2 + a3);
                     }
                 }
                 consumer_bar();
+                if (r0 == 0) stamp(12);
             }
+            stamp(4);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int idx = tid + 256 * k;
@@ -767,16 +847,19 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
         }
         // arrival; the last CTA of (b, hk) combines the used chunks in order.
         // The barrier orders every thread's partial stores before thread 0's
-        // fence, which makes them visible before its arrival is counted.
+        // release, which makes them visible before its arrival is counted.
         consumer_bar();
         int* ctr = &P.attn_ctr[b * P.n_kv + hk];
         if (tid == 0) {
-            __threadfence();
-            s_last = (atomicAdd(ctr, 1) == nch - 1);
+            // release: the CTA's partials before the count; acquire: the
+            // other CTAs' partials before the combine reads them
+            int prev;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+            s_last = (prev == nch - 1);
         }
         consumer_bar();
+        stamp(5);
         if (s_last) {
-            __threadfence();
             const int hpw = max(1, min(G, P.attn_floats / (nch * stride)));
             for (int h0 = 0; h0 < G; h0 += hpw) {
                 const int nh = min(hpw, G - h0);
@@ -785,6 +868,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 for (int i = tid; i < n4; i += 256) cp_async16(sm + 4 * i, src + 4 * i);
                 cp_async_wait_all();
                 consumer_bar();
+                stamp(6);
                 for (int hl = warp; hl < nh; hl += 8) {
                     float* ph = sm + hl * nch * stride;
                     float M = -INFINITY;
@@ -810,9 +894,12 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 consumer_bar();
             }
             if (tid == 0) *ctr = 0;
+            stamp(7);
         }
         consumer_bar();
+        detail = nullptr;   // stamps of the first item only
     }
+    if (det0 && tid == 0) det0[8] = global_ns();
 }
 
 template <int TYPE, int CTYPE, int NT>
@@ -847,6 +934,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         s_base = P.bar[1];
     }
     if (tid < 16) s_best[tid] = 0ull;
+    if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
     __syncthreads();
 
     if (warp == 8) {
@@ -906,6 +994,15 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         mark();
     };
     const RopeRegs rope = load_rope(P);
+    // The next phase's RMSNorm weight is copied into shared memory, beside
+    // the input vector where prep_phase reads it, while this phase
+    // multiplies (issued after this phase's prep, when `vec` is free again;
+    // waited for by the next prep_phase).  Not for Gemma3, whose prep also
+    // stages its post-norm weight there.
+    auto stage_norm = [&](const float* nw) {
+        if (!gem) stage_async(reinterpret_cast<float4*>(vec) + P.dim / 4, reinterpret_cast<const float4*>(nw), nullptr,
+                              nullptr, P.dim / 4);
+    };
     for (int l = 0; l < L && !aborted; ++l) {
         // the small vectors of the next phase go to L2 one phase ahead (HBM
         // misses otherwise; fetched earlier they would be evicted again by
@@ -924,7 +1021,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l, tr ? &twave : nullptr);
+                       vec, s_red, lsum_l, tr ? &twave : nullptr, true);
         }
         mark_prep();
         {
@@ -935,7 +1032,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- attention ----
-        attn_phase(P, l, vec, tr ? &twave : nullptr, rope);
+        attn_phase(P, l, vec, tr ? &twave : nullptr, rope, det(l, PH_ATTN));
         markv(twave);   // the first load wave landed
         twave = 0;
         markv(0);
@@ -943,9 +1040,9 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- wo (+ residual) ----
-        pf(P.rms_ffn + (int64_t)l * P.dim, P.dim);
         prep_phase(P, SRC_PLAIN, P.xb, P.n_heads * P.hd, P.n_heads * P.hd, nullptr, nullptr, nullptr, nullptr, prep,
                    vec, s_red, lsum_l, tr ? &twave : nullptr);
+        stage_norm(P.rms_ffn + (int64_t)l * P.dim);
         mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_O, xcur);
@@ -961,7 +1058,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
             float* tmp = xcur; xcur = xalt; xalt = tmp;
         } else {
             prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l, tr ? &twave : nullptr);
+                       vec, s_red, lsum_l, tr ? &twave : nullptr, true);
         }
         mark_prep();
         {
@@ -972,8 +1069,8 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         barrier();
         if (aborted) break;
         // ---- down (+ residual) ----
-        pf(l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final, P.dim);
         prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
+        stage_norm(l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final);
         mark_prep();
         {
             const DPhase f = make_phase(P, l, PH_DOWN, xcur);
@@ -988,7 +1085,8 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
             prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_final, P.xb2, P.post_ffn + (int64_t)(L - 1) * P.dim,
                        nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr);
         else
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr);
+            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr,
+                       true);
         mark_prep();
         const DPhase f = make_phase(P, 0, PH_CLS, xcur);
         mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(L, PH_CLS));
