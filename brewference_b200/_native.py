@@ -103,6 +103,7 @@ def lib():
         "brew_comm_init": (I, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
         "brew_comm_free": (I, [V]),
         "brew_model_set_tp": (I, [V, V]),
+        "brew_model_set_prefill": (I, [V, ctypes.c_int32]),
         "brew_matmul_dev_static": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),
         "brew_model_create": (I, [ctypes.POINTER(BrewConfig), ctypes.POINTER(ModelWeights), ctypes.c_int32, c_void_pp]),
         "brew_model_synthesize": (I, [ctypes.POINTER(BrewConfig), ctypes.c_uint64, ctypes.c_int32, c_void_pp]),

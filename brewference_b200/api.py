@@ -32,6 +32,9 @@ def _i32(a):
     return a.ctypes.data_as(N.c_i32p)
 
 
+PREFILL_TOKENS, PREFILL_BATCHED = 0, 1   # brew_model_set_prefill modes
+
+
 class PackedTensor:
     """A weight tensor of GGUF blocks resident in HBM (the device-side Q8Block)."""
 
@@ -262,6 +265,13 @@ class DeviceModel:
 
     def reset(self):
         N.check(N.lib().brew_model_reset(self.handle), "reset")
+
+    def set_prefill(self, mode: int) -> None:
+        """How prefill / generate fill the KV cache with the prompt:
+        PREFILL_TOKENS (token by token, the reference's order) or
+        PREFILL_BATCHED (prompt chunks through each layer together, the
+        matrices on the tcgen05 GEMM)."""
+        N.check(N.lib().brew_model_set_prefill(self.handle, int(mode)), "set_prefill")
 
     def set_tp(self, comm: "Communicator") -> None:
         """Shards this model's matrices by rows over `comm` (every rank holds

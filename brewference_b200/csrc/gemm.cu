@@ -66,14 +66,14 @@ __global__ void gemm_pack_q8_kernel(const uint8_t* w, int N, int K, int8_t* wq, 
     for (int j = 0; j < 32; ++j) q[j] = (int8_t)b[2 + j];
 }
 
-// One warp per (token, block).
-__global__ void gemm_limbs_kernel(const float* x, int T, int K, int8_t* limbs, float* scales) {
+// One warp per (token, block); tokens T .. Tp-1 are zero padding.
+__global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K, int8_t* limbs, float* scales) {
     const int lane = threadIdx.x & 31;
     const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int KB = K / 32;
-    if (wid >= (int64_t)T * KB) return;
+    if (wid >= (int64_t)Tp * KB) return;
     const int t = (int)(wid / KB), kb = (int)(wid % KB);
-    const float v = x[(int64_t)t * K + 32 * kb + lane];
+    const float v = t < T ? x[(int64_t)t * ldx + 32 * kb + lane] : 0.0f;
     const float amax = warp_max(fabsf(v));
     const float inv = amax > 0.0f ? PREP_RANGE / amax : 0.0f;
     const int q = __float2int_rn(v * inv);
@@ -81,11 +81,11 @@ __global__ void gemm_limbs_kernel(const float* x, int T, int K, int8_t* limbs, f
     const int q1 = (q - lo) >> 8;
     const int mid = ((q1 + 128) & 255) - 128;
     const int hi = (q1 - mid) >> 8;
-    int8_t* base = limbs + ((int64_t)kb * 3 * T + 3 * t) * 32;
+    int8_t* base = limbs + ((int64_t)kb * 3 * Tp + 3 * t) * 32;
     base[lane] = (int8_t)hi;
     base[32 + lane] = (int8_t)mid;
     base[64 + lane] = (int8_t)lo;
-    if (lane == 0) scales[(int64_t)kb * T + t] = amax / PREP_RANGE;
+    if (lane == 0) scales[(int64_t)kb * Tp + t] = amax / PREP_RANGE;
 }
 
 // CTA = 128 weight rows x 32 tokens, 4 warps; thread i owns tensor-memory
@@ -199,9 +199,12 @@ int gemm_pack_q8_launch(const uint8_t* w, int N, int K, int8_t* wq, uint16_t* wd
     return BREW_OK;
 }
 
-int gemm_limbs_launch(const float* x, int T, int K, int8_t* limbs, float* scales, cudaStream_t stream) {
-    const int64_t warps = (int64_t)T * (K / 32);
-    gemm_limbs_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(x, T, K, limbs, scales);
+int gemm_limbs_launch(const float* x, int ldx, int T, int Tp, int K, int8_t* limbs, float* scales,
+                      cudaStream_t stream) {
+    BREW_CHECK(T >= 0 && Tp >= T && K % 32 == 0, BREW_ERR_INVALID_ARG, "gemm limbs: T=%d Tp=%d K=%d", T, Tp, K);
+    const int64_t warps = (int64_t)Tp * (K / 32);
+    if (warps == 0) return BREW_OK;
+    gemm_limbs_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(x, ldx, T, Tp, K, limbs, scales);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;
@@ -248,7 +251,7 @@ extern "C" int brew_gemm_q8_dev(float* y, const float* x, brew_tensor w, int64_t
     BREW_CUDA(cudaMalloc(&limbs, (size_t)KB * 3 * T * 32));
     BREW_CUDA(cudaMalloc(&sc, (size_t)KB * T * 4));
     rc = gemm_pack_q8_launch(w->d + off / 32 * 34, N, K, wq, wd, s);
-    if (!rc) rc = gemm_limbs_launch(x, T, K, limbs, sc, s);
+    if (!rc) rc = gemm_limbs_launch(x, K, T, T, K, limbs, sc, s);
     if (!rc) rc = gemm_q8_launch(wq, wd, limbs, sc, N, K, T, y, ctx().err_word, s);
     cudaStreamSynchronize(s);
     cudaFree(wq);

@@ -21,9 +21,11 @@ constexpr int GEMM_TT = 32;    // tokens per CTA (tcgen05 N = 3 * 32 = 96)
 
 // Q8_0 GGUF rows [N][K/32 blocks of 34 B] -> quants [N][K] + scales [N][K/32].
 int gemm_pack_q8_launch(const uint8_t* w, int N, int K, int8_t* wq, uint16_t* wd, cudaStream_t stream);
-// x [T][K] fp32 -> limbs [K/32][3T][32] int8 + block scales [K/32][T] fp32
-// (the records' arithmetic of prep.cuh, one token per row).
-int gemm_limbs_launch(const float* x, int T, int K, int8_t* limbs, float* scales, cudaStream_t stream);
+// x [T][ldx] fp32 (first K columns) -> limbs [K/32][3Tp][32] int8 + block
+// scales [K/32][Tp] fp32 (the records' arithmetic of prep.cuh, one token per
+// row); tokens T .. Tp-1 are zero.
+int gemm_limbs_launch(const float* x, int ldx, int T, int Tp, int K, int8_t* limbs, float* scales,
+                      cudaStream_t stream);
 // y [T][N] = W x (T a multiple of GEMM_TT, N of GEMM_TM, K of 32).
 int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, const float* scales, int N, int K, int T,
                    float* y, unsigned int* err, cudaStream_t stream);

@@ -18,12 +18,15 @@
 #include "brew_internal.cuh"
 #include "decode.cuh"
 #include "eltwise.cuh"
+#include "gemm.cuh"
+#include "prefill.cuh"
 #include "tp.cuh"
 
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <string>
 #include <vector>
 
 namespace brew {
@@ -97,6 +100,16 @@ struct brew_model_s {
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
     int trace_n = 0;
+    // batched prefill (brew_model_set_prefill): GEMM-layout copies of the
+    // layer matrices and the activations of one prompt chunk
+    int prefill_mode = BREW_PREFILL_TOKENS;
+    bool pf_ready = false;
+    int pf_cap = 0;                         // tokens per chunk (multiple of GEMM_TT)
+    int8_t* pf_wq[4] = {};                  // Q|K|V, wo, gate|up, down: [layer][N][K] quants
+    uint16_t* pf_wd[4] = {};                // [layer][N][K/32] fp16 block scales
+    float *pf_x = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_xb = nullptr, *pf_xb2 = nullptr, *pf_h = nullptr;
+    int8_t* pf_limbs = nullptr;
+    float* pf_lsc = nullptr;
 };
 
 namespace brew {
@@ -659,8 +672,178 @@ int launch_step(brew_model_s* m, const int32_t* tok_src, int pos, int32_t* recor
     return BREW_OK;
 }
 
+// ---- batched prefill (prefill.cuh) ----
+
+constexpr int PF_CHUNK = 512;   // prompt tokens per pass through the layers
+
+bool prefill_supported(const brew_config& c, std::string* why) {
+    const int qw = c.n_heads * c.head_size, kvd = c.n_kv_heads * c.head_size;
+    const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down};
+    for (int t : types)
+        if (t != BREW_TYPE_Q8_0) {
+            *why = "the batched prefill takes Q8_0 layer matrices";
+            return false;
+        }
+    if ((qw + 2 * kvd) % GEMM_TM || c.dim % GEMM_TM || (2 * c.hidden_dim) % GEMM_TM) {
+        *why = "the batched prefill needs q|k|v, dim and 2*hidden_dim rows in multiples of 128";
+        return false;
+    }
+    if (!prefill_shapes_supported(c.n_heads, c.n_kv_heads, c.head_size)) {
+        *why = "the batched prefill takes head size 64, 128 or 256 and at most 32 q heads per kv head";
+        return false;
+    }
+    return true;
+}
+
+// RoPE tables [2][seq_len][hd/2] (0: global / default base, 1: Gemma3 local).
+int ensure_rope_tables(brew_model_s* m) {
+    if (m->rope_cos) return BREW_OK;
+    const brew_config& c = m->c;
+    const int hd = c.head_size, half = hd / 2;
+    int rc;
+    if ((rc = dalloc(m, &m->rope_cos, (size_t)2 * c.seq_len * half))) return rc;
+    if ((rc = dalloc(m, &m->rope_sin, (size_t)2 * c.seq_len * half))) return rc;
+    const bool gem = c.arch == BREW_ARCH_GEMMA3;
+    const float base0 = c.rope_base > 0.0f ? c.rope_base : (c.arch == BREW_ARCH_LLAMA ? 10000.0f : 1000000.0f);
+    const float base1 = c.rope_base > 0.0f ? c.rope_base : (gem ? 10000.0f : base0);
+    const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
+    return rope_tables_launch(m->rope_cos, m->rope_sin, c.seq_len, hd, base0, base1, scale, ctx().stream);
+}
+
+// GEMM-layout copies of every layer's matrices (Q|K|V and gate|up each
+// concatenated by rows) and the buffers of one chunk.
+int setup_prefill(brew_model_s* m) {
+    if (m->pf_ready) return BREW_OK;
+    const brew_config& c = m->c;
+    const int L = c.n_layers, dim = c.dim, hid = c.hidden_dim;
+    const int qw = c.n_heads * c.head_size, kvd = c.n_kv_heads * c.head_size, qkvw = qw + 2 * kvd;
+    int rc;
+    if ((rc = ensure_rope_tables(m))) return rc;
+    const int N[4] = {qkvw, dim, 2 * hid, dim}, K[4] = {dim, qw, dim, hid};
+    for (int f = 0; f < 4; ++f) {
+        if ((rc = dalloc(m, &m->pf_wq[f], (size_t)L * N[f] * K[f]))) return rc;
+        if ((rc = dalloc(m, &m->pf_wd[f], (size_t)L * N[f] * (K[f] / 32)))) return rc;
+    }
+    cudaStream_t s = ctx().stream;
+    // one GGUF matrix (rows x cols) of layer l into rows [row0, row0 + rows) of family f
+    auto pack = [&](int f, int l, int row0, int which, int rows, int cols) {
+        int8_t* wq = m->pf_wq[f] + ((int64_t)l * N[f] + row0) * K[f];
+        uint16_t* wd = m->pf_wd[f] + ((int64_t)l * N[f] + row0) * (K[f] / 32);
+        return gemm_pack_q8_launch(layer_ptr(m->t[which], l, rows, cols), rows, cols, wq, wd, s);
+    };
+    for (int l = 0; l < L; ++l) {
+        if ((rc = pack(0, l, 0, T_Q, qw, dim)) || (rc = pack(0, l, qw, T_K, kvd, dim)) ||
+            (rc = pack(0, l, qw + kvd, T_V, kvd, dim)) || (rc = pack(1, l, 0, T_O, dim, qw)) ||
+            (rc = pack(2, l, 0, T_GATE, hid, dim)) || (rc = pack(2, l, hid, T_UP, hid, dim)) ||
+            (rc = pack(3, l, 0, T_DOWN, dim, hid)))
+            return rc;
+    }
+    const int cap = std::min(PF_CHUNK, (c.seq_len + GEMM_TT - 1) / GEMM_TT * GEMM_TT);
+    const int kmax = std::max(std::max(dim, qw), hid);
+    if ((rc = dalloc(m, &m->pf_x, (size_t)cap * dim)) || (rc = dalloc(m, &m->pf_xn, (size_t)cap * dim)) ||
+        (rc = dalloc(m, &m->pf_qkv, (size_t)cap * qkvw)) || (rc = dalloc(m, &m->pf_xb, (size_t)cap * qw)) ||
+        (rc = dalloc(m, &m->pf_xb2, (size_t)cap * dim)) || (rc = dalloc(m, &m->pf_h, (size_t)cap * 2 * hid)) ||
+        (rc = dalloc(m, &m->pf_limbs, (size_t)(kmax / 32) * 3 * cap * 32)) ||
+        (rc = dalloc(m, &m->pf_lsc, (size_t)(kmax / 32) * cap)))
+        return rc;
+    BREW_CUDA(cudaStreamSynchronize(s));
+    m->pf_cap = cap;
+    m->pf_ready = true;
+    return BREW_OK;
+}
+
+// The prompt tokens tok_d[0 .. n) at positions 0 .. n-1 through every layer,
+// in chunks of pf_cap tokens: the K / V cache rows of sequence 0 (the
+// prompt's logits are not computed; the last layer stops after attention).
+// Per layer, the op order of the reference's forward methods
+// (model/*/...Transformer.java), each step over the chunk's rows.
+int prefill_batched(brew_model_s* m, const int32_t* tok_d, int n, cudaStream_t s) {
+    const brew_config& c = m->c;
+    const int L = c.n_layers, dim = c.dim, hid = c.hidden_dim, hd = c.head_size;
+    const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd, qkvw = qw + 2 * kvd;
+    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
+    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    unsigned int* err = ctx().err_word;
+    const int N[4] = {qkvw, dim, 2 * hid, dim}, K[4] = {dim, qw, dim, hid};
+    int rc;
+    for (int c0 = 0; c0 < n; c0 += m->pf_cap) {
+        const int T = std::min(m->pf_cap, n - c0), Tp = (T + GEMM_TT - 1) / GEMM_TT * GEMM_TT;
+        // y [Tp][N[f]] = W_f(layer l) x, x [T][ldx]
+        auto gemm = [&](int f, int l, const float* x, int ldx, float* y) {
+            int r = gemm_limbs_launch(x, ldx, T, Tp, K[f], m->pf_limbs, m->pf_lsc, s);
+            if (!r)
+                r = gemm_q8_launch(m->pf_wq[f] + (int64_t)l * N[f] * K[f], m->pf_wd[f] + (int64_t)l * N[f] * (K[f] / 32),
+                                   m->pf_limbs, m->pf_lsc, N[f], K[f], Tp, y, err, s);
+            return r;
+        };
+        if ((rc = prefill_embed_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, tok_d + c0, T, gemma, m->pf_x,
+                                       err, s)))
+            return rc;
+        for (int l = 0; l < L; ++l) {
+            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
+            if ((rc = rmsnorm_launch(m->pf_x, dim, m->rms_att + (int64_t)l * dim, c.eps, dim, T, m->pf_xn, dim, s)) ||
+                (rc = gemm(0, l, m->pf_xn, dim, m->pf_qkv)))
+                return rc;
+            if (m->q_bias &&
+                ((rc = add_bias_launch(m->pf_qkv, qkvw, m->q_bias + (int64_t)l * qw, qw, T, s)) ||
+                 (rc = add_bias_launch(m->pf_qkv + qw, qkvw, m->k_bias + (int64_t)l * kvd, kvd, T, s)) ||
+                 (rc = add_bias_launch(m->pf_qkv + qw + kvd, qkvw, m->v_bias + (int64_t)l * kvd, kvd, T, s))))
+                return rc;
+            float* kcache = m->kc + (int64_t)l * c.seq_len * kvd;
+            float* vcache = m->vc + (int64_t)l * c.seq_len * kvd;
+            PfQkParams qk = {};
+            qk.T = T;
+            qk.pos0 = c0;
+            qk.n_heads = c.n_heads;
+            qk.n_kv = c.n_kv_heads;
+            qk.hd = hd;
+            qk.seq_len = c.seq_len;
+            qk.table = (gemma && !global) ? 1 : 0;
+            qk.interleaved = c.arch == BREW_ARCH_LLAMA;
+            qk.eps = c.eps;
+            qk.qkv = m->pf_qkv;
+            qk.ldq = qkvw;
+            qk.qnorm_w = qknorm ? m->rms_q + (int64_t)l * hd : nullptr;
+            qk.knorm_w = qknorm ? m->rms_k + (int64_t)l * hd : nullptr;
+            qk.rope_cos = m->rope_cos;
+            qk.rope_sin = m->rope_sin;
+            qk.kcache = kcache;
+            qk.vcache = vcache;
+            if ((rc = prefill_qk_launch(qk, s))) return rc;
+            PfAttnParams at = {};
+            at.T = T;
+            at.pos0 = c0;
+            at.n_heads = c.n_heads;
+            at.n_kv = c.n_kv_heads;
+            at.hd = hd;
+            at.window = (gemma && !global) ? c.sliding_window : 0;
+            at.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
+            at.q = m->pf_qkv;
+            at.ldq = qkvw;
+            at.kcache = kcache;
+            at.vcache = vcache;
+            at.xb = m->pf_xb;
+            at.ldxb = qw;
+            if ((rc = prefill_attn_launch(at, s))) return rc;
+            if (l == L - 1) break;   // the rest of the last layer feeds only the logits
+            if ((rc = gemm(1, l, m->pf_xb, qw, m->pf_xb2)) ||
+                (rc = residual_launch(m->pf_x, dim, m->pf_xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr,
+                                      c.eps, dim, T, s)) ||
+                (rc = rmsnorm_launch(m->pf_x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, T, m->pf_xn, dim, s)) ||
+                (rc = gemm(2, l, m->pf_xn, dim, m->pf_h)) ||
+                (rc = glu_launch(m->pf_h, m->pf_h, m->pf_h + hid, 2 * hid, hid, T, gemma, s)) ||
+                (rc = gemm(3, l, m->pf_h, 2 * hid, m->pf_xb2)) ||
+                (rc = residual_launch(m->pf_x, dim, m->pf_xb2, dim, gemma ? m->post_ffn + (int64_t)l * dim : nullptr,
+                                      c.eps, dim, T, s)))
+                return rc;
+        }
+    }
+    return BREW_OK;
+}
+
 // GenericModelSession.prefill (runtime/ModelRunner.java:196-206) from a reset
-// session: forward(prompt[i], i) for each prompt token.
+// session: forward(prompt[i], i) for each prompt token (or the same cache
+// state from the batched prefill).
 int session_prefill(brew_model_s* m, const int32_t* prompt, int n_prompt, cudaStream_t s) {
     const brew_config& c = m->c;
     BREW_CHECK(n_prompt >= 0 && (prompt || n_prompt == 0), BREW_ERR_INVALID_ARG, "bad prompt");
@@ -681,9 +864,13 @@ int session_prefill(brew_model_s* m, const int32_t* prompt, int n_prompt, cudaSt
     BREW_CUDA(cudaMemcpyAsync(m->prompt_d, staged.data(), staged.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     BREW_CUDA(cudaStreamSynchronize(s));
     int rc;
-    for (int i = 0; i < n_prompt; ++i) {
-        if ((rc = launch_step(m, m->prompt_d + i, i, nullptr, s))) return rc;
-        if ((rc = launch_forward(m, 1, false, s))) return rc;
+    if (m->prefill_mode == BREW_PREFILL_BATCHED) {
+        if ((rc = prefill_batched(m, m->prompt_d, n_prompt, s))) return rc;
+    } else {
+        for (int i = 0; i < n_prompt; ++i) {
+            if ((rc = launch_step(m, m->prompt_d + i, i, nullptr, s))) return rc;
+            if ((rc = launch_forward(m, 1, false, s))) return rc;
+        }
     }
     m->sess_pos = n_prompt;
     m->sess_pending = n_prompt > 0 ? m->prompt_d + n_prompt - 1 : m->prompt_d + n_prompt;
@@ -970,6 +1157,23 @@ int brew_model_free(brew_model m) {
     return BREW_OK;
 }
 
+int brew_model_set_prefill(brew_model m, int32_t mode) {
+    BREW_CHECK(m, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(mode == BREW_PREFILL_TOKENS || mode == BREW_PREFILL_BATCHED, BREW_ERR_INVALID_ARG, "prefill mode %d",
+               mode);
+    std::lock_guard<std::mutex> lk(api_mutex());
+    int rc = ensure_init();
+    if (rc) return rc;
+    if (mode == BREW_PREFILL_BATCHED) {
+        std::string why;
+        BREW_CHECK(prefill_supported(m->c, &why), BREW_ERR_UNSUPPORTED, "%s", why.c_str());
+        BREW_CHECK(!m->comm, BREW_ERR_UNSUPPORTED, "the batched prefill runs on one GPU (the model is sharded)");
+        if ((rc = setup_prefill(m))) return rc;
+    }
+    m->prefill_mode = mode;
+    return BREW_OK;
+}
+
 int brew_model_set_tp(brew_model m, brew_comm comm) {
     BREW_CHECK(m && comm, BREW_ERR_INVALID_ARG, "null argument");
     BREW_CHECK(!m->comm, BREW_ERR_INVALID_ARG, "the model is already sharded");
@@ -990,6 +1194,7 @@ int brew_model_set_tp(brew_model m, brew_comm comm) {
     m->graphs.clear();
     m->graph_kernels.clear();
     m->use_decode = false;
+    m->prefill_mode = BREW_PREFILL_TOKENS;
     if ((rc = alloc_unfused(m))) return rc;
     const int B = m->max_batch;
     const int slice = std::max(std::max((qw + 2 * kvd) / P, c.dim / P), std::max(c.hidden_dim / P, c.vocab_size / P));

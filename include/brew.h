@@ -289,6 +289,22 @@ BREW_API int brew_session_generate(brew_model m, const int32_t* prompt, int32_t 
  * it synchronises and copies the generated ids there. */
 BREW_API int brew_session_prefill(brew_model m, const int32_t* prompt, int32_t n_prompt, void* stream);
 BREW_API int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out_tokens, void* stream);
+
+/* How brew_session_prefill / brew_session_generate fill the KV cache with
+ * the prompt.  BREW_PREFILL_TOKENS (default): forward(prompt[i], i) token by
+ * token, the reference's order (ModelRunner.java:196-206).
+ * BREW_PREFILL_BATCHED: chunks of up to 512 prompt tokens go through each
+ * layer together, the matrices multiplied on the tcgen05 tensor cores (int8
+ * MMA of the exact Q8_0 block products, fp32 block-scale epilogue).  The
+ * prompt's logits are never read, so the resulting state is the KV cache,
+ * equal to the token-by-token one up to fp32 summation order.  Needs every
+ * layer matrix in Q8_0, one GPU (no tensor parallelism), head size 64 / 128
+ * / 256 and matrix row counts (q|k|v, dim, 2 * hidden_dim) that are
+ * multiples of 128; otherwise BREW_ERR_UNSUPPORTED.  No reference
+ * counterpart: the reference has only the token-by-token prefill. */
+#define BREW_PREFILL_TOKENS 0
+#define BREW_PREFILL_BATCHED 1
+BREW_API int brew_model_set_prefill(brew_model m, int32_t mode);
 /* Kernels in one decode step's CUDA graph (for launch accounting). */
 BREW_API int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n_kernels);
 
