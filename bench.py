@@ -430,7 +430,7 @@ def run_tp(args):
 def run_gpu(args):
     import torch
     from brewference_b200 import _native as N
-    from brewference_b200.api import DeviceModel
+    from brewference_b200.api import PREFILL_BATCHED, DeviceModel
 
     rank, world, dist = dist_init(args.gpus)
     dev = torch.cuda.current_device() if world > 1 else 0
@@ -465,8 +465,13 @@ def run_gpu(args):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     s = stream.cuda_stream
-    dm.prefill(prompt, s)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    dm.prefill(prompt, s)   # token by token, the reference's order (untimed for the decode metric)
+    p1.record(stream)
     dm.decode(args.warmup, s, want_tokens=False)
+    stream.synchronize()
+    prefill_tokens_ms = p0.elapsed_time(p1)
     barrier(dist)
 
     clocks = ClockSampler(dev)
@@ -497,6 +502,26 @@ def run_gpu(args):
     e2e_s = time.perf_counter() - t0
     e2e_s = max_over_ranks(dist, e2e_s)
     e2e = world * e2e_steps / e2e_s
+
+    # the same prompt through the batched prefill (tcgen05 GEMM), after the
+    # decode measurements (it rewrites the session's cache)
+    prefill = {"prompt_tokens": int(args.prompt_len), "token_by_token_ms": prefill_tokens_ms}
+    if not args.no_prefill:
+        t0 = time.perf_counter()
+        dm.set_prefill(PREFILL_BATCHED)
+        setup_ms = 1000.0 * (time.perf_counter() - t0)
+        runs = []
+        for _ in range(4):
+            p0.record(stream)
+            dm.prefill(prompt, s)
+            p1.record(stream)
+            stream.synchronize()
+            runs.append(p0.elapsed_time(p1))
+        bms = float(np.median(runs[1:]))
+        prefill.update({"batched_ms": bms, "batched_setup_ms": setup_ms, "speedup": prefill_tokens_ms / bms,
+                        "batched_tok_per_s": args.prompt_len / (bms / 1000.0),
+                        "kernels": "gemm_q8_kernel (tcgen05.mma kind::i8, TMEM accumulators), prefill_attn_kernel, "
+                                   "prefill_qk_kernel, norms"})
 
     # roofline of the dominant kernel: the persistent decode kernel is one
     # launch per token and carries the whole forward; its algorithmic bytes
@@ -533,6 +558,7 @@ def run_gpu(args):
                      "bytes_per_launch": alg, "weight_bytes": wbytes, "kv_bytes": kvb,
                      "ms_per_launch": ms_max / args.steps},
         "matvec_sweep": sweep,
+        "prefill": prefill,
         "clocks": clk,
         "setup_s": {"synthesize": round(synth_s, 2)},
     }
@@ -562,6 +588,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the matvec sweep")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill timing")
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config over --gpus ranks")
     ap.add_argument("--batch", type=int, default=16, help="concurrent sequences of the --tp workload")

@@ -9,7 +9,6 @@ namespace {
 // ---- tcgen05 helpers (PTX forms as in CUTLASS's sm100 MMA / TMEM atoms) ----
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, K-major, no swizzle: core matrices of
 // 8 rows x 16 bytes (128 contiguous bytes), the two 16-byte K halves of a
@@ -42,28 +41,102 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.st of one 32-bit constant to 16 / 8 columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t c) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1};" ::"r"(taddr),
+        "r"(c)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st8_const(uint32_t taddr, uint32_t c) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(c)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(taddr)
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-constexpr int GEMM_N = 3 * GEMM_TT;       // limb columns per CTA (96)
-constexpr int GEMM_TMEM_COLS = 128;       // power of two >= GEMM_N
-constexpr int GEMM_SMEM = 48 * 1024;      // requested dynamic shared memory: at most 4 CTAs (4 x 128 TMEM columns) per SM
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): each half is an ordinary
+// IEEE fp32 operation with round-to-nearest, two per instruction.
+__device__ __forceinline__ uint64_t f2_pack(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_packf(float lo, float hi) {
+    return f2_pack(__float_as_uint(lo), __float_as_uint(hi));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 
-__global__ void gemm_pack_q8_kernel(const uint8_t* w, int N, int K, int8_t* wq, uint16_t* wd) {
+// The int32 accumulators start at the bits of the float 1.5 * 2^23 instead
+// of 0: the MMA adds the block's limb sum i (|i| <= 2^19) to it, and the
+// result's bits are the float 1.5 * 2^23 + i, exactly (the well-known
+// magic-number conversion).  Subtracting 1.5 * 2^23 gives i as a float.
+constexpr uint32_t GEMM_MAGIC = 0x4B400000u;
+constexpr float GEMM_MAGIC_F = 12582912.0f;
+
+constexpr int GEMM_N = 3 * GEMM_TT;        // limb columns per tile (96)
+constexpr int GEMM_STAGES = 4;             // shared-memory ring
+constexpr int GEMM_A_BYTES = GEMM_TM * 32; // one block column of 128 rows
+constexpr int GEMM_B_BYTES = GEMM_N * 32;  // and of the 96 limb columns
+constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
+constexpr int GEMM_TMEM_COLS = 256;        // two accumulator buffers of 128 columns
+// requested dynamic shared memory: also caps residency at two CTAs per SM,
+// so the CTAs of one SM never ask for more than its 512 tensor-memory columns
+constexpr int GEMM_SMEM = 96 * 1024;
+constexpr int GEMM_EPI_WARPS = 8;          // two per tensor-memory lane quadrant (16 tokens each)
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;   // loader warp, MMA warp, epilogue warps
+
+// Bounded mbarrier wait for the pipeline's short hand-offs: polls without
+// sleeping at first (try_wait itself suspends the thread for a while),
+// then backs off; ~2 s in all before it records `code` and gives up.
+__device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, unsigned int* err, unsigned int code) {
+    for (int i = 0; i < 32; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_bounded(bar, parity, err, code);
+}
+
+// Byte offset of quant j (0..31) of row r (0..127) inside a 4096-byte
+// block-column tile: the K-major core-matrix layout the MMA's shared-memory
+// descriptor reads (8-row groups of 256 B, the two 16-byte K halves 128 B
+// apart), so a stage is one contiguous copy.
+__host__ __device__ __forceinline__ int gemm_tile_off(int r, int j) {
+    return (r >> 3) * 256 + (j >> 4) * 128 + (r & 7) * 16 + (j & 15);
+}
+
+__global__ void gemm_pack_q8_kernel(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0) {
     const int KB = K / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)N * KB) return;
+    if (i >= (int64_t)rows * KB) return;
     const int64_t row = i / KB, kb = i % KB;
     const uint8_t* b = w + (row * KB + kb) * 34;
-    wd[row * KB + kb] = (uint16_t)(b[0] | (b[1] << 8));
-    int8_t* q = wq + row * K + kb * 32;
+    const int64_t grow = row0 + row;
+    wd[kb * ldn + grow] = (uint16_t)(b[0] | (b[1] << 8));
+    int8_t* tile = wq + ((grow / GEMM_TM) * KB + kb) * 4096;
+    const int r = (int)(grow % GEMM_TM);
 #pragma unroll 8
-    for (int j = 0; j < 32; ++j) q[j] = (int8_t)b[2 + j];
+    for (int j = 0; j < 32; ++j) tile[gemm_tile_off(r, j)] = (int8_t)b[2 + j];
 }
 
 // One warp per (token, block); tokens T .. Tp-1 are zero padding.
@@ -81,25 +154,43 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
     const int q1 = (q - lo) >> 8;
     const int mid = ((q1 + 128) & 255) - 128;
     const int hi = (q1 - mid) >> 8;
-    int8_t* base = limbs + ((int64_t)kb * 3 * Tp + 3 * t) * 32;
-    base[lane] = (int8_t)hi;
-    base[32 + lane] = (int8_t)mid;
-    base[64 + lane] = (int8_t)lo;
+    // limb column of (token t, limb l) inside its tile of 32 tokens: token
+    // pairs side by side, 6 (t / 2) + 2 l + (t % 2), so the epilogue reads
+    // both tokens of a pair from adjacent tensor-memory columns
+    int8_t* tile = limbs + (int64_t)kb * 3 * Tp * 32 + (int64_t)(t >> 5) * 3072;
+    const int c0 = 6 * ((t & 31) >> 1) + (t & 1);
+    tile[gemm_tile_off(c0, lane)] = (int8_t)hi;
+    tile[gemm_tile_off(c0 + 2, lane)] = (int8_t)mid;
+    tile[gemm_tile_off(c0 + 4, lane)] = (int8_t)lo;
     if (lane == 0) scales[(int64_t)kb * Tp + t] = amax / PREP_RANGE;
 }
 
-// CTA = 128 weight rows x 32 tokens, 4 warps; thread i owns tensor-memory
-// lane i (= weight row row0 + i) and accumulates its 32 outputs in fp32.
-__global__ void __launch_bounds__(128) gemm_q8_kernel(const int8_t* wq, const uint16_t* wd, const int8_t* limbs,
-                                                      const float* scales, int N, int K, int T, float* y,
-                                                      unsigned int* err) {
+// CTA = 128 weight rows x 32 tokens, warp-specialised:
+//   warp 0      one lane loads block column kb (A: 128 rows x 32 B, B: 96
+//               limb columns x 32 B) into ring stage kb % 4: two bulk copies,
+//               since both are stored in the K-major core-matrix layout
+//               (gemm_tile_off) already; all 4 stages can be in flight;
+//   warp 1      one thread issues tcgen05.mma for block column kb into tensor-
+//               memory buffer kb % 2 (each column needs its own product: the
+//               block scales differ per column) and commits to the stage's
+//               "empty" and the buffer's "full" barriers;
+//   warps 2-9   read the buffer back (warp w owns tensor-memory lanes
+//               32 (w % 4) ..: rows row0 + 32 (w % 4) + lane, and 16 of the
+//               32 tokens), release it as soon as it is in registers, and add
+//               d_row * s_token * ((lo + mid 2^8) + hi 2^16) to fp32
+//               accumulators.
+// So the loads run ahead, and the MMA of column kb + 1 overlaps the
+// epilogue of column kb.
+__global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* wq, const uint16_t* wd,
+                                                               const int8_t* limbs, const float* scales, int N, int K,
+                                                               int T, float* y, unsigned int* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* sa = smem;                                          // A: 128 rows x 32 B (4096 B)
-    uint8_t* sb = smem + 4096;                                   // B: 96 limb columns x 32 B (3072 B)
-    float* ss = reinterpret_cast<float*>(smem + 7168);           // the block's token scales [32]
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + 7296);   // MMA completion
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 7360);  // tensor-memory base address
-    const int tid = threadIdx.x, warp = tid >> 5;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
+    uint64_t* empty = full + GEMM_STAGES;
+    uint64_t* tfull = empty + GEMM_STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * GEMM_TM, t0 = blockIdx.y * GEMM_TT;
     const int KB = K / 32;
     if (warp == 0) {
@@ -109,77 +200,138 @@ __global__ void __launch_bounds__(128) gemm_q8_kernel(const int8_t* wq, const ui
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        mbar_init(mbar, 1);
+        for (int i = 0; i < GEMM_STAGES; ++i) {
+            mbar_init(&full[i], 1);    // the loader's arrive.expect_tx (+ the copies' bytes)
+            mbar_init(&empty[i], 1);   // tcgen05.commit
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);   // tcgen05.commit
+            mbar_init(&tempty[i], GEMM_EPI_WARPS);   // one arrival per epilogue warp
+        }
         fence_mbar_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);   // this warp's 32 lanes
-    const int row = row0 + tid;
-    constexpr uint32_t idesc = umma_idesc_s8(GEMM_TM, GEMM_N);
-    float acc[GEMM_TT];
-#pragma unroll
-    for (int t = 0; t < GEMM_TT; ++t) acc[t] = 0.0f;
-    bool ok = true;
-    for (int kb = 0; kb < KB; ++kb) {
-        // stage the block column: A 256 and B 192 pieces of 16 B, in the
-        // K-major core-matrix layout (row r at (r/8)*256 + half*128 + (r%8)*16)
-        for (int c = tid; c < 2 * GEMM_TM + 2 * GEMM_N; c += 128) {
-            if (c < 2 * GEMM_TM) {
-                const int m = c >> 1, h = c & 1;
-                cp_async16(sa + (m >> 3) * 256 + h * 128 + (m & 7) * 16,
-                           wq + (int64_t)(row0 + m) * K + (int64_t)kb * 32 + h * 16);
-            } else {
-                const int n = (c - 2 * GEMM_TM) >> 1, h = (c - 2 * GEMM_TM) & 1;
-                cp_async16(sb + (n >> 3) * 256 + h * 128 + (n & 7) * 16,
-                           limbs + ((int64_t)kb * 3 * T + 3 * t0 + n) * 32 + h * 16);
+    if (warp == 0) {
+        // ---------------------------------- loader ----------------------------------
+        // two bulk copies per block column: the weight tile and the limb tile
+        // are stored in the shared-memory layout already
+        if (lane == 0) {
+            const int8_t* asrc = wq + (int64_t)blockIdx.x * KB * GEMM_A_BYTES;
+            const int8_t* bsrc = limbs + (int64_t)blockIdx.y * GEMM_B_BYTES;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % GEMM_STAGES;
+                if (!gemm_wait(&empty[s], ((kb / GEMM_STAGES) + 1) & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
+                uint8_t* sa = smem + s * GEMM_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], GEMM_STAGE_BYTES);
+                bulk_g2s(sa, asrc + (int64_t)kb * GEMM_A_BYTES, GEMM_A_BYTES, &full[s]);
+                bulk_g2s(sa + GEMM_A_BYTES, bsrc + (int64_t)kb * 3 * T * 32, GEMM_B_BYTES, &full[s]);
             }
-        }
-        if (tid < GEMM_TT) ss[tid] = scales[(int64_t)kb * T + t0 + tid];
-        const float d = half_bits_to_float(wd[(int64_t)row * KB + kb]);
-        cp_async_wait_all();
-        fence_proxy_async_smem();   // the copies are read by the tensor cores (async proxy)
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            umma_s8(tmem, umma_desc_k(smem_u32(sa), 128, 256), umma_desc_k(smem_u32(sb), 128, 256), idesc, 0u);
-            umma_commit(mbar);
         }
         __syncwarp();
-        if (ok && !mbar_wait_bounded(mbar, kb & 1, err, BREW_DEVERR_TIMEOUT_FULL)) ok = false;
-        ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld is warp-collective
-        tc_fence_after();
-        if (ok) {
-            // columns 3t, 3t+1, 3t+2: limbs hi, mid, lo of token t
-#pragma unroll
-            for (int j = 0; j < GEMM_N / 24; ++j) {
-                uint32_t v0[8], v1[8], v2[8];
-                tmem_ld8(taddr + 24 * j, v0);
-                tmem_ld8(taddr + 24 * j + 8, v1);
-                tmem_ld8(taddr + 24 * j + 16, v2);
-                tmem_ld_wait();
-                uint32_t v[24];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    v[e] = v0[e];
-                    v[8 + e] = v1[e];
-                    v[16 + e] = v2[e];
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int t = 8 * j + u;
-                    const float hi = (float)(int)v[3 * u], mid = (float)(int)v[3 * u + 1], lo = (float)(int)v[3 * u + 2];
-                    acc[t] = fmaf((lo + mid * 256.0f) + hi * 65536.0f, d * ss[t], acc[t]);
-                }
+    } else if (warp == 1) {
+        // ------------------------------------ MMA ------------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_s8(GEMM_TM, GEMM_N);
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % GEMM_STAGES, b = kb & 1;
+                if (!gemm_wait(&full[s], (kb / GEMM_STAGES) & 1, err, BREW_DEVERR_TIMEOUT_FULL)) break;
+                if (!gemm_wait(&tempty[b], (kb >> 1) & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * GEMM_STAGE_BYTES);
+                umma_s8(tmem + b * 128, umma_desc_k(sa, 128, 256), umma_desc_k(sa + GEMM_A_BYTES, 128, 256), idesc,
+                        1u);   // onto the magic-number start value
+                umma_commit(&empty[s]);
+                umma_commit(&tfull[b]);
             }
         }
-        tc_fence_before();
-        __syncthreads();   // tensor memory and the staged tiles are free again
-    }
+        __syncwarp();
+    } else {
+        // ---------------------------------- epilogue ----------------------------------
+        // warp w: tensor-memory lanes 32 (w % 4) .. (rows row0 + 32 (w % 4) +
+        // lane) and tokens 16 hh .. 16 hh + 15 (columns 48 hh .. 48 hh + 47)
+        const int q = warp & 3, hh = (warp - 2) >> 2;
+        const int row = row0 + 32 * q + lane;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + 48 * hh;
+        // both buffers start at the magic value (their first "release")
 #pragma unroll
-    for (int t = 0; t < GEMM_TT; ++t) y[(int64_t)(t0 + t) * N + row] = acc[t];
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) tmem_st16_const(tq + b * 128 + 16 * c, GEMM_MAGIC);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&tempty[0]);
+            mbar_arrive(&tempty[1]);
+        }
+        uint64_t acc[8];   // token pairs (2p, 2p + 1)
+#pragma unroll
+        for (int p = 0; p < 8; ++p) acc[p] = 0ull;
+        const uint64_t negc = f2_packf(-GEMM_MAGIC_F, -GEMM_MAGIC_F);
+        const uint64_t k256 = f2_packf(256.0f, 256.0f), k65536 = f2_packf(65536.0f, 65536.0f);
+        // this column's weight scale and token scales, loaded one column ahead
+        uint16_t dbits = wd[row];
+        float4 sn[4];
+        const float* sbase = scales + t0 + 16 * hh;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) sn[g] = __ldg(reinterpret_cast<const float4*>(sbase) + g);
+        for (int kb = 0; kb < KB; ++kb) {
+            const int b = kb & 1;
+            bool ok = gemm_wait(&tfull[b], (kb >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL);
+            ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld / st are warp-collective
+            if (!ok) break;
+            tc_fence_after();
+            const float d = half_bits_to_float(dbits);
+            const uint64_t d2 = f2_packf(d, d);
+            // two halves of 24 columns (8 tokens): read, reset to the magic
+            // value, and after the second half release the buffer
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const uint32_t ta = tq + b * 128 + 24 * e;
+                uint32_t v[24];
+                tmem_ld8(ta, v);
+                tmem_ld8(ta + 8, v + 8);
+                tmem_ld8(ta + 16, v + 16);
+                tmem_ld_wait();
+                tmem_st16_const(ta, GEMM_MAGIC);
+                tmem_st8_const(ta + 16, GEMM_MAGIC);
+                if (e == 1) {
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                }
+#pragma unroll
+                for (int pp = 0; pp < 4; ++pp) {
+                    // tokens 2p, 2p + 1 of this warp's 16: columns 6 pp + (0, 1) hi,
+                    // (2, 3) mid, (4, 5) lo of this half
+                    const int p = 4 * e + pp;
+                    const float4 sg = sn[p >> 1];
+                    const uint64_t s2 = (p & 1) ? f2_packf(sg.z, sg.w) : f2_packf(sg.x, sg.y);
+                    const uint64_t hi = f2_add(f2_pack(v[6 * pp], v[6 * pp + 1]), negc);
+                    const uint64_t mid = f2_add(f2_pack(v[6 * pp + 2], v[6 * pp + 3]), negc);
+                    const uint64_t lo = f2_add(f2_pack(v[6 * pp + 4], v[6 * pp + 5]), negc);
+                    const uint64_t val = f2_fma(hi, k65536, f2_fma(mid, k256, lo));   // (lo + mid 2^8) + hi 2^16
+                    acc[p] = f2_fma(val, f2_mul(d2, s2), acc[p]);
+                }
+            }
+            if (kb + 1 < KB) {   // the next column's scales, while the next MMA runs
+                dbits = wd[(int64_t)(kb + 1) * N + row];
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                    sn[g] = __ldg(reinterpret_cast<const float4*>(sbase + (int64_t)(kb + 1) * T) + g);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            const float a0 = __uint_as_float((uint32_t)acc[p]), a1 = __uint_as_float((uint32_t)(acc[p] >> 32));
+            y[(int64_t)(t0 + 16 * hh + 2 * p) * N + row] = a0;
+            y[(int64_t)(t0 + 16 * hh + 2 * p + 1) * N + row] = a1;
+        }
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -191,9 +343,10 @@ __global__ void __launch_bounds__(128) gemm_q8_kernel(const int8_t* wq, const ui
 
 }  // namespace
 
-int gemm_pack_q8_launch(const uint8_t* w, int N, int K, int8_t* wq, uint16_t* wd, cudaStream_t stream) {
-    const int64_t n = (int64_t)N * (K / 32);
-    gemm_pack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w, N, K, wq, wd);
+int gemm_pack_q8_launch(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0,
+                        cudaStream_t stream) {
+    const int64_t n = (int64_t)rows * (K / 32);
+    gemm_pack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w, rows, K, wq, wd, ldn, row0);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;
@@ -214,12 +367,15 @@ int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, co
                    float* y, unsigned int* err, cudaStream_t stream) {
     BREW_CHECK(N % GEMM_TM == 0 && T % GEMM_TT == 0 && K % 32 == 0 && K > 0, BREW_ERR_INVALID_ARG,
                "gemm: N=%d (multiple of %d), T=%d (multiple of %d), K=%d (multiple of 32)", N, GEMM_TM, T, GEMM_TT, K);
-    static bool attr = false;
-    if (!attr) {
+    static uint64_t attr_devs = 0;   // devices whose attribute is set
+    int dev = 0;
+    BREW_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !(attr_devs >> dev & 1)) {
         BREW_CUDA(cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
-        attr = true;
+        attr_devs |= 1ull << dev;
     }
-    gemm_q8_kernel<<<dim3(N / GEMM_TM, T / GEMM_TT), 128, GEMM_SMEM, stream>>>(wq, wd, limbs, scales, N, K, T, y, err);
+    gemm_q8_kernel<<<dim3(N / GEMM_TM, T / GEMM_TT), GEMM_THREADS, GEMM_SMEM, stream>>>(wq, wd, limbs, scales, N, K,
+                                                                                        T, y, err);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;
@@ -250,7 +406,7 @@ extern "C" int brew_gemm_q8_dev(float* y, const float* x, brew_tensor w, int64_t
     BREW_CUDA(cudaMalloc(&wd, (size_t)N * KB * 2));
     BREW_CUDA(cudaMalloc(&limbs, (size_t)KB * 3 * T * 32));
     BREW_CUDA(cudaMalloc(&sc, (size_t)KB * T * 4));
-    rc = gemm_pack_q8_launch(w->d + off / 32 * 34, N, K, wq, wd, s);
+    rc = gemm_pack_q8_launch(w->d + off / 32 * 34, N, K, wq, wd, N, 0, s);
     if (!rc) rc = gemm_limbs_launch(x, K, T, T, K, limbs, sc, s);
     if (!rc) rc = gemm_q8_launch(wq, wd, limbs, sc, N, K, T, y, ctx().err_word, s);
     cudaStreamSynchronize(s);

@@ -105,8 +105,8 @@ struct brew_model_s {
     int prefill_mode = BREW_PREFILL_TOKENS;
     bool pf_ready = false;
     int pf_cap = 0;                         // tokens per chunk (multiple of GEMM_TT)
-    int8_t* pf_wq[4] = {};                  // Q|K|V, wo, gate|up, down: [layer][N][K] quants
-    uint16_t* pf_wd[4] = {};                // [layer][N][K/32] fp16 block scales
+    int8_t* pf_wq[4] = {};                  // Q|K|V, wo, gate|up, down: [layer][N/128][K/32] 4 KB quant tiles
+    uint16_t* pf_wd[4] = {};                // [layer][K/32][N] fp16 block scales
     float *pf_x = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_xb = nullptr, *pf_xb2 = nullptr, *pf_h = nullptr;
     int8_t* pf_limbs = nullptr;
     float* pf_lsc = nullptr;
@@ -727,9 +727,9 @@ int setup_prefill(brew_model_s* m) {
     cudaStream_t s = ctx().stream;
     // one GGUF matrix (rows x cols) of layer l into rows [row0, row0 + rows) of family f
     auto pack = [&](int f, int l, int row0, int which, int rows, int cols) {
-        int8_t* wq = m->pf_wq[f] + ((int64_t)l * N[f] + row0) * K[f];
-        uint16_t* wd = m->pf_wd[f] + ((int64_t)l * N[f] + row0) * (K[f] / 32);
-        return gemm_pack_q8_launch(layer_ptr(m->t[which], l, rows, cols), rows, cols, wq, wd, s);
+        int8_t* wq = m->pf_wq[f] + (int64_t)l * N[f] * K[f];            // this layer's quant tiles
+        uint16_t* wd = m->pf_wd[f] + (int64_t)l * N[f] * (K[f] / 32);   // this layer's [K/32][N] scales
+        return gemm_pack_q8_launch(layer_ptr(m->t[which], l, rows, cols), rows, cols, wq, wd, N[f], row0, s);
     };
     for (int l = 0; l < L; ++l) {
         if ((rc = pack(0, l, 0, T_Q, qw, dim)) || (rc = pack(0, l, qw, T_K, kvd, dim)) ||
