@@ -85,27 +85,32 @@ __global__ void __launch_bounds__(256) prefill_qk_kernel(const __grid_constant__
 
 constexpr int PF_TILE = 32;    // key positions per tile (one per lane)
 constexpr int PF_PAIRS = 32;   // (query, head) pairs per CTA: 4 per warp
+constexpr int PF_KS = 33;      // float4 stride between the K^T rows of a tile
 
 // CTA = (kv head hk, block of qb query tokens); the qb * G (query, q head)
-// pairs share each 32-position K / V tile staged in shared memory: K
-// transposed with a 33-float row ([hd][33], lane j reads key j without bank
-// conflicts), V row-major.  Warp w owns pairs 4w .. 4w + 3.  Scores: lane j
-// computes q.k_j; the softmax is online over tiles (running max m, sum l);
-// the weighted sum keeps hd/32 outputs per lane.
+// pairs share each 32-position K / V tile in shared memory, double-buffered
+// with asynchronous copies (tile k + 1 lands while tile k is used).  K is
+// stored transposed by quads: float4 kt[i/4][j] = k_j[i .. i+3], so lane j
+// reads key j's quads without bank conflicts; V row-major.  Warp w owns
+// pairs 4w .. 4w + 3.  Scores: lane j computes q.k_j; the softmax is online
+// over tiles (running max m, sum l); the weighted sum keeps hd/32 outputs
+// per lane.
 template <int R>
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant__ PfAttnParams p, int qb) {
     extern __shared__ __align__(16) float sm[];
-    const int hd = R * 32;
+    constexpr int hd = R * 32, hd4 = hd / 4;
     const int G = p.n_heads / p.n_kv, kvd = p.n_kv * hd;
     const int hk = blockIdx.x, t0 = blockIdx.y * qb;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* qs = sm;                           // [PF_PAIRS][hd]
-    float* kt = qs + PF_PAIRS * hd;           // [hd][33]
-    float* vt = kt + hd * 33;                 // [PF_TILE][hd]
+    float4* qs = reinterpret_cast<float4*>(sm);          // [PF_PAIRS][hd/4]
+    float4* kt = qs + PF_PAIRS * hd4;                    // [2][hd/4][PF_KS]
+    float4* vt = kt + 2 * hd4 * PF_KS;                   // [2][PF_TILE][hd/4]
     const int npairs = qb * G;
-    for (int e = tid; e < npairs * hd; e += 256) {
-        const int pi = e / hd, i = e % hd, qi = pi / G, h = pi % G;
-        qs[e] = (t0 + qi < p.T) ? p.q[(int64_t)(t0 + qi) * p.ldq + (int64_t)(hk * G + h) * hd + i] : 0.0f;
+    for (int e = tid; e < npairs * hd4; e += 256) {
+        const int pi = e / hd4, i4 = e % hd4, qi = pi / G, h = pi % G;
+        qs[e] = (t0 + qi < p.T)
+                    ? *reinterpret_cast<const float4*>(p.q + (int64_t)(t0 + qi) * p.ldq + (int64_t)(hk * G + h) * hd + 4 * i4)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     int qpos[4];
     bool act[4];
@@ -116,8 +121,27 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant
         qpos[r] = p.pos0 + t0 + qi;
     }
     const int tlast = min(p.T, t0 + qb) - 1;
-    const int kmax = p.pos0 + tlast;                                        // last key any query sees
+    const int kmax = p.pos0 + tlast;                                          // last key any query sees
     const int kmin = p.window > 0 ? max(0, p.pos0 + t0 - p.window + 1) : 0;   // first key any query sees
+    const float* kc = p.kcache + (int64_t)hk * hd;
+    const float* vc = p.vcache + (int64_t)hk * hd;
+    // tile at key k0 into buffer bf: keys past kmax are zero (never scored,
+    // and their zero values keep the weighted sum finite)
+    auto load_tile = [&](int k0, int bf) {
+        float4* ktb = kt + bf * hd4 * PF_KS;
+        float4* vtb = vt + bf * PF_TILE * hd4;
+        for (int e = tid; e < PF_TILE * hd4; e += 256) {
+            const int j = e / hd4, i4 = e % hd4, key = k0 + j;
+            if (key <= kmax) {
+                cp_async16(ktb + i4 * PF_KS + j, kc + (int64_t)key * kvd + 4 * i4);
+                cp_async16(vtb + j * hd4 + i4, vc + (int64_t)key * kvd + 4 * i4);
+            } else {
+                ktb[i4 * PF_KS + j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                vtb[j * hd4 + i4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
     float m[4], l[4], o[4][R];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -126,29 +150,32 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant
 #pragma unroll
         for (int c = 0; c < R; ++c) o[r][c] = 0.0f;
     }
-    const float* kc = p.kcache + (int64_t)hk * hd;
-    const float* vc = p.vcache + (int64_t)hk * hd;
-    for (int k0 = kmin; k0 <= kmax; k0 += PF_TILE) {
-        __syncthreads();   // the previous tile is no longer read
-        for (int e = tid; e < PF_TILE * hd; e += 256) {
-            const int j = e / hd, i = e % hd, key = k0 + j;
-            float kv = 0.0f, vv = 0.0f;
-            if (key <= kmax) {
-                kv = kc[(int64_t)key * kvd + i];
-                vv = vc[(int64_t)key * kvd + i];
-            }
-            kt[i * 33 + j] = kv;
-            vt[j * hd + i] = vv;
+    load_tile(kmin, 0);
+    int bf = 0;
+    for (int k0 = kmin; k0 <= kmax; k0 += PF_TILE, bf ^= 1) {
+        if (k0 + PF_TILE <= kmax) {   // the next tile into the other buffer (freed by the last barrier)
+            load_tile(k0 + PF_TILE, bf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
+        const float4* ktb = kt + bf * hd4 * PF_KS;
+        const float* vtb = reinterpret_cast<const float*>(vt + bf * PF_TILE * hd4);
         const int key = k0 + lane;
         float s[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) s[r] = 0.0f;
-        for (int i = 0; i < hd; ++i) {
-            const float kv = kt[i * 33 + lane];
+        for (int i4 = 0; i4 < hd4; ++i4) {
+            const float4 kv = ktb[i4 * PF_KS + lane];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) s[r] = fmaf(qs[(warp * 4 + r) * hd + i], kv, s[r]);
+            for (int r = 0; r < 4; ++r) {
+                const float4 qv = qs[(warp * 4 + r) * hd4 + i4];
+                s[r] = fmaf(qv.x, kv.x, s[r]);
+                s[r] = fmaf(qv.y, kv.y, s[r]);
+                s[r] = fmaf(qv.z, kv.z, s[r]);
+                s[r] = fmaf(qv.w, kv.w, s[r]);
+            }
         }
         float pj[4];
 #pragma unroll
@@ -171,7 +198,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant
         for (int j = 0; j < PF_TILE; ++j) {
             float vj[R];
 #pragma unroll
-            for (int c = 0; c < R; ++c) vj[c] = vt[j * hd + lane + 32 * c];
+            for (int c = 0; c < R; ++c) vj[c] = vtb[j * hd + lane + 32 * c];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const float w = __shfl_sync(0xffffffffu, pj[r], j);
@@ -179,6 +206,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant
                 for (int c = 0; c < R; ++c) o[r][c] = fmaf(w, vj[c], o[r][c]);
             }
         }
+        __syncthreads();   // this buffer is refilled two tiles later
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -193,7 +221,8 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const __grid_constant
 
 template <int R>
 size_t pf_attn_smem() {
-    return sizeof(float) * ((size_t)PF_PAIRS * R * 32 + (size_t)R * 32 * 33 + (size_t)PF_TILE * R * 32);
+    constexpr int hd4 = R * 8;
+    return sizeof(float4) * ((size_t)PF_PAIRS * hd4 + 2 * (size_t)hd4 * PF_KS + 2 * (size_t)PF_TILE * hd4);
 }
 
 template <int R>
