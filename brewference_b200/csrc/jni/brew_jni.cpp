@@ -137,6 +137,13 @@ JNIEXPORT void JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_modelFree(J
     brew_model_free(reinterpret_cast<brew_model>(m));
 }
 
+// brew_model_set_prefill: 0 token by token (default), 1 batched (tcgen05 GEMM).
+JNIEXPORT void JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_setPrefill(JNIEnv* env, jclass, jlong m,
+                                                                                jint mode) {
+    const int rc = brew_model_set_prefill(reinterpret_cast<brew_model>(m), mode);
+    if (rc) throw_for(env, rc);
+}
+
 // TransformerGraph.forward(token, pos) + Kernels.argMax; logits copied into
 // `logits` when it is not null.  Returns the argmax id.
 JNIEXPORT jint JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_forward(JNIEnv* env, jclass, jlong m, jint token,
