@@ -76,89 +76,224 @@ int Scratch::reserve(size_t need_bytes) {
     return BREW_OK;
 }
 
-// ---- generic GPU matvec for the K-quants ---------------------------------
-// One warp per output row; each 32-element group is dequantized with the
-// GGML formulas and summed in fp32 (the oracle's K-quant order per group).
+// ---- GPU matvec for the K-quants -----------------------------------------
+// Q4_K / Q6_K rows (super-blocks of 256 elements) times up to 16 fp32
+// vectors per launch, on CUDA cores.  Each weight is dequantized once, with
+// the GGML formulas and their fp32 rounding per element
+// (d*sc*q - dmin*m for Q4_K, d*scale*(q - 32) for Q6_K), and multiplied into
+// every vector's sum.
+//
+// A warp owns RW rows (4, or 2 with 16 vectors, whose accumulators would
+// not fit the registers of two CTAs per SM otherwise) and walks their super-blocks; lane l owns 4 bytes
+// of each super-block's quant array (so a warp's weight reads are one
+// coalesced 128-byte run per row) and the 8 elements they hold:
+//   Q4_K  qs bytes 4l .. 4l+3: elements 4 (l % 8) + 0..3 of sub-block
+//         2 (l / 8) (low nibbles) and of the next sub-block (high nibbles);
+//   Q6_K  ql bytes 4l .. 4l+3: elements 128 h + 32 g + 4 (l % 8) + 0..3
+//         (h = l / 16, g = (l / 8) % 2; low nibbles, high bits of qh at 2g)
+//         and the same + 64 (high nibbles, qh bits at 2g + 4).
+// The vectors' matching 4-element pieces are read as float4 (L1-cached:
+// every warp of the CTA reads them), and the lanes' partial sums meet in a
+// warp reduction at the end.
 namespace {
-__device__ __forceinline__ float ldh(const uint8_t* p) { return half_bits_to_float((uint16_t)(p[0] | (p[1] << 8))); }
+constexpr int KQ_WARPS = 8;       // warps per CTA
+constexpr int KQ_MAXV = 16;       // vectors per launch
 
-// One warp per output row for up to MAXB vectors: each weight is dequantized
-// once and multiplied into every vector's sum (the per-vector summation
-// order is the same for any batch).
-template <int MAXB>
-__global__ void kquant_matvec_kernel(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K,
-                                     int N, float* y, int ldy, int batch) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int b0 = blockIdx.y * MAXB;
-    if (row >= N) return;
-    const uint8_t* wr = w + (int64_t)row * row_bytes;
-    float acc[MAXB];
-#pragma unroll
-    for (int b = 0; b < MAXB; ++b) acc[b] = 0.0f;
-    for (int k0 = 0; k0 < K; k0 += 256) {
-        const int s = lane >> 2;  // 8 sub-blocks of 32 per super-block, 4 lanes each
-        const uint8_t* blk = wr + (int64_t)(k0 / 256) * (type == BREW_TYPE_Q4_K ? 144 : 210);
-        float part[MAXB];
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b) part[b] = 0.0f;
-        for (int i = (lane & 3) * 8; i < (lane & 3) * 8 + 8; ++i) {
-            const int r = s * 32 + i;
-            float wv;
-            if (type == BREW_TYPE_Q4_K) {
-                const uint8_t* sb = blk + 4;
-                int sc, m;
-                if (s < 4) { sc = sb[s] & 63; m = sb[s + 4] & 63; }
-                else { sc = (sb[s + 4] & 0xF) | ((sb[s - 4] >> 6) << 4); m = (sb[s + 4] >> 4) | ((sb[s] >> 6) << 4); }
-                const uint8_t qb = blk[16 + 32 * (s / 2) + i];
-                const int q = (s & 1) ? (qb >> 4) : (qb & 15);
-                wv = __fsub_rn(__fmul_rn(__fmul_rn(ldh(blk), (float)sc), (float)q), __fmul_rn(ldh(blk + 2), (float)m));
-            } else {
-                const int h = r / 128, rr = r % 128, grp = rr / 32, l = rr % 32;
-                const int lq = blk[64 * h + (grp & 1) * 32 + l];
-                const int low = grp < 2 ? (lq & 15) : (lq >> 4);
-                const int high = (blk[128 + 32 * h + l] >> (2 * grp)) & 3;
-                const int q = (low | (high << 4)) - 32;
-                wv = __fmul_rn(__fmul_rn(ldh(blk + 208), (float)(int8_t)blk[192 + r / 16]), (float)q);
-            }
-#pragma unroll
-            for (int b = 0; b < MAXB; ++b)
-                if (b0 + b < batch) part[b] += wv * x[(int64_t)(b0 + b) * ldx + k0 + r];
-        }
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b) acc[b] += part[b];
-    }
-#pragma unroll
-    for (int b = 0; b < MAXB; ++b) {
-        const float v = warp_sum(acc[b]);
-        if (lane == 0 && b0 + b < batch) y[(int64_t)(b0 + b) * ldy + row] = v;
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+// 6-bit scale and min of Q4_K sub-block s from the 12 scale bytes (held in
+// the header words h1 = bytes 4..7, h2 = 8..11, h3 = 12..15 of the block):
+// GGML's get_scale_min_k4.
+__device__ __forceinline__ void q4k_sm(uint32_t h1, uint32_t h2, uint32_t h3, int s, int& sc, int& m) {
+    auto sb = [&](int i) -> int { return (int)byte_of(i < 4 ? h1 : (i < 8 ? h2 : h3), i & 3); };
+    if (s < 4) {
+        sc = sb(s) & 63;
+        m = sb(s + 4) & 63;
+    } else {
+        sc = (sb(s + 4) & 0xF) | ((sb(s - 4) >> 6) << 4);
+        m = (sb(s + 4) >> 4) | ((sb(s) >> 6) << 4);
     }
 }
-}  // namespace
 
-int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K, int N, float* y,
-                         int ldy, int batch, cudaStream_t stream, bool pdl) {
-    BREW_CHECK(K % 256 == 0, BREW_ERR_INVALID_ARG, "K-quant matvec: K=%d not a multiple of 256", K);
-    const int maxb = batch <= 1 ? 1 : (batch <= 4 ? 4 : 16);
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// The raw bytes of lane l's share of one super-block of a row (loaded one
+// super-block ahead of their use, so the weight stream's latency overlaps
+// the multiplication):
+//   Q4_K  hd = d, dmin, scales[12]; q = the lane's 4 quant bytes
+//   Q6_K  q = 4 ql bytes, h = the 4 qh bytes over them, hd.x = the two
+//         scale bytes (low, high set) and d
+struct KqRaw {
+    uint4 hd;
+    uint32_t q, h;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void kq_load(const uint8_t* blk, int lane, KqRaw& r) {
+    if (TYPE == BREW_TYPE_Q4_K) {
+        r.hd = __ldg(reinterpret_cast<const uint4*>(blk));
+        r.q = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 4 * lane));
+    } else {
+        // 210-byte super-blocks are only 2-byte aligned: 16-bit loads
+        const int h = lane >> 4, g = (lane >> 3) & 1, e0 = 4 * (lane & 7);
+        const int rlo = 128 * h + 32 * g + e0;
+        r.q = ld_u16(blk + 4 * lane) | (ld_u16(blk + 4 * lane + 2) << 16);
+        const uint8_t* qhp = blk + 128 + 32 * h + e0;
+        r.h = ld_u16(qhp) | (ld_u16(qhp + 2) << 16);
+        r.hd.x = (uint32_t)blk[192 + (rlo >> 4)] | ((uint32_t)blk[192 + ((rlo + 64) >> 4)] << 8) |
+                 (ld_u16(blk + 208) << 16);
+    }
+}
+
+// Dequantized elements of lane l: w[0..3] at super-block offset lo, w[4..7]
+// at hi (kq_offsets).
+template <int TYPE>
+__device__ __forceinline__ void kq_decode(const KqRaw& r, int lane, float (&w)[8]) {
+    if (TYPE == BREW_TYPE_Q4_K) {
+        const float d = half_bits_to_float((uint16_t)(r.hd.x & 0xFFFFu));
+        const float dmin = half_bits_to_float((uint16_t)(r.hd.x >> 16));
+        const int s0 = 2 * (lane >> 3);
+        int sc0, m0, sc1, m1;
+        q4k_sm(r.hd.y, r.hd.z, r.hd.w, s0, sc0, m0);
+        q4k_sm(r.hd.y, r.hd.z, r.hd.w, s0 + 1, sc1, m1);
+        const float D0 = __fmul_rn(d, (float)sc0), M0 = __fmul_rn(dmin, (float)m0);
+        const float D1 = __fmul_rn(d, (float)sc1), M1 = __fmul_rn(dmin, (float)m1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            w[j] = __fsub_rn(__fmul_rn(D0, (float)((r.q >> (8 * j)) & 15u)), M0);
+            w[4 + j] = __fsub_rn(__fmul_rn(D1, (float)((r.q >> (8 * j + 4)) & 15u)), M1);
+        }
+    } else {
+        const int g = (lane >> 3) & 1;
+        const float d = half_bits_to_float((uint16_t)(r.hd.x >> 16));
+        const float Dlo = __fmul_rn(d, (float)(int8_t)(r.hd.x & 0xFFu));
+        const float Dhi = __fmul_rn(d, (float)(int8_t)((r.hd.x >> 8) & 0xFFu));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t qb = byte_of(r.q, j), hb = byte_of(r.h, j);
+            const int qlo = (int)((qb & 15u) | (((hb >> (2 * g)) & 3u) << 4)) - 32;
+            const int qhi = (int)((qb >> 4) | (((hb >> (2 * g + 4)) & 3u) << 4)) - 32;
+            w[j] = __fmul_rn(Dlo, (float)qlo);
+            w[4 + j] = __fmul_rn(Dhi, (float)qhi);
+        }
+    }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void kq_offsets(int lane, int& lo, int& hi) {
+    if (TYPE == BREW_TYPE_Q4_K) {
+        lo = 64 * (lane >> 3) + 4 * (lane & 7);
+        hi = lo + 32;
+    } else {
+        lo = 128 * (lane >> 4) + 32 * ((lane >> 3) & 1) + 4 * (lane & 7);
+        hi = lo + 64;
+    }
+}
+
+template <int TYPE, int NV, int RW = (NV >= 16 ? 2 : 4)>
+__global__ void __launch_bounds__(KQ_WARPS * 32, 2) kq_matvec_kernel(const uint8_t* w, int64_t row_bytes, const float* x,
+                                                                   int ldx, int K, int N, float* y, int ldy, int batch) {
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int SB = TYPE == BREW_TYPE_Q4_K ? 144 : 210;
+    const int lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * KQ_WARPS + (threadIdx.x >> 5)) * RW;
+    const int b0 = blockIdx.y * KQ_MAXV;
+    const int nv = min(NV, batch - b0);
+    if (row0 >= N) return;   // whole warps
+    int lo, hi;
+    kq_offsets<TYPE>(lane, lo, hi);
+    float acc[RW][NV];
+#pragma unroll
+    for (int r = 0; r < RW; ++r)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = 0.0f;
+    const int nsb = K / 256;
+    const uint8_t* wr[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r)   // rows past N compute row N-1 again and are not stored
+        wr[r] = w + (int64_t)min(row0 + r, N - 1) * row_bytes;
+    KqRaw raw[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) kq_load<TYPE>(wr[r], lane, raw[r]);
+    for (int sbi = 0; sbi < nsb; ++sbi) {
+        float wv[RW][8];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) kq_decode<TYPE>(raw[r], lane, wv[r]);
+        if (sbi + 1 < nsb) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r) kq_load<TYPE>(wr[r] + (int64_t)(sbi + 1) * SB, lane, raw[r]);
+        }
+        const float* xs = x + (int64_t)b0 * ldx + (int64_t)sbi * 256;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            if (v < nv) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(xs + (int64_t)v * ldx + lo));
+                const float4 c = __ldg(reinterpret_cast<const float4*>(xs + (int64_t)v * ldx + hi));
+#pragma unroll
+                for (int r = 0; r < RW; ++r) {
+                    float t = acc[r][v];
+                    t = fmaf(wv[r][0], a.x, t);
+                    t = fmaf(wv[r][1], a.y, t);
+                    t = fmaf(wv[r][2], a.z, t);
+                    t = fmaf(wv[r][3], a.w, t);
+                    t = fmaf(wv[r][4], c.x, t);
+                    t = fmaf(wv[r][5], c.y, t);
+                    t = fmaf(wv[r][6], c.z, t);
+                    t = fmaf(wv[r][7], c.w, t);
+                    acc[r][v] = t;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RW; ++r)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float s = warp_sum(acc[r][v]);
+            if (lane == 0 && v < nv && row0 + r < N) y[(int64_t)(b0 + v) * ldy + row0 + r] = s;
+        }
+}
+
+template <int TYPE>
+int kq_launch(const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K, int N, float* y, int ldy, int batch,
+              cudaStream_t stream, bool pdl) {
+    const int per = std::min(batch, KQ_MAXV);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + 7) / 8, (batch + maxb - 1) / maxb);
-    cfg.blockDim = dim3(256);
+    const int rw = per >= 16 ? 2 : 4;   // the kernel's RW for this vector count
+    cfg.gridDim = dim3((N + KQ_WARPS * rw - 1) / (KQ_WARPS * rw), (batch + KQ_MAXV - 1) / KQ_MAXV);
+    cfg.blockDim = dim3(KQ_WARPS * 32);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (maxb == 1)
-        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<1>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
-    else if (maxb == 4)
-        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<4>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    if (per == 1)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kq_matvec_kernel<TYPE, 1>, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    else if (per <= 2)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kq_matvec_kernel<TYPE, 2>, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    else if (per <= 4)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kq_matvec_kernel<TYPE, 4>, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+    else if (per <= 8)
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kq_matvec_kernel<TYPE, 8>, w, row_bytes, x, ldx, K, N, y, ldy, batch));
     else
-        BREW_CUDA(cudaLaunchKernelEx(&cfg, kquant_matvec_kernel<16>, type, w, row_bytes, x, ldx, K, N, y, ldy, batch));
+        BREW_CUDA(cudaLaunchKernelEx(&cfg, kq_matvec_kernel<TYPE, 16>, w, row_bytes, x, ldx, K, N, y, ldy, batch));
     count_launch();
     return BREW_OK;
+}
+}  // namespace
+
+int kquant_matvec_launch(int type, const uint8_t* w, int64_t row_bytes, const float* x, int ldx, int K, int N, float* y,
+                         int ldy, int batch, cudaStream_t stream, bool pdl) {
+    BREW_CHECK(K % 256 == 0, BREW_ERR_INVALID_ARG, "K-quant matvec: K=%d not a multiple of 256", K);
+    BREW_CHECK(type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K, BREW_ERR_INVALID_ARG, "K-quant matvec: type %d", type);
+    // the float4 reads of x need 16-byte aligned vectors
+    BREW_CHECK((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0, BREW_ERR_INVALID_ARG,
+               "K-quant matvec: x must be 16-byte aligned with a row pitch that is a multiple of 4 floats");
+    if (batch <= 0 || N <= 0) return BREW_OK;
+    if (type == BREW_TYPE_Q4_K) return kq_launch<BREW_TYPE_Q4_K>(w, row_bytes, x, ldx, K, N, y, ldy, batch, stream, pdl);
+    return kq_launch<BREW_TYPE_Q6_K>(w, row_bytes, x, ldx, K, N, y, ldy, batch, stream, pdl);
 }
 
 // Runs one matvec (any supported type) on device buffers: the shared core of

@@ -85,6 +85,27 @@ def test_kquant_matmul_matches_oracle(device, qt, K, N):
     assert rel(y, oracle.matvec(qt, w, 0, x, K, N)) < TOL
 
 
+@pytest.mark.parametrize("qt", [C.TYPE_Q4_K, C.TYPE_Q6_K])
+@pytest.mark.parametrize("batch", [2, 3, 8, 16, 21])
+def test_kquant_matmul_batched(device, qt, batch):
+    """The batched K-quant matvec (up to 16 vectors per launch, more in
+    launch groups; 37 rows: a partial row group) against the oracle, vector
+    by vector."""
+    K, Nr = 3584, 37
+    rng = np.random.default_rng(batch)
+    w = oracle.synth_quantized(qt, 17, K, K * Nr)
+    t = PackedTensor.upload(qt, w, K * Nr)
+    x = rng.standard_normal((batch, K)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.full((batch, Nr), float("nan"), dtype=torch.float32, device="cuda")
+    Linear.matmul_device(yd.data_ptr(), xd.data_ptr(), t, 0, K, Nr, batch)
+    torch.cuda.synchronize()
+    y = yd.cpu().numpy()
+    for b in range(batch):
+        assert rel(y[b], oracle.matvec(qt, w, 0, x[b], K, Nr)) < TOL, b
+    t.free()
+
+
 def test_matmul_classifier_shape(device):
     K, N = 2048, 151936
     w = oracle.synth_quantized(C.TYPE_Q8_0, 8, 1, K * N)
