@@ -591,7 +591,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill timing")
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config over --gpus ranks")
-    ap.add_argument("--batch", type=int, default=16, help="concurrent sequences of the --tp workload")
+    ap.add_argument("--batch", type=int, default=32, help="concurrent sequences of the --tp workload")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     args = ap.parse_args()

@@ -126,6 +126,8 @@ int dalloc(brew_model_s* m, T** p, size_t count) {
     return BREW_OK;
 }
 
+constexpr int MODEL_MAX_BATCH = 32;   // sequences per step of the unfused forward
+
 // Any Q4_K / Q6_K matrix: the model runs the unfused forward (separate
 // norm / bias / residual / activation kernels around each matvec).
 bool uses_kquants(const brew_config& c) {
@@ -144,7 +146,12 @@ int check_config(const brew_config& c, int max_batch) {
                BREW_ERR_INVALID_ARG, "layers/heads %d/%d/%d", c.n_layers, c.n_heads, c.n_kv_heads);
     BREW_CHECK(c.head_size > 0 && c.head_size % 32 == 0, BREW_ERR_INVALID_ARG, "head_size %d", c.head_size);
     BREW_CHECK(c.vocab_size > 0 && c.seq_len > 0, BREW_ERR_INVALID_ARG, "vocab/seq_len");
-    BREW_CHECK(max_batch >= 1 && max_batch <= MV_MAX_BATCH, BREW_ERR_INVALID_ARG, "max_batch %d", max_batch);
+    // the fused forward runs up to MV_MAX_BATCH sequences per step; the
+    // unfused (K-quant) forward, whose matvecs loop over vector groups, up to
+    // MODEL_MAX_BATCH
+    const int bmax = uses_kquants(c) ? MODEL_MAX_BATCH : MV_MAX_BATCH;
+    BREW_CHECK(max_batch >= 1 && max_batch <= bmax, BREW_ERR_INVALID_ARG, "max_batch %d (at most %d for this model)",
+               max_batch, bmax);
     const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down,
                          c.tied_embeddings ? c.type_embed : c.type_output, c.type_embed};
     for (int t : types)
@@ -194,7 +201,7 @@ int alloc_unfused(brew_model_s* m) {
     int rc;
     if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
     if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
-    if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * prep_rec_bytes(B)))) return rc;
+    if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * prep_rec_bytes(std::min(B, MV_MAX_BATCH))))) return rc;
     m->unfused = true;
     return BREW_OK;
 }
@@ -268,20 +275,24 @@ int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx,
     const int64_t rb = row_bytes_of(type, K);
     if (type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K)
         return kquant_matvec_launch(type, w, rb, x, ldx, K, N, y, ldy, B, s, false);
-    int rc = prep_launch(x, ldx, K, B, nullptr, 0.0f, m->prep_any, s, false);
-    if (rc) return rc;
-    MvParams p = {};
-    p.type = type;
-    p.K = K;
-    p.row_bytes = rb;
-    p.batch = B;
-    p.ldy = ldy;
-    p.epi = MV_EPI_STORE;
-    p.nseg = 1;
-    p.seg[0] = {w, y, nullptr, nullptr, N, 0};
-    p.prep = m->prep_any;
-    p.err = ctx().err_word;
-    return mv_launch(p, s, false);
+    for (int b0 = 0; b0 < B; b0 += MV_MAX_BATCH) {   // the MMA matvec takes up to MV_MAX_BATCH vectors
+        const int nb = std::min(MV_MAX_BATCH, B - b0);
+        int rc = prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, nullptr, 0.0f, m->prep_any, s, false);
+        if (rc) return rc;
+        MvParams p = {};
+        p.type = type;
+        p.K = K;
+        p.row_bytes = rb;
+        p.batch = nb;
+        p.ldy = ldy;
+        p.epi = MV_EPI_STORE;
+        p.nseg = 1;
+        p.seg[0] = {w, y + (int64_t)b0 * ldy, nullptr, nullptr, N, 0};
+        p.prep = m->prep_any;
+        p.err = ctx().err_word;
+        if ((rc = mv_launch(p, s, false))) return rc;
+    }
+    return BREW_OK;
 }
 
 // The forward of a model with K-quant matrices (the Qwen2.5-7B Q4_K/Q6_K

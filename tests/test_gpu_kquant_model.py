@@ -80,3 +80,33 @@ def test_qwen25_7b_width_two_layers(device):
     layers and a reduced vocabulary."""
     cfg = C.qwen25_7b().replace(n_layers=2, vocab_size=8192, seq_len=128)
     parity(cfg, 7, prompt_len=6, n_gen=16, check_steps=2)
+
+
+def test_kquant_32_sequences(device):
+    """32 concurrent sequences (the 7B config's workload size; the K-quant
+    matvec takes 16 vectors per launch, so the step runs two vector groups):
+    a sequence's logits in the batch equal those of the same sequence
+    forwarded alone, and sequence 0 matches the oracle."""
+    cfg = kquant(C.qwen25_7b(), dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4, **SMALL)
+    B, steps = 32, 3
+    dm = DeviceModel.synthesize(cfg, 91, max_batch=B)
+    toks = np.random.default_rng(5).integers(0, cfg.vocab_size, (steps, B)).astype(np.int32)
+    batched = []
+    for pos in range(steps):
+        lg, am = dm.forward(toks[pos], np.full(B, pos, np.int32))
+        assert all(am[b] == int(np.argmax(lg[b])) for b in range(B))
+        batched.append(lg)
+    dm.close()
+    single = DeviceModel.synthesize(cfg, 91)
+    for b in (0, 17, 31):
+        single.reset()
+        for pos in range(steps):
+            lg, _ = single.forward([toks[pos][b]], [pos])
+            assert rel(batched[pos][b], lg[0]) < 1e-6, (b, pos)
+    single.close()
+    om = oracle.OracleModel(cfg, 91)
+    om.reset()
+    for pos in range(steps):
+        ref = om.forward(int(toks[pos][0]), pos)
+        assert rel(batched[pos][0], ref) < LOGIT_TOL, (pos, rel(batched[pos][0], ref))
+    om.close()
