@@ -19,6 +19,7 @@
 #include "decode.cuh"
 #include "eltwise.cuh"
 #include "gemm.cuh"
+#include "kqmma.cuh"
 #include "prefill.cuh"
 #include "tp.cuh"
 
@@ -92,6 +93,7 @@ struct brew_model_s {
     bool unfused = false;
     float *xn = nullptr, *hb2 = nullptr;    // normed input of a matvec; the up projection
     uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
+    uint8_t* kqp[T_COUNT] = {};             // K-quant matrices repacked for the int8 MMA matvec (kqmma.cuh)
     // tensor parallelism (brew_model_set_tp): this rank's row slices
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
@@ -191,6 +193,8 @@ void matrix_shape(const brew_config& c, int which, int64_t* rows, int64_t* cols,
     }
 }
 
+const uint8_t* layer_ptr(brew_tensor t, int layer, int64_t rows, int64_t cols);
+
 // Buffers of the unfused forward (K-quant models, tensor parallelism).
 int alloc_unfused(brew_model_s* m) {
     if (m->unfused) return BREW_OK;
@@ -202,6 +206,20 @@ int alloc_unfused(brew_model_s* m) {
     if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
     if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
     if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * prep_rec_bytes(std::min(B, MV_MAX_BATCH))))) return rc;
+    // the K-quant matrices, repacked once for the int8 MMA matvec
+    for (int which = T_OUTPUT; which < T_COUNT; ++which) {
+        int64_t rows, cols;
+        int type, layers;
+        matrix_shape(c, which, &rows, &cols, &type, &layers);
+        if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
+        const size_t per = kq_packed_bytes(type, rows, cols);
+        if ((rc = dalloc(m, &m->kqp[which], per * layers))) return rc;
+        for (int l = 0; l < layers; ++l)
+            if ((rc = kq_pack_launch(type, layer_ptr(m->t[which], l, rows, cols), rows, (int)cols, m->kqp[which] + per * l,
+                                     ctx().stream)))
+                return rc;
+    }
+    BREW_CUDA(cudaStreamSynchronize(ctx().stream));
     m->unfused = true;
     return BREW_OK;
 }
@@ -295,6 +313,27 @@ int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx,
     return BREW_OK;
 }
 
+// y[b][0:n] = rows row0 .. row0+n-1 of matrix `which` (layer l, rows x K)
+// times x[b]: the int8 MMA matvec on the repacked tiles for K-quant
+// matrices (row0 on a 16-row tile), mv_any on the GGUF rows otherwise.
+int mv_w(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0, int n, const float* x, int ldx, float* y,
+         int ldy, int B, cudaStream_t s) {
+    brew_tensor t = m->t[which];
+    const int type = t->type;
+    if (m->kqp[which] && row0 % 16 == 0) {
+        const uint8_t* pk = m->kqp[which] + (size_t)l * kq_packed_bytes(type, rows, K) +
+                            (size_t)(row0 / 16) * (K / 32) * kq_tile_bytes(type);
+        for (int b0 = 0; b0 < B; b0 += MV_MAX_BATCH) {
+            const int nb = std::min(MV_MAX_BATCH, B - b0);
+            int rc = prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, nullptr, 0.0f, m->prep_any, s, false);
+            if (!rc) rc = kq_mma_launch(type, pk, n, K, m->prep_any, nb, y + (int64_t)b0 * ldy, ldy, s);
+            if (rc) return rc;
+        }
+        return BREW_OK;
+    }
+    return mv_any(m, type, layer_ptr(t, l, rows, K) + row0 * row_bytes_of(type, K), x, ldx, K, n, y, ldy, B, s);
+}
+
 // The forward of a model with K-quant matrices (the Qwen2.5-7B Q4_K/Q6_K
 // config): each matvec reads fp32 activations, and RMSNorm, bias, residual
 // and the gated activation are separate kernels.  Op order of the
@@ -311,9 +350,6 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
     // tensor parallelism: this rank multiplies rows [R*N/P, (R+1)*N/P) of
     // every matrix and the slices are all-gathered
     const int P = m->comm ? m->comm->nranks : 1, R = m->comm ? m->comm->rank : 0;
-    auto shard = [&](brew_tensor t, int type, int l, int N, int K) {
-        return layer_ptr(t, l, N, K) + (int64_t)(N / P) * R * row_bytes_of(type, K);
-    };
     auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd) {
         int r = tp_allgather(m->comm, m->tp_send, m->tp_recv, (size_t)B * slice, s);
         if (!r) r = tp_unshard_launch(m->tp_recv, P, B, slice, segs, nseg, dst, ldd, s);
@@ -329,9 +365,9 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         float* k = m->qkv + qw;
         float* v = m->qkv + qw + kvd;
         if (P == 1) {
-            if ((rc = mv_any(m, c.type_q, layer_ptr(m->t[T_Q], l, qw, dim), m->xn, dim, dim, qw, q, m->qkvw, B, s)) ||
-                (rc = mv_any(m, c.type_k, layer_ptr(m->t[T_K], l, kvd, dim), m->xn, dim, dim, kvd, k, m->qkvw, B, s)) ||
-                (rc = mv_any(m, c.type_v, layer_ptr(m->t[T_V], l, kvd, dim), m->xn, dim, dim, kvd, v, m->qkvw, B, s)))
+            if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s)) ||
+                (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s)) ||
+                (rc = mv_w(m, T_V, l, kvd, dim, 0, kvd, m->xn, dim, v, m->qkvw, B, s)))
                 return rc;
             if (m->q_bias &&
                 ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
@@ -342,11 +378,9 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             // slices [q_R | k_R | v_R] per rank, gathered into q | k | v
             const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
             float* sq = m->tp_send;
-            if ((rc = mv_any(m, c.type_q, shard(m->t[T_Q], c.type_q, l, qw, dim), m->xn, dim, dim, qs, sq, sl, B, s)) ||
-                (rc = mv_any(m, c.type_k, shard(m->t[T_K], c.type_k, l, kvd, dim), m->xn, dim, dim, ks, sq + qs, sl, B,
-                             s)) ||
-                (rc = mv_any(m, c.type_v, shard(m->t[T_V], c.type_v, l, kvd, dim), m->xn, dim, dim, ks, sq + qs + ks,
-                             sl, B, s)))
+            if ((rc = mv_w(m, T_Q, l, qw, dim, (int64_t)R * qs, qs, m->xn, dim, sq, sl, B, s)) ||
+                (rc = mv_w(m, T_K, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs, sl, B, s)) ||
+                (rc = mv_w(m, T_V, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs + ks, sl, B, s)))
                 return rc;
             if (m->q_bias &&
                 ((rc = add_bias_launch(sq, sl, m->q_bias + (int64_t)l * qw + (int64_t)R * qs, qs, B, s)) ||
@@ -395,12 +429,11 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             if ((rc = attn_launch(a, s, false))) return rc;
         }
         if (P == 1) {
-            if ((rc = mv_any(m, c.type_o, layer_ptr(m->t[T_O], l, dim, qw), m->xb, qw, qw, dim, m->xb2, dim, B, s)))
+            if ((rc = mv_w(m, T_O, l, dim, qw, 0, dim, m->xb, qw, m->xb2, dim, B, s)))
                 return rc;
         } else {
             const TpSeg seg = {dim / P, 0, 0};
-            if ((rc = mv_any(m, c.type_o, shard(m->t[T_O], c.type_o, l, dim, qw), m->xb, qw, qw, dim / P, m->tp_send,
-                             dim / P, B, s)) ||
+            if ((rc = mv_w(m, T_O, l, dim, qw, (int64_t)R * (dim / P), dim / P, m->xb, qw, m->tp_send, dim / P, B, s)) ||
                 (rc = gather(dim / P, &seg, 1, m->xb2, dim)))
                 return rc;
         }
@@ -409,25 +442,20 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)))
             return rc;
         if (P == 1) {
-            if ((rc = mv_any(m, c.type_gate, layer_ptr(m->t[T_GATE], l, hid, dim), m->xn, dim, dim, hid, m->hb, hid, B,
-                             s)) ||
-                (rc = mv_any(m, c.type_up, layer_ptr(m->t[T_UP], l, hid, dim), m->xn, dim, dim, hid, m->hb2, hid, B,
-                             s)) ||
+            if ((rc = mv_w(m, T_GATE, l, hid, dim, 0, hid, m->xn, dim, m->hb, hid, B, s)) ||
+                (rc = mv_w(m, T_UP, l, hid, dim, 0, hid, m->xn, dim, m->hb2, hid, B, s)) ||
                 (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
-                (rc = mv_any(m, c.type_down, layer_ptr(m->t[T_DOWN], l, dim, hid), m->hb, hid, hid, dim, m->xb2, dim,
-                             B, s)))
+                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hb, hid, m->xb2, dim, B, s)))
                 return rc;
         } else {
             const int hs = hid / P;
             const TpSeg hseg = {hs, 0, 0}, dseg = {dim / P, 0, 0};
-            if ((rc = mv_any(m, c.type_gate, shard(m->t[T_GATE], c.type_gate, l, hid, dim), m->xn, dim, dim, hs, m->tp_g,
-                             hs, B, s)) ||
-                (rc = mv_any(m, c.type_up, shard(m->t[T_UP], c.type_up, l, hid, dim), m->xn, dim, dim, hs, m->tp_u, hs,
-                             B, s)) ||
+            if ((rc = mv_w(m, T_GATE, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_g, hs, B, s)) ||
+                (rc = mv_w(m, T_UP, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_u, hs, B, s)) ||
                 (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s)) ||
                 (rc = gather(hs, &hseg, 1, m->hb, hid)) ||
-                (rc = mv_any(m, c.type_down, shard(m->t[T_DOWN], c.type_down, l, dim, hid), m->hb, hid, hid, dim / P,
-                             m->tp_send, dim / P, B, s)) ||
+                (rc = mv_w(m, T_DOWN, l, dim, hid, (int64_t)R * (dim / P), dim / P, m->hb, hid, m->tp_send, dim / P, B,
+                           s)) ||
                 (rc = gather(dim / P, &dseg, 1, m->xb2, dim)))
                 return rc;
         }
@@ -436,18 +464,17 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             return rc;
     }
     if (!with_classifier) return BREW_OK;
-    const int otype = c.tied_embeddings ? c.type_embed : c.type_output;
     const int V = c.vocab_size;
     if ((rc = rmsnorm_launch(m->x, dim, m->rms_final, c.eps, dim, B, m->xn, dim, s))) return rc;
     if (P == 1) {
-        if ((rc = mv_any(m, otype, m->t[T_OUTPUT]->d, m->xn, dim, dim, V, m->logits, V, B, s))) return rc;
+        if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, 0, V, m->xn, dim, m->logits, V, B, s))) return rc;
         return argmax_launch(m->logits, V, V, B, m->am_out, s, false);
     }
     // sharded classifier: per-rank argmax keys, gathered and reduced; the
     // logits slices are gathered too (brew_model_forward returns them)
     const int vs = V / P;
     const TpSeg vseg = {vs, 0, 0};
-    if ((rc = mv_any(m, otype, shard(m->t[T_OUTPUT], otype, 0, V, dim), m->xn, dim, dim, vs, m->tp_send, vs, B, s)) ||
+    if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, (int64_t)R * vs, vs, m->xn, dim, m->tp_send, vs, B, s)) ||
         (rc = tp_argmax_keys_launch(m->tp_send, vs, vs, B, R * vs, m->tp_keys, s)) ||
         (rc = tp_allgather_u64(m->comm, m->tp_keys, m->tp_keys_all, (size_t)B, s)) ||
         (rc = tp_argmax_reduce_launch(m->tp_keys_all, P, B, m->am_out, s)) ||
