@@ -125,18 +125,26 @@ __host__ __device__ __forceinline__ int gemm_tile_off(int r, int j) {
     return (r >> 3) * 256 + (j >> 4) * 128 + (r & 7) * 16 + (j & 15);
 }
 
-__global__ void gemm_pack_q8_kernel(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0) {
+// Q8_0 blocks (34 B: fp16 d, 32 int8 q) or Q4_0 blocks (18 B: fp16 d, 32
+// nibbles, value d * (q - 8)): the integer factors q (Q8_0) or q - 8 (Q4_0)
+// as int8, the scales d as they are.
+template <int TYPE>
+__global__ void gemm_pack_kernel(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0) {
+    constexpr int BB = TYPE == BREW_TYPE_Q8_0 ? 34 : 18;
     const int KB = K / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)rows * KB) return;
     const int64_t row = i / KB, kb = i % KB;
-    const uint8_t* b = w + (row * KB + kb) * 34;
+    const uint8_t* b = w + (row * KB + kb) * BB;
     const int64_t grow = row0 + row;
     wd[kb * ldn + grow] = (uint16_t)(b[0] | (b[1] << 8));
     int8_t* tile = wq + ((grow / GEMM_TM) * KB + kb) * 4096;
     const int r = (int)(grow % GEMM_TM);
 #pragma unroll 8
-    for (int j = 0; j < 32; ++j) tile[gemm_tile_off(r, j)] = (int8_t)b[2 + j];
+    for (int j = 0; j < 32; ++j) {
+        const int q = TYPE == BREW_TYPE_Q8_0 ? (int)(int8_t)b[2 + j] : (j < 16 ? (b[2 + j] & 15) : (b[2 + j - 16] >> 4)) - 8;
+        tile[gemm_tile_off(r, j)] = (int8_t)q;
+    }
 }
 
 // One warp per (token, block); tokens T .. Tp-1 are zero padding.
@@ -343,10 +351,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
 
 }  // namespace
 
-int gemm_pack_q8_launch(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0,
-                        cudaStream_t stream) {
+int gemm_pack_launch(int type, const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0,
+                     cudaStream_t stream) {
+    BREW_CHECK(type == BREW_TYPE_Q8_0 || type == BREW_TYPE_Q4_0, BREW_ERR_UNSUPPORTED,
+               "the GEMM takes Q8_0 or Q4_0 blocks (type %d)", type);
     const int64_t n = (int64_t)rows * (K / 32);
-    gemm_pack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(w, rows, K, wq, wd, ldn, row0);
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (type == BREW_TYPE_Q8_0) gemm_pack_kernel<BREW_TYPE_Q8_0><<<blocks, 256, 0, stream>>>(w, rows, K, wq, wd, ldn, row0);
+    else gemm_pack_kernel<BREW_TYPE_Q4_0><<<blocks, 256, 0, stream>>>(w, rows, K, wq, wd, ldn, row0);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;
@@ -406,7 +418,7 @@ extern "C" int brew_gemm_q8_dev(float* y, const float* x, brew_tensor w, int64_t
     BREW_CUDA(cudaMalloc(&wd, (size_t)N * KB * 2));
     BREW_CUDA(cudaMalloc(&limbs, (size_t)KB * 3 * T * 32));
     BREW_CUDA(cudaMalloc(&sc, (size_t)KB * T * 4));
-    rc = gemm_pack_q8_launch(w->d + off / 32 * 34, N, K, wq, wd, N, 0, s);
+    rc = gemm_pack_launch(BREW_TYPE_Q8_0, w->d + off / 32 * 34, N, K, wq, wd, N, 0, s);
     if (!rc) rc = gemm_limbs_launch(x, K, T, T, K, limbs, sc, s);
     if (!rc) rc = gemm_q8_launch(wq, wd, limbs, sc, N, K, T, y, ctx().err_word, s);
     cudaStreamSynchronize(s);

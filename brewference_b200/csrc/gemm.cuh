@@ -2,7 +2,8 @@
 // tokens t at once, on the 5th-generation tensor cores (tcgen05, int8, TMEM
 // accumulators).
 //
-// The weights are a GEMM-layout copy of a Q8_0 matrix: for every 128-row
+// The weights are a GEMM-layout copy of a Q8_0 (or Q4_0, its quants as
+// q - 8) matrix: for every 128-row
 // tile and 32-element block column, the 4096 quant bytes in the K-major
 // core-matrix layout the MMA reads from shared memory (8-row groups of 256 B,
 // the two 16-byte halves of a row's block 128 B apart), tiles [N/128][K/32];
@@ -23,13 +24,13 @@ namespace brew {
 constexpr int GEMM_TM = 128;   // weight rows per CTA (tcgen05 M)
 constexpr int GEMM_TT = 32;    // tokens per CTA (tcgen05 N = 3 * 32 = 96)
 
-// `rows` Q8_0 GGUF rows [rows][K/32 blocks of 34 B] -> rows row0 .. of an
+// `rows` Q8_0 or Q4_0 GGUF rows [rows][K/32 blocks] -> rows row0 .. of an
 // ldn-row matrix: quant tiles in wq (the matrix's [ldn/128][K/32][4096 B])
 // and block scales wd[kb][row0 + row] of its [K/32][ldn] scale matrix
 // (block-column major: a column's scales of consecutive rows are contiguous
 // for the GEMM epilogue).
-int gemm_pack_q8_launch(const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0,
-                        cudaStream_t stream);
+int gemm_pack_launch(int type, const uint8_t* w, int rows, int K, int8_t* wq, uint16_t* wd, int ldn, int row0,
+                     cudaStream_t stream);
 // x [T][ldx] fp32 (first K columns) -> limb tiles [K/32][Tp/32][3072 B]
 // int8 + block scales [K/32][Tp] fp32 (the records' arithmetic of prep.cuh,
 // one token per row); tokens T .. Tp-1 are zero.

@@ -718,8 +718,8 @@ bool prefill_supported(const brew_config& c, std::string* why) {
     const int qw = c.n_heads * c.head_size, kvd = c.n_kv_heads * c.head_size;
     const int types[] = {c.type_q, c.type_k, c.type_v, c.type_o, c.type_gate, c.type_up, c.type_down};
     for (int t : types)
-        if (t != BREW_TYPE_Q8_0) {
-            *why = "the batched prefill takes Q8_0 layer matrices";
+        if (t != BREW_TYPE_Q8_0 && t != BREW_TYPE_Q4_0) {
+            *why = "the batched prefill takes Q8_0 or Q4_0 layer matrices";
             return false;
         }
     if ((qw + 2 * kvd) % GEMM_TM || c.dim % GEMM_TM || (2 * c.hidden_dim) % GEMM_TM) {
@@ -767,7 +767,8 @@ int setup_prefill(brew_model_s* m) {
     auto pack = [&](int f, int l, int row0, int which, int rows, int cols) {
         int8_t* wq = m->pf_wq[f] + (int64_t)l * N[f] * K[f];            // this layer's quant tiles
         uint16_t* wd = m->pf_wd[f] + (int64_t)l * N[f] * (K[f] / 32);   // this layer's [K/32][N] scales
-        return gemm_pack_q8_launch(layer_ptr(m->t[which], l, rows, cols), rows, cols, wq, wd, N[f], row0, s);
+        return gemm_pack_launch(m->t[which]->type, layer_ptr(m->t[which], l, rows, cols), rows, cols, wq, wd, N[f],
+                                row0, s);
     };
     for (int l = 0; l < L; ++l) {
         if ((rc = pack(0, l, 0, T_Q, qw, dim)) || (rc = pack(0, l, qw, T_K, kvd, dim)) ||

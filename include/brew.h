@@ -298,7 +298,7 @@ BREW_API int brew_session_decode(brew_model m, int32_t n_steps, int32_t* out_tok
  * MMA of the exact Q8_0 block products, fp32 block-scale epilogue).  The
  * prompt's logits are never read, so the resulting state is the KV cache,
  * equal to the token-by-token one up to fp32 summation order.  Needs every
- * layer matrix in Q8_0, one GPU (no tensor parallelism), head size 64 / 128
+ * layer matrix in Q8_0 or Q4_0, one GPU (no tensor parallelism), head size 64 / 128
  * / 256 and matrix row counts (q|k|v, dim, 2 * hidden_dim) that are
  * multiples of 128; otherwise BREW_ERR_UNSUPPORTED.  No reference
  * counterpart: the reference has only the token-by-token prefill. */

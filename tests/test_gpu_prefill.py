@@ -102,11 +102,34 @@ def test_batched_prefill_chunks(device):
     dm.close()
 
 
+Q4_LAYERS = dict(type_q=C.TYPE_Q4_0, type_k=C.TYPE_Q4_0, type_v=C.TYPE_Q4_0, type_o=C.TYPE_Q4_0,
+                 type_gate=C.TYPE_Q4_0, type_up=C.TYPE_Q4_0, type_down=C.TYPE_Q4_0)
+
+
+@pytest.mark.parametrize("arch", [C.ARCH_QWEN3, C.ARCH_GEMMA3])
+def test_batched_prefill_q4_0_layers(device, arch):
+    """Q4_0 layer matrices (the Gemma-3-1B config's format): the GEMM takes
+    their quants as q - 8 with the same fp16 scales."""
+    cfg = small(arch, n_layers=3 if arch != C.ARCH_GEMMA3 else 7).replace(**Q4_LAYERS)
+    seed = 3100 + arch
+    prompt = np.random.default_rng(seed).integers(0, cfg.vocab_size, 70).tolist()
+    dm = DeviceModel.synthesize(cfg, seed)
+    ref = oracle_logits(cfg, seed, prompt)
+    lb = next_logits(dm, prompt, PREFILL_BATCHED)
+    assert rel(lb, ref) < LOGIT_TOL, rel(lb, ref)
+    dm.set_prefill(PREFILL_TOKENS)
+    gt = dm.generate(prompt, 16)
+    dm.set_prefill(PREFILL_BATCHED)
+    gb = dm.generate(prompt, 16)
+    assert gt == gb
+    dm.close()
+
+
 def test_batched_prefill_unsupported(device):
-    # Q4_0 layers: no GEMM layout for them
-    cfg = small(C.ARCH_QWEN3).replace(type_q=C.TYPE_Q4_0, type_k=C.TYPE_Q4_0, type_v=C.TYPE_Q4_0,
-                                      type_o=C.TYPE_Q4_0, type_gate=C.TYPE_Q4_0, type_up=C.TYPE_Q4_0,
-                                      type_down=C.TYPE_Q4_0)
+    # K-quant layers: no GEMM layout for them
+    cfg = small(C.ARCH_QWEN3).replace(type_q=C.TYPE_Q4_K, type_k=C.TYPE_Q4_K, type_v=C.TYPE_Q4_K,
+                                      type_o=C.TYPE_Q4_K, type_gate=C.TYPE_Q4_K, type_up=C.TYPE_Q4_K,
+                                      type_down=C.TYPE_Q6_K)
     dm = DeviceModel.synthesize(cfg, 5)
     with pytest.raises(N.BrewError) as e:
         dm.set_prefill(PREFILL_BATCHED)
