@@ -138,3 +138,30 @@ def test_batched_prefill_unsupported(device):
         dm.set_prefill(7)
     dm.set_prefill(PREFILL_TOKENS)   # the default stays available
     dm.close()
+
+
+@pytest.mark.parametrize("n", [1, 32, 512, 513])
+def test_batched_prefill_lengths(device, n):
+    """Prompt lengths at the edges of the token tile (32) and of a chunk
+    (512; 513 leaves a 1-token second chunk)."""
+    cfg = small(C.ARCH_QWEN3, n_layers=2, seq_len=640)
+    seed = 40 + n
+    prompt = np.random.default_rng(seed).integers(0, cfg.vocab_size, n).tolist()
+    dm = DeviceModel.synthesize(cfg, seed)
+    lb = next_logits(dm, prompt, PREFILL_BATCHED)
+    lt = next_logits(dm, prompt, PREFILL_TOKENS)
+    assert rel(lb, lt) < LOGIT_TOL, rel(lb, lt)
+    dm.close()
+
+
+def test_batched_prefill_context_full(device):
+    """A prompt longer than the context is refused before any work, as in
+    the token-by-token prefill (ModelRunner.java:208-216)."""
+    cfg = small(C.ARCH_QWEN3, n_layers=1, seq_len=64)
+    dm = DeviceModel.synthesize(cfg, 3)
+    dm.set_prefill(PREFILL_BATCHED)
+    with pytest.raises(N.BrewError) as e:
+        dm.prefill(list(range(65)))
+    assert e.value.code == N.ERR_CONTEXT_FULL
+    dm.prefill(list(range(64)))   # a full context is accepted
+    dm.close()
