@@ -67,13 +67,17 @@ def q4_cfg(cfg):
 TRAFFIC_PROFILE = "decode_kernel_qwen3-1.7b_q8_0.md"
 
 
-def measured_peaks():
+def measured_peaks(kind: str = "hbm_gbs"):
+    """(peak, "measured" | "fallback"): HBM copy GB/s (`hbm_gbs`) or dense
+    bf16 TFLOP/s (`bf16_tflops`) from MEASURED_PEAKS.json, else the
+    fallback figures."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        if kind in d:
+            return float(d[kind]), "measured"
+    return (6650.0 if kind == "hbm_gbs" else 1590.0), "fallback"
 
 
 class ClockSampler:
@@ -285,9 +289,49 @@ def time_matvec(w, K, Nr, layers, batch, iters):
     return alg, ms
 
 
+def time_gemm(w, K, Nr, layers, T, iters):
+    """Times the tcgen05 GEMM through GEMM plans (the matrix repacked once) of
+    up to 4 layers of tensor `w`, run in turn from a CUDA graph on a
+    dedicated stream with CUDA events on it; x [T][K] and y [T][N] stay on
+    the device.  Returns (weight bytes per run, ms per run)."""
+    import torch
+    from brewference_b200.api import GemmPlan
+    nl = min(layers, 4)
+    plans = [GemmPlan(w, l * K * Nr, K, Nr) for l in range(nl)]
+    x = torch.randn(T, K, device="cuda", dtype=torch.float32)
+    y = torch.empty(T, Nr, device="cuda", dtype=torch.float32)
+    st = torch.cuda.Stream()
+    prev = torch.cuda.current_stream()
+    torch.cuda.set_stream(st)
+    for pl in plans:   # sizes each plan's scratch before the capture
+        pl.run(y.data_ptr(), x.data_ptr(), T, st.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(iters):
+            plans[i % nl].run(y.data_ptr(), x.data_ptr(), T, torch.cuda.current_stream().cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    del g
+    torch.cuda.set_stream(prev)
+    for pl in plans:
+        pl.free()
+    eb, bb = C.TYPE_BLOCK[w.type]
+    return Nr * K // eb * bb, ms
+
+
 def matvec_sweep(models, cfg, peak):
-    """The quant-matvec half of the metric: HBM GB/s of the matvec kernel on
-    the decode shapes (W = N x K) for each weight type and batch 1 / 8."""
+    """The quant-matvec half of the metric on the decode shapes (W = N x K)
+    for each weight type: HBM GB/s of the matvec kernel at batch 1 / 8, and
+    the tcgen05 GEMM at 64 / 512 token vectors (weight GB/s and
+    TFLOP/s-equivalent of the fp32 product)."""
+    bf16_peak = measured_peaks(kind="bf16_tflops")[0]
     shapes = [("2048x2048 (wq)", C.W_Q, cfg.n_heads * cfg.head_size, cfg.dim, cfg.n_layers),
               ("6144x2048 (gate)", C.W_GATE, cfg.hidden_dim, cfg.dim, cfg.n_layers),
               ("2048x6144 (down)", C.W_DOWN, cfg.dim, cfg.hidden_dim, cfg.n_layers),
@@ -301,8 +345,15 @@ def matvec_sweep(models, cfg, peak):
             for batch in (1, 8):
                 alg, ms = time_matvec(w, K, Nr, layers, batch, iters=56 if layers > 1 else 16)
                 gbs = alg / (ms / 1000.0) / 1e9
-                out.append({"type": tname, "shape": name, "batch": batch, "GBps": round(gbs, 1),
+                out.append({"type": tname, "shape": name, "batch": batch, "path": "matvec", "GBps": round(gbs, 1),
                             "frac": round(gbs / peak, 4), "us": round(ms * 1000.0, 2)})
+            for T in (64, 512):
+                wb, ms = time_gemm(w, K, Nr, layers, T, iters=24 if layers > 1 else 8)
+                tflops = 2.0 * Nr * K * T / (ms / 1000.0) / 1e12
+                out.append({"type": tname, "shape": name, "batch": T, "path": "gemm",
+                            "GBps": round(wb / (ms / 1000.0) / 1e9, 1), "TFLOPs": round(tflops, 1),
+                            "tensor_frac": round(tflops / bf16_peak, 4) if bf16_peak else None,
+                            "us": round(ms * 1000.0, 2)})
     return out
 
 
@@ -585,7 +636,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt-len", type=int, default=None,
                     help=f"prompt tokens (default {PROMPT_LEN}; 256 with --tp)")
-    ap.add_argument("--cpu-tokens", type=int, default=48)
+    ap.add_argument("--cpu-tokens", type=int, default=224, help="decode tokens of the CPU-baseline sample (~13 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the matvec sweep")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill timing")

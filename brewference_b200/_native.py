@@ -98,6 +98,9 @@ def lib():
         "brew_matmul": (I, [c_f32p, c_f32p, V, I64, ctypes.c_int32, ctypes.c_int32]),
         "brew_matmul_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),
         "brew_gemm_q8_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),
+        "brew_gemm_plan_create": (I, [V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
+        "brew_gemm_plan_run": (I, [V, V, V, ctypes.c_int32, V]),
+        "brew_gemm_plan_free": (I, [V]),
         "brew_tp_rows": (I, [I64, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
         "brew_comm_unique_id": (I, [ctypes.c_char_p]),
         "brew_comm_init": (I, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),

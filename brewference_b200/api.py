@@ -136,6 +136,33 @@ class Linear:
                                         stream), "Linear.matmul_device")
 
 
+class GemmPlan:
+    """A Q8_0 / Q4_0 matrix repacked for the tcgen05 GEMM
+    (brew_gemm_plan_*): run() multiplies T token vectors at once."""
+
+    def __init__(self, weights: PackedTensor, weights_offset: int, input_size: int, output_size: int):
+        h = ctypes.c_void_p()
+        N.check(N.lib().brew_gemm_plan_create(weights.handle, weights_offset, input_size, output_size,
+                                              ctypes.byref(h)), "gemm_plan_create")
+        self.handle = h.value
+        self.input_size, self.output_size = input_size, output_size
+
+    def run(self, y_ptr: int, x_ptr: int, tokens: int, stream: int = 0) -> None:
+        """y [tokens][output_size] = W x for x [tokens][input_size] (device pointers)."""
+        N.check(N.lib().brew_gemm_plan_run(self.handle, y_ptr, x_ptr, tokens, stream or None), "gemm_plan_run")
+
+    def free(self):
+        if self.handle:
+            N.lib().brew_gemm_plan_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 def tp_rows(rows: int, nranks: int, rank: int):
     """Rows [r0, r1) of an N-row matrix that `rank` of `nranks` owns in the
     tensor-parallel forward."""

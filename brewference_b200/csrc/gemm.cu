@@ -191,7 +191,7 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
 // epilogue of column kb.
 __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* wq, const uint16_t* wd,
                                                                const int8_t* limbs, const float* scales, int N, int K,
-                                                               int T, float* y, unsigned int* err) {
+                                                               int T, int Tvalid, float* y, unsigned int* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
     uint64_t* empty = full + GEMM_STAGES;
@@ -334,10 +334,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
             }
         }
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
+        for (int p = 0; p < 8; ++p) {   // tokens past Tvalid are padding: not stored
             const float a0 = __uint_as_float((uint32_t)acc[p]), a1 = __uint_as_float((uint32_t)(acc[p] >> 32));
-            y[(int64_t)(t0 + 16 * hh + 2 * p) * N + row] = a0;
-            y[(int64_t)(t0 + 16 * hh + 2 * p + 1) * N + row] = a1;
+            const int tk = t0 + 16 * hh + 2 * p;
+            if (tk < Tvalid) y[(int64_t)tk * N + row] = a0;
+            if (tk + 1 < Tvalid) y[(int64_t)(tk + 1) * N + row] = a1;
         }
     }
     tc_fence_before();
@@ -376,7 +377,7 @@ int gemm_limbs_launch(const float* x, int ldx, int T, int Tp, int K, int8_t* lim
 }
 
 int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, const float* scales, int N, int K, int T,
-                   float* y, unsigned int* err, cudaStream_t stream) {
+                   int Tvalid, float* y, unsigned int* err, cudaStream_t stream) {
     BREW_CHECK(N % GEMM_TM == 0 && T % GEMM_TT == 0 && K % 32 == 0 && K > 0, BREW_ERR_INVALID_ARG,
                "gemm: N=%d (multiple of %d), T=%d (multiple of %d), K=%d (multiple of 32)", N, GEMM_TM, T, GEMM_TT, K);
     static uint64_t attr_devs = 0;   // devices whose attribute is set
@@ -387,7 +388,7 @@ int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, co
         attr_devs |= 1ull << dev;
     }
     gemm_q8_kernel<<<dim3(N / GEMM_TM, T / GEMM_TT), GEMM_THREADS, GEMM_SMEM, stream>>>(wq, wd, limbs, scales, N, K,
-                                                                                        T, y, err);
+                                                                                        T, Tvalid, y, err);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;
@@ -397,35 +398,117 @@ int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, co
 
 using namespace brew;
 
-extern "C" int brew_gemm_q8_dev(float* y, const float* x, brew_tensor w, int64_t off, int32_t K, int32_t N,
-                                int32_t T, void* stream) {
-    BREW_CHECK(y && x && w && w->d, BREW_ERR_INVALID_ARG, "null argument");
-    BREW_CHECK(w->type == BREW_TYPE_Q8_0, BREW_ERR_UNSUPPORTED, "the prefill GEMM takes Q8_0 weights");
+// A GEMM-layout copy of one Q8_0 / Q4_0 matrix and the activation scratch of
+// its runs.
+struct brew_gemm_plan_s {
+    int type = 0, K = 0, N = 0, device = -1;
+    int8_t* wq = nullptr;       // [N/128][K/32] quant tiles
+    uint16_t* wd = nullptr;     // [K/32][N] block scales
+    int8_t* limbs = nullptr;    // [K/32][cap/32][3072 B]
+    float* scales = nullptr;    // [K/32][cap]
+    int cap = 0;                // tokens the scratch holds (multiple of GEMM_TT)
+};
+
+namespace {
+
+void plan_release(brew_gemm_plan p) {
+    if (!p) return;
+    cudaFree(p->wq);
+    cudaFree(p->wd);
+    cudaFree(p->limbs);
+    cudaFree(p->scales);
+    delete p;
+}
+
+int plan_create(brew_tensor w, int64_t off, int K, int N, bool q8_only, brew_gemm_plan* out) {
+    BREW_CHECK(w && w->d && out, BREW_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    BREW_CHECK(w->type == BREW_TYPE_Q8_0 || (!q8_only && w->type == BREW_TYPE_Q4_0), BREW_ERR_UNSUPPORTED,
+               "the GEMM takes %s weights (type %d)", q8_only ? "Q8_0" : "Q8_0 or Q4_0", w->type);
     BREW_CHECK(K > 0 && K % 32 == 0 && off >= 0 && off % 32 == 0, BREW_ERR_INVALID_ARG, "K=%d off=%lld", K,
                (long long)off);
+    BREW_CHECK(N > 0 && N % GEMM_TM == 0, BREW_ERR_INVALID_ARG, "gemm: N=%d must be a multiple of %d", N, GEMM_TM);
     BREW_CHECK(off + (int64_t)N * K <= w->n, BREW_ERR_OUT_OF_BOUNDS, "matrix past the tensor end");
-    BREW_CHECK(N % GEMM_TM == 0 && T % GEMM_TT == 0 && T > 0, BREW_ERR_INVALID_ARG,
-               "gemm: N=%d must be a multiple of %d and T=%d of %d", N, GEMM_TM, T, GEMM_TT);
     int rc = ensure_init();
     if (rc) return rc;
+    brew_gemm_plan p = new brew_gemm_plan_s();
+    p->type = w->type;
+    p->K = K;
+    p->N = N;
+    p->device = ctx().device;
+    cudaStream_t s = ctx().stream;
+    const int bb = w->type == BREW_TYPE_Q8_0 ? 34 : 18;
+    if (cudaMalloc(&p->wq, (size_t)N * K) != cudaSuccess || cudaMalloc(&p->wd, (size_t)N * (K / 32) * 2) != cudaSuccess) {
+        plan_release(p);
+        return set_error(BREW_ERR_CUDA, "gemm plan: out of device memory");
+    }
+    rc = gemm_pack_launch(w->type, w->d + off / 32 * bb, N, K, p->wq, p->wd, N, 0, s);
+    if (!rc && cudaStreamSynchronize(s) != cudaSuccess) rc = set_error(BREW_ERR_CUDA, "gemm plan: pack failed");
+    if (rc) {
+        plan_release(p);
+        return rc;
+    }
+    *out = p;
+    return BREW_OK;
+}
+
+int plan_run(brew_gemm_plan p, float* y, const float* x, int T, cudaStream_t s) {
+    BREW_CHECK(p && y && x, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(T >= 1, BREW_ERR_INVALID_ARG, "gemm: T=%d", T);
+    BREW_CHECK(p->device == ctx().device, BREW_ERR_INVALID_ARG, "gemm plan of device %d used on device %d", p->device,
+               ctx().device);
+    const int Tp = (T + GEMM_TT - 1) / GEMM_TT * GEMM_TT, KB = p->K / 32;
+    if (Tp > p->cap) {   // the scratch grows to the largest T seen
+        cudaStreamSynchronize(s);
+        cudaFree(p->limbs);
+        cudaFree(p->scales);
+        p->limbs = nullptr;
+        p->scales = nullptr;
+        p->cap = 0;
+        BREW_CUDA(cudaMalloc(&p->limbs, (size_t)KB * 3 * Tp * 32));
+        BREW_CUDA(cudaMalloc(&p->scales, (size_t)KB * Tp * 4));
+        p->cap = Tp;
+    }
+    int rc = gemm_limbs_launch(x, p->K, T, Tp, p->K, p->limbs, p->scales, s);
+    if (!rc) rc = gemm_q8_launch(p->wq, p->wd, p->limbs, p->scales, p->N, p->K, Tp, T, y, ctx().err_word, s);
+    return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int brew_gemm_plan_create(brew_tensor w, int64_t off, int32_t K, int32_t N, brew_gemm_plan* out) {
     std::lock_guard<std::mutex> lk(api_mutex());
+    return plan_create(w, off, K, N, false, out);
+}
+
+int brew_gemm_plan_run(brew_gemm_plan p, float* y, const float* x, int32_t T, void* stream) {
+    std::lock_guard<std::mutex> lk(api_mutex());
+    return plan_run(p, y, x, T, static_cast<cudaStream_t>(stream));
+}
+
+int brew_gemm_plan_free(brew_gemm_plan p) {
+    std::lock_guard<std::mutex> lk(api_mutex());
+    if (p) cudaDeviceSynchronize();   // no run of this plan still in flight
+    plan_release(p);
+    return BREW_OK;
+}
+
+int brew_gemm_q8_dev(float* y, const float* x, brew_tensor w, int64_t off, int32_t K, int32_t N, int32_t T,
+                     void* stream) {
+    BREW_CHECK(y && x && w && w->d, BREW_ERR_INVALID_ARG, "null argument");
+    BREW_CHECK(T > 0, BREW_ERR_INVALID_ARG, "gemm: T=%d", T);
+    std::lock_guard<std::mutex> lk(api_mutex());
+    brew_gemm_plan p = nullptr;
+    int rc = plan_create(w, off, K, N, true, &p);
+    if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int KB = K / 32;
-    int8_t *wq = nullptr, *limbs = nullptr;
-    uint16_t* wd = nullptr;
-    float* sc = nullptr;
-    BREW_CUDA(cudaMalloc(&wq, (size_t)N * K));
-    BREW_CUDA(cudaMalloc(&wd, (size_t)N * KB * 2));
-    BREW_CUDA(cudaMalloc(&limbs, (size_t)KB * 3 * T * 32));
-    BREW_CUDA(cudaMalloc(&sc, (size_t)KB * T * 4));
-    rc = gemm_pack_launch(BREW_TYPE_Q8_0, w->d + off / 32 * 34, N, K, wq, wd, N, 0, s);
-    if (!rc) rc = gemm_limbs_launch(x, K, T, T, K, limbs, sc, s);
-    if (!rc) rc = gemm_q8_launch(wq, wd, limbs, sc, N, K, T, y, ctx().err_word, s);
+    rc = plan_run(p, y, x, T, s);
     cudaStreamSynchronize(s);
-    cudaFree(wq);
-    cudaFree(wd);
-    cudaFree(limbs);
-    cudaFree(sc);
+    plan_release(p);
     if (rc) return rc;
     return check_device_error("brew_gemm_q8_dev");
 }
+
+}  // extern "C"

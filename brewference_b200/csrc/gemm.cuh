@@ -36,8 +36,9 @@ int gemm_pack_launch(int type, const uint8_t* w, int rows, int K, int8_t* wq, ui
 // one token per row); tokens T .. Tp-1 are zero.
 int gemm_limbs_launch(const float* x, int ldx, int T, int Tp, int K, int8_t* limbs, float* scales,
                       cudaStream_t stream);
-// y [T][N] = W x (T a multiple of GEMM_TT, N of GEMM_TM, K of 32).
+// y [Tvalid][N] = W x (T the padded token count, a multiple of GEMM_TT; N a
+// multiple of GEMM_TM, K of 32; rows Tvalid .. T-1 are not written).
 int gemm_q8_launch(const int8_t* wq, const uint16_t* wd, const int8_t* limbs, const float* scales, int N, int K, int T,
-                   float* y, unsigned int* err, cudaStream_t stream);
+                   int Tvalid, float* y, unsigned int* err, cudaStream_t stream);
 
 }  // namespace brew

@@ -812,7 +812,7 @@ int prefill_batched(brew_model_s* m, const int32_t* tok_d, int n, cudaStream_t s
             int r = gemm_limbs_launch(x, ldx, T, Tp, K[f], m->pf_limbs, m->pf_lsc, s);
             if (!r)
                 r = gemm_q8_launch(m->pf_wq[f] + (int64_t)l * N[f] * K[f], m->pf_wd[f] + (int64_t)l * N[f] * (K[f] / 32),
-                                   m->pf_limbs, m->pf_lsc, N[f], K[f], Tp, y, err, s);
+                                   m->pf_limbs, m->pf_lsc, N[f], K[f], Tp, T, y, err, s);
             return r;
         };
         if ((rc = prefill_embed_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, tok_d + c0, T, gemma, m->pf_x,

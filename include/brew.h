@@ -176,13 +176,25 @@ BREW_API int brew_matmul_dev_static(float* output_dev, const float* input_dev, b
 
 /* Prefill GEMM on the tcgen05 tensor cores: output_dev [T][N] = W x for T
  * token vectors input_dev [T][K] at once (the prompt of ModelRunner.prefill,
- * runtime/ModelRunner.java:196-206, instead of T matvecs).  Q8_0 weights;
- * N a multiple of 128, T of 32.  Each 32-element block's integer dot product
- * is exact (24-bit limb split of x) and scaled by d_row * s_block in fp32,
- * as brew_matmul does per token. */
+ * runtime/ModelRunner.java:196-206, instead of T matvecs).  N a multiple of
+ * 128, any T >= 1.  Each 32-element block's integer dot product is exact
+ * (24-bit limb split of x) and scaled by d_row * s_block in fp32, as
+ * brew_matmul does per token.  No reference counterpart.
+ *
+ * brew_gemm_q8_dev: one call on a Q8_0 tensor (repacks the matrix, allocates
+ * scratch, synchronises).  A plan keeps the repacked matrix (Q8_0 or Q4_0)
+ * for repeated runs: brew_gemm_plan_run enqueues on `stream` without
+ * synchronising (its scratch grows, with an allocation, the first time a
+ * larger T is run); runs of one plan must not overlap. */
 BREW_API int brew_gemm_q8_dev(float* output_dev, const float* input_dev, brew_tensor weights,
                               int64_t weights_offset, int32_t input_size, int32_t output_size,
                               int32_t tokens, void* stream);
+typedef struct brew_gemm_plan_s* brew_gemm_plan;
+BREW_API int brew_gemm_plan_create(brew_tensor weights, int64_t weights_offset, int32_t input_size,
+                                   int32_t output_size, brew_gemm_plan* out);
+BREW_API int brew_gemm_plan_run(brew_gemm_plan plan, float* output_dev, const float* input_dev, int32_t tokens,
+                                void* stream);
+BREW_API int brew_gemm_plan_free(brew_gemm_plan plan);
 
 /* Two-step form for callers that multiply one input by several matrices
  * (Q, K and V share their input): brew_prepare_input_dev writes the
