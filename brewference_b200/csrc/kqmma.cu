@@ -1,6 +1,7 @@
 // kqmma.cu — K-quant matvec on the int8 tensor cores (layout in kqmma.cuh).
 #include "brew_internal.cuh"
 #include "kqmma.cuh"
+#include "matvec.cuh"
 #include "mv_device.cuh"
 #include "prep.cuh"
 
@@ -81,17 +82,17 @@ __global__ void kq_pack_kernel(const uint8_t* w, int64_t N, int K, uint8_t* out)
 }
 
 constexpr int KQM_WARPS = 8;
-constexpr int KQM_NG = 2;   // 16-row tiles per CTA
 
 // An int32 block sum |i| < 2^22 as a float, exactly, with full-rate adds
 // (the bits of 1.5 * 2^23 plus i are the float 1.5 * 2^23 + i).
 __device__ __forceinline__ float kq_i2f(int i) { return __int_as_float(i + 0x4B400000) - 12582912.0f; }
 
-// CTA = KQM_NG tiles (32 rows) x up to 2 NT vectors.  The 8 warps split the
+// CTA = NG 16-row tiles (2 for matrices of many tiles, 1 otherwise, so that
+// a 3584-row matrix still spreads over 224 CTAs) x up to 2 NT vectors.  The 8 warps split the
 // block columns (warp w takes kb = w, w + 8, ...), each keeping fp32
 // accumulators per limb column; at the end each warp combines its limbs,
 // the warps' sums meet in shared memory and 256 threads write the outputs.
-template <int TYPE, int NT>
+template <int TYPE, int NT, int KQM_NG>
 __global__ void __launch_bounds__(KQM_WARPS * 32, 2) kq_mma_kernel(const uint8_t* pk, int KB, int tiles, int N,
                                                                    const uint8_t* prep, int rec_bytes, int nv,
                                                                    float* y, int ldy) {
@@ -204,9 +205,12 @@ template <int TYPE, int NT>
 int kq_mma_launch_t(const uint8_t* packed, int64_t N, int K, const uint8_t* prep, int nv, float* y, int ldy,
                     cudaStream_t stream) {
     const int tiles = (int)((N + 15) / 16);
-    const int grid = (tiles + KQM_NG - 1) / KQM_NG;
-    kq_mma_kernel<TYPE, NT><<<grid, KQM_WARPS * 32, 0, stream>>>(packed, K / 32, tiles, (int)N, prep,
-                                                                 prep_rec_bytes(nv), nv, y, ldy);
+    if (tiles >= 4 * num_sms())
+        kq_mma_kernel<TYPE, NT, 2><<<(tiles + 1) / 2, KQM_WARPS * 32, 0, stream>>>(packed, K / 32, tiles, (int)N, prep,
+                                                                                  prep_rec_bytes(nv), nv, y, ldy);
+    else
+        kq_mma_kernel<TYPE, NT, 1><<<tiles, KQM_WARPS * 32, 0, stream>>>(packed, K / 32, tiles, (int)N, prep,
+                                                                        prep_rec_bytes(nv), nv, y, ldy);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;

@@ -94,6 +94,7 @@ struct brew_model_s {
     float *xn = nullptr, *hb2 = nullptr;    // normed input of a matvec; the up projection
     uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
     uint8_t* kqp[T_COUNT] = {};             // K-quant matrices repacked for the int8 MMA matvec (kqmma.cuh)
+    uint8_t* kqp_qkv = nullptr;             // ... Q, K and V of one type as one [q|k|v]-row family per layer
     // tensor parallelism (brew_model_set_tp): this rank's row slices
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
@@ -206,12 +207,32 @@ int alloc_unfused(brew_model_s* m) {
     if ((rc = dalloc(m, &m->xn, (size_t)B * std::max<int64_t>(qw, c.dim)))) return rc;
     if ((rc = dalloc(m, &m->hb2, (size_t)B * c.hidden_dim))) return rc;
     if ((rc = dalloc(m, &m->prep_any, (size_t)(kmax / 32) * prep_rec_bytes(std::min(B, MV_MAX_BATCH))))) return rc;
-    // the K-quant matrices, repacked once for the int8 MMA matvec
+    // the K-quant matrices, repacked once for the int8 MMA matvec; Q, K and
+    // V of one K-quant type as one family (rows q | k | v per layer), so that
+    // one launch multiplies all three
+    const int64_t kvd = (int64_t)c.n_kv_heads * c.head_size;
+    const bool kq_qkv = (c.type_q == BREW_TYPE_Q4_K || c.type_q == BREW_TYPE_Q6_K) && c.type_k == c.type_q &&
+                        c.type_v == c.type_q && qw % 16 == 0 && kvd % 16 == 0;
+    if (kq_qkv) {
+        const size_t pq = kq_packed_bytes(c.type_q, qw, c.dim), pkv = kq_packed_bytes(c.type_q, kvd, c.dim);
+        const size_t per = pq + 2 * pkv;
+        if ((rc = dalloc(m, &m->kqp_qkv, per * c.n_layers))) return rc;
+        for (int l = 0; l < c.n_layers; ++l) {
+            uint8_t* base = m->kqp_qkv + per * l;
+            if ((rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_Q], l, qw, c.dim), qw, c.dim, base, ctx().stream)) ||
+                (rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_K], l, kvd, c.dim), kvd, c.dim, base + pq,
+                                     ctx().stream)) ||
+                (rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_V], l, kvd, c.dim), kvd, c.dim, base + pq + pkv,
+                                     ctx().stream)))
+                return rc;
+        }
+    }
     for (int which = T_OUTPUT; which < T_COUNT; ++which) {
         int64_t rows, cols;
         int type, layers;
         matrix_shape(c, which, &rows, &cols, &type, &layers);
         if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
+        if (kq_qkv && (which == T_Q || which == T_K || which == T_V)) continue;
         const size_t per = kq_packed_bytes(type, rows, cols);
         if ((rc = dalloc(m, &m->kqp[which], per * layers))) return rc;
         for (int l = 0; l < layers; ++l)
@@ -316,21 +337,40 @@ int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx,
 // y[b][0:n] = rows row0 .. row0+n-1 of matrix `which` (layer l, rows x K)
 // times x[b]: the int8 MMA matvec on the repacked tiles for K-quant
 // matrices (row0 on a 16-row tile), mv_any on the GGUF rows otherwise.
+// The repacked tiles of rows row0.. of matrix `which` (layer l, rows x K),
+// or null when the matrix has none or row0 is not on a 16-row tile.
+const uint8_t* kq_tiles(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0) {
+    if (row0 % 16) return nullptr;
+    const brew_config& c = m->c;
+    const int type = m->t[which]->type;
+    const size_t tb = (size_t)(K / 32) * kq_tile_bytes(type);   // one 16-row tile
+    if (m->kqp_qkv && (which == T_Q || which == T_K || which == T_V)) {
+        const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
+        const int64_t frow = (which == T_Q ? 0 : which == T_K ? qw : qw + kvd) + row0;   // row in the q|k|v family
+        return m->kqp_qkv + (size_t)l * kq_packed_bytes(type, qw + 2 * kvd, K) + (size_t)(frow / 16) * tb;
+    }
+    if (!m->kqp[which]) return nullptr;
+    return m->kqp[which] + (size_t)l * kq_packed_bytes(type, rows, K) + (size_t)(row0 / 16) * tb;
+}
+
+// y[b][0:n] = the n rows of packed tiles `pk` times x[b], in groups of
+// MV_MAX_BATCH vectors (the limb records of a group, then the MMA matvec).
+int kq_run(brew_model_s* m, int type, const uint8_t* pk, int n, int K, const float* x, int ldx, float* y, int ldy, int B,
+           cudaStream_t s) {
+    for (int b0 = 0; b0 < B; b0 += MV_MAX_BATCH) {
+        const int nb = std::min(MV_MAX_BATCH, B - b0);
+        int rc = prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, nullptr, 0.0f, m->prep_any, s, false);
+        if (!rc) rc = kq_mma_launch(type, pk, n, K, m->prep_any, nb, y + (int64_t)b0 * ldy, ldy, s);
+        if (rc) return rc;
+    }
+    return BREW_OK;
+}
+
 int mv_w(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0, int n, const float* x, int ldx, float* y,
          int ldy, int B, cudaStream_t s) {
     brew_tensor t = m->t[which];
     const int type = t->type;
-    if (m->kqp[which] && row0 % 16 == 0) {
-        const uint8_t* pk = m->kqp[which] + (size_t)l * kq_packed_bytes(type, rows, K) +
-                            (size_t)(row0 / 16) * (K / 32) * kq_tile_bytes(type);
-        for (int b0 = 0; b0 < B; b0 += MV_MAX_BATCH) {
-            const int nb = std::min(MV_MAX_BATCH, B - b0);
-            int rc = prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, nullptr, 0.0f, m->prep_any, s, false);
-            if (!rc) rc = kq_mma_launch(type, pk, n, K, m->prep_any, nb, y + (int64_t)b0 * ldy, ldy, s);
-            if (rc) return rc;
-        }
-        return BREW_OK;
-    }
+    if (const uint8_t* pk = kq_tiles(m, which, l, rows, K, row0)) return kq_run(m, type, pk, n, K, x, ldx, y, ldy, B, s);
     return mv_any(m, type, layer_ptr(t, l, rows, K) + row0 * row_bytes_of(type, K), x, ldx, K, n, y, ldy, B, s);
 }
 
@@ -365,9 +405,13 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         float* k = m->qkv + qw;
         float* v = m->qkv + qw + kvd;
         if (P == 1) {
-            if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s)) ||
-                (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s)) ||
-                (rc = mv_w(m, T_V, l, kvd, dim, 0, kvd, m->xn, dim, v, m->qkvw, B, s)))
+            if (m->kqp_qkv) {   // q | k | v in one launch per vector group
+                if ((rc = kq_run(m, c.type_q, kq_tiles(m, T_Q, l, qw, dim, 0), m->qkvw, dim, m->xn, dim, q, m->qkvw, B,
+                                 s)))
+                    return rc;
+            } else if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s)) ||
+                       (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s)) ||
+                       (rc = mv_w(m, T_V, l, kvd, dim, 0, kvd, m->xn, dim, v, m->qkvw, B, s)))
                 return rc;
             if (m->q_bias &&
                 ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
