@@ -83,6 +83,14 @@ __global__ void kq_pack_kernel(const uint8_t* w, int64_t N, int K, uint8_t* out)
 
 constexpr int KQM_WARPS = 8;
 
+// int8 MMA over 16 of the block's 32 elements (one Q6_K scale's half):
+// a0 / a1 hold rows g / g + 8, k = 4t .. 4t + 3; b holds k = 4t .. 4t + 3.
+__device__ __forceinline__ void mma_s8s8_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
 // An int32 block sum |i| < 2^22 as a float, exactly, with full-rate adds
 // (the bits of 1.5 * 2^23 plus i are the float 1.5 * 2^23 + i).
 __device__ __forceinline__ float kq_i2f(int i) { return __int_as_float(i + 0x4B400000) - 12582912.0f; }
@@ -162,8 +170,8 @@ __global__ void __launch_bounds__(KQM_WARPS * 32, 2) kq_mma_kernel(const uint8_t
 #pragma unroll
                     for (int n = 0; n < NT; ++n) {
                         int cl[4], ch[4];
-                        mma_s8s8(cl, A.x, A.y, 0u, 0u, b0[n], b1[n]);   // k 0..15
-                        mma_s8s8(ch, 0u, 0u, A.z, A.w, b0[n], b1[n]);   // k 16..31
+                        mma_s8s8_k16(cl, A.x, A.y, b0[n]);   // k 0..15
+                        mma_s8s8_k16(ch, A.z, A.w, b1[n]);   // k 16..31
                         // s * (D_lo * sum_lo + D_hi * sum_hi); rows g (f.x, f.y), g + 8 (f.z, f.w)
                         acc[a][n][0] = fmaf(s[n], fmaf(f.y, kq_i2f(ch[0]), f.x * kq_i2f(cl[0])), acc[a][n][0]);
                         acc[a][n][1] = fmaf(s[n], fmaf(f.y, kq_i2f(ch[1]), f.x * kq_i2f(cl[1])), acc[a][n][1]);

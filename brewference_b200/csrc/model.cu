@@ -95,6 +95,8 @@ struct brew_model_s {
     uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
     uint8_t* kqp[T_COUNT] = {};             // K-quant matrices repacked for the int8 MMA matvec (kqmma.cuh)
     uint8_t* kqp_qkv = nullptr;             // ... Q, K and V of one type as one [q|k|v]-row family per layer
+    uint8_t* kqp_gu = nullptr;              // ... gate and up of one type as one [gate|up]-row family per layer
+    float* hgu = nullptr;                   // [batch][2 * hidden]: gate | up outputs of that family
     // tensor parallelism (brew_model_set_tp): this rank's row slices
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
@@ -227,12 +229,30 @@ int alloc_unfused(brew_model_s* m) {
                 return rc;
         }
     }
+    // gate and up likewise (rows gate | up), their outputs side by side
+    const int64_t hid = c.hidden_dim;
+    const bool kq_gu = (c.type_gate == BREW_TYPE_Q4_K || c.type_gate == BREW_TYPE_Q6_K) && c.type_up == c.type_gate &&
+                       hid % 16 == 0;
+    if (kq_gu) {
+        const size_t ph = kq_packed_bytes(c.type_gate, hid, c.dim);
+        if ((rc = dalloc(m, &m->kqp_gu, 2 * ph * c.n_layers)) || (rc = dalloc(m, &m->hgu, (size_t)B * 2 * hid)))
+            return rc;
+        for (int l = 0; l < c.n_layers; ++l) {
+            uint8_t* base = m->kqp_gu + 2 * ph * l;
+            if ((rc = kq_pack_launch(c.type_gate, layer_ptr(m->t[T_GATE], l, hid, c.dim), hid, c.dim, base,
+                                     ctx().stream)) ||
+                (rc = kq_pack_launch(c.type_gate, layer_ptr(m->t[T_UP], l, hid, c.dim), hid, c.dim, base + ph,
+                                     ctx().stream)))
+                return rc;
+        }
+    }
     for (int which = T_OUTPUT; which < T_COUNT; ++which) {
         int64_t rows, cols;
         int type, layers;
         matrix_shape(c, which, &rows, &cols, &type, &layers);
         if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
         if (kq_qkv && (which == T_Q || which == T_K || which == T_V)) continue;
+        if (kq_gu && (which == T_GATE || which == T_UP)) continue;
         const size_t per = kq_packed_bytes(type, rows, cols);
         if ((rc = dalloc(m, &m->kqp[which], per * layers))) return rc;
         for (int l = 0; l < layers; ++l)
@@ -348,6 +368,10 @@ const uint8_t* kq_tiles(brew_model_s* m, int which, int l, int64_t rows, int K, 
         const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
         const int64_t frow = (which == T_Q ? 0 : which == T_K ? qw : qw + kvd) + row0;   // row in the q|k|v family
         return m->kqp_qkv + (size_t)l * kq_packed_bytes(type, qw + 2 * kvd, K) + (size_t)(frow / 16) * tb;
+    }
+    if (m->kqp_gu && (which == T_GATE || which == T_UP)) {
+        const int64_t hid = c.hidden_dim, frow = (which == T_GATE ? 0 : hid) + row0;   // row in the gate|up family
+        return m->kqp_gu + (size_t)l * kq_packed_bytes(type, 2 * hid, K) + (size_t)(frow / 16) * tb;
     }
     if (!m->kqp[which]) return nullptr;
     return m->kqp[which] + (size_t)l * kq_packed_bytes(type, rows, K) + (size_t)(row0 / 16) * tb;
@@ -485,7 +509,14 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                                   dim, B, s)) ||
             (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)))
             return rc;
-        if (P == 1) {
+        if (P == 1 && m->kqp_gu) {
+            // gate | up in one launch per vector group; GLU into the gate half
+            if ((rc = kq_run(m, c.type_gate, kq_tiles(m, T_GATE, l, hid, dim, 0), 2 * hid, dim, m->xn, dim, m->hgu,
+                             2 * hid, B, s)) ||
+                (rc = glu_launch(m->hgu, m->hgu, m->hgu + hid, 2 * hid, hid, B, gemma, s)) ||
+                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hgu, 2 * hid, m->xb2, dim, B, s)))
+                return rc;
+        } else if (P == 1) {
             if ((rc = mv_w(m, T_GATE, l, hid, dim, 0, hid, m->xn, dim, m->hb, hid, B, s)) ||
                 (rc = mv_w(m, T_UP, l, hid, dim, 0, hid, m->xn, dim, m->hb2, hid, B, s)) ||
                 (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
