@@ -97,6 +97,10 @@ struct brew_model_s {
     uint8_t* kqp_qkv = nullptr;             // ... Q, K and V of one type as one [q|k|v]-row family per layer
     uint8_t* kqp_gu = nullptr;              // ... gate and up of one type as one [gate|up]-row family per layer
     float* hgu = nullptr;                   // [batch][2 * hidden]: gate | up outputs of that family
+    uint8_t* kq_rec = nullptr;              // x records of a K-quant matvec (kqmma.cuh)
+    float* kq_part = nullptr;               // its split-K partial sums
+    int* kq_ctr = nullptr;                  // and their arrival counters
+    size_t kq_nctr = 0;
     // tensor parallelism (brew_model_set_tp): this rank's row slices
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
@@ -198,6 +202,21 @@ void matrix_shape(const brew_config& c, int which, int64_t* rows, int64_t* cols,
 
 const uint8_t* layer_ptr(brew_tensor t, int layer, int64_t rows, int64_t cols);
 
+// Rows of the family a K-quant matrix is multiplied with at one GPU (q|k|v,
+// gate|up, or the matrix itself): its split-K count derives from this, so
+// a sharded launch sums each row in the one-GPU order.
+int64_t kq_basis(const brew_model_s* m, int which, int64_t rows) {
+    const brew_config& c = m->c;
+    const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
+    const int tq = c.type_q, tg = c.type_gate;
+    const bool kq_qkv = (tq == BREW_TYPE_Q4_K || tq == BREW_TYPE_Q6_K) && c.type_k == tq && c.type_v == tq &&
+                        qw % 16 == 0 && kvd % 16 == 0;
+    const bool kq_gu = (tg == BREW_TYPE_Q4_K || tg == BREW_TYPE_Q6_K) && c.type_up == tg && c.hidden_dim % 16 == 0;
+    if (kq_qkv && (which == T_Q || which == T_K || which == T_V)) return qw + 2 * kvd;
+    if (kq_gu && (which == T_GATE || which == T_UP)) return 2 * (int64_t)c.hidden_dim;
+    return rows;
+}
+
 // Buffers of the unfused forward (K-quant models, tensor parallelism).
 int alloc_unfused(brew_model_s* m) {
     if (m->unfused) return BREW_OK;
@@ -245,6 +264,27 @@ int alloc_unfused(brew_model_s* m) {
                                      ctx().stream)))
                 return rc;
         }
+    }
+    // scratch of the K-quant matvecs: x records, and the split-K partial
+    // sums of the largest launch (kq_basis gives each matrix's split)
+    size_t kq_part = 0, kq_ctr = 0;
+    bool any_kq = false;
+    for (int which = T_OUTPUT; which < T_COUNT; ++which) {
+        int64_t rows, cols;
+        int type, layers;
+        matrix_shape(c, which, &rows, &cols, &type, &layers);
+        if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
+        any_kq = true;
+        const int64_t basis = kq_basis(m, which, rows);
+        kq_part = std::max(kq_part, kq_part_floats(kq_splits(cols, basis), basis));
+        kq_ctr = std::max(kq_ctr, kq_counters(basis));
+    }
+    if (any_kq) {
+        if ((rc = dalloc(m, &m->kq_rec, kq_rec_bytes(std::min(B, KQ_MAX_VECTORS), kmax))) ||
+            (rc = dalloc(m, &m->kq_part, std::max<size_t>(kq_part, 1))) ||
+            (rc = dalloc(m, &m->kq_ctr, std::max<size_t>(kq_ctr, 1))))
+            return rc;
+        m->kq_nctr = std::max<size_t>(kq_ctr, 1);
     }
     for (int which = T_OUTPUT; which < T_COUNT; ++which) {
         int64_t rows, cols;
@@ -363,7 +403,7 @@ const uint8_t* kq_tiles(brew_model_s* m, int which, int l, int64_t rows, int K, 
     if (row0 % 16) return nullptr;
     const brew_config& c = m->c;
     const int type = m->t[which]->type;
-    const size_t tb = (size_t)(K / 32) * kq_tile_bytes(type);   // one 16-row tile
+    const size_t tb = kq_tile_bytes(type, K);   // one 16-row tile
     if (m->kqp_qkv && (which == T_Q || which == T_K || which == T_V)) {
         const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
         const int64_t frow = (which == T_Q ? 0 : which == T_K ? qw : qw + kvd) + row0;   // row in the q|k|v family
@@ -378,13 +418,17 @@ const uint8_t* kq_tiles(brew_model_s* m, int which, int l, int64_t rows, int K, 
 }
 
 // y[b][0:n] = the n rows of packed tiles `pk` times x[b], in groups of
-// MV_MAX_BATCH vectors (the limb records of a group, then the MMA matvec).
-int kq_run(brew_model_s* m, int type, const uint8_t* pk, int n, int K, const float* x, int ldx, float* y, int ldy, int B,
-           cudaStream_t s) {
-    for (int b0 = 0; b0 < B; b0 += MV_MAX_BATCH) {
-        const int nb = std::min(MV_MAX_BATCH, B - b0);
-        int rc = prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, nullptr, 0.0f, m->prep_any, s, false);
-        if (!rc) rc = kq_mma_launch(type, pk, n, K, m->prep_any, nb, y + (int64_t)b0 * ldy, ldy, s);
+// KQ_MAX_VECTORS vectors (the x records of a group, then the MMA matvec);
+// `basis`: the rows of the matrix's family (kq_basis).
+int kq_run(brew_model_s* m, int type, const uint8_t* pk, int n, int64_t basis, int K, const float* x, int ldx, float* y,
+           int ldy, int B, cudaStream_t s) {
+    const int splits = kq_splits(K, basis);
+    for (int b0 = 0; b0 < B; b0 += KQ_MAX_VECTORS) {
+        const int nb = std::min(KQ_MAX_VECTORS, B - b0);
+        int rc = kq_prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, m->kq_rec, s);
+        if (!rc)
+            rc = kq_mma_launch(type, pk, n, K, m->kq_rec, nb, splits, m->kq_part, m->kq_ctr, y + (int64_t)b0 * ldy, ldy,
+                               ctx().err_word, s);
         if (rc) return rc;
     }
     return BREW_OK;
@@ -394,7 +438,8 @@ int mv_w(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0, i
          int ldy, int B, cudaStream_t s) {
     brew_tensor t = m->t[which];
     const int type = t->type;
-    if (const uint8_t* pk = kq_tiles(m, which, l, rows, K, row0)) return kq_run(m, type, pk, n, K, x, ldx, y, ldy, B, s);
+    if (const uint8_t* pk = kq_tiles(m, which, l, rows, K, row0))
+        return kq_run(m, type, pk, n, kq_basis(m, which, rows), K, x, ldx, y, ldy, B, s);
     return mv_any(m, type, layer_ptr(t, l, rows, K) + row0 * row_bytes_of(type, K), x, ldx, K, n, y, ldy, B, s);
 }
 
@@ -430,8 +475,8 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         float* v = m->qkv + qw + kvd;
         if (P == 1) {
             if (m->kqp_qkv) {   // q | k | v in one launch per vector group
-                if ((rc = kq_run(m, c.type_q, kq_tiles(m, T_Q, l, qw, dim, 0), m->qkvw, dim, m->xn, dim, q, m->qkvw, B,
-                                 s)))
+                if ((rc = kq_run(m, c.type_q, kq_tiles(m, T_Q, l, qw, dim, 0), m->qkvw, qw + 2 * kvd, dim, m->xn, dim,
+                                 q, m->qkvw, B, s)))
                     return rc;
             } else if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s)) ||
                        (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s)) ||
@@ -511,8 +556,8 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             return rc;
         if (P == 1 && m->kqp_gu) {
             // gate | up in one launch per vector group; GLU into the gate half
-            if ((rc = kq_run(m, c.type_gate, kq_tiles(m, T_GATE, l, hid, dim, 0), 2 * hid, dim, m->xn, dim, m->hgu,
-                             2 * hid, B, s)) ||
+            if ((rc = kq_run(m, c.type_gate, kq_tiles(m, T_GATE, l, hid, dim, 0), 2 * hid, 2 * (int64_t)hid, dim,
+                             m->xn, dim, m->hgu, 2 * hid, B, s)) ||
                 (rc = glu_launch(m->hgu, m->hgu, m->hgu + hid, 2 * hid, hid, B, gemma, s)) ||
                 (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hgu, 2 * hid, m->xb2, dim, B, s)))
                 return rc;
@@ -1123,6 +1168,10 @@ int launch_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s)
 // inconsistent: clear them (and the abort flag) so the next step starts clean.
 int after_step_check(brew_model_s* m, const char* where) {
     const int rc = check_device_error(where);
+    if (rc && m->kq_ctr) {   // a K-quant matvec that stopped early may leave split counters raised
+        cudaMemset(m->kq_ctr, 0, m->kq_nctr * sizeof(int));
+        cudaDeviceSynchronize();
+    }
     if (rc && m->use_decode) {
         cudaMemset(m->bar, 0, 2 * sizeof(unsigned long long));
         cudaMemset(m->abort_flag, 0, sizeof(int));
