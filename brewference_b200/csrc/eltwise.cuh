@@ -21,4 +21,17 @@ int residual_launch(float* x, int ldx, const float* t, int ldt, const float* nor
 // geGlu, transformer/ffn/FfnActivation.java:23-58).
 int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s);
 
+// The residual of the previous sub-layer, the RMSNorm of the next, and the
+// next matvec's x records, in one kernel (one CTA of 1024 threads per
+// vector): with t, x[b] += t[b] (or + rmsnorm(t[b], post_w) with post_w) as
+// residual_launch; then out[b] = rmsnorm(x[b], w) as rmsnorm_launch (the
+// same operations, the sums of squares split over 1024 threads); then, with
+// rec, the records of out for a tcgen05 K-quant matvec (kqtc.cuh) of the B
+// vectors.
+int norm_prep_launch(float* x, int ldx, const float* t, int ldt, const float* post_w, const float* w, float eps, int K,
+                     int B, float* out, int ldo, uint8_t* rec, cudaStream_t s);
+// glu_launch, then (with rec) the records of hb for a tcgen05 K-quant matvec.
+int glu_prep_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, uint8_t* rec,
+                    cudaStream_t s);
+
 }  // namespace brew

@@ -2,99 +2,10 @@
 #include "brew_internal.cuh"
 #include "gemm.cuh"
 #include "prep.cuh"
+#include "tc_device.cuh"
 
 namespace brew {
 namespace {
-
-// ---- tcgen05 helpers (PTX forms as in CUTLASS's sm100 MMA / TMEM atoms) ----
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of
-// 8 rows x 16 bytes (128 contiguous bytes), the two 16-byte K halves of a
-// 32-byte block `lbo` bytes apart, groups of 8 rows `sbo` bytes apart.
-__device__ __forceinline__ uint64_t umma_desc_k(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;   // descriptor version of sm_100
-    return d;                  // base offset 0, layout type 0 (no swizzle)
-}
-
-// Instruction descriptor of kind::i8: D s32, A s8, B s8, both K-major.
-constexpr uint32_t umma_idesc_s8(int M, int N) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// tcgen05.st of one 32-bit constant to 16 / 8 columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t c) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1};" ::"r"(taddr),
-        "r"(c)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_st8_const(uint32_t taddr, uint32_t c) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(c)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// Packed fp32 pairs (sm_100 f32x2 arithmetic): each half is an ordinary
-// IEEE fp32 operation with round-to-nearest, two per instruction.
-__device__ __forceinline__ uint64_t f2_pack(uint32_t lo, uint32_t hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_packf(float lo, float hi) {
-    return f2_pack(__float_as_uint(lo), __float_as_uint(hi));
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-
-// The int32 accumulators start at the bits of the float 1.5 * 2^23 instead
-// of 0: the MMA adds the block's limb sum i (|i| <= 2^19) to it, and the
-// result's bits are the float 1.5 * 2^23 + i, exactly (the well-known
-// magic-number conversion).  Subtracting 1.5 * 2^23 gives i as a float.
-constexpr uint32_t GEMM_MAGIC = 0x4B400000u;
-constexpr float GEMM_MAGIC_F = 12582912.0f;
 
 constexpr int GEMM_N = 3 * GEMM_TT;        // limb columns per tile (96)
 constexpr int GEMM_STAGES = 4;             // shared-memory ring
@@ -117,13 +28,6 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, unsign
     return mbar_wait_bounded(bar, parity, err, code);
 }
 
-// Byte offset of quant j (0..31) of row r (0..127) inside a 4096-byte
-// block-column tile: the K-major core-matrix layout the MMA's shared-memory
-// descriptor reads (8-row groups of 256 B, the two 16-byte K halves 128 B
-// apart), so a stage is one contiguous copy.
-__host__ __device__ __forceinline__ int gemm_tile_off(int r, int j) {
-    return (r >> 3) * 256 + (j >> 4) * 128 + (r & 7) * 16 + (j & 15);
-}
 
 // Q8_0 blocks (34 B: fp16 d, 32 int8 q) or Q4_0 blocks (18 B: fp16 d, 32
 // nibbles, value d * (q - 8)): the integer factors q (Q8_0) or q - 8 (Q4_0)
@@ -143,7 +47,7 @@ __global__ void gemm_pack_kernel(const uint8_t* w, int rows, int K, int8_t* wq, 
 #pragma unroll 8
     for (int j = 0; j < 32; ++j) {
         const int q = TYPE == BREW_TYPE_Q8_0 ? (int)(int8_t)b[2 + j] : (j < 16 ? (b[2 + j] & 15) : (b[2 + j - 16] >> 4)) - 8;
-        tile[gemm_tile_off(r, j)] = (int8_t)q;
+        tile[tc_tile_off(r, j)] = (int8_t)q;
     }
 }
 
@@ -167,9 +71,9 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
     // both tokens of a pair from adjacent tensor-memory columns
     int8_t* tile = limbs + (int64_t)kb * 3 * Tp * 32 + (int64_t)(t >> 5) * 3072;
     const int c0 = 6 * ((t & 31) >> 1) + (t & 1);
-    tile[gemm_tile_off(c0, lane)] = (int8_t)hi;
-    tile[gemm_tile_off(c0 + 2, lane)] = (int8_t)mid;
-    tile[gemm_tile_off(c0 + 4, lane)] = (int8_t)lo;
+    tile[tc_tile_off(c0, lane)] = (int8_t)hi;
+    tile[tc_tile_off(c0 + 2, lane)] = (int8_t)mid;
+    tile[tc_tile_off(c0 + 4, lane)] = (int8_t)lo;
     if (lane == 0) scales[(int64_t)kb * Tp + t] = amax / PREP_RANGE;
 }
 
@@ -177,7 +81,7 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
 //   warp 0      one lane loads block column kb (A: 128 rows x 32 B, B: 96
 //               limb columns x 32 B) into ring stage kb % 4: two bulk copies,
 //               since both are stored in the K-major core-matrix layout
-//               (gemm_tile_off) already; all 4 stages can be in flight;
+//               (tc_tile_off) already; all 4 stages can be in flight;
 //   warp 1      one thread issues tcgen05.mma for block column kb into tensor-
 //               memory buffer kb % 2 (each column needs its own product: the
 //               block scales differ per column) and commits to the stage's
@@ -267,7 +171,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
 #pragma unroll
         for (int b = 0; b < 2; ++b)
 #pragma unroll
-            for (int c = 0; c < 3; ++c) tmem_st16_const(tq + b * 128 + 16 * c, GEMM_MAGIC);
+            for (int c = 0; c < 3; ++c) tmem_st16_const(tq + b * 128 + 16 * c, TC_MAGIC);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -278,7 +182,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
         uint64_t acc[8];   // token pairs (2p, 2p + 1)
 #pragma unroll
         for (int p = 0; p < 8; ++p) acc[p] = 0ull;
-        const uint64_t negc = f2_packf(-GEMM_MAGIC_F, -GEMM_MAGIC_F);
+        const uint64_t negc = f2_packf(-TC_MAGIC_F, -TC_MAGIC_F);
         const uint64_t k256 = f2_packf(256.0f, 256.0f), k65536 = f2_packf(65536.0f, 65536.0f);
         // this column's weight scale and token scales, loaded one column ahead
         uint16_t dbits = wd[row];
@@ -304,8 +208,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
                 tmem_ld8(ta + 8, v + 8);
                 tmem_ld8(ta + 16, v + 16);
                 tmem_ld_wait();
-                tmem_st16_const(ta, GEMM_MAGIC);
-                tmem_st8_const(ta + 16, GEMM_MAGIC);
+                tmem_st16_const(ta, TC_MAGIC);
+                tmem_st8_const(ta + 16, TC_MAGIC);
                 if (e == 1) {
                     tmem_st_wait();
                     tc_fence_before();

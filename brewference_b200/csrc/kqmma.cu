@@ -422,11 +422,11 @@ int kq_mma_launch_t(const uint8_t* packed, int64_t N, int K, const uint8_t* rec,
 }  // namespace
 
 int kq_splits(int64_t K, int64_t n_basis) {
-    // about two CTAs per SM of a B200 (148 SMs) for the whole family, at
-    // least two super-blocks per split
-    constexpr int64_t target = 296;
+    // as many splits as keep the family's 128-row groups within one wave of
+    // one CTA per SM of a B200 (148 SMs), at least two super-blocks each
+    constexpr int64_t wave = 148;
     const int64_t groups = std::max<int64_t>(1, (n_basis + 127) / 128), ksb = K / 256;
-    int64_t s = (target + groups - 1) / groups;
+    int64_t s = wave / groups;
     s = std::min<int64_t>(s, std::max<int64_t>(1, ksb / 2));
     return (int)std::max<int64_t>(1, s);
 }

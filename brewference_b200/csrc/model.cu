@@ -20,6 +20,7 @@
 #include "eltwise.cuh"
 #include "gemm.cuh"
 #include "kqmma.cuh"
+#include "kqtc.cuh"
 #include "prefill.cuh"
 #include "tp.cuh"
 
@@ -93,11 +94,12 @@ struct brew_model_s {
     bool unfused = false;
     float *xn = nullptr, *hb2 = nullptr;    // normed input of a matvec; the up projection
     uint8_t* prep_any = nullptr;            // x records of a Q8_0 / Q4_0 matvec in that forward
-    uint8_t* kqp[T_COUNT] = {};             // K-quant matrices repacked for the int8 MMA matvec (kqmma.cuh)
+    uint8_t* kqp[T_COUNT] = {};             // K-quant matrices expanded for the tcgen05 matvec (kqtc.cuh)
     uint8_t* kqp_qkv = nullptr;             // ... Q, K and V of one type as one [q|k|v]-row family per layer
     uint8_t* kqp_gu = nullptr;              // ... gate and up of one type as one [gate|up]-row family per layer
     float* hgu = nullptr;                   // [batch][2 * hidden]: gate | up outputs of that family
-    uint8_t* kq_rec = nullptr;              // x records of a K-quant matvec (kqmma.cuh)
+    uint8_t* kq_rec = nullptr;              // x records of a K-quant matvec (kqtc.cuh)
+    float* qkv_bias = nullptr;              // [layers][q|k|v rows]: the biases indexed by q|k|v family row
     float* kq_part = nullptr;               // its split-K partial sums
     int* kq_ctr = nullptr;                  // and their arrival counters
     size_t kq_nctr = 0;
@@ -235,17 +237,29 @@ int alloc_unfused(brew_model_s* m) {
     const bool kq_qkv = (c.type_q == BREW_TYPE_Q4_K || c.type_q == BREW_TYPE_Q6_K) && c.type_k == c.type_q &&
                         c.type_v == c.type_q && qw % 16 == 0 && kvd % 16 == 0;
     if (kq_qkv) {
-        const size_t pq = kq_packed_bytes(c.type_q, qw, c.dim), pkv = kq_packed_bytes(c.type_q, kvd, c.dim);
-        const size_t per = pq + 2 * pkv;
+        const int64_t nf = qw + 2 * kvd;
+        const size_t per = kx_bytes(c.type_q, nf, c.dim);
         if ((rc = dalloc(m, &m->kqp_qkv, per * c.n_layers))) return rc;
         for (int l = 0; l < c.n_layers; ++l) {
             uint8_t* base = m->kqp_qkv + per * l;
-            if ((rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_Q], l, qw, c.dim), qw, c.dim, base, ctx().stream)) ||
-                (rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_K], l, kvd, c.dim), kvd, c.dim, base + pq,
+            if ((rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_Q], l, qw, c.dim), qw, c.dim, base, nf, 0,
                                      ctx().stream)) ||
-                (rc = kq_pack_launch(c.type_q, layer_ptr(m->t[T_V], l, kvd, c.dim), kvd, c.dim, base + pq + pkv,
+                (rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_K], l, kvd, c.dim), kvd, c.dim, base, nf, qw,
+                                     ctx().stream)) ||
+                (rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_V], l, kvd, c.dim), kvd, c.dim, base, nf, qw + kvd,
                                      ctx().stream)))
                 return rc;
+        }
+        if (m->q_bias) {   // the family launch adds the bias in its epilogue
+            BREW_CUDA(cudaDeviceSynchronize());
+            if ((rc = dalloc(m, &m->qkv_bias, (size_t)nf * c.n_layers))) return rc;
+            for (int l = 0; l < c.n_layers; ++l) {
+                float* fb = m->qkv_bias + (size_t)nf * l;
+                BREW_CUDA(cudaMemcpy(fb, m->q_bias + (size_t)qw * l, qw * sizeof(float), cudaMemcpyDeviceToDevice));
+                BREW_CUDA(cudaMemcpy(fb + qw, m->k_bias + (size_t)kvd * l, kvd * sizeof(float), cudaMemcpyDeviceToDevice));
+                BREW_CUDA(cudaMemcpy(fb + qw + kvd, m->v_bias + (size_t)kvd * l, kvd * sizeof(float),
+                                     cudaMemcpyDeviceToDevice));
+            }
         }
     }
     // gate and up likewise (rows gate | up), their outputs side by side
@@ -253,14 +267,14 @@ int alloc_unfused(brew_model_s* m) {
     const bool kq_gu = (c.type_gate == BREW_TYPE_Q4_K || c.type_gate == BREW_TYPE_Q6_K) && c.type_up == c.type_gate &&
                        hid % 16 == 0;
     if (kq_gu) {
-        const size_t ph = kq_packed_bytes(c.type_gate, hid, c.dim);
-        if ((rc = dalloc(m, &m->kqp_gu, 2 * ph * c.n_layers)) || (rc = dalloc(m, &m->hgu, (size_t)B * 2 * hid)))
+        const size_t per = kx_bytes(c.type_gate, 2 * hid, c.dim);
+        if ((rc = dalloc(m, &m->kqp_gu, per * c.n_layers)) || (rc = dalloc(m, &m->hgu, (size_t)B * 2 * hid)))
             return rc;
         for (int l = 0; l < c.n_layers; ++l) {
-            uint8_t* base = m->kqp_gu + 2 * ph * l;
-            if ((rc = kq_pack_launch(c.type_gate, layer_ptr(m->t[T_GATE], l, hid, c.dim), hid, c.dim, base,
+            uint8_t* base = m->kqp_gu + per * l;
+            if ((rc = kx_pack_launch(c.type_gate, layer_ptr(m->t[T_GATE], l, hid, c.dim), hid, c.dim, base, 2 * hid, 0,
                                      ctx().stream)) ||
-                (rc = kq_pack_launch(c.type_gate, layer_ptr(m->t[T_UP], l, hid, c.dim), hid, c.dim, base + ph,
+                (rc = kx_pack_launch(c.type_gate, layer_ptr(m->t[T_UP], l, hid, c.dim), hid, c.dim, base, 2 * hid, hid,
                                      ctx().stream)))
                 return rc;
         }
@@ -276,11 +290,12 @@ int alloc_unfused(brew_model_s* m) {
         if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
         any_kq = true;
         const int64_t basis = kq_basis(m, which, rows);
-        kq_part = std::max(kq_part, kq_part_floats(kq_splits(cols, basis), basis));
-        kq_ctr = std::max(kq_ctr, kq_counters(basis));
+        const int sp = kq_splits(cols, basis);
+        if (sp > 1) kq_part = std::max(kq_part, (size_t)sp * KX_MAX_VECTORS * (size_t)((basis + KX_TM - 1) / KX_TM * KX_TM));
+        kq_ctr = std::max(kq_ctr, (size_t)((basis + KX_TM - 1) / KX_TM));
     }
     if (any_kq) {
-        if ((rc = dalloc(m, &m->kq_rec, kq_rec_bytes(std::min(B, KQ_MAX_VECTORS), kmax))) ||
+        if ((rc = dalloc(m, &m->kq_rec, kx_rec_bytes(std::min(B, KX_MAX_VECTORS), kmax))) ||
             (rc = dalloc(m, &m->kq_part, std::max<size_t>(kq_part, 1))) ||
             (rc = dalloc(m, &m->kq_ctr, std::max<size_t>(kq_ctr, 1))))
             return rc;
@@ -293,11 +308,11 @@ int alloc_unfused(brew_model_s* m) {
         if (type != BREW_TYPE_Q4_K && type != BREW_TYPE_Q6_K) continue;
         if (kq_qkv && (which == T_Q || which == T_K || which == T_V)) continue;
         if (kq_gu && (which == T_GATE || which == T_UP)) continue;
-        const size_t per = kq_packed_bytes(type, rows, cols);
+        const size_t per = kx_bytes(type, rows, cols);
         if ((rc = dalloc(m, &m->kqp[which], per * layers))) return rc;
         for (int l = 0; l < layers; ++l)
-            if ((rc = kq_pack_launch(type, layer_ptr(m->t[which], l, rows, cols), rows, (int)cols, m->kqp[which] + per * l,
-                                     ctx().stream)))
+            if ((rc = kx_pack_launch(type, layer_ptr(m->t[which], l, rows, cols), rows, (int)cols, m->kqp[which] + per * l,
+                                     rows, 0, ctx().stream)))
                 return rc;
     }
     BREW_CUDA(cudaStreamSynchronize(ctx().stream));
@@ -394,52 +409,63 @@ int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx,
     return BREW_OK;
 }
 
-// y[b][0:n] = rows row0 .. row0+n-1 of matrix `which` (layer l, rows x K)
-// times x[b]: the int8 MMA matvec on the repacked tiles for K-quant
-// matrices (row0 on a 16-row tile), mv_any on the GGUF rows otherwise.
-// The repacked tiles of rows row0.. of matrix `which` (layer l, rows x K),
-// or null when the matrix has none or row0 is not on a 16-row tile.
-const uint8_t* kq_tiles(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0) {
-    if (row0 % 16) return nullptr;
+// The expanded copy holding rows row0.. of matrix `which` (layer l, rows x
+// K): the copy of its family (q|k|v, gate|up) or its own, with the rows'
+// offset in it; base null when the matrix has none.
+struct KxRef {
+    const uint8_t* base;
+    int64_t N, row0;
+};
+
+KxRef kx_ref(const brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0) {
     const brew_config& c = m->c;
     const int type = m->t[which]->type;
-    const size_t tb = kq_tile_bytes(type, K);   // one 16-row tile
     if (m->kqp_qkv && (which == T_Q || which == T_K || which == T_V)) {
-        const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size;
-        const int64_t frow = (which == T_Q ? 0 : which == T_K ? qw : qw + kvd) + row0;   // row in the q|k|v family
-        return m->kqp_qkv + (size_t)l * kq_packed_bytes(type, qw + 2 * kvd, K) + (size_t)(frow / 16) * tb;
+        const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size, nf = qw + 2 * kvd;
+        const int64_t off = which == T_Q ? 0 : which == T_K ? qw : qw + kvd;   // rows before it in the family
+        return {m->kqp_qkv + (size_t)l * kx_bytes(type, nf, K), nf, off + row0};
     }
     if (m->kqp_gu && (which == T_GATE || which == T_UP)) {
-        const int64_t hid = c.hidden_dim, frow = (which == T_GATE ? 0 : hid) + row0;   // row in the gate|up family
-        return m->kqp_gu + (size_t)l * kq_packed_bytes(type, 2 * hid, K) + (size_t)(frow / 16) * tb;
+        const int64_t hid = c.hidden_dim;
+        return {m->kqp_gu + (size_t)l * kx_bytes(type, 2 * hid, K), 2 * hid, (which == T_GATE ? 0 : hid) + row0};
     }
-    if (!m->kqp[which]) return nullptr;
-    return m->kqp[which] + (size_t)l * kq_packed_bytes(type, rows, K) + (size_t)(row0 / 16) * tb;
+    if (!m->kqp[which]) return {nullptr, 0, 0};
+    return {m->kqp[which] + (size_t)l * kx_bytes(type, rows, K), rows, row0};
 }
 
-// y[b][0:n] = the n rows of packed tiles `pk` times x[b], in groups of
-// KQ_MAX_VECTORS vectors (the x records of a group, then the MMA matvec);
-// `basis`: the rows of the matrix's family (kq_basis).
-int kq_run(brew_model_s* m, int type, const uint8_t* pk, int n, int64_t basis, int K, const float* x, int ldx, float* y,
-           int ldy, int B, cudaStream_t s) {
-    const int splits = kq_splits(K, basis);
-    for (int b0 = 0; b0 < B; b0 += KQ_MAX_VECTORS) {
-        const int nb = std::min(KQ_MAX_VECTORS, B - b0);
-        int rc = kq_prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, m->kq_rec, s);
+// y[b][0:n] = rows r.row0 .. r.row0 + n - 1 of the expanded copy r times
+// x[b] (+ the family-indexed bias), in groups of KX_MAX_VECTORS vectors
+// (the x records of a group, then the tcgen05 matvec); `rec`: the records
+// of all B <= KX_MAX_VECTORS vectors, made already by the kernel that
+// produced x.  The split of K follows the family's rows, so a sharded
+// launch sums each row as the one-GPU launch does.
+int kq_run(brew_model_s* m, int type, const KxRef& r, int n, int K, const float* x, int ldx, float* y, int ldy, int B,
+           cudaStream_t s, const uint8_t* rec = nullptr, const float* bias = nullptr) {
+    const int splits = kq_splits(K, r.N);
+    if (rec) {
+        BREW_CHECK(B <= KX_MAX_VECTORS, BREW_ERR_INVALID_ARG, "records of %d vectors", B);
+        return kx_mma_launch(type, r.base, r.N, r.row0, n, K, rec, B, splits, m->kq_part, m->kq_ctr, bias, y, ldy,
+                             ctx().err_word, s);
+    }
+    for (int b0 = 0; b0 < B; b0 += KX_MAX_VECTORS) {
+        const int nb = std::min(KX_MAX_VECTORS, B - b0);
+        int rc = kx_prep_launch(x + (int64_t)b0 * ldx, ldx, K, nb, m->kq_rec, s);
         if (!rc)
-            rc = kq_mma_launch(type, pk, n, K, m->kq_rec, nb, splits, m->kq_part, m->kq_ctr, y + (int64_t)b0 * ldy, ldy,
-                               ctx().err_word, s);
+            rc = kx_mma_launch(type, r.base, r.N, r.row0, n, K, m->kq_rec, nb, splits, m->kq_part, m->kq_ctr, bias,
+                               y + (int64_t)b0 * ldy, ldy, ctx().err_word, s);
         if (rc) return rc;
     }
     return BREW_OK;
 }
 
+// One matvec of the unfused forward; `rec` (records of x for a tcgen05
+// K-quant matvec, or null) is used when the matrix runs on that path.
 int mv_w(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0, int n, const float* x, int ldx, float* y,
-         int ldy, int B, cudaStream_t s) {
+         int ldy, int B, cudaStream_t s, const uint8_t* rec = nullptr) {
     brew_tensor t = m->t[which];
     const int type = t->type;
-    if (const uint8_t* pk = kq_tiles(m, which, l, rows, K, row0))
-        return kq_run(m, type, pk, n, kq_basis(m, which, rows), K, x, ldx, y, ldy, B, s);
+    const KxRef r = kx_ref(m, which, l, rows, K, row0);
+    if (r.base) return kq_run(m, type, r, n, K, x, ldx, y, ldy, B, s, rec);
     return mv_any(m, type, layer_ptr(t, l, rows, K) + row0 * row_bytes_of(type, K), x, ldx, K, n, y, ldy, B, s);
 }
 
@@ -468,21 +494,34 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
     if ((rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x,
                                 m->rms_att, c.eps, m->prep_x, err, s, false)))
         return rc;
+    // The x records of a tcgen05 K-quant matvec's input are made by the
+    // kernel that produces the input (norm_prep / glu_prep) when the next
+    // matvec runs on that path; the residual of each sub-layer is applied by
+    // the next norm_prep.
+    auto rec_for = [&](int which, int l, int64_t rows, int K) -> uint8_t* {
+        return B <= KX_MAX_VECTORS && kx_ref(m, which, l, rows, K, 0).base ? m->kq_rec : nullptr;
+    };
     for (int l = 0; l < L; ++l) {
-        if ((rc = rmsnorm_launch(m->x, dim, m->rms_att + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s))) return rc;
+        // the previous layer's FFN residual, then the attention RMSNorm
+        uint8_t* rq = rec_for(T_Q, l, qw, dim);
+        if ((rc = norm_prep_launch(m->x, dim, l ? m->xb2 : nullptr, dim,
+                                   gemma && l ? m->post_ffn + (int64_t)(l - 1) * dim : nullptr,
+                                   m->rms_att + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, rq, s)))
+            return rc;
         float* q = m->qkv;
         float* k = m->qkv + qw;
         float* v = m->qkv + qw + kvd;
         if (P == 1) {
-            if (m->kqp_qkv) {   // q | k | v in one launch per vector group
-                if ((rc = kq_run(m, c.type_q, kq_tiles(m, T_Q, l, qw, dim, 0), m->qkvw, qw + 2 * kvd, dim, m->xn, dim,
-                                 q, m->qkvw, B, s)))
+            if (m->kqp_qkv) {   // q | k | v in one launch per vector group, the bias in its epilogue
+                const float* fb = m->qkv_bias ? m->qkv_bias + (int64_t)l * (qw + 2 * kvd) : nullptr;
+                if ((rc = kq_run(m, c.type_q, kx_ref(m, T_Q, l, qw, dim, 0), m->qkvw, dim, m->xn, dim, q, m->qkvw, B,
+                                 s, rq, fb)))
                     return rc;
-            } else if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s)) ||
-                       (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s)) ||
-                       (rc = mv_w(m, T_V, l, kvd, dim, 0, kvd, m->xn, dim, v, m->qkvw, B, s)))
+            } else if ((rc = mv_w(m, T_Q, l, qw, dim, 0, qw, m->xn, dim, q, m->qkvw, B, s, rq)) ||
+                       (rc = mv_w(m, T_K, l, kvd, dim, 0, kvd, m->xn, dim, k, m->qkvw, B, s, rq)) ||
+                       (rc = mv_w(m, T_V, l, kvd, dim, 0, kvd, m->xn, dim, v, m->qkvw, B, s, rq)))
                 return rc;
-            if (m->q_bias &&
+            if (m->q_bias && !(m->kqp_qkv && m->qkv_bias) &&
                 ((rc = add_bias_launch(q, m->qkvw, m->q_bias + (int64_t)l * qw, qw, B, s)) ||
                  (rc = add_bias_launch(k, m->qkvw, m->k_bias + (int64_t)l * kvd, kvd, B, s)) ||
                  (rc = add_bias_launch(v, m->qkvw, m->v_bias + (int64_t)l * kvd, kvd, B, s))))
@@ -491,9 +530,9 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             // slices [q_R | k_R | v_R] per rank, gathered into q | k | v
             const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
             float* sq = m->tp_send;
-            if ((rc = mv_w(m, T_Q, l, qw, dim, (int64_t)R * qs, qs, m->xn, dim, sq, sl, B, s)) ||
-                (rc = mv_w(m, T_K, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs, sl, B, s)) ||
-                (rc = mv_w(m, T_V, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs + ks, sl, B, s)))
+            if ((rc = mv_w(m, T_Q, l, qw, dim, (int64_t)R * qs, qs, m->xn, dim, sq, sl, B, s, rq)) ||
+                (rc = mv_w(m, T_K, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs, sl, B, s, rq)) ||
+                (rc = mv_w(m, T_V, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs + ks, sl, B, s, rq)))
                 return rc;
             if (m->q_bias &&
                 ((rc = add_bias_launch(sq, sl, m->q_bias + (int64_t)l * qw + (int64_t)R * qs, qs, B, s)) ||
@@ -550,28 +589,30 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                 (rc = gather(dim / P, &seg, 1, m->xb2, dim)))
                 return rc;
         }
-        if ((rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr, c.eps,
-                                  dim, B, s)) ||
-            (rc = rmsnorm_launch(m->x, dim, m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, s)))
+        // the attention residual, then the FFN RMSNorm
+        uint8_t* rg = rec_for(T_GATE, l, hid, dim);
+        if ((rc = norm_prep_launch(m->x, dim, m->xb2, dim, gemma ? m->post_att + (int64_t)l * dim : nullptr,
+                                   m->rms_ffn + (int64_t)l * dim, c.eps, dim, B, m->xn, dim, rg, s)))
             return rc;
+        uint8_t* rd = rec_for(T_DOWN, l, dim, hid);
         if (P == 1 && m->kqp_gu) {
             // gate | up in one launch per vector group; GLU into the gate half
-            if ((rc = kq_run(m, c.type_gate, kq_tiles(m, T_GATE, l, hid, dim, 0), 2 * hid, 2 * (int64_t)hid, dim,
-                             m->xn, dim, m->hgu, 2 * hid, B, s)) ||
-                (rc = glu_launch(m->hgu, m->hgu, m->hgu + hid, 2 * hid, hid, B, gemma, s)) ||
-                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hgu, 2 * hid, m->xb2, dim, B, s)))
+            if ((rc = kq_run(m, c.type_gate, kx_ref(m, T_GATE, l, hid, dim, 0), 2 * hid, dim, m->xn, dim, m->hgu,
+                             2 * hid, B, s, rg)) ||
+                (rc = glu_prep_launch(m->hgu, m->hgu, m->hgu + hid, 2 * hid, hid, B, gemma, rd, s)) ||
+                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hgu, 2 * hid, m->xb2, dim, B, s, rd)))
                 return rc;
         } else if (P == 1) {
-            if ((rc = mv_w(m, T_GATE, l, hid, dim, 0, hid, m->xn, dim, m->hb, hid, B, s)) ||
-                (rc = mv_w(m, T_UP, l, hid, dim, 0, hid, m->xn, dim, m->hb2, hid, B, s)) ||
-                (rc = glu_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, s)) ||
-                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hb, hid, m->xb2, dim, B, s)))
+            if ((rc = mv_w(m, T_GATE, l, hid, dim, 0, hid, m->xn, dim, m->hb, hid, B, s, rg)) ||
+                (rc = mv_w(m, T_UP, l, hid, dim, 0, hid, m->xn, dim, m->hb2, hid, B, s, rg)) ||
+                (rc = glu_prep_launch(m->hb, m->hb, m->hb2, hid, hid, B, gemma, rd, s)) ||
+                (rc = mv_w(m, T_DOWN, l, dim, hid, 0, dim, m->hb, hid, m->xb2, dim, B, s, rd)))
                 return rc;
         } else {
             const int hs = hid / P;
             const TpSeg hseg = {hs, 0, 0}, dseg = {dim / P, 0, 0};
-            if ((rc = mv_w(m, T_GATE, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_g, hs, B, s)) ||
-                (rc = mv_w(m, T_UP, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_u, hs, B, s)) ||
+            if ((rc = mv_w(m, T_GATE, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_g, hs, B, s, rg)) ||
+                (rc = mv_w(m, T_UP, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_u, hs, B, s, rg)) ||
                 (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s)) ||
                 (rc = gather(hs, &hseg, 1, m->hb, hid)) ||
                 (rc = mv_w(m, T_DOWN, l, dim, hid, (int64_t)R * (dim / P), dim / P, m->hb, hid, m->tp_send, dim / P, B,
@@ -579,22 +620,23 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                 (rc = gather(dim / P, &dseg, 1, m->xb2, dim)))
                 return rc;
         }
-        if ((rc = residual_launch(m->x, dim, m->xb2, dim, gemma ? m->post_ffn + (int64_t)l * dim : nullptr, c.eps,
-                                  dim, B, s)))
-            return rc;
     }
-    if (!with_classifier) return BREW_OK;
+    const float* post_last = gemma ? m->post_ffn + (int64_t)(L - 1) * dim : nullptr;
+    if (!with_classifier) return residual_launch(m->x, dim, m->xb2, dim, post_last, c.eps, dim, B, s);
     const int V = c.vocab_size;
-    if ((rc = rmsnorm_launch(m->x, dim, m->rms_final, c.eps, dim, B, m->xn, dim, s))) return rc;
+    // the last FFN residual, then the final RMSNorm
+    uint8_t* rcls = rec_for(T_OUTPUT, 0, V, dim);
+    if ((rc = norm_prep_launch(m->x, dim, m->xb2, dim, post_last, m->rms_final, c.eps, dim, B, m->xn, dim, rcls, s)))
+        return rc;
     if (P == 1) {
-        if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, 0, V, m->xn, dim, m->logits, V, B, s))) return rc;
+        if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, 0, V, m->xn, dim, m->logits, V, B, s, rcls))) return rc;
         return argmax_launch(m->logits, V, V, B, m->am_out, s, false);
     }
     // sharded classifier: per-rank argmax keys, gathered and reduced; the
     // logits slices are gathered too (brew_model_forward returns them)
     const int vs = V / P;
     const TpSeg vseg = {vs, 0, 0};
-    if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, (int64_t)R * vs, vs, m->xn, dim, m->tp_send, vs, B, s)) ||
+    if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, (int64_t)R * vs, vs, m->xn, dim, m->tp_send, vs, B, s, rcls)) ||
         (rc = tp_argmax_keys_launch(m->tp_send, vs, vs, B, R * vs, m->tp_keys, s)) ||
         (rc = tp_allgather_u64(m->comm, m->tp_keys, m->tp_keys_all, (size_t)B, s)) ||
         (rc = tp_argmax_reduce_launch(m->tp_keys_all, P, B, m->am_out, s)) ||
