@@ -204,7 +204,9 @@ arrive:
 }  // namespace
 
 int attn_pick_nchunk(int n_kv, int batch, int seq_len) {
-    int nc = (2 * 148) / std::max(1, n_kv * batch);
+    // about two CTAs per SM for the whole batch, and at most 256 positions
+    // per CTA at a full context (a CTA walks its positions one after another)
+    int nc = std::max((2 * 148) / std::max(1, n_kv * batch), (seq_len + 255) / 256);
     nc = std::max(1, std::min(nc, 64));
     while (nc < 256 && (seq_len + nc - 1) / nc > 2048) nc *= 2;
     return nc;

@@ -1,6 +1,5 @@
 // kqtc.cu — the K-quant matvec on tcgen05 (layouts and arithmetic in kqtc.cuh).
 #include "brew_internal.cuh"
-#include "kqmma.cuh"
 #include "kqtc.cuh"
 #include "prep.cuh"
 #include "tc_device.cuh"
@@ -390,6 +389,16 @@ int kx_launch_t(const uint8_t* base, int64_t N, int64_t row0, int n, int K, cons
 }
 
 }  // namespace
+
+int kq_splits(int64_t K, int64_t n_basis) {
+    // as many splits as keep the family's 128-row groups within one wave of
+    // one CTA per SM of a B200 (148 SMs), at least two super-blocks each
+    constexpr int64_t wave = 148;
+    const int64_t groups = std::max<int64_t>(1, (n_basis + KX_TM - 1) / KX_TM), ksb = K / 256;
+    int64_t s = wave / groups;
+    s = std::min<int64_t>(s, std::max<int64_t>(1, ksb / 2));
+    return (int)std::max<int64_t>(1, s);
+}
 
 int kx_pack_launch(int type, const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t N, int64_t row_off,
                    cudaStream_t stream) {

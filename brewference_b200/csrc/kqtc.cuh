@@ -60,6 +60,12 @@ inline size_t kx_rec_bytes(int nv, int64_t K) {
     return (size_t)(K / 256) * (kx_rec_tile_bytes(nv) + 4 * 16 * (size_t)((nv + 15) / 16));
 }
 
+// Split of the super-blocks over CTAs for a matrix whose row family has
+// n_basis rows: a function of the full (unsharded) shape only, so that a
+// row is summed in the same order whatever share of the rows a launch has
+// (tensor-parallel ranks reproduce the one-GPU outputs bit for bit).
+int kq_splits(int64_t K, int64_t n_basis);
+
 // Rows [0, rows) of GGUF matrix w (rows x K) -> rows [row_off, row_off + rows)
 // of the expanded copy `base` of a family of N rows (zeroed beforehand).
 int kx_pack_launch(int type, const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t N, int64_t row_off,

@@ -19,7 +19,6 @@
 #include "decode.cuh"
 #include "eltwise.cuh"
 #include "gemm.cuh"
-#include "kqmma.cuh"
 #include "kqtc.cuh"
 #include "prefill.cuh"
 #include "tp.cuh"
