@@ -111,14 +111,25 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     }
     __syncthreads();
 
-    // scores
-    for (int t = warp; t < n; t += 4) {
-        const float* kr = kc + (int64_t)(p0 + t) * kvd + hk * hd;
-        for (int h = 0; h < G; ++h) {
-            float s = 0.0f;
-            for (int i = lane; i < hd; i += 32) s += qs[h * hd + i] * kr[i];
-            s = warp_sum(s);
-            if (lane == 0) sc[h * cap + t] = s * p.inv_scale;
+    // scores: one position per thread, its K row against up to 4 heads per
+    // pass (q from shared memory, the same address for all lanes)
+    for (int t = tid; t < n; t += blockDim.x) {
+        const float4* kr = reinterpret_cast<const float4*>(kc + (int64_t)(p0 + t) * kvd + hk * hd);
+        for (int h0 = 0; h0 < G; h0 += 4) {
+            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int i = 0; i < hd / 4; ++i) {
+                const float4 kv = kr[i];
+#pragma unroll
+                for (int hh = 0; hh < 4; ++hh) {
+                    if (h0 + hh < G) {
+                        const float4 qv = reinterpret_cast<const float4*>(qs + (h0 + hh) * hd)[i];
+                        s[hh] += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int hh = 0; hh < 4; ++hh)
+                if (h0 + hh < G) sc[(h0 + hh) * cap + t] = s[hh] * p.inv_scale;
         }
     }
     __syncthreads();
@@ -139,9 +150,18 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     __syncthreads();
     for (int idx = tid; idx < G * hd; idx += blockDim.x) {
         const int h = idx / hd, i = idx % hd;
-        float acc = 0.0f;
-        for (int t = 0; t < n; ++t) acc += sc[h * cap + t] * vc[(int64_t)(p0 + t) * kvd + hk * hd + i];
-        __stcg(&pbase[((int64_t)h * p.nchunk + c) * stride + 2 + i], acc);
+        const float* vr = vc + (int64_t)p0 * kvd + hk * hd + i;
+        const float* sh = sc + h * cap;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;   // four chains of positions in flight
+        int t = 0;
+        for (; t + 4 <= n; t += 4) {
+            a0 += sh[t] * vr[(int64_t)t * kvd];
+            a1 += sh[t + 1] * vr[(int64_t)(t + 1) * kvd];
+            a2 += sh[t + 2] * vr[(int64_t)(t + 2) * kvd];
+            a3 += sh[t + 3] * vr[(int64_t)(t + 3) * kvd];
+        }
+        for (; t < n; ++t) a0 += sh[t] * vr[(int64_t)t * kvd];
+        __stcg(&pbase[((int64_t)h * p.nchunk + c) * stride + 2 + i], (a0 + a1) + (a2 + a3));
     }
     if (tid < G) {
         __stcg(&pbase[((int64_t)tid * p.nchunk + c) * stride + 0], n > 0 ? s_m[tid] : -INFINITY);
