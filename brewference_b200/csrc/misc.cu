@@ -1,7 +1,10 @@
 // misc.cu — embedding + prep, dequantization, synthetic weights, argmax.
 #include "misc.cuh"
+#include "mv_device.cuh"
 #include "prep.cuh"
 #include "quant_device.cuh"
+
+#include <algorithm>
 
 namespace brew {
 
@@ -191,36 +194,46 @@ __global__ void fill_kernel(float* out, int64_t n, float v) {
 }
 
 // Kernels.argMax (transformer/math/Kernels.java:150-162): first index of the
-// maximum, strict '>' so ties keep the lowest index.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int ld, int n, int32_t* out) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
+// maximum, strict '>' so ties keep the lowest index (and a NaN is never the
+// maximum).  CTA (chunk, sequence) reduces `chunk` logits to an orderable
+// key (value, then lower index) and merges it into keys[b] with atomicMax;
+// the last CTA of the sequence writes out[b] and leaves keys[b] and ctr[b]
+// zero again.
+constexpr int AM_THREADS = 256;
+
+__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const float* logits, int ld, int n, int chunk,
+                                                            unsigned long long* keys, int* ctr, int32_t* out) {
+    __shared__ unsigned long long red[AM_THREADS / 32];
+    __shared__ int s_last;
     pdl_launch_dependents();
     pdl_wait();
-    const float* l = logits + (int64_t)blockIdx.x * ld;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int b = blockIdx.y;
+    const float* l = logits + (int64_t)b * ld;
+    const int i0 = blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+    unsigned long long best = 0ull;
+    for (int i = i0 + threadIdx.x; i < i1; i += AM_THREADS) {
         const float v = l[i];
-        if (v > bv) { bv = v; bi = i; }
+        const unsigned long long k = v == v ? argmax_key(v, i) : 0ull;
+        best = k > best ? k : best;
     }
     for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+    if (lane == 0) red[warp] = best;
     __syncthreads();
-    if (warp == 0) {
-        bv = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
-        bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < AM_THREADS / 32; ++w) best = red[w] > best ? red[w] : best;
+        atomicMax(&keys[b], best);
+        __threadfence();
+        s_last = atomicAdd(&ctr[b], 1) == (int)gridDim.x - 1;
+        if (s_last) {
+            __threadfence();
+            const unsigned long long k = atomicExch(&keys[b], 0ull);
+            ctr[b] = 0;
+            out[b] = k == 0ull ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         }
-        if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
     }
 }
 
@@ -289,10 +302,13 @@ int fill_f32_launch(float* out, int64_t n, float v, cudaStream_t stream) {
     return BREW_OK;
 }
 
-int argmax_launch(const float* logits, int ld, int n, int batch, int32_t* out, cudaStream_t stream, bool pdl) {
+int argmax_launch(const float* logits, int ld, int n, int batch, unsigned long long* keys, int* ctr, int32_t* out,
+                  cudaStream_t stream, bool pdl) {
+    constexpr int chunk = 16 * AM_THREADS;   // logits per CTA
+    const int chunks = std::max(1, (n + chunk - 1) / chunk);
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(batch), dim3(1024), 0, stream, pdl, attr);
-    BREW_CUDA(cudaLaunchKernelEx(&cfg, argmax_kernel, logits, ld, n, out));
+    cudaLaunchConfig_t cfg = make_cfg(dim3(chunks, batch), dim3(AM_THREADS), 0, stream, pdl, attr);
+    BREW_CUDA(cudaLaunchKernelEx(&cfg, argmax_kernel, logits, ld, n, chunk, keys, ctr, out));
     count_launch();
     return BREW_OK;
 }

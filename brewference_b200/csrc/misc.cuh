@@ -23,7 +23,9 @@ int synth_launch(int type, uint64_t seed, uint32_t tensor_id, int64_t n, float s
 int synth_f32_launch(uint64_t seed, uint32_t tensor_id, int64_t n, float std_dev, float* out, cudaStream_t stream);
 int fill_f32_launch(float* out, int64_t n, float v, cudaStream_t stream);
 
-// out[b] = argmax(logits[b][0..n)) with Kernels.argMax semantics.
-int argmax_launch(const float* logits, int ld, int n, int batch, int32_t* out, cudaStream_t stream, bool pdl);
+// out[b] = argmax(logits[b][0..n)) with Kernels.argMax semantics; keys and
+// ctr: `batch` zeroed scratch words each, left zero.
+int argmax_launch(const float* logits, int ld, int n, int batch, unsigned long long* keys, int* ctr, int32_t* out,
+                  cudaStream_t stream, bool pdl);
 
 }  // namespace brew

@@ -68,6 +68,7 @@ struct brew_model_s {
     int n_counters = 0;
     float* attn_part = nullptr;
     unsigned long long* am_key = nullptr;
+    int* am_ctr = nullptr;                  // [batch] arrival counters of the batched argmax
     int32_t* am_out = nullptr;
     int32_t *tokens_d = nullptr, *pos_d = nullptr;
     int32_t* gen_d = nullptr;      // generated ids of brew_session_generate
@@ -343,6 +344,7 @@ int alloc_state(brew_model_s* m) {
     m->nchunk = attn_pick_nchunk(c.n_kv_heads, B, c.seq_len);
     if ((rc = dalloc(m, &m->attn_part, attn_part_floats(B, c.n_heads, m->nchunk, c.head_size)))) return rc;
     if ((rc = dalloc(m, &m->am_key, (size_t)B))) return rc;
+    if ((rc = dalloc(m, &m->am_ctr, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->am_out, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
@@ -629,7 +631,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         return rc;
     if (P == 1) {
         if ((rc = mv_w(m, T_OUTPUT, 0, V, dim, 0, V, m->xn, dim, m->logits, V, B, s, rcls))) return rc;
-        return argmax_launch(m->logits, V, V, B, m->am_out, s, false);
+        return argmax_launch(m->logits, V, V, B, m->am_key, m->am_ctr, m->am_out, s, false);
     }
     // sharded classifier: per-rank argmax keys, gathered and reduced; the
     // logits slices are gathered too (brew_model_forward returns them)
@@ -810,7 +812,9 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
         p.am_out = m->am_out;
         p.err = err;
         if ((rc = mv_launch(p, s, true))) return rc;
-        if (!fused && (rc = argmax_launch(m->logits, c.vocab_size, c.vocab_size, B, m->am_out, s, true))) return rc;
+        if (!fused && (rc = argmax_launch(m->logits, c.vocab_size, c.vocab_size, B, m->am_key, m->am_ctr, m->am_out, s,
+                                          true)))
+            return rc;
     }
     return BREW_OK;
 }
@@ -1217,6 +1221,7 @@ int after_step_check(brew_model_s* m, const char* where) {
         cudaMemset(m->bar, 0, 2 * sizeof(unsigned long long));
         cudaMemset(m->abort_flag, 0, sizeof(int));
         cudaMemset(m->am_key, 0, (size_t)m->max_batch * sizeof(unsigned long long));
+        cudaMemset(m->am_ctr, 0, (size_t)m->max_batch * sizeof(int));
         cudaDeviceSynchronize();
     }
     return rc;
