@@ -52,10 +52,10 @@ __global__ void __launch_bounds__(EW_THREADS) residual_kernel(float* x, int ldx,
     for (int i = threadIdx.x; i < K; i += EW_THREADS) xr[i] = xr[i] + (norm_w ? tr[i] * scale * norm_w[i] : tr[i]);
 }
 
-__global__ void glu_kernel(float* hb, const float* g, const float* u, int ld, int N, int epi) {
-    const int64_t off = (int64_t)blockIdx.y * ld;
+__global__ void glu_kernel(float* hb, int ldo, const float* g, const float* u, int ld, int N, int epi) {
+    const int64_t off = (int64_t)blockIdx.y * ld, oo = (int64_t)blockIdx.y * ldo;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x)
-        hb[off + i] = act_glu(g[off + i], epi) * u[off + i];
+        hb[oo + i] = act_glu(g[off + i], epi) * u[off + i];
 }
 
 constexpr int NP_THREADS = 1024;   // norm_prep: one CTA of 32 warps per vector
@@ -203,8 +203,9 @@ int residual_launch(float* x, int ldx, const float* t, int ldt, const float* nor
     return BREW_OK;
 }
 
-int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s) {
-    glu_kernel<<<dim3(grid_for(N), B), 256, 0, s>>>(hb, g, u, ld, N, gelu ? MV_EPI_GLU_GELU : MV_EPI_GLU_SILU);
+int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s, int ldo) {
+    glu_kernel<<<dim3(grid_for(N), B), 256, 0, s>>>(hb, ldo > 0 ? ldo : ld, g, u, ld, N,
+                                                     gelu ? MV_EPI_GLU_GELU : MV_EPI_GLU_SILU);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;

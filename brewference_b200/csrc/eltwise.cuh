@@ -18,8 +18,9 @@ int add_bias_launch(float* y, int ldy, const float* bias, int N, int B, cudaStre
 int residual_launch(float* x, int ldx, const float* t, int ldt, const float* norm_w, float eps, int K, int B,
                     cudaStream_t s);
 // hb[b][i] = (float)act((double)g[b][i]) * u[b][i] (FfnActivation.swiGlu /
-// geGlu, transformer/ffn/FfnActivation.java:23-58).
-int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s);
+// geGlu, transformer/ffn/FfnActivation.java:23-58); hb's row stride is ldo
+// when given, else ld.
+int glu_launch(float* hb, const float* g, const float* u, int ld, int N, int B, bool gelu, cudaStream_t s, int ldo = 0);
 
 // The residual of the previous sub-layer, the RMSNorm of the next, and the
 // next matvec's x records, in one kernel (one CTA of 1024 threads per

@@ -100,6 +100,13 @@ struct brew_model_s {
     float* hgu = nullptr;                   // [batch][2 * hidden]: gate | up outputs of that family
     uint8_t* kq_rec = nullptr;              // x records of a K-quant matvec (kqtc.cuh)
     float* qkv_bias = nullptr;              // [layers][q|k|v rows]: the biases indexed by q|k|v family row
+    // tensor parallelism: this rank's rows of the q|k|v and gate|up families
+    // as families of their own ([q_R | k_R | v_R], [gate_R | up_R]), one
+    // launch each; their biases; the gate|up outputs
+    uint8_t* kqp_qkv_tp = nullptr;
+    uint8_t* kqp_gu_tp = nullptr;
+    float* qkv_bias_tp = nullptr;
+    float* tp_gu = nullptr;
     float* kq_part = nullptr;               // its split-K partial sums
     int* kq_ctr = nullptr;                  // and their arrival counters
     size_t kq_nctr = 0;
@@ -416,6 +423,7 @@ int mv_any(brew_model_s* m, int type, const uint8_t* w, const float* x, int ldx,
 struct KxRef {
     const uint8_t* base;
     int64_t N, row0;
+    int64_t basis;   // rows of the one-GPU family: its split of K
 };
 
 KxRef kx_ref(const brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0) {
@@ -424,14 +432,14 @@ KxRef kx_ref(const brew_model_s* m, int which, int l, int64_t rows, int K, int64
     if (m->kqp_qkv && (which == T_Q || which == T_K || which == T_V)) {
         const int64_t qw = (int64_t)c.n_heads * c.head_size, kvd = (int64_t)c.n_kv_heads * c.head_size, nf = qw + 2 * kvd;
         const int64_t off = which == T_Q ? 0 : which == T_K ? qw : qw + kvd;   // rows before it in the family
-        return {m->kqp_qkv + (size_t)l * kx_bytes(type, nf, K), nf, off + row0};
+        return {m->kqp_qkv + (size_t)l * kx_bytes(type, nf, K), nf, off + row0, nf};
     }
     if (m->kqp_gu && (which == T_GATE || which == T_UP)) {
         const int64_t hid = c.hidden_dim;
-        return {m->kqp_gu + (size_t)l * kx_bytes(type, 2 * hid, K), 2 * hid, (which == T_GATE ? 0 : hid) + row0};
+        return {m->kqp_gu + (size_t)l * kx_bytes(type, 2 * hid, K), 2 * hid, (which == T_GATE ? 0 : hid) + row0, 2 * hid};
     }
-    if (!m->kqp[which]) return {nullptr, 0, 0};
-    return {m->kqp[which] + (size_t)l * kx_bytes(type, rows, K), rows, row0};
+    if (!m->kqp[which]) return {nullptr, 0, 0, 0};
+    return {m->kqp[which] + (size_t)l * kx_bytes(type, rows, K), rows, row0, rows};
 }
 
 // y[b][0:n] = rows r.row0 .. r.row0 + n - 1 of the expanded copy r times
@@ -442,7 +450,7 @@ KxRef kx_ref(const brew_model_s* m, int which, int l, int64_t rows, int K, int64
 // launch sums each row as the one-GPU launch does.
 int kq_run(brew_model_s* m, int type, const KxRef& r, int n, int K, const float* x, int ldx, float* y, int ldy, int B,
            cudaStream_t s, const uint8_t* rec = nullptr, const float* bias = nullptr) {
-    const int splits = kq_splits(K, r.N);
+    const int splits = kq_splits(K, r.basis);
     if (rec) {
         BREW_CHECK(B <= KX_MAX_VECTORS, BREW_ERR_INVALID_ARG, "records of %d vectors", B);
         return kx_mma_launch(type, r.base, r.N, r.row0, n, K, rec, B, splits, m->kq_part, m->kq_ctr, bias, y, ldy,
@@ -531,11 +539,16 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             // slices [q_R | k_R | v_R] per rank, gathered into q | k | v
             const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
             float* sq = m->tp_send;
-            if ((rc = mv_w(m, T_Q, l, qw, dim, (int64_t)R * qs, qs, m->xn, dim, sq, sl, B, s, rq)) ||
+            if (m->kqp_qkv_tp) {   // this rank's q|k|v rows: one launch, the bias in its epilogue
+                const KxRef r = {m->kqp_qkv_tp + (size_t)l * kx_bytes(c.type_q, sl, dim), sl, 0, qw + 2 * kvd};
+                if ((rc = kq_run(m, c.type_q, r, sl, dim, m->xn, dim, sq, sl, B, s, rq,
+                                 m->qkv_bias_tp ? m->qkv_bias_tp + (int64_t)l * sl : nullptr)))
+                    return rc;
+            } else if ((rc = mv_w(m, T_Q, l, qw, dim, (int64_t)R * qs, qs, m->xn, dim, sq, sl, B, s, rq)) ||
                 (rc = mv_w(m, T_K, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs, sl, B, s, rq)) ||
                 (rc = mv_w(m, T_V, l, kvd, dim, (int64_t)R * ks, ks, m->xn, dim, sq + qs + ks, sl, B, s, rq)))
                 return rc;
-            if (m->q_bias &&
+            if (m->q_bias && !(m->kqp_qkv_tp && m->qkv_bias_tp) &&
                 ((rc = add_bias_launch(sq, sl, m->q_bias + (int64_t)l * qw + (int64_t)R * qs, qs, B, s)) ||
                  (rc = add_bias_launch(sq + qs, sl, m->k_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s)) ||
                  (rc = add_bias_launch(sq + qs + ks, sl, m->v_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s))))
@@ -612,10 +625,17 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         } else {
             const int hs = hid / P;
             const TpSeg hseg = {hs, 0, 0}, dseg = {dim / P, 0, 0};
-            if ((rc = mv_w(m, T_GATE, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_g, hs, B, s, rg)) ||
-                (rc = mv_w(m, T_UP, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_u, hs, B, s, rg)) ||
-                (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s)) ||
-                (rc = gather(hs, &hseg, 1, m->hb, hid)) ||
+            if (m->kqp_gu_tp) {   // this rank's gate|up rows: one launch, then the GLU of the local slice
+                const KxRef r = {m->kqp_gu_tp + (size_t)l * kx_bytes(c.type_gate, 2 * hs, dim), 2 * hs, 0, 2 * hid};
+                if ((rc = kq_run(m, c.type_gate, r, 2 * hs, dim, m->xn, dim, m->tp_gu, 2 * hs, B, s, rg)) ||
+                    (rc = glu_launch(m->tp_send, m->tp_gu, m->tp_gu + hs, 2 * hs, hs, B, gemma, s, hs)))
+                    return rc;
+            } else if ((rc = mv_w(m, T_GATE, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_g, hs, B, s, rg)) ||
+                       (rc = mv_w(m, T_UP, l, hid, dim, (int64_t)R * hs, hs, m->xn, dim, m->tp_u, hs, B, s, rg)) ||
+                       (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s))) {
+                return rc;
+            }
+            if ((rc = gather(hs, &hseg, 1, m->hb, hid)) ||
                 (rc = mv_w(m, T_DOWN, l, dim, hid, (int64_t)R * (dim / P), dim / P, m->hb, hid, m->tp_send, dim / P, B,
                            s)) ||
                 (rc = gather(dim / P, &dseg, 1, m->xb2, dim)))
@@ -1412,6 +1432,57 @@ int brew_model_set_tp(brew_model m, brew_comm comm) {
         (rc = dalloc(m, &m->tp_u, (size_t)B * (c.hidden_dim / P))) || (rc = dalloc(m, &m->tp_keys, (size_t)B)) ||
         (rc = dalloc(m, &m->tp_keys_all, (size_t)P * B)))
         return rc;
+    // this rank's rows of the K-quant q|k|v and gate|up families as families
+    // of their own (one launch each; the split of K stays the one-GPU one)
+    const int R = comm->rank;
+    if (P > 1 && m->kqp_qkv) {
+        const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
+        const size_t per = kx_bytes(c.type_q, sl, c.dim);
+        const int64_t rb = row_bytes_of(c.type_q, c.dim);
+        if ((rc = dalloc(m, &m->kqp_qkv_tp, per * c.n_layers))) return rc;
+        for (int l = 0; l < c.n_layers && !rc; ++l) {
+            uint8_t* base = m->kqp_qkv_tp + per * l;
+            rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_Q], l, qw, c.dim) + (int64_t)R * qs * rb, qs, c.dim, base, sl,
+                                0, ctx().stream);
+            if (!rc)
+                rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_K], l, kvd, c.dim) + (int64_t)R * ks * rb, ks, c.dim,
+                                    base, sl, qs, ctx().stream);
+            if (!rc)
+                rc = kx_pack_launch(c.type_q, layer_ptr(m->t[T_V], l, kvd, c.dim) + (int64_t)R * ks * rb, ks, c.dim,
+                                    base, sl, qs + ks, ctx().stream);
+        }
+        if (rc) return rc;
+        if (m->q_bias) {
+            BREW_CUDA(cudaDeviceSynchronize());
+            if ((rc = dalloc(m, &m->qkv_bias_tp, (size_t)sl * c.n_layers))) return rc;
+            for (int l = 0; l < c.n_layers; ++l) {
+                float* fb = m->qkv_bias_tp + (size_t)sl * l;
+                BREW_CUDA(cudaMemcpy(fb, m->q_bias + (size_t)qw * l + (size_t)R * qs, qs * sizeof(float),
+                                     cudaMemcpyDeviceToDevice));
+                BREW_CUDA(cudaMemcpy(fb + qs, m->k_bias + (size_t)kvd * l + (size_t)R * ks, ks * sizeof(float),
+                                     cudaMemcpyDeviceToDevice));
+                BREW_CUDA(cudaMemcpy(fb + qs + ks, m->v_bias + (size_t)kvd * l + (size_t)R * ks, ks * sizeof(float),
+                                     cudaMemcpyDeviceToDevice));
+            }
+        }
+    }
+    if (P > 1 && m->kqp_gu) {
+        const int hs = c.hidden_dim / P;
+        const size_t per = kx_bytes(c.type_gate, 2 * hs, c.dim);
+        const int64_t rb = row_bytes_of(c.type_gate, c.dim);
+        if ((rc = dalloc(m, &m->kqp_gu_tp, per * c.n_layers)) || (rc = dalloc(m, &m->tp_gu, (size_t)B * 2 * hs)))
+            return rc;
+        for (int l = 0; l < c.n_layers && !rc; ++l) {
+            uint8_t* base = m->kqp_gu_tp + per * l;
+            rc = kx_pack_launch(c.type_gate, layer_ptr(m->t[T_GATE], l, c.hidden_dim, c.dim) + (int64_t)R * hs * rb, hs,
+                                c.dim, base, 2 * hs, 0, ctx().stream);
+            if (!rc)
+                rc = kx_pack_launch(c.type_gate, layer_ptr(m->t[T_UP], l, c.hidden_dim, c.dim) + (int64_t)R * hs * rb,
+                                    hs, c.dim, base, 2 * hs, hs, ctx().stream);
+        }
+        if (rc) return rc;
+    }
+    BREW_CUDA(cudaStreamSynchronize(ctx().stream));
     m->comm = comm;
     return BREW_OK;
 }
