@@ -169,9 +169,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
     }
     }
 arrive:
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(ctr, 1) == p.nchunk - 1);
+    __syncthreads();   // the CTA's partials are written before thread 0's fence and arrival
+    if (tid == 0) {
+        __threadfence();
+        s_last = (atomicAdd(ctr, 1) == p.nchunk - 1);
+    }
     __syncthreads();
     if (!s_last) return;
     __threadfence();

@@ -590,7 +590,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             a.part = m->attn_part;
             a.counters = attn_ctr;
             a.nchunk = m->nchunk;
-            a.prep_out = m->prep_q;
+            a.prep_out = nullptr;   // the matvecs of this forward make their own x records
             a.err = err;
             if ((rc = attn_launch(a, s, false))) return rc;
         }
