@@ -118,7 +118,8 @@ __global__ void kx_prep_kernel(const float* x, int ldx, int K, int nv, int nvp, 
 constexpr int KX_AH = 0, KX_AL = 32768, KX_AM = 65536, KX_Z = 67584, KX_B = 69632;
 constexpr int KX_STAGE = KX_B + 10 * 96 * 32;   // 100352
 constexpr int KX_SMEM = 2 * KX_STAGE + 128;
-constexpr int KX_THREADS = 320;                 // loader warp, MMA warp, 8 epilogue warps
+constexpr int KX_EPI = 16;                      // epilogue warps: 4 per tensor-memory lane quadrant
+constexpr int KX_THREADS = 64 + 32 * KX_EPI;    // loader warp, MMA warp, epilogue warps
 constexpr int KX_TMEM_COLS = 512;               // h, l, min-Xl, min-Xh accumulators at 0, 128, 256, 384
 
 __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned int* err, unsigned int code) {
@@ -136,8 +137,8 @@ __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned
 //               tile against the two min-term tiles), all onto the preset
 //               magic value, and commits to the stage's "empty" and the
 //               accumulators' "full" barriers;
-//   warps 2-9   read the four accumulators back (warp w: lanes 32 (w % 4),
-//               half of the columns), reset them, release them, and add
+//   warps 2-17  read the four accumulators back (warp w: lanes 32 (w % 4),
+//               a quarter of the columns), reset them, release them, and add
 //               s_v (d (F h + l) - dmin (m1 + 256 m2)) to fp32 accumulators
 //               per (vector, limb).
 // The copies of the next super-block overlap the MMAs and the readout.
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
                   unsigned int* err) {
     constexpr bool Q4 = TYPE == BREW_TYPE_Q4_K;
     constexpr int NVP = 16 * NVG, NC = 3 * NVP;   // vectors and limb columns of the MMA
-    constexpr int CW = NC / 2, TPW = CW / 3;      // columns and vectors per epilogue warp
+    constexpr int CW = NC / (KX_EPI / 4), TPW = CW / 3;   // columns and vectors per epilogue warp
     constexpr int NACC = Q4 ? 4 : 2;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * KX_STAGE);
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             mbar_init(&empty[i], 1);
         }
         mbar_init(tfull, 1);
-        mbar_init(tempty, 8);
+        mbar_init(tempty, KX_EPI);
         fence_mbar_init();
     }
     if (Q4) {   // the min tile's second K-half: zeros, read by the tensor cores
@@ -340,17 +341,17 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         }
         if (S > 1) {   // the last CTA of this row group adds the splits in split order
             __threadfence();
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * KX_EPI) : "memory");
             if (tid == 64) {
                 const int old = atomicAdd(&ctr[blockIdx.x], 1);
                 s_last = old == S - 1;
                 if (s_last) ctr[blockIdx.x] = 0;   // every split has arrived: ready for the next launch
             }
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * KX_EPI) : "memory");
             if (s_last) {
                 __threadfence();
                 const int rbase = (int)(r0 - row0);
-                for (int i = tid - 64; i < nv * KX_TM; i += 256) {
+                for (int i = tid - 64; i < nv * KX_TM; i += 32 * KX_EPI) {
                     const int tk = i / KX_TM, lr = rbase + i % KX_TM;
                     if (lr >= n) continue;
                     float sum = 0.0f;
