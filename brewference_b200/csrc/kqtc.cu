@@ -246,9 +246,11 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         const int64_t frow = r0 + 32 * q + lane;             // row within the family (< pitch)
         const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + CW * hh;
 #pragma unroll
-        for (int a = 0; a < NACC; ++a)
+        for (int a = 0; a < NACC; ++a) {   // exactly this warp's CW columns (a multiple of 4)
 #pragma unroll
-            for (int c = 0; c < CW; c += 8) tmem_st8_const(tq + 128 * a + c, TC_MAGIC);
+            for (int c = 0; c + 8 <= CW; c += 8) tmem_st8_const(tq + 128 * a + c, TC_MAGIC);
+            if (CW % 8) tmem_st4_const(tq + 128 * a + CW - 4, TC_MAGIC);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
