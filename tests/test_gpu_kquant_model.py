@@ -82,13 +82,15 @@ def test_qwen25_7b_width_two_layers(device):
     parity(cfg, 7, prompt_len=6, n_gen=16, check_steps=2)
 
 
-def test_kquant_32_sequences(device):
-    """32 concurrent sequences (the 7B config's workload size; the K-quant
-    matvec takes 16 vectors per launch, so the step runs two vector groups):
-    a sequence's logits in the batch equal those of the same sequence
-    forwarded alone, and sequence 0 matches the oracle."""
+@pytest.mark.parametrize("B", [5, 20, 32])
+def test_kquant_many_sequences(device, B):
+    """Concurrent sequences up to 32 (the 7B config's workload size; the
+    K-quant matvec takes up to 32 vectors per launch in one or two groups of
+    16 MMA vectors, 5 and 20 leaving padded columns): a sequence's logits in
+    the batch equal those of the same sequence forwarded alone, and
+    sequence 0 matches the oracle."""
     cfg = kquant(C.qwen25_7b(), dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4, **SMALL)
-    B, steps = 32, 3
+    steps = 3
     dm = DeviceModel.synthesize(cfg, 91, max_batch=B)
     toks = np.random.default_rng(5).integers(0, cfg.vocab_size, (steps, B)).astype(np.int32)
     batched = []
@@ -98,7 +100,7 @@ def test_kquant_32_sequences(device):
         batched.append(lg)
     dm.close()
     single = DeviceModel.synthesize(cfg, 91)
-    for b in (0, 17, 31):
+    for b in sorted({0, B // 2 + 1, B - 1}):
         single.reset()
         for pos in range(steps):
             lg, _ = single.forward([toks[pos][b]], [pos])
