@@ -479,9 +479,12 @@ int mv_w(brew_model_s* m, int which, int l, int64_t rows, int K, int64_t row0, i
 }
 
 // The forward of a model with K-quant matrices (the Qwen2.5-7B Q4_K/Q6_K
-// config): each matvec reads fp32 activations, and RMSNorm, bias, residual
-// and the gated activation are separate kernels.  Op order of the
-// reference's forward methods (model/*/...Transformer.java).
+// config) and of tensor-parallel models: per layer, residual + RMSNorm (+ the
+// next tcgen05 K-quant matvec's x records) in one kernel, the q|k|v matvec
+// (bias in its epilogue when q|k|v is one family), attention, wo, residual +
+// RMSNorm, gate|up, GLU (+ records), down; each residual is applied by the
+// next norm kernel.  Op order of the reference's forward methods
+// (model/*/...Transformer.java).
 int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaStream_t s) {
     const brew_config& c = m->c;
     const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
