@@ -398,7 +398,7 @@ int brew_init(int device) {
     const unsigned int zero = 0;
     BREW_CUDA(cudaMemcpyToSymbol(g_brew_device_error, &zero, sizeof(zero)));
     g_ctx.initialized = true;
-    return BREW_OK;
+    return static_scratch_setup();
 }
 
 int64_t brew_type_bytes(int type, int64_t n) {

@@ -15,6 +15,7 @@
 #include "prep.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace brew {
 
@@ -247,10 +248,11 @@ int attn_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
     const int cap = std::max(ATTN_MIN_CHUNK, (p.seq_len + p.nchunk - 1) / p.nchunk);
     const size_t smem = sizeof(float) * ((size_t)G * p.hd + p.hd + (size_t)G * cap + 32 + p.hd + (size_t)G * p.nchunk);
     BREW_CHECK(smem <= 200 * 1024, BREW_ERR_INVALID_ARG, "attention: %zu bytes of shared memory", smem);
-    static bool attr_done = false;
-    if (!attr_done) {
-        BREW_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_done = true;
+    static std::mutex mu;
+    static unsigned long long attr_set = 0;   // one bit per device
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        BREW_CUDA(smem_attr_per_device((const void*)attn_kernel, 200 * 1024, &attr_set));
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv, p.nchunk, p.batch);

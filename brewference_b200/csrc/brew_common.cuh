@@ -50,6 +50,36 @@ inline bool is_quant_matrix_type(int type) {
     return type == BREW_TYPE_Q4_0 || type == BREW_TYPE_Q8_0 || type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K;
 }
 
+// Per-architecture rules of the reference's forward methods
+// (model/*/...Transformer.java and their AttentionPattern classes).
+// Gemma family: embeddings scaled by sqrt(dim), post-attention and post-FFN
+// norms, GeGLU, local (sliding-window, base 1e4) and global (base 1e6) layers.
+__host__ __device__ inline bool arch_gemma(int a) { return a == BREW_ARCH_GEMMA3 || a == BREW_ARCH_GEMMA2; }
+// head-wise RMSNorm of q and k (Qwen3Transformer.java, Gemma3Transformer.java:42-43)
+__host__ __device__ inline bool arch_qknorm(int a) { return a == BREW_ARCH_QWEN3 || a == BREW_ARCH_GEMMA3; }
+// InterleavedRope pairs (2d, 2d+1) (Llama2Transformer.java:45, SmolLM3Transformer.java:60)
+__host__ __device__ inline bool arch_interleaved(int a) { return a == BREW_ARCH_LLAMA || a == BREW_ARCH_SMOLLM3; }
+// global attention layer: Gemma3AttentionPattern.java:10-12 (every 6th),
+// Gemma2AttentionPattern.java:10-12 (every 2nd); other architectures attend
+// to every position
+__host__ __device__ inline bool arch_global_layer(int a, int l) {
+    return a == BREW_ARCH_GEMMA3 ? (l + 1) % 6 == 0 : a == BREW_ARCH_GEMMA2 ? (l + 1) % 2 == 0 : true;
+}
+// RoPE applied at layer l (SmolLM3Transformer.java:48: not on every 4th layer)
+__host__ __device__ inline bool arch_rope_layer(int a, int l) { return a != BREW_ARCH_SMOLLM3 || (l + 1) % 4 != 0; }
+// sliding window of layer l (0: none)
+__host__ __device__ inline int arch_window(int a, int l, int window) {
+    return (arch_gemma(a) && !arch_global_layer(a, l)) ? window : 0;
+}
+// RoPE base of the global (or only) table and of the Gemma local table: the
+// configured base when > 0, else the architecture's supplier value
+inline float arch_rope_base(int a, float cfg_base, bool local) {
+    if (cfg_base > 0.0f) return cfg_base;
+    if (a == BREW_ARCH_LLAMA || a == BREW_ARCH_SMOLLM3) return 10000.0f;
+    if (arch_gemma(a)) return local ? 10000.0f : 1000000.0f;
+    return 1000000.0f;
+}
+
 // device-side error flags (one word per device, written by bounded waits)
 #define BREW_DEVERR_TIMEOUT_FULL   1u
 #define BREW_DEVERR_TIMEOUT_EMPTY  2u
@@ -58,6 +88,19 @@ inline bool is_quant_matrix_type(int type) {
 
 unsigned int* device_error_word();      // device pointer of this device's flag word
 int check_device_error(const char* where);  // reads + clears the flag (synchronising)
+
+// Sets a kernel's dynamic shared-memory limit on the current device the first
+// time that device launches it.  The attribute is per device, so `done` keeps
+// one bit per device ordinal (devices 64 and up set it on every call).
+inline cudaError_t smem_attr_per_device(const void* fn, int bytes, unsigned long long* done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && ((*done >> dev) & 1ull)) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && dev < 64) *done |= 1ull << dev;
+    return e;
+}
 
 }  // namespace brew
 

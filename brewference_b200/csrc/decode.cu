@@ -134,6 +134,11 @@ struct PGeom {
 
 __device__ __forceinline__ int pk_gs(const DecodeParams& P, int ph, int nt) { return P.geo_gs[ph][min(nt, 9)]; }
 
+// Tile groups hold 1, 2, 4 or 8 tiles (the largest of those <= n): four
+// instantiations of the group loop keep the kernel's code small enough for
+// the instruction caches.
+__device__ __forceinline__ int ng_pow2(int n) { return n >= 8 ? 8 : n >= 4 ? 4 : n >= 2 ? 2 : 1; }
+
 __device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, int KB) {
     PGeom g;
     g.KC = P.geo_kc[ph][ng];
@@ -194,6 +199,7 @@ enum { SRC_EMBED = 0, SRC_PLAIN = 1, SRC_GEMMA_ADD = 2 };
 // second array beside it, as asynchronous copies that are all in flight at
 // once (completed by cp_async_wait_all).
 __device__ __forceinline__ void stage_async(float4* d0, const float4* s0, float4* d1, const float4* s1, int n4) {
+    #pragma unroll 1
     for (int i = threadIdx.x; i < n4; i += 256) {
         if (s0) cp_async16(d0 + i, s0 + i);
         if (s1) cp_async16(d1 + i, s1 + i);
@@ -203,6 +209,7 @@ __device__ __forceinline__ void stage_async(float4* d0, const float4* s0, float4
 // This thread's sum of squares over the float4 it staged (i = tid + 256 k).
 __device__ __forceinline__ float sumsq4(const float4* v, int n4) {
     float ss = 0.0f;
+    #pragma unroll 1
     for (int i = threadIdx.x; i < n4; i += 256) {
         const float4 a = v[i];
         ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
@@ -229,6 +236,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
     float4* v4 = reinterpret_cast<float4*>(vec);
     float4* w4 = v4 + K4;
     const float4* nw4 = reinterpret_cast<const float4*>(nw);
+    #pragma unroll 1
     for (int b = 0; b < P.batch; ++b) {
         float ss = 0.0f;
         if (mode == SRC_EMBED) {
@@ -238,6 +246,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
                 tok = 0;
             }
             const float es = (float)sqrt((double)K);   // Kernels.scaleEmbeddings
+            #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += 256) {
                 float v = dequant_elem(P.type_embed, P.embed, (int64_t)tok * K + i);
                 vec[i] = P.arch == BREW_ARCH_GEMMA3 ? __fmul_rn(v, es) : v;
@@ -245,6 +254,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
             consumer_bar();
+            #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
         } else if (mode == SRC_GEMMA_ADD) {
             stage_async(v4, reinterpret_cast<const float4*>(t + (int64_t)b * ld), w4,
@@ -253,10 +263,12 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             consumer_bar();
             const float tsc = rms_scale(consumer_sum(sumsq4(v4, K4), red), K, P.eps);
             const float* sb = src + (int64_t)b * ld;
+            #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += 256) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * vec[K + i];
             consumer_bar();
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
+            #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
         } else {
             stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4,
@@ -282,6 +294,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
         // two independent block quads per iteration (their shuffle and
         // divide chains overlap)
         const int gq = lane >> 3, e = (lane & 7) * 4;
+        #pragma unroll 1
         for (int j0 = warp * 4; j0 < KB; j0 += 64) {
             int jj[2];
             bool ok[2];
@@ -424,7 +437,6 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
     if (nt <= 0) return;
     const int batch = P.batch;
     const int gs = pk_gs(P, f.ph, nt);
-    const int ngroups = (nt + gs - 1) / gs;
     const bool glu = f.epi != MV_EPI_STORE;
     const int per_tile = (glu ? 8 : 16) * batch;
     LaneOps o;
@@ -440,9 +452,8 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
         o.loff0 = prep_lsum_off(batch) + 4 * (3 * bCs + o.l0);
         o.loff1 = prep_lsum_off(batch) + 4 * (3 * bCs + 1);
     }
-    for (int grp = 0; grp < ngroups; ++grp) {
-        const int tg0 = t0 + grp * gs;
-        const int ng = min(gs, t1 - tg0);
+    for (int tg0 = t0; tg0 < t1; tg0 += ng_pow2(min(gs, t1 - tg0))) {
+        const int ng = ng_pow2(min(gs, t1 - tg0));
         const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
         // this thread's output of the group: its bias and residual are read
         // now, so that their latency overlaps the MMA loop
@@ -460,11 +471,7 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
         switch (ng) {
             case 1: mv_group<TT, 1>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
             case 2: mv_group<TT, 2>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 3: mv_group<TT, 3>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
             case 4: mv_group<TT, 4>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 5: mv_group<TT, 5>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 6: mv_group<TT, 6>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 7: mv_group<TT, 7>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
             default: mv_group<TT, 8>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
         }
         consumer_bar();
@@ -510,10 +517,8 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
     const int nt = t1 - t0;
     if (nt <= 0) return;
     const int gs = pk_gs(P, f.ph, nt);
-    const int ngroups = (nt + gs - 1) / gs;
-    for (int grp = 0; grp < ngroups; ++grp) {
-        const int tg0 = t0 + grp * gs;
-        const int ng = min(gs, t1 - tg0);
+    for (int tg0 = t0; tg0 < t1; tg0 += ng_pow2(min(gs, t1 - tg0))) {
+        const int ng = ng_pow2(min(gs, t1 - tg0));
         const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
         const uint32_t cbytes = (uint32_t)geo.KC * BS;
         for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
@@ -629,6 +634,7 @@ __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, cons
     const int ns = min(attn_sub(hd), it.n - r0);
     const float* kc = P.kc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     const float* vc = P.vc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
+    #pragma unroll 1
     for (int i = threadIdx.x; i < ns * hd4; i += 256) {
         const int r = i / hd4, ci = i % hd4;
         const int p = it.p0 + r0 + r;
@@ -672,6 +678,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     };
     stamp(0);
     const int items = P.batch * P.n_kv * nch;
+    #pragma unroll 1
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         AttnItem it;
         if (!attn_item(P, l, item, it)) {
@@ -686,7 +693,9 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             const float* qsrc = P.qkv + (int64_t)b * ldq + (int64_t)hk * G * hd;
             const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
             const float* vsrc = ksrc + kvd;
+            #pragma unroll 1
             for (int i = tid; i < G * hd4; i += 256) cp_async16(qs + 4 * i, qsrc + 4 * i);
+            #pragma unroll 1
             for (int i = tid; i < hd4; i += 256) {
                 cp_async16(ks + 4 * i, ksrc + 4 * i);
                 cp_async16(vs + 4 * i, vsrc + 4 * i);
@@ -705,18 +714,22 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             if (t_wave) *t_wave = global_ns();
             stamp(1);
             if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
+                #pragma unroll 1
                 for (int hh = warp; hh <= G; hh += 8) {
                     float* vecp = hh < G ? qs + hh * hd : ks;
                     const float* w = hh < G ? wq : wk;
                     float ss = 0.0f;
+                    #pragma unroll 1
                     for (int i = lane; i < hd; i += 32) ss += vecp[i] * vecp[i];
                     const float scale = rms_scale(warp_sum(ss), hd, P.eps);
                     __syncwarp();
+                    #pragma unroll 1
                     for (int i = lane; i < hd; i += 32) vecp[i] = vecp[i] * scale * w[i];
                 }
                 consumer_bar();
             }
             stamp(2);
+            #pragma unroll 1
             for (int idx = tid; idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
                 const int hh = idx / half, d = idx % half;
                 float* vecp = hh < G ? qs + hh * hd : ks;
@@ -730,12 +743,14 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             stamp(3);
             const bool has_pos = pos >= p0 && pos < p0 + n;
             if (has_pos) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
+                #pragma unroll 1
                 for (int i = tid; i < hd; i += 256) {
                     kc[(int64_t)pos * kvd + hk * hd + i] = ks[i];
                     vc[(int64_t)pos * kvd + hk * hd + i] = vs[i];
                 }
             }
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // outputs tid + 256 k of [G][hd] (G * hd <= 1024)
+            #pragma unroll 1
             for (int r0 = 0; r0 < n; r0 += SUB) {
                 const int ns = min(SUB, n - r0);
                 if (r0 > 0) {
@@ -744,6 +759,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 }
                 if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
                     const int r = pos - p0 - r0;
+                    #pragma unroll 1
                     for (int i = tid; i < hd; i += 256) {
                         kb[r * hd + i] = ks[i];
                         vb[r * hd + i] = vs[i];
@@ -758,6 +774,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 {
                     const int npair = G * ns, ppi = 256 / tpp;
                     const int j = tid & (tpp - 1);
+                    #pragma unroll 1
                     for (int p00 = 0; p00 < npair; p00 += ppi) {
                         const int pr = p00 + tid / tpp;
                         const int pc = pr < npair ? pr : npair - 1;
@@ -765,6 +782,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         const float4* q4 = reinterpret_cast<const float4*>(qs + h * hd);
                         const float4* k4 = reinterpret_cast<const float4*>(kb + tt * hd);
                         float s0 = 0.0f, s1 = 0.0f;
+                        #pragma unroll 1
                         for (int m = j; m < hd4; m += 2 * tpp) {
                             const float4 a = q4[m], kk = k4[m];
                             s0 = fmaf(a.x, kk.x, s0);
@@ -787,12 +805,15 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 consumer_bar();
                 if (r0 == 0) stamp(10);
                 // running softmax: weights of this round relative to the new maximum
+                #pragma unroll 1
                 for (int h = warp; h < G; h += 8) {
                     float m = -INFINITY;
+                    #pragma unroll 1
                     for (int tt = lane; tt < ns; tt += 32) m = fmaxf(m, sc[h * SUB + tt]);
                     m = warp_max(m);
                     const float mo = st[4 * h], mn = fmaxf(mo, m);
                     float ls = 0.0f;
+                    #pragma unroll 1
                     for (int tt = lane; tt < ns; tt += 32) {
                         const float e = expf(sc[h * SUB + tt] - mn);
                         sc[h * SUB + tt] = e;
@@ -818,12 +839,14 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         const float* vcol = vb + i;
                         float a0 = acc[k] * st[4 * h + 2], a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
                         int tt = 0;
+                        #pragma unroll 1
                         for (; tt + 4 <= ns; tt += 4) {
                             a0 = fmaf(sh[tt], vcol[tt * hd], a0);
                             a1 = fmaf(sh[tt + 1], vcol[(tt + 1) * hd], a1);
                             a2 = fmaf(sh[tt + 2], vcol[(tt + 2) * hd], a2);
                             a3 = fmaf(sh[tt + 3], vcol[(tt + 3) * hd], a3);
                         }
+                        #pragma unroll 1
                         for (; tt < ns; ++tt) a0 = fmaf(sh[tt], vcol[tt * hd], a0);
                         acc[k] = (a0 + a1) + (a2 + a3);
                     }
@@ -861,20 +884,25 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
         stamp(5);
         if (s_last) {
             const int hpw = max(1, min(G, P.attn_floats / (nch * stride)));
+            #pragma unroll 1
             for (int h0 = 0; h0 < G; h0 += hpw) {
                 const int nh = min(hpw, G - h0);
                 const float* src = pbase + (int64_t)h0 * nch * stride;
                 const int n4 = nh * nch * stride / 4;
+                #pragma unroll 1
                 for (int i = tid; i < n4; i += 256) cp_async16(sm + 4 * i, src + 4 * i);
                 cp_async_wait_all();
                 consumer_bar();
                 stamp(6);
+                #pragma unroll 1
                 for (int hl = warp; hl < nh; hl += 8) {
                     float* ph = sm + hl * nch * stride;
                     float M = -INFINITY;
+                    #pragma unroll 1
                     for (int k = lane; k < used; k += 32) M = fmaxf(M, ph[k * stride]);
                     M = warp_max(M);
                     float Ls = 0.0f;
+                    #pragma unroll 1
                     for (int k = lane; k < used; k += 32) {
                         const float w = expf(ph[k * stride] - M);
                         ph[k * stride + 2] = w;
@@ -884,10 +912,12 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     if (lane == 0) ph[3] = 1.0f / Ls;
                 }
                 consumer_bar();
+                #pragma unroll 1
                 for (int idx = tid; idx < nh * hd; idx += 256) {
                     const int hl = idx / hd, i = idx % hd;
                     const float* ph = sm + hl * nch * stride;
                     float o = 0.0f;
+                    #pragma unroll 1
                     for (int k = 0; k < used; ++k) o += ph[k * stride + 2] * ph[k * stride + 4 + i];
                     P.xb[(int64_t)b * qw + (int64_t)(hk * G + h0 + hl) * hd + i] = o * ph[3];
                 }
@@ -942,15 +972,22 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         int q = 0;
         unsigned long long* dtr =
             P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots + P.trace_slots - 3 * DK_DETAIL : nullptr;
-        for (int l = 0; l < L && q < (1 << 29); ++l) {
-            for (int ph = PH_QKV; ph <= PH_DOWN && q < (1 << 29); ++ph) {
-                const DPhase f = make_phase(P, l, ph, P.x0);
-                produce_phase<TYPE>(P, f, ring, q, (l == P.detail_l && ph == P.detail_ph) ? dtr : nullptr);
+        // the consumers' phase steps, without attention (no weights)
+        for (int s = 0; s < 5 * L + 1 && q < (1 << 29); ++s) {
+            const int l = s / 5, ph = s - 5 * l;
+            const bool cls = s == 5 * L;
+            if (ph == 1) continue;
+            const int mph = cls ? PH_CLS : ph == 0 ? PH_QKV : ph == 2 ? PH_O : ph == 3 ? PH_GU : PH_DOWN;
+            const DPhase f = make_phase(P, l, mph, P.x0);
+            unsigned long long* d = (l == P.detail_l && mph == P.detail_ph) ? dtr : nullptr;
+            if constexpr (TYPE == CTYPE) {
+                produce_phase<TYPE>(P, f, ring, q, d);
+            } else {
+                if (cls)
+                    produce_phase<CTYPE>(P, f, ring, q, d);
+                else
+                    produce_phase<TYPE>(P, f, ring, q, d);
             }
-        }
-        if (q < (1 << 29)) {
-            const DPhase f = make_phase(P, 0, PH_CLS, P.x0);
-            produce_phase<CTYPE>(P, f, ring, q, (L == P.detail_l && PH_CLS == P.detail_ph) ? dtr : nullptr);
         }
         return;
     }
@@ -1003,104 +1040,104 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         if (!gem) stage_async(reinterpret_cast<float4*>(vec) + P.dim / 4, reinterpret_cast<const float4*>(nw), nullptr,
                               nullptr, P.dim / 4);
     };
-    for (int l = 0; l < L && !aborted; ++l) {
-        // the small vectors of the next phase go to L2 one phase ahead (HBM
-        // misses otherwise; fetched earlier they would be evicted again by
-        // the weight stream)
-        auto pf = [&](const float* v, int n) {
-            if (v && blockIdx.x == 0 && tid == 0) prefetch_l2(v, (uint32_t)n * 4u);
-        };
-        pf(P.rms_q ? P.rms_q + (int64_t)l * P.hd : nullptr, P.hd);
-        pf(P.rms_k ? P.rms_k + (int64_t)l * P.hd : nullptr, P.hd);
-        // ---- RMSNorm (attention) + Q|K|V ----
-        if (l == 0) {
-            prep_phase(P, SRC_EMBED, xcur, P.dim, P.dim, P.rms_att, nullptr, nullptr, xcur, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
-        } else if (gem) {
-            prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, P.xb2,
-                       P.post_ffn + (int64_t)(l - 1) * P.dim, xalt, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
-            float* tmp = xcur; xcur = xalt; xalt = tmp;
+    // One step per phase: s = 5 l + p, p = 0 Q|K|V, 1 attention, 2 wo,
+    // 3 gate|up, 4 down; s = 5 L is the classifier.  Every phase function
+    // has one call site (the kernel's code stays small: its instruction
+    // fetches compete with the weight stream for L2).
+    const int nsteps = 5 * L + 1;
+    for (int s = 0; s < nsteps && !aborted; ++s) {
+        const int l = s / 5, ph = s - 5 * l;
+        const bool cls = s == 5 * L;
+        if (ph == 0 && !cls && blockIdx.x == 0 && tid == 0) {
+            // the head-norm weights go to L2 one phase ahead (HBM misses
+            // otherwise; fetched earlier the weight stream would evict them)
+            if (P.rms_q) prefetch_l2(P.rms_q + (int64_t)l * P.hd, (uint32_t)P.hd * 4u);
+            if (P.rms_k) prefetch_l2(P.rms_k + (int64_t)l * P.hd, (uint32_t)P.hd * 4u);
+        }
+        if (ph == 1) {
+            attn_phase(P, l, vec, tr ? &twave : nullptr, rope, det(l, PH_ATTN));
+            markv(twave);   // the first load wave landed
+            twave = 0;
+            markv(0);
+            markv(0);
+            barrier();
+            continue;
+        }
+        // the phase's input vector -> prep records in shared memory
+        int mode = SRC_PLAIN, ld = P.dim, K = P.dim, mph;
+        const float* src = xcur;
+        const float *nw = nullptr, *t = nullptr, *tw = nullptr, *next_norm = nullptr;
+        float* xout = nullptr;
+        bool staged = false, swap = false;
+        if (ph == 0) {   // RMSNorm + Q|K|V, or the final RMSNorm + classifier
+            mph = cls ? PH_CLS : PH_QKV;
+            nw = cls ? P.rms_final : P.rms_att + (int64_t)l * P.dim;
+            if (l == 0) {
+                mode = SRC_EMBED;
+                xout = xcur;
+            } else if (gem) {   // the previous layer's post-FFN norm + residual
+                mode = SRC_GEMMA_ADD;
+                t = P.xb2;
+                tw = P.post_ffn + (int64_t)(l - 1) * P.dim;
+                xout = cls ? nullptr : xalt;
+                swap = !cls;
+            } else {
+                staged = true;
+            }
+        } else if (ph == 2) {   // wo (+ residual)
+            mph = PH_O;
+            src = P.xb;
+            ld = K = P.n_heads * P.hd;
+            next_norm = P.rms_ffn + (int64_t)l * P.dim;
+        } else if (ph == 3) {   // RMSNorm (FFN) + gate|up
+            mph = PH_GU;
+            nw = P.rms_ffn + (int64_t)l * P.dim;
+            if (gem) {   // post-attention norm + residual
+                mode = SRC_GEMMA_ADD;
+                t = P.xb2;
+                tw = P.post_att + (int64_t)l * P.dim;
+                xout = xalt;
+                swap = true;
+            } else {
+                staged = true;
+            }
+        } else {   // down (+ residual)
+            mph = PH_DOWN;
+            src = P.hb;
+            ld = K = P.hidden;
+            next_norm = l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final;
+        }
+        prep_phase(P, mode, src, ld, K, nw, t, tw, xout, prep, vec, s_red, cls ? lsum_c : lsum_l,
+                   tr ? &twave : nullptr, staged);
+        if (swap) {
+            float* tmp = xcur;
+            xcur = xalt;
+            xalt = tmp;
+        }
+        if (next_norm) stage_norm(next_norm);
+        mark_prep();
+        const DPhase f = make_phase(P, l, mph, xcur);
+        if constexpr (TYPE == CTYPE) {
+            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
         } else {
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_att + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l, tr ? &twave : nullptr, true);
+            if (cls)
+                mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+            else
+                mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
         }
-        mark_prep();
-        {
-            const DPhase f = make_phase(P, l, PH_QKV, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_QKV));
-            markv(tfull);
-        }
-        barrier();
-        if (aborted) break;
-        // ---- attention ----
-        attn_phase(P, l, vec, tr ? &twave : nullptr, rope, det(l, PH_ATTN));
-        markv(twave);   // the first load wave landed
-        twave = 0;
-        markv(0);
-        markv(0);
-        barrier();
-        if (aborted) break;
-        // ---- wo (+ residual) ----
-        prep_phase(P, SRC_PLAIN, P.xb, P.n_heads * P.hd, P.n_heads * P.hd, nullptr, nullptr, nullptr, nullptr, prep,
-                   vec, s_red, lsum_l, tr ? &twave : nullptr);
-        stage_norm(P.rms_ffn + (int64_t)l * P.dim);
-        mark_prep();
-        {
-            const DPhase f = make_phase(P, l, PH_O, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_O));
-            markv(tfull);
-        }
-        barrier();
-        if (aborted) break;
-        // ---- RMSNorm (FFN) + gate|up ----
-        if (gem) {
-            prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, P.xb2,
-                       P.post_att + (int64_t)l * P.dim, xalt, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
-            float* tmp = xcur; xcur = xalt; xalt = tmp;
-        } else {
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_ffn + (int64_t)l * P.dim, nullptr, nullptr, nullptr, prep,
-                       vec, s_red, lsum_l, tr ? &twave : nullptr, true);
-        }
-        mark_prep();
-        {
-            const DPhase f = make_phase(P, l, PH_GU, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_GU));
-            markv(tfull);
-        }
-        barrier();
-        if (aborted) break;
-        // ---- down (+ residual) ----
-        prep_phase(P, SRC_PLAIN, P.hb, P.hidden, P.hidden, nullptr, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_l, tr ? &twave : nullptr);
-        stage_norm(l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final);
-        mark_prep();
-        {
-            const DPhase f = make_phase(P, l, PH_DOWN, xcur);
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, PH_DOWN));
-            markv(tfull);
+        markv(tfull);
+        if (cls) {
+            consumer_bar();
+            if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);
         }
         barrier();
     }
-    if (!aborted) {
-        // ---- final RMSNorm + classifier + argmax ----
-        if (gem)
-            prep_phase(P, SRC_GEMMA_ADD, xcur, P.dim, P.dim, P.rms_final, P.xb2, P.post_ffn + (int64_t)(L - 1) * P.dim,
-                       nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr);
-        else
-            prep_phase(P, SRC_PLAIN, xcur, P.dim, P.dim, P.rms_final, nullptr, nullptr, nullptr, prep, vec, s_red, lsum_c, tr ? &twave : nullptr,
-                       true);
-        mark_prep();
-        const DPhase f = make_phase(P, 0, PH_CLS, xcur);
-        mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(L, PH_CLS));
-        markv(tfull);
-        consumer_bar();
-        if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);
-        barrier();
-        if (!aborted && blockIdx.x == 0) {
-            if (tid < P.batch) {
-                const unsigned long long k = atomicExch(&P.am_key[tid], 0ull);
-                P.am_out[tid] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-            }
-            if (tid == 0) P.bar[1] = target;   // arrival count at the start of the next step
+    if (!aborted && blockIdx.x == 0) {
+        if (tid < P.batch) {
+            const unsigned long long k = atomicExch(&P.am_key[tid], 0ull);
+            P.am_out[tid] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         }
+        if (tid == 0) P.bar[1] = target;   // arrival count at the start of the next step
     }
 }
 
@@ -1226,8 +1263,8 @@ int decode_prepare(DecodeParams* p) {
         p->geo_gs[ph][0] = 1;
         for (int nt = 1; nt <= 9; ++nt) {
             int best = 1, fill = 0;
-            for (int gs = std::min(8, nt); gs >= 1; --gs)
-                if (gs * kc[gs] * bs > fill) {
+            for (int gs = 8; gs >= 1; gs >>= 1)
+                if (gs <= nt && gs * kc[gs] * bs > fill) {
                     fill = gs * kc[gs] * bs;
                     best = gs;
                 }

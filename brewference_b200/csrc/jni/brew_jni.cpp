@@ -1,8 +1,9 @@
 // brew_jni.cpp — JNI glue between the Java reference's classes and the C ABI
 // (include/brew.h).  Java side: class
-// com.epicmonstrosity.brewference.gpu.Brew (its source is shown in
-// INTEGRATION.md).  Built into libbrew.so by brewference_b200/build.py when
-// a JDK's jni.h is found (JAVA_HOME); this image has no JDK.
+// com.epicmonstrosity.brewference.gpu.Brew, a class of static native methods
+// that the reference's Linear, loader and ModelRunner call.  Built into
+// libbrew.so by brewference_b200/build.py when a JDK's jni.h is found
+// (JAVA_HOME).
 //
 // Errors become the Java exceptions the reference throws for the same
 // conditions: BREW_ERR_INVALID_ARG -> IllegalArgumentException

@@ -18,9 +18,14 @@
 // Larger requests fail with BREW_ERR_INVALID_ARG.  Q4_K / Q6_K weights use no
 // scratch and run the same kernel as brew_matmul_dev.
 //
-// Set-up: the first call on a device (with that device current) looks up the
-// array's device address with cudaGetSymbolAddress and keeps it; make that
-// first call before any stream capture begins.
+// Set-up: brew_init looks up the array's device address on the device it
+// makes current (cudaGetSymbolAddress, which also loads this file's module),
+// so the array is in place before the first call.  A later brew_init of
+// another device does the same there; a call on a device whose address is
+// still unknown looks it up first.  The kernels the call launches are loaded
+// by the CUDA runtime on their first launch (lazy module loading), so make
+// one call before entering a region that must not allocate or block, and
+// before any stream capture begins.
 //
 // Nothing in the array has to start at zero: every byte the matvec kernel
 // reads is written by the prep kernel earlier in the same call.
@@ -66,6 +71,13 @@ int static_scratch(uint8_t** out) {
 }
 
 }  // namespace
+
+// Called by brew_init with the new device current.
+int static_scratch_setup() {
+    uint8_t* p = nullptr;
+    return static_scratch(&p);
+}
+
 }  // namespace brew
 
 using namespace brew;

@@ -412,12 +412,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* x, int ldx, int 
 
 template <int TYPE, int NT>
 int launch_typed(const MvParams& p, cudaStream_t stream, bool pdl, int grid, size_t smem) {
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(mv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
-    BREW_CUDA(attr_err);
+    static std::mutex mu;
+    static unsigned long long attr_set = 0;   // one bit per device
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        BREW_CUDA(smem_attr_per_device((const void*)mv_kernel<TYPE, NT>, 200 * 1024, &attr_set));
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(MV_THREADS);

@@ -130,6 +130,8 @@ int tp_argmax_keys_launch(const float* logits, int ld, int n, int B, int row0, u
 }
 
 int tp_argmax_reduce_launch(const unsigned long long* keys, int P, int B, int32_t* out, cudaStream_t stream) {
+    // one thread per sequence in a single warp
+    BREW_CHECK(B >= 1 && B <= 32, BREW_ERR_INVALID_ARG, "sharded argmax: %d sequences (at most 32)", B);
     argmax_reduce_kernel<<<1, 32, 0, stream>>>(keys, P, B, out);
     BREW_CUDA(cudaGetLastError());
     count_launch();

@@ -63,12 +63,18 @@ extern "C" {
 #define BREW_ARCH_QWEN2  1   /* model/qwen2/Qwen2Transformer.java:27-84     */
 #define BREW_ARCH_QWEN3  2   /* model/qwen3/Qwen3Transformer.java:27-85     */
 #define BREW_ARCH_GEMMA3 3   /* model/gemma3/Gemma3Transformer.java:27-92   */
+#define BREW_ARCH_GEMMA2 4   /* model/gemma2/Gemma2Transformer.java:27-87   */
+#define BREW_ARCH_SMOLLM3 5  /* model/smollm3/SmolLM3Transformer.java:40-94 */
 
 /* Model hyper-parameters: the fields of gguf/Config.java that the forward
  * pass reads (GgufConfigParser.java:9-59), plus the GGML type of each weight
  * matrix.  `rope_base` <= 0 selects the architecture's fallback exactly as the
- * reference's suppliers do (Llama2Transformer.java:45 -> 1e4,
- * Qwen2/Qwen3 -> 1e6, Gemma3Transformer.java:51 -> 1e6 global / 1e4 local). */
+ * reference's suppliers do (Llama2Transformer.java:45 and
+ * SmolLM3Transformer.java:60 -> 1e4, Qwen2/Qwen3 -> 1e6,
+ * Gemma3Transformer.java:51 and Gemma2Transformer.java:47 -> 1e6 global /
+ * 1e4 local).  SmolLM3 skips RoPE on every 4th layer
+ * (SmolLM3Transformer.java:48); Gemma2 attends globally on every 2nd layer
+ * (Gemma2AttentionPattern.java:10-12), Gemma3 on every 6th. */
 typedef struct brew_config {
     int32_t arch;
     int32_t dim;             /* {arch}.embedding_length                      */
@@ -166,10 +172,11 @@ BREW_API int brew_matmul_dev(float* output_dev, const float* input_dev, brew_ten
  * errors as brew_matmul_dev, plus: brew_init must have been called
  * (BREW_ERR_INVALID_ARG otherwise); (input_size / 32) * record bytes of
  * min(batch, 16) vectors must fit in 256 KiB (input_size <= 74880 at batch
- * 1, <= 4672 at batch 16), else BREW_ERR_INVALID_ARG.  The first call on a
- * device looks up the array's address; make it before any stream capture
- * starts.  Calls whose device work may overlap (different unordered streams)
- * race on the one array. */
+ * 1, <= 4672 at batch 16), else BREW_ERR_INVALID_ARG.  brew_init looks up
+ * the array's address on its device; the kernels themselves are loaded on
+ * their first launch, so make one call before entering a region that must
+ * not allocate and before any stream capture starts.  Calls whose device
+ * work may overlap (different unordered streams) race on the one array. */
 BREW_API int brew_matmul_dev_static(float* output_dev, const float* input_dev, brew_tensor weights,
                     int64_t weights_offset, int32_t input_size, int32_t output_size,
                     int32_t batch, void* stream);

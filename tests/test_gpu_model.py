@@ -78,22 +78,26 @@ def test_gemma_window_crossing(device):
 
 
 def test_batched_forward_matches_single(device):
+    """Four sequences forwarded together, each with its own KV cache: every
+    step's logits of every sequence against the oracle run on that sequence
+    alone, and the device argmax against the logits."""
     cfg = small(C.ARCH_QWEN3)
     dm = DeviceModel.synthesize(cfg, 5, max_batch=4)
     om = oracle.OracleModel(cfg, 5)
-    # sequence 0 advances through 6 positions; the batch rows use their own caches
     toks = [[3, 9, 27, 81], [4, 8, 15, 16], [1, 1, 2, 3]]
+    got = []
     for step in range(len(toks)):
         lg, am = dm.forward(toks[step], [step] * 4)
+        got.append(lg.copy())
         for b in range(4):
-            pass
-    # oracle per sequence b
+            assert am[b] == int(np.argmax(lg[b])), (step, b)
     for b in range(4):
         om.reset()
         for step in range(len(toks)):
             ref = om.forward(toks[step][b], step)
-        assert rel(lg[b], ref) < LOGIT_TOL, b
+            assert rel(got[step][b], ref) < LOGIT_TOL, (step, b, rel(got[step][b], ref))
     dm.close()
+    om.close()
 
 
 def test_smollm2_135m_full_shape(device):
