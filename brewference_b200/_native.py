@@ -111,6 +111,7 @@ def lib():
         "brew_model_create": (I, [ctypes.POINTER(BrewConfig), ctypes.POINTER(ModelWeights), ctypes.c_int32, c_void_pp]),
         "brew_model_synthesize": (I, [ctypes.POINTER(BrewConfig), ctypes.c_uint64, ctypes.c_int32, c_void_pp]),
         "brew_model_free": (I, [V]),
+        "brew_model_config": (I, [V, ctypes.POINTER(BrewConfig)]),
         "brew_model_tensor": (I, [V, I, c_void_pp]),
         "brew_model_forward": (I, [V, c_i32p, c_i32p, ctypes.c_int32, c_f32p, c_i32p]),
         "brew_model_forward_dev": (I, [V, V, V, ctypes.c_int32, V, V, V]),
@@ -121,6 +122,13 @@ def lib():
         "brew_model_step_kernels": (I, [V, ctypes.c_int32, c_i32p]),
         "brew_model_set_trace": (I, [V, ctypes.c_int32]),
         "brew_model_trace": (I, [V, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32, c_i32p]),
+        "brew_gguf_open": (I, [ctypes.c_char_p, c_void_pp]),
+        "brew_gguf_close": (I, [V]),
+        "brew_gguf_config": (I, [V, ctypes.POINTER(BrewConfig)]),
+        "brew_gguf_tensor_count": (I, [V, ctypes.POINTER(I64)]),
+        "brew_gguf_tensor_info": (I, [V, I64, ctypes.c_char_p, S, ctypes.POINTER(I), ctypes.POINTER(I64),
+                                      ctypes.POINTER(I64)]),
+        "brew_model_load_gguf": (I, [ctypes.c_char_p, ctypes.c_int32, c_void_pp]),
         "brew_prep_bytes": (I64, [ctypes.c_int32, ctypes.c_int32]),
         "brew_prepare_input_dev": (I, [V, ctypes.c_int32, ctypes.c_int32, V, V]),
         "brew_matmul_prepared_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),

@@ -16,6 +16,7 @@ IllegalStateException (see _native).
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -194,6 +195,49 @@ class Communicator:
             self.handle = None
 
 
+class GgufFile:
+    """A memory-mapped GGUF checkpoint (brew_gguf_open): the header, metadata
+    and tensor infos as the reference's gguf/Reader.java reads them, and the
+    model config as GgufConfigParser and the per-architecture loaders derive
+    it.  Needs no GPU."""
+
+    def __init__(self, path: str):
+        h = ctypes.c_void_p()
+        N.check(N.lib().brew_gguf_open(os.fsencode(path), ctypes.byref(h)), "gguf_open")
+        self.handle = h.value
+        self.path = path
+
+    def config(self) -> ModelConfig:
+        c = BrewConfig()
+        N.check(N.lib().brew_gguf_config(self.handle, ctypes.byref(c)), "gguf_config")
+        kw = {f: getattr(c, f) for f, _ in BrewConfig._fields_}
+        return ModelConfig(name=os.path.basename(self.path), **kw)
+
+    def tensors(self) -> list:
+        """[(name, ggml type, elements, absolute file offset of the data)]"""
+        n = ctypes.c_int64()
+        N.check(N.lib().brew_gguf_tensor_count(self.handle, ctypes.byref(n)))
+        out = []
+        name = ctypes.create_string_buffer(512)
+        t, ne, off = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+        for i in range(n.value):
+            N.check(N.lib().brew_gguf_tensor_info(self.handle, i, name, len(name), ctypes.byref(t), ctypes.byref(ne),
+                                                  ctypes.byref(off)))
+            out.append((name.value.decode(), t.value, ne.value, off.value))
+        return out
+
+    def close(self):
+        if self.handle:
+            N.lib().brew_gguf_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
 class DeviceModel:
     """A device-resident model: weights, fp32 KV caches and the CUDA graphs of
     its forward pass."""
@@ -208,6 +252,16 @@ class DeviceModel:
         c = cfg.to_c()
         h = ctypes.c_void_p()
         N.check(N.lib().brew_model_synthesize(ctypes.byref(c), seed, max_batch, ctypes.byref(h)), "model_synthesize")
+        return cls(h.value, cfg, max_batch)
+
+    @classmethod
+    def load_gguf(cls, path: str, max_batch: int = 1) -> "DeviceModel":
+        """GgufCheckpointLoader.loadWeights + model creation in one call
+        (brew_model_load_gguf): packed blocks from the file to HBM unchanged."""
+        with GgufFile(path) as g:
+            cfg = g.config()
+        h = ctypes.c_void_p()
+        N.check(N.lib().brew_model_load_gguf(os.fsencode(path), max_batch, ctypes.byref(h)), "model_load_gguf")
         return cls(h.value, cfg, max_batch)
 
     @classmethod

@@ -17,8 +17,11 @@ TYPE_NAMES = {0: "F32", 1: "F16", 2: "Q4_0", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
 # (elements per block, bytes per block) of each GGML type
 TYPE_BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
 
-ARCH_LLAMA, ARCH_QWEN2, ARCH_QWEN3, ARCH_GEMMA3 = 0, 1, 2, 3
-ARCH_NAMES = {0: "llama", 1: "qwen2", 2: "qwen3", 3: "gemma3"}
+ARCH_LLAMA, ARCH_QWEN2, ARCH_QWEN3, ARCH_GEMMA3, ARCH_GEMMA2, ARCH_SMOLLM3 = 0, 1, 2, 3, 4, 5
+# general.architecture values the reference's ModelRunnerFactory accepts
+# (model/ModelRunnerFactory.java:29-47); "llama2" runs the llama graph
+ARCH_NAMES = {0: "llama", 1: "qwen2", 2: "qwen3", 3: "gemma3", 4: "gemma2", 5: "smollm3"}
+ARCH_IDS = {"llama": 0, "llama2": 0, "qwen2": 1, "qwen3": 2, "gemma3": 3, "gemma2": 4, "smollm3": 5}
 
 # tensor indices used by brew_model_tensor / the synthetic generator
 W_EMBED, W_OUTPUT, W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(9)
@@ -148,9 +151,37 @@ def qwen25_7b(**kw) -> ModelConfig:
                        name="qwen2.5-7b-shaped", **kw)
 
 
+def gemma2_2b(**kw) -> ModelConfig:
+    """Gemma-2-2B-shaped model, Q8_0: head size 256 (hard-coded by the
+    reference's Gemma2CheckpointLoader), sliding window 4096 on every other
+    layer, GeGLU, pre/post norms."""
+    return ModelConfig(arch=ARCH_GEMMA2, dim=2304, hidden_dim=9216, n_layers=26, n_heads=8, n_kv_heads=4,
+                       head_size=256, vocab_size=256000, seq_len=8192, eps=1e-6, rope_base=0.0,
+                       sliding_window=4096, name="gemma2-2b-shaped", **kw)
+
+
+def smollm3_3b(**kw) -> ModelConfig:
+    """SmolLM3-3B-shaped model, Q8_0: Llama layout (q and wo are dim x dim),
+    no RoPE on every 4th layer."""
+    return ModelConfig(arch=ARCH_SMOLLM3, dim=2048, hidden_dim=11008, n_layers=36, n_heads=16, n_kv_heads=4,
+                       head_size=128, vocab_size=128256, seq_len=4096, eps=1e-6, rope_base=0.0,
+                       name="smollm3-3b-shaped", **kw)
+
+
+def llama2_7b(**kw) -> ModelConfig:
+    """Llama-2-7B-shaped model, Q8_0, untied output (the reference's largest
+    published Q8_0 run)."""
+    return ModelConfig(arch=ARCH_LLAMA, dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, n_kv_heads=32,
+                       head_size=128, vocab_size=32000, seq_len=4096, eps=1e-5, rope_base=0.0,
+                       tied_embeddings=0, name="llama2-7b-shaped", **kw)
+
+
 PRESETS = {
     "smollm2-135m": smollm2_135m,
     "qwen3-1.7b": qwen3_1_7b,
     "gemma3-1b": gemma3_1b,
     "qwen2.5-7b": qwen25_7b,
+    "gemma2-2b": gemma2_2b,
+    "smollm3-3b": smollm3_3b,
+    "llama2-7b": llama2_7b,
 }

@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const __grid_constant__ AttnP
         }
         __syncthreads();
     }
-    const bool inter = p.arch == BREW_ARCH_LLAMA;
-    for (int idx = tid; idx < (G + 1) * half; idx += blockDim.x) {
+    const bool inter = arch_interleaved(p.arch);
+    for (int idx = tid; p.rope && idx < (G + 1) * half; idx += blockDim.x) {
         const int hh = idx / half, d = idx % half;
         float* vec = hh < G ? qs + hh * hd : ks;
         const int i0 = inter ? 2 * d : d;

@@ -9,6 +9,7 @@ struct AttnParams {
     int batch, n_heads, n_kv, hd, seq_len;
     int arch;                  // BREW_ARCH_*: selects QK-norm and RoPE layout
     int window;                // > 0: sliding window start = pos - window + 1
+    int rope;                  // 1: rotate q and k (0: SmolLM3's no-RoPE layers)
     float eps, rope_base, rope_scale, inv_scale;
     const float* q;            // [batch][ldq]  (after bias)
     const float* k;            // [batch][ldkv]

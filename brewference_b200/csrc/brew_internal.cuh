@@ -45,6 +45,8 @@ int run_matvec_prepared(brew_tensor t, int64_t weights_offset, const uint8_t* pr
                         cudaStream_t stream);
 int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const uint8_t* prep, int K, int N, float* y,
                     int nb, cudaStream_t stream);
+// Makes a model created with brew_model_create own (and free) its tensors.
+void model_adopt_tensors(brew_model m);
 // Looks up the device address of brew_matmul_dev_static's module array on
 // the current device (brew_init calls it).
 int static_scratch_setup();

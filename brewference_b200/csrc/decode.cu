@@ -63,7 +63,7 @@ struct DPhase {
 __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int ph, float* xcur) {
     DPhase f = {};
     const int qw = P.n_heads * P.hd, kvd = P.n_kv * P.hd;
-    const bool gem = P.arch == BREW_ARCH_GEMMA3;
+    const bool gem = arch_gemma(P.arch);
     f.epi = MV_EPI_STORE;
     f.tt = P.type_layer;
     f.ph = ph;
@@ -249,7 +249,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += 256) {
                 float v = dequant_elem(P.type_embed, P.embed, (int64_t)tok * K + i);
-                vec[i] = P.arch == BREW_ARCH_GEMMA3 ? __fmul_rn(v, es) : v;
+                vec[i] = arch_gemma(P.arch) ? __fmul_rn(v, es) : v;
             }
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
@@ -580,7 +580,7 @@ struct RopeRegs {
 __device__ __forceinline__ RopeRegs load_rope(const DecodeParams& P) {
     RopeRegs r = {};
     const int half = P.hd / 2, d = threadIdx.x % half;
-    const bool two = P.arch == BREW_ARCH_GEMMA3;
+    const bool two = arch_gemma(P.arch);
     float* cv[2][2] = {{&r.c00, &r.c01}, {&r.c10, &r.c11}};
     float* sv[2][2] = {{&r.s00, &r.s01}, {&r.s10, &r.s11}};
 #pragma unroll
@@ -609,8 +609,7 @@ __shared__ int s_pos[DK_MAX_BATCH];
 
 __device__ __forceinline__ bool attn_item(const DecodeParams& P, int l, int item, AttnItem& it) {
     const int nch = P.nchunk;
-    const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
-    const int window = (P.arch == BREW_ARCH_GEMMA3 && !global) ? P.window : 0;
+    const int window = arch_window(P.arch, l, P.window);   // Gemma2/Gemma3AttentionPattern.java:10-16
     it.c = item % nch;
     it.hk = (item / nch) % P.n_kv;
     it.b = item / (nch * P.n_kv);
@@ -650,10 +649,9 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool gem = P.arch == BREW_ARCH_GEMMA3;
-    const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
-    const int table = (gem && !global) ? 1 : 0;
-    const bool inter = P.arch == BREW_ARCH_LLAMA;
+    const int table = (arch_gemma(P.arch) && !arch_global_layer(P.arch, l)) ? 1 : 0;   // local-layer base
+    const bool inter = arch_interleaved(P.arch);
+    const bool rope_on = arch_rope_layer(P.arch, l);
     const int nch = P.nchunk;
     const int SUB = attn_sub(hd);
     const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
@@ -730,7 +728,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             }
             stamp(2);
             #pragma unroll 1
-            for (int idx = tid; idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
+            for (int idx = tid; rope_on && idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
                 const int hh = idx / half, d = idx % half;
                 float* vecp = hh < G ? qs + hh * hd : ks;
                 const int i0 = inter ? 2 * d : d;
@@ -997,7 +995,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     unsigned long long target = s_base;
     int q = 0;
     bool aborted = false;
-    const bool gem = P.arch == BREW_ARCH_GEMMA3;
+    const bool gem = arch_gemma(P.arch);
     constexpr bool lsum_l = TYPE == BREW_TYPE_Q4_0, lsum_c = CTYPE == BREW_TYPE_Q4_0;
     float* xcur = P.x0;
     float* xalt = P.x1;

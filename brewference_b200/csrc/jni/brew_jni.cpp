@@ -134,6 +134,26 @@ JNIEXPORT jlong JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_modelCreat
     return reinterpret_cast<jlong>(m);
 }
 
+// GgufCheckpointLoader.loadWeights + GgufWeightsLoader.load in one call: the
+// checkpoint's packed blocks go from the file to HBM (brew_model_load_gguf).
+JNIEXPORT jlong JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_loadGguf(JNIEnv* env, jclass, jstring path,
+                                                                               jint maxBatch) {
+    if (!path) {
+        jclass c = env->FindClass("java/lang/IllegalArgumentException");
+        if (c) env->ThrowNew(c, "path cannot be null");
+        return 0;
+    }
+    const char* p = env->GetStringUTFChars(path, nullptr);
+    brew_model m = nullptr;
+    const int rc = brew_model_load_gguf(p, maxBatch, &m);
+    env->ReleaseStringUTFChars(path, p);
+    if (rc) {
+        throw_for(env, rc);
+        return 0;
+    }
+    return reinterpret_cast<jlong>(m);
+}
+
 JNIEXPORT void JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_modelFree(JNIEnv*, jclass, jlong m) {
     brew_model_free(reinterpret_cast<brew_model>(m));
 }
@@ -159,11 +179,19 @@ JNIEXPORT jint JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_forward(JNI
     return am;
 }
 
-// Greedy generation with ModelRunner's token order; returns the new ids.
+// Greedy generation with ModelRunner's token order; returns the new ids
+// (maxNew <= 0: up to the rest of the context).
 JNIEXPORT jintArray JNICALL Java_com_epicmonstrosity_brewference_gpu_Brew_generate(JNIEnv* env, jclass, jlong m,
                                                                                    jintArray prompt, jint maxNew) {
     const jsize n = env->GetArrayLength(prompt);
-    std::vector<int32_t> pr(n), out(maxNew > 0 ? maxNew : 0);
+    brew_config c = {};
+    const int rc0 = brew_model_config(reinterpret_cast<brew_model>(m), &c);
+    if (rc0) {
+        throw_for(env, rc0);
+        return nullptr;
+    }
+    const int cap = maxNew > 0 ? maxNew : (c.seq_len > n ? c.seq_len - n : 0);
+    std::vector<int32_t> pr(n), out(cap > 0 ? cap : 1);
     env->GetIntArrayRegion(prompt, 0, n, reinterpret_cast<jint*>(pr.data()));
     int32_t n_out = 0;
     const int rc = brew_session_generate(reinterpret_cast<brew_model>(m), pr.data(), n, maxNew, out.data(), &n_out);

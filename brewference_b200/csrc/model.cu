@@ -157,7 +157,7 @@ bool uses_kquants(const brew_config& c) {
 }
 
 int check_config(const brew_config& c, int max_batch) {
-    BREW_CHECK(c.arch >= BREW_ARCH_LLAMA && c.arch <= BREW_ARCH_GEMMA3, BREW_ERR_UNSUPPORTED, "arch %d", c.arch);
+    BREW_CHECK(c.arch >= BREW_ARCH_LLAMA && c.arch <= BREW_ARCH_SMOLLM3, BREW_ERR_UNSUPPORTED, "arch %d", c.arch);
     BREW_CHECK(c.dim > 0 && c.dim % 32 == 0, BREW_ERR_INVALID_ARG, "dim %d", c.dim);
     BREW_CHECK(c.hidden_dim > 0 && c.hidden_dim % 32 == 0, BREW_ERR_INVALID_ARG, "hidden_dim %d", c.hidden_dim);
     BREW_CHECK(c.n_layers > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0,
@@ -489,8 +489,8 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
     const brew_config& c = m->c;
     const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
     const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
-    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
-    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    const bool gemma = arch_gemma(c.arch);
+    const bool qknorm = arch_qknorm(c.arch);
     unsigned int* err = ctx().err_word;
     int* attn_ctr = m->counters + hid / 32 + 8;
     int rc;
@@ -567,15 +567,10 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             a.hd = hd;
             a.seq_len = c.seq_len;
             a.arch = c.arch;
-            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
-            a.window = (gemma && !global) ? c.sliding_window : 0;
+            a.window = arch_window(c.arch, l, c.sliding_window);   // Gemma2/Gemma3AttentionPattern.java:10-16
+            a.rope = arch_rope_layer(c.arch, l) ? 1 : 0;
             a.eps = c.eps;
-            float base;
-            if (c.rope_base > 0.0f) base = c.rope_base;
-            else if (c.arch == BREW_ARCH_LLAMA) base = 10000.0f;
-            else if (gemma) base = global ? 1000000.0f : 10000.0f;
-            else base = 1000000.0f;
-            a.rope_base = base;
+            a.rope_base = arch_rope_base(c.arch, c.rope_base, gemma && !arch_global_layer(c.arch, l));
             a.rope_scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
             a.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
             a.q = q;
@@ -674,8 +669,8 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
     const brew_config& c = m->c;
     const int L = c.n_layers, dim = c.dim, hd = c.head_size, hid = c.hidden_dim;
     const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd;
-    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
-    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    const bool gemma = arch_gemma(c.arch);
+    const bool qknorm = arch_qknorm(c.arch);
     unsigned int* err = ctx().err_word;
     int* group_ctr = m->counters;
     int* post_ctr = group_ctr + hid / 32;
@@ -716,15 +711,10 @@ int enqueue_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s
             a.hd = hd;
             a.seq_len = c.seq_len;
             a.arch = c.arch;
-            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
-            a.window = (gemma && !global) ? c.sliding_window : 0;
+            a.window = arch_window(c.arch, l, c.sliding_window);   // Gemma2/Gemma3AttentionPattern.java:10-16
+            a.rope = arch_rope_layer(c.arch, l) ? 1 : 0;
             a.eps = c.eps;
-            float base;
-            if (c.rope_base > 0.0f) base = c.rope_base;
-            else if (c.arch == BREW_ARCH_LLAMA) base = 10000.0f;
-            else if (gemma) base = global ? 1000000.0f : 10000.0f;
-            else base = 1000000.0f;
-            a.rope_base = base;
+            a.rope_base = arch_rope_base(c.arch, c.rope_base, gemma && !arch_global_layer(c.arch, l));
             a.rope_scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
             a.inv_scale = 1.0f / (float)std::sqrt((double)hd);   // AttentionEngine.java:18-19
             a.q = m->qkv;
@@ -929,9 +919,8 @@ int ensure_rope_tables(brew_model_s* m) {
     int rc;
     if ((rc = dalloc(m, &m->rope_cos, (size_t)2 * c.seq_len * half))) return rc;
     if ((rc = dalloc(m, &m->rope_sin, (size_t)2 * c.seq_len * half))) return rc;
-    const bool gem = c.arch == BREW_ARCH_GEMMA3;
-    const float base0 = c.rope_base > 0.0f ? c.rope_base : (c.arch == BREW_ARCH_LLAMA ? 10000.0f : 1000000.0f);
-    const float base1 = c.rope_base > 0.0f ? c.rope_base : (gem ? 10000.0f : base0);
+    const float base0 = arch_rope_base(c.arch, c.rope_base, false);   // global / only table
+    const float base1 = arch_rope_base(c.arch, c.rope_base, true);    // Gemma local layers
     const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
     return rope_tables_launch(m->rope_cos, m->rope_sin, c.seq_len, hd, base0, base1, scale, ctx().stream);
 }
@@ -988,8 +977,8 @@ int prefill_batched(brew_model_s* m, const int32_t* tok_d, int n, cudaStream_t s
     const brew_config& c = m->c;
     const int L = c.n_layers, dim = c.dim, hid = c.hidden_dim, hd = c.head_size;
     const int qw = c.n_heads * hd, kvd = c.n_kv_heads * hd, qkvw = qw + 2 * kvd;
-    const bool gemma = c.arch == BREW_ARCH_GEMMA3;
-    const bool qknorm = c.arch == BREW_ARCH_QWEN3 || gemma;
+    const bool gemma = arch_gemma(c.arch);
+    const bool qknorm = arch_qknorm(c.arch);
     unsigned int* err = ctx().err_word;
     const int N[4] = {qkvw, dim, 2 * hid, dim}, K[4] = {dim, qw, dim, hid};
     int rc;
@@ -1007,7 +996,7 @@ int prefill_batched(brew_model_s* m, const int32_t* tok_d, int n, cudaStream_t s
                                        err, s)))
             return rc;
         for (int l = 0; l < L; ++l) {
-            const bool global = ((l + 1) % 6) == 0;   // Gemma3AttentionPattern.java:10-12
+            const bool global = arch_global_layer(c.arch, l);
             if ((rc = rmsnorm_launch(m->pf_x, dim, m->rms_att + (int64_t)l * dim, c.eps, dim, T, m->pf_xn, dim, s)) ||
                 (rc = gemm(0, l, m->pf_xn, dim, m->pf_qkv)))
                 return rc;
@@ -1026,7 +1015,8 @@ int prefill_batched(brew_model_s* m, const int32_t* tok_d, int n, cudaStream_t s
             qk.hd = hd;
             qk.seq_len = c.seq_len;
             qk.table = (gemma && !global) ? 1 : 0;
-            qk.interleaved = c.arch == BREW_ARCH_LLAMA;
+            qk.interleaved = arch_interleaved(c.arch);
+            qk.rope = arch_rope_layer(c.arch, l);
             qk.eps = c.eps;
             qk.qkv = m->pf_qkv;
             qk.ldq = qkvw;
@@ -1140,9 +1130,8 @@ int setup_decode(brew_model_s* m) {
     if ((rc = dalloc(m, &m->rope_sin, (size_t)2 * c.seq_len * half))) return rc;
     if ((rc = dalloc(m, &m->bar, 2))) return rc;
     if ((rc = dalloc(m, &m->abort_flag, 1))) return rc;
-    const bool gem = c.arch == BREW_ARCH_GEMMA3;
-    const float base0 = c.rope_base > 0.0f ? c.rope_base : (c.arch == BREW_ARCH_LLAMA ? 10000.0f : 1000000.0f);
-    const float base1 = c.rope_base > 0.0f ? c.rope_base : (gem ? 10000.0f : base0);
+    const float base0 = arch_rope_base(c.arch, c.rope_base, false);   // global / only table
+    const float base1 = arch_rope_base(c.arch, c.rope_base, true);    // Gemma local layers
     const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
     if ((rc = rope_tables_launch(m->rope_cos, m->rope_sin, c.seq_len, hd, base0, base1, scale, ctx().stream))) return rc;
     DecodeParams& p = m->dp;
@@ -1259,6 +1248,21 @@ int model_finish_create(brew_model_s* m) {
     return BREW_OK;
 }
 
+void model_destroy(brew_model_s* m);
+
+}  // namespace
+
+void model_adopt_tensors(brew_model_s* m) {
+    if (m->c.tied_embeddings) {   // the classifier becomes a view of the embedding
+        brew_tensor v = new brew_tensor_s(*m->t[T_EMBED]);
+        v->owned = false;
+        m->t[T_OUTPUT] = v;
+    }
+    m->owns_tensors = true;
+}
+
+namespace {
+
 void model_destroy(brew_model_s* m) {
     if (!m) return;
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
@@ -1295,9 +1299,9 @@ int brew_model_create(const brew_config* cfg, const brew_model_weights* w, int32
         BREW_CHECK(ts[i]->n == rows * cols * layers, BREW_ERR_INVALID_ARG, "tensor %d has %lld elements, expected %lld", i,
                    (long long)ts[i]->n, (long long)(rows * cols * layers));
     }
-    const bool gemma = c.arch == BREW_ARCH_GEMMA3, qk = c.arch == BREW_ARCH_QWEN3 || gemma, bias = c.arch == BREW_ARCH_QWEN2;
+    const bool gemma = arch_gemma(c.arch), qk = arch_qknorm(c.arch), bias = c.arch == BREW_ARCH_QWEN2;
     BREW_CHECK(w->rms_att && w->rms_ffn && w->rms_final, BREW_ERR_INVALID_ARG, "norm weights missing");
-    BREW_CHECK(!gemma || (w->post_att && w->post_ffn), BREW_ERR_INVALID_ARG, "Gemma3 post-norm weights missing");
+    BREW_CHECK(!gemma || (w->post_att && w->post_ffn), BREW_ERR_INVALID_ARG, "Gemma post-norm weights missing");
     BREW_CHECK(!qk || (w->rms_q && w->rms_k), BREW_ERR_INVALID_ARG, "QK-norm weights missing");
     BREW_CHECK(!bias || (w->q_bias && w->k_bias && w->v_bias), BREW_ERR_INVALID_ARG, "QKV bias missing");
     brew_model_s* m = new brew_model_s();
@@ -1354,11 +1358,11 @@ int brew_model_synthesize(const brew_config* cfg, uint64_t seed, int32_t max_bat
     if (!rc) rc = fill_vec(m, &m->rms_att, L * dim, 1.0f);
     if (!rc) rc = fill_vec(m, &m->rms_ffn, L * dim, 1.0f);
     if (!rc) rc = fill_vec(m, &m->rms_final, dim, 1.0f);
-    if (!rc && c.arch == BREW_ARCH_GEMMA3) {
+    if (!rc && arch_gemma(c.arch)) {
         rc = fill_vec(m, &m->post_att, L * dim, 1.0f);
         if (!rc) rc = fill_vec(m, &m->post_ffn, L * dim, 1.0f);
     }
-    if (!rc && (c.arch == BREW_ARCH_QWEN3 || c.arch == BREW_ARCH_GEMMA3)) {
+    if (!rc && arch_qknorm(c.arch)) {
         rc = fill_vec(m, &m->rms_q, L * hs, 1.0f);
         if (!rc) rc = fill_vec(m, &m->rms_k, L * hs, 1.0f);
     }
@@ -1378,6 +1382,12 @@ int brew_model_synthesize(const brew_config* cfg, uint64_t seed, int32_t max_bat
         return rc;
     }
     *out = m;
+    return BREW_OK;
+}
+
+int brew_model_config(brew_model m, brew_config* out) {
+    BREW_CHECK(m && out, BREW_ERR_INVALID_ARG, "null argument");
+    *out = m->c;
     return BREW_OK;
 }
 

@@ -58,7 +58,9 @@ __global__ void __launch_bounds__(256) prefill_qk_kernel(const __grid_constant__
     }
     const float* ct = p.rope_cos + ((int64_t)p.table * p.seq_len + pos) * half;
     const float* st = p.rope_sin + ((int64_t)p.table * p.seq_len + pos) * half;
-    if (p.interleaved) {
+    if (!p.rope) {
+        // no rotation on this layer
+    } else if (p.interleaved) {
         // pair (2d, 2d + 1): partner in the neighbouring lane, same register
 #pragma unroll
         for (int r = 0; r < R; ++r) {

@@ -29,6 +29,7 @@ struct PfQkParams {
     int T, pos0, n_heads, n_kv, hd, seq_len;
     int table;                    // RoPE table: 0 global / default base, 1 Gemma3 local
     bool interleaved;             // Llama pairs (2d, 2d+1); others (d, d + hd/2)
+    bool rope;                    // rotate q and k (false: SmolLM3's no-RoPE layers)
     float eps;
     float* qkv;                   // [T][ldq]
     int ldq;

@@ -245,6 +245,37 @@ typedef struct brew_model_weights {
 BREW_API int brew_model_create(const brew_config* cfg, const brew_model_weights* w,
                       int32_t max_batch, brew_model* out);
 
+/* ---- GGUF checkpoints (gguf/Reader.java, gguf/GgufConfigParser.java,
+ *      gguf/GgufWeightsLoader.java) ---------------------------------------
+ * brew_gguf_open memory-maps a GGUF v2/v3 file and parses its header,
+ * metadata and tensor infos as Reader.read does (Reader.java:25-58); errors
+ * (bad magic, version, truncation, alignment) are BREW_ERR_IO.
+ * brew_gguf_config fills a brew_config the way GgufConfigParser.parseCommon
+ * (GgufConfigParser.java:9-59) and the per-architecture loaders do
+ * (general.architecture -> arch, vocab = length of tokenizer.ggml.tokens,
+ * head size 128 for qwen3 (Qwen3CheckpointLoader.java:16), 256 for gemma2 /
+ * gemma3 (Gemma2/Gemma3CheckpointLoader.java:18), else dim / heads; tied
+ * when there is no output.weight, GgufWeightsLoader.java:159-162) plus the
+ * GGML type of each matrix family.  brew_gguf_tensor_info lists the tensors
+ * (name, GGML type, elements, absolute file offset of the data). */
+typedef struct brew_gguf_s* brew_gguf;
+BREW_API int brew_gguf_open(const char* path, brew_gguf* out);
+BREW_API int brew_gguf_close(brew_gguf g);
+BREW_API int brew_gguf_config(brew_gguf g, brew_config* cfg);
+BREW_API int brew_gguf_tensor_count(brew_gguf g, int64_t* n);
+BREW_API int brew_gguf_tensor_info(brew_gguf g, int64_t index, char* name, size_t name_size, int* type,
+                                   int64_t* n_elements, int64_t* file_offset);
+/* Loads a GGUF checkpoint into a device-resident model in one call: the
+ * replacement of GgufCheckpointLoader.loadWeights + GgufWeightsLoader.load
+ * (GgufWeightsLoader.java:24-165).  Packed Q8_0 / Q4_0 / Q4_K / Q6_K blocks
+ * go from the memory-mapped file to HBM unchanged through pinned staging
+ * buffers, each family's layers concatenated; F32 / F16 norm and bias
+ * vectors (readFloatArray, :249-278) are converted to fp32.  Unlike
+ * readQ8Block the tensor types are checked (BREW_ERR_UNSUPPORTED for other
+ * types, or a family whose layers differ in type).  The model owns its
+ * tensors. */
+BREW_API int brew_model_load_gguf(const char* path, int32_t max_batch, brew_model* out);
+
 /* Creates a model whose weights are generated on the device from `seed`
  * (seeded N(0, 0.02) quantized to the configured GGML types, norms 1.0).
  * The bytes equal those of the CPU generator used by the tests. */
@@ -272,6 +303,9 @@ BREW_API int brew_comm_free(brew_comm c);
 /* Shards model `m` over `comm` (same model on every rank, same seed or same
  * tensors).  The model then runs the unfused forward with the gathers. */
 BREW_API int brew_model_set_tp(brew_model m, brew_comm comm);
+
+/* The model's hyper-parameters and matrix types (as created or loaded). */
+BREW_API int brew_model_config(brew_model m, brew_config* out);
 
 /* Returns the model's tensors (borrowed handles) for inspection. */
 BREW_API int brew_model_tensor(brew_model m, int which, brew_tensor* out);

@@ -688,7 +688,10 @@ ob_model* ob_model_synth(const brew_config* cfg, uint64_t seed) {
     m->rms_att = filled(L * dim, 1.0f);
     m->rms_ffn = filled(L * dim, 1.0f);
     m->rms_final = filled(dim, 1.0f);
-    if (c->arch == BREW_ARCH_GEMMA3) { m->post_att = filled(L * dim, 1.0f); m->post_ffn = filled(L * dim, 1.0f); }
+    if (c->arch == BREW_ARCH_GEMMA3 || c->arch == BREW_ARCH_GEMMA2) {
+        m->post_att = filled(L * dim, 1.0f);
+        m->post_ffn = filled(L * dim, 1.0f);
+    }
     if (c->arch == BREW_ARCH_QWEN3 || c->arch == BREW_ARCH_GEMMA3) { m->rms_q = filled(L * hs, 1.0f); m->rms_k = filled(L * hs, 1.0f); }
     if (c->arch == BREW_ARCH_QWEN2) {
         m->q_bias = (float*)malloc((size_t)(L * qw) * sizeof(float));
@@ -789,19 +792,24 @@ static void attn_task(void* vctx, int64_t h0, int64_t h1) {
 
 static void accum(float* a, const float* b, int n) { for (int i = 0; i < n; i++) a[i] += b[i]; }
 
-/* The four forward passes (model/llama2/Llama2Transformer.java:27-79,
+/* The six forward passes (model/llama2/Llama2Transformer.java:27-79,
  * model/qwen2/Qwen2Transformer.java:27-84, model/qwen3/Qwen3Transformer.java:27-85,
- * model/gemma3/Gemma3Transformer.java:27-92) share this body; the switches
- * mark where they differ. */
+ * model/gemma3/Gemma3Transformer.java:27-92, model/gemma2/Gemma2Transformer.java:28-87,
+ * model/smollm3/SmolLM3Transformer.java:28-81) share this body; the switches
+ * mark where they differ.  Gemma2 is Gemma3 without the head-wise q/k norms
+ * and with a global layer every 2nd layer; SmolLM3 is Llama2 without RoPE on
+ * every 4th layer. */
 int ob_model_forward(ob_model* m, int token, int pos, float* logits_out) {
     const brew_config* c = &m->c;
     const int dim = c->dim, hs = c->head_size, hid = c->hidden_dim;
     const int qw = c->n_heads * hs, kvd = c->n_kv_heads * hs;
     const int arch = c->arch;
+    const int gemma = arch == BREW_ARCH_GEMMA3 || arch == BREW_ARCH_GEMMA2;
+    const int interleaved = arch == BREW_ARCH_LLAMA || arch == BREW_ARCH_SMOLLM3;
     if (token < 0 || token >= c->vocab_size || pos < 0 || pos >= c->seq_len) return -1;
 
     ob_dequantize(c->type_embed, m->t[OB_W_EMBED], (int64_t)token * dim, dim, m->x);
-    if (arch == BREW_ARCH_GEMMA3) {                       /* Kernels.scaleEmbeddings */
+    if (gemma) {                                          /* Kernels.scaleEmbeddings */
         const float s = (float)sqrt((double)dim);
         for (int i = 0; i < dim; i++) m->x[i] *= s;
     }
@@ -821,33 +829,37 @@ int ob_model_forward(ob_model* m, int token, int pos, float* logits_out) {
             ob_headwise_rmsnorm(m->q, m->rms_q + (int64_t)l * hs, c->n_heads, hs, c->eps);
             ob_headwise_rmsnorm(m->k, m->rms_k + (int64_t)l * hs, c->n_kv_heads, hs, c->eps);
         }
-        const int global = ((l + 1) % 6) == 0;            /* Gemma3AttentionPattern.java:10-12 */
+        int global = 1;
+        if (arch == BREW_ARCH_GEMMA3) global = ((l + 1) % 6) == 0;       /* Gemma3AttentionPattern.java:10-12 */
+        else if (arch == BREW_ARCH_GEMMA2) global = ((l + 1) % 2) == 0;  /* Gemma2AttentionPattern.java:10-12 */
         float base;
         if (c->rope_base > 0.0f) base = c->rope_base;
-        else if (arch == BREW_ARCH_LLAMA) base = 10000.0f;
-        else if (arch == BREW_ARCH_GEMMA3) base = global ? 1000000.0f : 10000.0f;
+        else if (interleaved) base = 10000.0f;            /* Llama2Transformer.java:45, SmolLM3Transformer.java:47 */
+        else if (gemma) base = global ? 1000000.0f : 10000.0f;  /* Gemma3Transformer.java:51, Gemma2Transformer.java:47 */
         else base = 1000000.0f;
         const float position = (float)pos * (c->rope_scale > 0.0f ? c->rope_scale : 1.0f);
-        ob_rope(m->q, m->k, c->n_heads, c->n_kv_heads, hs, base, position, arch == BREW_ARCH_LLAMA);
+        /* SmolLM3Transformer.java:35,46-47: no RoPE on every 4th layer */
+        if (!(arch == BREW_ARCH_SMOLLM3 && (l + 1) % 4 == 0))
+            ob_rope(m->q, m->k, c->n_heads, c->n_kv_heads, hs, base, position, interleaved);
         /* storeKeyValueInCache (AttentionEngine.java:34-38) */
         memcpy(m->kc + layer_off + (int64_t)pos * kvd, m->k, (size_t)kvd * sizeof(float));
         memcpy(m->vc + layer_off + (int64_t)pos * kvd, m->v, (size_t)kvd * sizeof(float));
         int start = 0;                                    /* Gemma3AttentionPattern.java:14-16 */
-        if (arch == BREW_ARCH_GEMMA3 && !global) {
+        if (gemma && !global) {
             start = pos - c->sliding_window + 1;
             if (start < 0) start = 0;
         }
         attn_ctx ac = {m, l, pos, start, layer_off, inv_scale};
         parallel_for(c->n_heads, 1, attn_task, &ac);
         ob_matvec(c->type_o, m->t[OB_W_O], (int64_t)l * dim * qw, m->xb, m->xb2, qw, dim);
-        if (arch == BREW_ARCH_GEMMA3) ob_rmsnorm(m->xb2, m->xb2, m->post_att + (int64_t)l * dim, dim, c->eps);
+        if (gemma) ob_rmsnorm(m->xb2, m->xb2, m->post_att + (int64_t)l * dim, dim, c->eps);
         accum(m->x, m->xb2, dim);
         ob_rmsnorm(m->xb, m->x, m->rms_ffn + (int64_t)l * dim, dim, c->eps);
         ob_matvec(c->type_gate, m->t[OB_W_GATE], (int64_t)l * dim * hid, m->xb, m->hb, dim, hid);
         ob_matvec(c->type_up, m->t[OB_W_UP], (int64_t)l * dim * hid, m->xb, m->hb2, dim, hid);
-        ob_glu(m->hb, m->hb2, hid, arch == BREW_ARCH_GEMMA3);
+        ob_glu(m->hb, m->hb2, hid, gemma);
         ob_matvec(c->type_down, m->t[OB_W_DOWN], (int64_t)l * dim * hid, m->hb, m->xb, hid, dim);
-        if (arch == BREW_ARCH_GEMMA3) ob_rmsnorm(m->xb, m->xb, m->post_ffn + (int64_t)l * dim, dim, c->eps);
+        if (gemma) ob_rmsnorm(m->xb, m->xb, m->post_ffn + (int64_t)l * dim, dim, c->eps);
         accum(m->x, m->xb, dim);
     }
     ob_rmsnorm(m->x, m->x, m->rms_final, dim, c->eps);

@@ -57,15 +57,21 @@ def test_qwen2_kquant_small(device):
     parity(cfg, 71, prompt_len=16, n_gen=64)
 
 
-@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN3, C.ARCH_GEMMA3])
+@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN3, C.ARCH_GEMMA3, C.ARCH_GEMMA2, C.ARCH_SMOLLM3])
 def test_other_archs_kquant(device, arch):
+    kw = dict(SMALL)
     if arch == C.ARCH_LLAMA:
         base = C.smollm2_135m().replace(dim=512, hidden_dim=1536, n_heads=8, n_kv_heads=4, head_size=64)
     elif arch == C.ARCH_QWEN3:
         base = C.qwen3_1_7b().replace(dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4)
+    elif arch == C.ARCH_GEMMA2:
+        base = C.gemma2_2b().replace(dim=1024, hidden_dim=2048, n_heads=4, n_kv_heads=2, sliding_window=8)
+    elif arch == C.ARCH_SMOLLM3:   # layer 3 runs without RoPE
+        base = C.smollm3_3b().replace(dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4)
+        kw["n_layers"] = 5
     else:
         base = C.gemma3_1b().replace(dim=1024, hidden_dim=2048, sliding_window=8)
-    cfg = kquant(base, tied_embeddings=0, **SMALL)
+    cfg = kquant(base, tied_embeddings=0, **kw)
     parity(cfg, 80 + arch, prompt_len=12, n_gen=48)
 
 

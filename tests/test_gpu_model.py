@@ -22,16 +22,20 @@ def rel(a, b):
 
 def small(arch, **kw):
     base = {C.ARCH_LLAMA: C.smollm2_135m, C.ARCH_QWEN3: C.qwen3_1_7b, C.ARCH_GEMMA3: C.gemma3_1b,
-            C.ARCH_QWEN2: C.qwen25_7b}[arch]()
-    kw.setdefault("n_layers", 3)
+            C.ARCH_QWEN2: C.qwen25_7b, C.ARCH_GEMMA2: C.gemma2_2b, C.ARCH_SMOLLM3: C.smollm3_3b}[arch]()
+    # SmolLM3: layer 3 is a no-RoPE layer; Gemma2: local / global layers alternate
+    kw.setdefault("n_layers", 5 if arch == C.ARCH_SMOLLM3 else 3)
     kw.setdefault("vocab_size", 4096)
     kw.setdefault("seq_len", 256)
     if arch == C.ARCH_QWEN2:   # the device forward streams Q8_0/Q4_0 matrices
         kw.update(type_embed=C.TYPE_Q8_0, type_output=C.TYPE_Q8_0, type_q=C.TYPE_Q8_0, type_k=C.TYPE_Q8_0,
                   type_v=C.TYPE_Q8_0, type_o=C.TYPE_Q8_0, type_gate=C.TYPE_Q8_0, type_up=C.TYPE_Q8_0,
                   type_down=C.TYPE_Q8_0, dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4)
-    if arch == C.ARCH_GEMMA3:
+    if arch in (C.ARCH_GEMMA3, C.ARCH_GEMMA2):
         kw.setdefault("sliding_window", 16)
+    if arch in (C.ARCH_GEMMA2, C.ARCH_SMOLLM3):   # smaller widths, same head layout
+        kw.setdefault("dim", 1024)
+        kw.setdefault("hidden_dim", 2048)
     return base.replace(**kw)
 
 
@@ -57,7 +61,8 @@ def run_parity(cfg, seed, prompt_len, n_gen, check_steps=4):
     return got
 
 
-@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN2, C.ARCH_QWEN3, C.ARCH_GEMMA3])
+@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN2, C.ARCH_QWEN3, C.ARCH_GEMMA3, C.ARCH_GEMMA2,
+                                  C.ARCH_SMOLLM3])
 def test_small_models_tokens_and_logits(device, arch):
     cfg = small(arch)
     run_parity(cfg, 1000 + arch, prompt_len=20, n_gen=64)
@@ -71,9 +76,11 @@ def test_untied_output_varied_tokens(device):
     assert len(set(toks)) > 4
 
 
-def test_gemma_window_crossing(device):
-    """Sliding-window layers (window 16) with a 40-token prompt."""
-    cfg = small(C.ARCH_GEMMA3, n_layers=7)
+@pytest.mark.parametrize("arch", [C.ARCH_GEMMA3, C.ARCH_GEMMA2])
+def test_gemma_window_crossing(device, arch):
+    """Sliding-window layers (window 16) with a 40-token prompt: Gemma3's
+    global layer is the 6th, Gemma2's every 2nd."""
+    cfg = small(arch, n_layers=7)
     run_parity(cfg, 77, prompt_len=40, n_gen=24)
 
 

@@ -37,7 +37,12 @@ def small(arch, **kw):
         return C.qwen25_7b().replace(dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4, tied_embeddings=1, **kw)
     if arch == C.ARCH_QWEN3:     # QK-norm
         return C.qwen3_1_7b().replace(dim=512, hidden_dim=1536, n_heads=8, n_kv_heads=4, **kw)
-    kw.setdefault("sliding_window", 16)   # Gemma3: head size 256, local / global layers, post-norms, GeGLU
+    if arch == C.ARCH_SMOLLM3:   # interleaved RoPE, none on layer 3
+        kw["n_layers"] = 5
+        return C.smollm3_3b().replace(dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4, **kw)
+    kw.setdefault("sliding_window", 16)   # Gemma: head size 256, local / global layers, post-norms, GeGLU
+    if arch == C.ARCH_GEMMA2:    # no QK-norm, global every 2nd layer
+        return C.gemma2_2b().replace(dim=1024, hidden_dim=2048, n_heads=4, n_kv_heads=2, **kw)
     return C.gemma3_1b().replace(dim=1152, hidden_dim=2304, **kw)
 
 
@@ -60,7 +65,7 @@ def oracle_logits(cfg, seed, prompt):
     return out
 
 
-@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN2, C.ARCH_QWEN3, C.ARCH_GEMMA3])
+@pytest.mark.parametrize("arch", [C.ARCH_LLAMA, C.ARCH_QWEN2, C.ARCH_QWEN3, C.ARCH_GEMMA3, C.ARCH_GEMMA2, C.ARCH_SMOLLM3])
 def test_batched_prefill_matches_oracle_and_tokens(device, arch):
     cfg = small(arch, n_layers=3 if arch != C.ARCH_GEMMA3 else 7)
     seed = 2000 + arch
