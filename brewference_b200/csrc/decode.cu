@@ -5,16 +5,16 @@
 // Qwen3-1.7B shape) and the per-layer dependency chain (norm -> QKV ->
 // attention -> wo -> norm -> gate/up -> down) is long.  As separate kernels
 // each link pays a launch/ramp/drain gap and the HBM idles in between.  Here:
-//   * one CTA per SM (cooperative launch); warp 8 of every CTA is a producer
+//   * one CTA per SM (cooperative launch); the last warp of every CTA is a producer
 //     that streams the CTA's share of EVERY phase's weight tiles into a ring
 //     of shared-memory stages, running ahead across phase boundaries.  The
 //     weights are a fragment-packed copy (packed.cuh): a tile's block columns
 //     are contiguous, so a stage is one 1-D bulk copy per tile into this
 //     CTA's own shared memory;
-//   * warps 0-7 consume: each phase starts by building its own prep records
+//   * the other DK_CW warps consume: each phase starts by building its own prep records
 //     (RMSNorm + limb split of the input vector, prep.cuh) in shared memory,
 //     then multiplies the staged tiles (int8 MMA, warp w taking block columns
-//     w, w+8, ... of every tile) and writes its output rows after a
+//     w, w + DK_CW, ... of every tile) and writes its output rows after a
 //     cross-warp sum;
 //   * phases are separated by a grid barrier among the consumer warps
 //     (acquire/release counter in global memory, bounded wait);
@@ -45,7 +45,18 @@ constexpr int ATTN_MIN_POS = 32;   // positions per attention CTA at least
 // dynamic shared memory of the decode kernel, at most: 226 KB of the 227 KB a
 // block may opt in to (the kernel's static shared variables take the rest)
 constexpr size_t DK_SMEM_BUDGET = 226 * 1024;
-constexpr int DK_RED_BYTES = 8 * 8 * 16 * 2 * 4;   // cross-warp partial sums of a tile group
+// consumer warps per CTA (one more warp streams the weights)
+#ifndef DK_CONSUMER_WARPS
+#define DK_CONSUMER_WARPS 8
+#endif
+constexpr int DK_CW = DK_CONSUMER_WARPS;
+constexpr int DK_CT = DK_CW * 32;             // consumer threads
+constexpr int DK_GMAX = 4;                    // tiles per group at most
+constexpr int DK_PVK = 1024 / DK_CT;          // attention outputs per thread ([G][hd] <= 1024)
+constexpr int DK_RED_BYTES = DK_CW * DK_GMAX * 16 * 2 * 4;   // cross-warp partial sums of a tile group
+
+// Named barrier among the consumer warps.
+__device__ __forceinline__ void dk_bar() { asm volatile("bar.sync 1, %0;" ::"n"(DK_CT) : "memory"); }
 constexpr int DK_STAGE_BYTES = 64 * 544;           // one pipeline stage: 64 Q8_0 block-tiles
 
 // One matvec phase over fragment-packed tiles (packed.cuh): y = W x for the
@@ -134,10 +145,10 @@ struct PGeom {
 
 __device__ __forceinline__ int pk_gs(const DecodeParams& P, int ph, int nt) { return P.geo_gs[ph][min(nt, 9)]; }
 
-// Tile groups hold 1, 2, 4 or 8 tiles (the largest of those <= n): four
+// Tile groups hold 1, 2 or 4 tiles (the largest of those <= n): three
 // instantiations of the group loop keep the kernel's code small enough for
 // the instruction caches.
-__device__ __forceinline__ int ng_pow2(int n) { return n >= 8 ? 8 : n >= 4 ? 4 : n >= 2 ? 2 : 1; }
+__device__ __forceinline__ int ng_pow2(int n) { return n >= 4 ? 4 : n >= 2 ? 2 : 1; }
 
 __device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, int KB) {
     PGeom g;
@@ -158,7 +169,7 @@ __device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpr
 // (or when another CTA already gave up) it records a timeout and raises the
 // abort flag instead of waiting forever.
 __device__ bool grid_sync(const DecodeParams& P, unsigned long long target, int* s_ok) {
-    consumer_bar();   // the CTA's writes happen before thread 0's release
+    dk_bar();   // the CTA's writes happen before thread 0's release
     if (threadIdx.x == 0) {
         int ok = 1;
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(P.bar) : "memory");
@@ -175,20 +186,20 @@ __device__ bool grid_sync(const DecodeParams& P, unsigned long long target, int*
         }
         *s_ok = ok;
     }
-    consumer_bar();   // ... and the acquire happens before every thread's reads
+    dk_bar();   // ... and the acquire happens before every thread's reads
     return *s_ok != 0;
 }
 
-// Sum over the 256 consumer threads.
+// Sum over the consumer threads.
 __device__ __forceinline__ float consumer_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     v = warp_sum(v);
     if (lane == 0) red[warp] = v;
-    consumer_bar();
+    dk_bar();
     float t = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += red[w];
-    consumer_bar();
+    for (int w = 0; w < DK_CW; ++w) t += red[w];
+    dk_bar();
     return t;
 }
 
@@ -200,17 +211,17 @@ enum { SRC_EMBED = 0, SRC_PLAIN = 1, SRC_GEMMA_ADD = 2 };
 // once (completed by cp_async_wait_all).
 __device__ __forceinline__ void stage_async(float4* d0, const float4* s0, float4* d1, const float4* s1, int n4) {
     #pragma unroll 1
-    for (int i = threadIdx.x; i < n4; i += 256) {
+    for (int i = threadIdx.x; i < n4; i += DK_CT) {
         if (s0) cp_async16(d0 + i, s0 + i);
         if (s1) cp_async16(d1 + i, s1 + i);
     }
 }
 
-// This thread's sum of squares over the float4 it staged (i = tid + 256 k).
+// This thread's sum of squares over the float4 it staged (i = tid + DK_CT k).
 __device__ __forceinline__ float sumsq4(const float4* v, int n4) {
     float ss = 0.0f;
     #pragma unroll 1
-    for (int i = threadIdx.x; i < n4; i += 256) {
+    for (int i = threadIdx.x; i < n4; i += DK_CT) {
         const float4 a = v[i];
         ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
     }
@@ -247,29 +258,29 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             }
             const float es = (float)sqrt((double)K);   // Kernels.scaleEmbeddings
             #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += 256) {
+            for (int i = threadIdx.x; i < K; i += DK_CT) {
                 float v = dequant_elem(P.type_embed, P.embed, (int64_t)tok * K + i);
                 vec[i] = arch_gemma(P.arch) ? __fmul_rn(v, es) : v;
             }
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
-            consumer_bar();
+            dk_bar();
             #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
+            for (int i = threadIdx.x; i < K; i += DK_CT) ss += vec[i] * vec[i];
         } else if (mode == SRC_GEMMA_ADD) {
             stage_async(v4, reinterpret_cast<const float4*>(t + (int64_t)b * ld), w4,
                         reinterpret_cast<const float4*>(tw), K4);
             cp_async_wait_all();
-            consumer_bar();
+            dk_bar();
             const float tsc = rms_scale(consumer_sum(sumsq4(v4, K4), red), K, P.eps);
             const float* sb = src + (int64_t)b * ld;
             #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += 256) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * vec[K + i];
-            consumer_bar();
+            for (int i = threadIdx.x; i < K; i += DK_CT) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * vec[K + i];
+            dk_bar();
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
             #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += 256) ss += vec[i] * vec[i];
+            for (int i = threadIdx.x; i < K; i += DK_CT) ss += vec[i] * vec[i];
         } else {
             stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4,
                         (nw && !(nw_staged && b == 0)) ? nw4 : nullptr, K4);
@@ -282,26 +293,26 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             ss = warp_sum(ss);
             if (lane == 0) red[warp] = ss;
         }
-        consumer_bar();
+        dk_bar();
         if (t_wave && b == 0) *t_wave = global_ns();
         float scale = 1.0f;
         if (nw) {
             float tot = 0.0f;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) tot += red[w];
+            for (int w = 0; w < DK_CW; ++w) tot += red[w];
             scale = rms_scale(tot, K, P.eps);
         }
         // two independent block quads per iteration (their shuffle and
         // divide chains overlap)
         const int gq = lane >> 3, e = (lane & 7) * 4;
         #pragma unroll 1
-        for (int j0 = warp * 4; j0 < KB; j0 += 64) {
+        for (int j0 = warp * 4; j0 < KB; j0 += 8 * DK_CW) {
             int jj[2];
             bool ok[2];
             float4 v[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                const int j = j0 + 32 * u + gq;
+                const int j = j0 + 4 * DK_CW * u + gq;
                 ok[u] = j < KB;
                 jj[u] = ok[u] ? j : KB - 1;
                 v[u] = v4[(32 * jj[u] + e) >> 2];
@@ -318,7 +329,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
 #pragma unroll
             for (int u = 0; u < 2; ++u) prep_emit_quad(prep + (size_t)jj[u] * P.rec_bytes, P.batch, b, v[u], ok[u], lsum);
         }
-        consumer_bar();
+        dk_bar();
     }
 }
 
@@ -362,7 +373,7 @@ __device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo
         if (detail && tid == 0 && dch < DK_DETAIL) detail[DK_DETAIL + dch] = global_ns();
         if (!aborted) {
             const uint32_t sb = smem_u32(ring.stages + (size_t)stage * ring.stage_bytes);
-            for (int kb = warp; kb < geo.KC; kb += 8) {
+            for (int kb = warp; kb < geo.KC; kb += DK_CW) {
                 const uint32_t rec = prep_s + (chunk * geo.KC + kb) * P.rec_bytes;
                 uint32_t b0 = lds32(rec + o.boff), b1 = lds32(rec + o.boff + 16);
                 if (!o.vB) b0 = b1 = 0u;
@@ -409,8 +420,8 @@ __device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo
         const float lo0 = __shfl_down_sync(0xffffffffu, acc[k][0], 1);
         const float lo1 = __shfl_down_sync(0xffffffffu, acc[k][2], 1);
         if ((t & 1) == 0 && o.vC) {
-            red[((warp * 8 + k) * 16 + g) * 2 + o.bC] = (lo0 + acc[k][1] * 256.0f) + acc[k][0] * 65536.0f;
-            red[((warp * 8 + k) * 16 + g + 8) * 2 + o.bC] = (lo1 + acc[k][3] * 256.0f) + acc[k][2] * 65536.0f;
+            red[((warp * DK_GMAX + k) * 16 + g) * 2 + o.bC] = (lo0 + acc[k][1] * 256.0f) + acc[k][0] * 65536.0f;
+            red[((warp * DK_GMAX + k) * 16 + g + 8) * 2 + o.bC] = (lo1 + acc[k][3] * 256.0f) + acc[k][2] * 65536.0f;
         }
     }
 }
@@ -471,15 +482,14 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
         switch (ng) {
             case 1: mv_group<TT, 1>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
             case 2: mv_group<TT, 2>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 4: mv_group<TT, 4>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            default: mv_group<TT, 8>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            default: mv_group<TT, 4>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
         }
-        consumer_bar();
+        dk_bar();
         if (ok < ng) {
             auto V = [&](int r) {
                 float v = 0.0f;
 #pragma unroll
-                for (int w = 0; w < 8; ++w) v += red[((w * 8 + ok) * 16 + r) * 2 + ob];
+                for (int w = 0; w < DK_CW; ++w) v += red[((w * DK_GMAX + ok) * 16 + r) * 2 + ob];
                 return v;
             };
             if (!glu) {
@@ -498,7 +508,7 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
                 f.y[(int64_t)ob * f.ldy + i] = act_glu(V(orow), f.epi) * V(orow + 8);
             }
         }
-        consumer_bar();
+        dk_bar();
     }
 }
 
@@ -567,36 +577,6 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
 //   q-norm w [hd] | k-norm w [hd] | cos [hd/2] | sin [hd/2] |
 //   scores [G][SUB] | per head: running max, running sum, round rescale, -
 // and, for the combine, the partials [heads][nchunk][hd + 4].
-// The RoPE cos/sin of this step's positions: thread t always rotates pair
-// d = t % (hd/2) (hd/2 divides 256), so each thread keeps its column for both
-// sequences and both tables (global / Gemma3 local) in registers for the
-// whole step.
-struct RopeRegs {
-    float c00, c01, c10, c11, s00, s01, s10, s11;   // [sequence][table]
-    __device__ __forceinline__ float cosv(int b, int t) const { return b ? (t ? c11 : c10) : (t ? c01 : c00); }
-    __device__ __forceinline__ float sinv(int b, int t) const { return b ? (t ? s11 : s10) : (t ? s01 : s00); }
-};
-
-__device__ __forceinline__ RopeRegs load_rope(const DecodeParams& P) {
-    RopeRegs r = {};
-    const int half = P.hd / 2, d = threadIdx.x % half;
-    const bool two = arch_gemma(P.arch);
-    float* cv[2][2] = {{&r.c00, &r.c01}, {&r.c10, &r.c11}};
-    float* sv[2][2] = {{&r.s00, &r.s01}, {&r.s10, &r.s11}};
-#pragma unroll
-    for (int b = 0; b < 2; ++b)
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            if (b >= P.batch || (t == 1 && !two)) continue;
-            const int pos = P.pos[b];
-            if (pos < 0 || pos >= P.seq_len) continue;
-            const int64_t o = ((int64_t)t * P.seq_len + pos) * half + d;
-            *cv[b][t] = __ldg(P.rope_cos + o);
-            *sv[b][t] = __ldg(P.rope_sin + o);
-        }
-    return r;
-}
-
 // One attention item: sequence b, kv head hk, chunk c of the positions
 // start .. pos (Gemma3's local layers: the last `window` positions), split
 // into chunks of `per` positions; `used` chunks are non-empty.
@@ -634,7 +614,7 @@ __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, cons
     const float* kc = P.kc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     const float* vc = P.vc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     #pragma unroll 1
-    for (int i = threadIdx.x; i < ns * hd4; i += 256) {
+    for (int i = threadIdx.x; i < ns * hd4; i += DK_CT) {
         const int r = i / hd4, ci = i % hd4;
         const int p = it.p0 + r0 + r;
         if (p == it.pos) continue;
@@ -644,7 +624,7 @@ __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, cons
     }
 }
 
-__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave, const RopeRegs& rope,
+__device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave,
                            unsigned long long* detail) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
     const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
@@ -656,7 +636,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     const int SUB = attn_sub(hd);
     const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
     int tpp = 1;                 // lanes per (position, head) score (power of two <= 8)
-    while (tpp < 8 && 2 * tpp * G * SUB <= 256) tpp *= 2;
+    while (tpp < 8 && 2 * tpp * G * SUB <= DK_CT) tpp *= 2;
     float* kb = sm;
     float* vb = kb + SUB * hd;
     float* qs = vb + SUB * hd;
@@ -664,7 +644,9 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     float* vs = ks + hd;
     float* wq = vs + hd;
     float* wk = wq + hd;
-    float* sc = wk + hd;
+    float* cs = wk + hd;   // RoPE cos / sin of this item's position (RopeCache.precomputeAngles rows)
+    float* sn = cs + half;
+    float* sc = sn + half;
     float* st = sc + G * SUB;
     __shared__ int s_last;
     // detail trace (first item of the CTA): 0 start, 1 wave landed, 2 head
@@ -692,14 +674,22 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
             const float* vsrc = ksrc + kvd;
             #pragma unroll 1
-            for (int i = tid; i < G * hd4; i += 256) cp_async16(qs + 4 * i, qsrc + 4 * i);
+            for (int i = tid; i < G * hd4; i += DK_CT) cp_async16(qs + 4 * i, qsrc + 4 * i);
             #pragma unroll 1
-            for (int i = tid; i < hd4; i += 256) {
+            for (int i = tid; i < hd4; i += DK_CT) {
                 cp_async16(ks + 4 * i, ksrc + 4 * i);
                 cp_async16(vs + 4 * i, vsrc + 4 * i);
                 if (P.rms_q) {
                     cp_async16(wq + 4 * i, P.rms_q + (int64_t)l * hd + 4 * i);
                     cp_async16(wk + 4 * i, P.rms_k + (int64_t)l * hd + 4 * i);
+                }
+            }
+            if (rope_on) {
+                const int64_t ro = ((int64_t)table * P.seq_len + pos) * half;
+                #pragma unroll 1
+                for (int i = tid; i < half / 4; i += DK_CT) {
+                    cp_async16(cs + 4 * i, P.rope_cos + ro + 4 * i);
+                    cp_async16(sn + 4 * i, P.rope_sin + ro + 4 * i);
                 }
             }
             attn_issue_kv(P, l, it, 0, kb, vb);
@@ -708,12 +698,12 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 st[4 * tid + 1] = 0.0f;
             }
             cp_async_wait_all();
-            consumer_bar();
+            dk_bar();
             if (t_wave) *t_wave = global_ns();
             stamp(1);
             if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
                 #pragma unroll 1
-                for (int hh = warp; hh <= G; hh += 8) {
+                for (int hh = warp; hh <= G; hh += DK_CW) {
                     float* vecp = hh < G ? qs + hh * hd : ks;
                     const float* w = hh < G ? wq : wk;
                     float ss = 0.0f;
@@ -724,30 +714,30 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     #pragma unroll 1
                     for (int i = lane; i < hd; i += 32) vecp[i] = vecp[i] * scale * w[i];
                 }
-                consumer_bar();
+                dk_bar();
             }
             stamp(2);
             #pragma unroll 1
-            for (int idx = tid; rope_on && idx < (G + 1) * half; idx += 256) {   // RoPE on q heads and k
+            for (int idx = tid; rope_on && idx < (G + 1) * half; idx += DK_CT) {   // RoPE on q heads and k
                 const int hh = idx / half, d = idx % half;
                 float* vecp = hh < G ? qs + hh * hd : ks;
                 const int i0 = inter ? 2 * d : d;
                 const int i1 = inter ? 2 * d + 1 : d + half;
-                const float a = vecp[i0], bb = vecp[i1], cc = rope.cosv(b, table), ss = rope.sinv(b, table);
+                const float a = vecp[i0], bb = vecp[i1], cc = cs[d], ss = sn[d];
                 vecp[i0] = __fsub_rn(__fmul_rn(a, cc), __fmul_rn(bb, ss));
                 vecp[i1] = __fadd_rn(__fmul_rn(a, ss), __fmul_rn(bb, cc));
             }
-            consumer_bar();
+            dk_bar();
             stamp(3);
             const bool has_pos = pos >= p0 && pos < p0 + n;
             if (has_pos) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
                 #pragma unroll 1
-                for (int i = tid; i < hd; i += 256) {
+                for (int i = tid; i < hd; i += DK_CT) {
                     kc[(int64_t)pos * kvd + hk * hd + i] = ks[i];
                     vc[(int64_t)pos * kvd + hk * hd + i] = vs[i];
                 }
             }
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // outputs tid + 256 k of [G][hd] (G * hd <= 1024)
+            float acc[DK_PVK] = {};   // outputs tid + DK_CT k of [G][hd] (G * hd <= 1024)
             #pragma unroll 1
             for (int r0 = 0; r0 < n; r0 += SUB) {
                 const int ns = min(SUB, n - r0);
@@ -758,19 +748,19 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
                     const int r = pos - p0 - r0;
                     #pragma unroll 1
-                    for (int i = tid; i < hd; i += 256) {
+                    for (int i = tid; i < hd; i += DK_CT) {
                         kb[r * hd + i] = ks[i];
                         vb[r * hd + i] = vs[i];
                     }
                 }
-                consumer_bar();
+                dk_bar();
                 if (r0 == 0) stamp(9);
                 // scores q.k / sqrt(hd): tpp lanes per (position, head) pair,
                 // each summing every tpp-th float4 of the row, then a shuffle
                 // sum over the pair's lanes.  Every lane runs the same number
                 // of iterations (the shuffles need the whole warp).
                 {
-                    const int npair = G * ns, ppi = 256 / tpp;
+                    const int npair = G * ns, ppi = DK_CT / tpp;
                     const int j = tid & (tpp - 1);
                     #pragma unroll 1
                     for (int p00 = 0; p00 < npair; p00 += ppi) {
@@ -800,11 +790,11 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         if (j == 0 && pr < npair) sc[h * SUB + tt] = sv * P.inv_scale;
                     }
                 }
-                consumer_bar();
+                dk_bar();
                 if (r0 == 0) stamp(10);
                 // running softmax: weights of this round relative to the new maximum
                 #pragma unroll 1
-                for (int h = warp; h < G; h += 8) {
+                for (int h = warp; h < G; h += DK_CW) {
                     float m = -INFINITY;
                     #pragma unroll 1
                     for (int tt = lane; tt < ns; tt += 32) m = fmaxf(m, sc[h * SUB + tt]);
@@ -826,11 +816,11 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         st[4 * h + 1] = st[4 * h + 1] * corr + ls;
                     }
                 }
-                consumer_bar();
+                dk_bar();
                 if (r0 == 0) stamp(11);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int idx = tid + 256 * k;
+                for (int k = 0; k < DK_PVK; ++k) {
+                    const int idx = tid + DK_CT * k;
                     if (idx < G * hd) {
                         const int h = idx / hd, i = idx % hd;
                         const float* sh = sc + h * SUB;
@@ -849,13 +839,13 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         acc[k] = (a0 + a1) + (a2 + a3);
                     }
                 }
-                consumer_bar();
+                dk_bar();
                 if (r0 == 0) stamp(12);
             }
             stamp(4);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int idx = tid + 256 * k;
+            for (int k = 0; k < DK_PVK; ++k) {
+                const int idx = tid + DK_CT * k;
                 if (idx < G * hd) {
                     const int h = idx / hd, i = idx % hd;
                     __stcg(&pbase[((int64_t)h * nch + c) * stride + 4 + i], acc[k]);
@@ -869,7 +859,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
         // arrival; the last CTA of (b, hk) combines the used chunks in order.
         // The barrier orders every thread's partial stores before thread 0's
         // release, which makes them visible before its arrival is counted.
-        consumer_bar();
+        dk_bar();
         int* ctr = &P.attn_ctr[b * P.n_kv + hk];
         if (tid == 0) {
             // release: the CTA's partials before the count; acquire: the
@@ -878,7 +868,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
             s_last = (prev == nch - 1);
         }
-        consumer_bar();
+        dk_bar();
         stamp(5);
         if (s_last) {
             const int hpw = max(1, min(G, P.attn_floats / (nch * stride)));
@@ -888,12 +878,12 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 const float* src = pbase + (int64_t)h0 * nch * stride;
                 const int n4 = nh * nch * stride / 4;
                 #pragma unroll 1
-                for (int i = tid; i < n4; i += 256) cp_async16(sm + 4 * i, src + 4 * i);
+                for (int i = tid; i < n4; i += DK_CT) cp_async16(sm + 4 * i, src + 4 * i);
                 cp_async_wait_all();
-                consumer_bar();
+                dk_bar();
                 stamp(6);
                 #pragma unroll 1
-                for (int hl = warp; hl < nh; hl += 8) {
+                for (int hl = warp; hl < nh; hl += DK_CW) {
                     float* ph = sm + hl * nch * stride;
                     float M = -INFINITY;
                     #pragma unroll 1
@@ -907,11 +897,11 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                         Ls += w * ph[k * stride + 1];
                     }
                     Ls = warp_sum(Ls);
-                    if (lane == 0) ph[3] = 1.0f / Ls;
+                    if (lane == 0) ph[3] = __frcp_rn(Ls);   // = 1.0f / Ls, correctly rounded
                 }
-                consumer_bar();
+                dk_bar();
                 #pragma unroll 1
-                for (int idx = tid; idx < nh * hd; idx += 256) {
+                for (int idx = tid; idx < nh * hd; idx += DK_CT) {
                     const int hl = idx / hd, i = idx % hd;
                     const float* ph = sm + hl * nch * stride;
                     float o = 0.0f;
@@ -919,19 +909,19 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     for (int k = 0; k < used; ++k) o += ph[k * stride + 2] * ph[k * stride + 4 + i];
                     P.xb[(int64_t)b * qw + (int64_t)(hk * G + h0 + hl) * hd + i] = o * ph[3];
                 }
-                consumer_bar();
+                dk_bar();
             }
             if (tid == 0) *ctr = 0;
             stamp(7);
         }
-        consumer_bar();
+        dk_bar();
         detail = nullptr;   // stamps of the first item only
     }
     if (det0 && tid == 0) det0[8] = global_ns();
 }
 
 template <int TYPE, int CTYPE, int NT>
-__global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
+__global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = P.nstages;
     Ring ring;
@@ -943,7 +933,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     __shared__ unsigned long long s_base;
     __shared__ int s_ok;
     float* s_red = reinterpret_cast<float*>(smem + 640);                               // [32]
-    float* red = reinterpret_cast<float*>(smem + 768);                                 // [8][8][16][2]
+    float* red = reinterpret_cast<float*>(smem + 768);                                 // [DK_CW][DK_GMAX][16][2]
     float* vec = reinterpret_cast<float*>(smem + 768 + DK_RED_BYTES);
     vec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(vec) + 127) & ~uintptr_t(127));
     uint8_t* prep = reinterpret_cast<uint8_t*>(vec) + P.vec_bytes;
@@ -956,7 +946,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&ring.full[s], 1);
-            mbar_init(&ring.empty[s], 8);
+            mbar_init(&ring.empty[s], DK_CW);
         }
         fence_mbar_init();
         s_base = P.bar[1];
@@ -965,7 +955,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
     if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
     __syncthreads();
 
-    if (warp == 8) {
+    if (warp == DK_CW) {
         // ------------------------------- producer -------------------------------
         int q = 0;
         unsigned long long* dtr =
@@ -1028,7 +1018,6 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         if (!grid_sync(P, target, &s_ok)) aborted = true;
         mark();
     };
-    const RopeRegs rope = load_rope(P);
     // The next phase's RMSNorm weight is copied into shared memory, beside
     // the input vector where prep_phase reads it, while this phase
     // multiplies (issued after this phase's prep, when `vec` is free again;
@@ -1053,7 +1042,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
             if (P.rms_k) prefetch_l2(P.rms_k + (int64_t)l * P.hd, (uint32_t)P.hd * 4u);
         }
         if (ph == 1) {
-            attn_phase(P, l, vec, tr ? &twave : nullptr, rope, det(l, PH_ATTN));
+            attn_phase(P, l, vec, tr ? &twave : nullptr, det(l, PH_ATTN));
             markv(twave);   // the first load wave landed
             twave = 0;
             markv(0);
@@ -1125,7 +1114,7 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const __grid_constant__ 
         }
         markv(tfull);
         if (cls) {
-            consumer_bar();
+            dk_bar();
             if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);
         }
         barrier();
@@ -1170,7 +1159,7 @@ int launch_decode(const DecodeParams& p, cudaStream_t stream) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
-    cfg.blockDim = dim3(288);
+    cfg.blockDim = dim3(DK_CT + 32);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
     cudaLaunchAttribute a[1];
@@ -1199,7 +1188,6 @@ bool decode_supported(const brew_config& c, int batch) {
     // attention: a CTA holds the G * hd outputs of a kv head's queries in
     // four registers per thread; 16-byte copies of half rows
     if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
-    if (256 % (c.head_size / 2)) return false;   // each thread's RoPE column is fixed
     return true;
 }
 
@@ -1247,11 +1235,19 @@ int decode_prepare(DecodeParams* p) {
         int kc[9] = {0};
         for (int ng = 1; ng <= 8; ++ng) {
             const int cap = std::min(KB, p->stage_bytes / (ng * bs));
+            // a multiple of the consumer warp count when one fits (every warp
+            // takes the same number of block columns), else of 8
             kc[ng] = 8;
-            for (int c = (cap / 8) * 8; c >= 8; c -= 8)
+            bool found = false;
+            for (int c = (cap / DK_CW) * DK_CW; c >= DK_CW && !found; c -= DK_CW)
                 if (KB % c == 0) {
                     kc[ng] = c;
-                    break;
+                    found = true;
+                }
+            for (int c = (cap / 8) * 8; c >= 8 && !found; c -= 8)
+                if (KB % c == 0) {
+                    kc[ng] = c;
+                    found = true;
                 }
             BREW_CHECK(ng * kc[ng] * bs <= p->stage_bytes && kc[ng] < 32768, BREW_ERR_UNSUPPORTED,
                        "decode kernel: stage geometry");
@@ -1261,7 +1257,7 @@ int decode_prepare(DecodeParams* p) {
         p->geo_gs[ph][0] = 1;
         for (int nt = 1; nt <= 9; ++nt) {
             int best = 1, fill = 0;
-            for (int gs = 8; gs >= 1; gs >>= 1)
+            for (int gs = DK_GMAX; gs >= 1; gs >>= 1)
                 if (gs <= nt && gs * kc[gs] * bs > fill) {
                     fill = gs * kc[gs] * bs;
                     best = gs;

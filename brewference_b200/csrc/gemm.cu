@@ -60,7 +60,7 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
     const int t = (int)(wid / KB), kb = (int)(wid % KB);
     const float v = t < T ? x[(int64_t)t * ldx + 32 * kb + lane] : 0.0f;
     const float amax = warp_max(fabsf(v));
-    const float inv = amax > 0.0f ? PREP_RANGE / amax : 0.0f;
+    const float inv = prep_block_inv(amax);
     const int q = __float2int_rn(v * inv);
     const int lo = ((q + 128) & 255) - 128;
     const int q1 = (q - lo) >> 8;
@@ -74,7 +74,7 @@ __global__ void gemm_limbs_kernel(const float* x, int ldx, int T, int Tp, int K,
     tile[tc_tile_off(c0, lane)] = (int8_t)hi;
     tile[tc_tile_off(c0 + 2, lane)] = (int8_t)mid;
     tile[tc_tile_off(c0 + 4, lane)] = (int8_t)lo;
-    if (lane == 0) scales[(int64_t)kb * Tp + t] = amax / PREP_RANGE;
+    if (lane == 0) scales[(int64_t)kb * Tp + t] = prep_block_scale(amax);
 }
 
 // CTA = 128 weight rows x 32 tokens, warp-specialised:

@@ -103,7 +103,7 @@ __device__ __forceinline__ void kx_emit_sb(uint8_t* rec, int K, int nvp, int t, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(xs[i]));
     am = warp_max(am);
-    const float inv = am > 0.0f ? PREP_RANGE / am : 0.0f;
+    const float inv = prep_block_inv(am);
     int lim[3][8];
     int sum[3] = {0, 0, 0};
 #pragma unroll
@@ -143,7 +143,7 @@ __device__ __forceinline__ void kx_emit_sb(uint8_t* rec, int K, int nvp, int t, 
         const int tl = lane / 9, rem = lane % 9, l = rem / 3, k = 8 + 8 * (rem % 3);
         *reinterpret_cast<uint64_t*>(mt + tl * NC * 32 + tc_tile_off(c0 + 2 * l, k)) = 0ull;
     }
-    if (lane == 0) reinterpret_cast<float*>(rec + (int64_t)KSB * 10 * NC * 32)[(int64_t)sb * nvp + t] = am / PREP_RANGE;
+    if (lane == 0) reinterpret_cast<float*>(rec + (int64_t)KSB * 10 * NC * 32)[(int64_t)sb * nvp + t] = prep_block_scale(am);
 }
 
 #endif  // __CUDACC__

@@ -28,6 +28,19 @@ namespace brew {
 
 constexpr float PREP_RANGE = 8290000.0f;   // |v| <= 8290001 keeps hi in [-127, 127]
 
+// The two scales of a block whose largest magnitude is am: inv = R / am
+// (x * inv is the block fixed-point value) and s = am / R (its weight in the
+// product).  inv comes from the fast approximate division (within 2 ulp, no
+// IEEE slow path on the critical path of every phase's input), s from a
+// multiply by the constant 1 / R; |x * inv| <= R * (1 + 2^-21) keeps the top
+// limb in [-127, 127], and the products stay exact to fp32 rounding.  Blocks
+// whose maximum is below 1e-30 (R / am would overflow) are taken as zero.
+constexpr float PREP_TINY = 1e-30f;
+__host__ __device__ inline float prep_block_scale(float am) { return am * (1.0f / PREP_RANGE); }
+#ifdef __CUDACC__
+__device__ __forceinline__ float prep_block_inv(float am) { return am > PREP_TINY ? __fdividef(PREP_RANGE, am) : 0.0f; }
+#endif
+
 // n8 MMA column tiles for `batch` vectors (4 columns per vector)
 __host__ __device__ inline int prep_nt(int batch) { return (batch + 1) / 2; }
 __host__ __device__ inline int prep_rec_bytes(int batch) { return (batch * (3 * 32 + 4 + 3 * 4) + 15) & ~15; }
@@ -41,8 +54,8 @@ __host__ __device__ inline int prep_lsum_off(int batch) { return 3 * batch * 32 
 __device__ __forceinline__ void prep_emit_warp(uint8_t* rec, int batch, int b, float x) {
     const int lane = threadIdx.x & 31;
     const float amax = warp_max(fabsf(x));
-    const float inv = amax > 0.0f ? PREP_RANGE / amax : 0.0f;
-    const float s = amax / PREP_RANGE;
+    const float inv = prep_block_inv(amax);
+    const float s = prep_block_scale(amax);
     const int v = __float2int_rn(x * inv);
     const int lo = ((v + 128) & 255) - 128;
     const int v1 = (v - lo) >> 8;
@@ -74,8 +87,8 @@ __device__ __forceinline__ void prep_emit_quad(uint8_t* rec, int batch, int b, f
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-    const float inv = am > 0.0f ? PREP_RANGE / am : 0.0f;
-    const float s = am / PREP_RANGE;
+    const float inv = prep_block_inv(am);
+    const float s = prep_block_scale(am);
     const float xs[4] = {x.x, x.y, x.z, x.w};
     uint32_t phi = 0u, pmid = 0u, plo = 0u;
     int shi = 0, smid = 0, slo = 0;
