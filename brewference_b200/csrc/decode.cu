@@ -150,10 +150,14 @@ __device__ __forceinline__ int pk_gs(const DecodeParams& P, int ph, int nt) { re
 // the instruction caches.
 __device__ __forceinline__ int ng_pow2(int n) { return n >= 4 ? 4 : n >= 2 ? 2 : 1; }
 
+// This CTA's tile range [t0, t1) of each matvec phase (PH_QKV .. PH_CLS): the
+// tiles are split over the CTAs in order, computed once at kernel start.
+__shared__ int s_tiles[5][2];
+
 __device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, int KB) {
     PGeom g;
     g.KC = P.geo_kc[ph][ng];
-    g.nchunks = KB / g.KC;
+    g.nchunks = P.geo_nch[ph][ng];
     return g;
 }
 
@@ -340,6 +344,20 @@ struct Ring {
     int ns, stage_bytes;
 };
 
+// Position in the ring: the stage counter q, its slot q % ns and the parity
+// (q / ns) & 1 of the slot's barrier phase, advanced without divisions.
+struct RingPos {
+    int q = 0, slot = 0;
+    uint32_t par = 0;
+    __device__ __forceinline__ void advance(int ns) {
+        ++q;
+        if (++slot == ns) {
+            slot = 0;
+            par ^= 1u;
+        }
+    }
+};
+
 
 // This lane's operand offsets inside a prep record (prep.cuh): B column g =
 // limb (g & 3) of vector g >> 2; accumulator columns 2t, 2t+1 belong to
@@ -356,7 +374,7 @@ struct LaneOps {
 // of the MMAs (with a run-time count and predicated tile slots, the loop
 // measured 2.5-3x slower per block column for one and two tiles).
 template <int TT, int NG>
-__device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo, const Ring& ring, int& q,
+__device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo, const Ring& ring, RingPos& rp,
                                          uint32_t prep_s, const LaneOps& o, float* red, bool& aborted,
                                          unsigned long long* t_full, unsigned long long* detail, int& dch) {
     constexpr int BS = pk_block_bytes(TT), SO = pk_scale_off(TT);
@@ -365,9 +383,9 @@ __device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo
     float acc[NG][4];
 #pragma unroll
     for (int k = 0; k < NG; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.0f;
-    for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
-        const int stage = q % ring.ns;
-        if (!aborted && !mbar_wait_bounded(&ring.full[stage], (q / ring.ns) & 1, P.err, BREW_DEVERR_TIMEOUT_FULL))
+    for (int chunk = 0; chunk < geo.nchunks; ++chunk, rp.advance(ring.ns)) {
+        const int stage = rp.slot;
+        if (!aborted && !mbar_wait_bounded(&ring.full[stage], rp.par, P.err, BREW_DEVERR_TIMEOUT_FULL))
             aborted = true;
         if (t_full && warp == 0) *t_full = global_ns();
         if (detail && tid == 0 && dch < DK_DETAIL) detail[DK_DETAIL + dch] = global_ns();
@@ -433,7 +451,7 @@ __device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo
 // in shared memory (`red`, [8 warps][8 tiles][16 rows][2 vectors]) and each
 // of the 256 threads finishes one output.
 template <int TT, int NT>
-__device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q, uint32_t prep_s,
+__device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, RingPos& rp, uint32_t prep_s,
                          float* red, unsigned long long* s_best, bool& aborted, unsigned long long* t_full,
                          unsigned long long* detail) {
     int dch = 0;
@@ -441,15 +459,13 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
     constexpr int BS = pk_block_bytes(TT);
     const int tid = threadIdx.x, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int G = gridDim.x;
-    const int t0 = (int)((int64_t)blockIdx.x * f.tiles / G);
-    const int t1 = (int)((int64_t)(blockIdx.x + 1) * f.tiles / G);
+    const int t0 = s_tiles[f.ph][0], t1 = s_tiles[f.ph][1];
     const int nt = t1 - t0;
     if (nt <= 0) return;
     const int batch = P.batch;
     const int gs = pk_gs(P, f.ph, nt);
     const bool glu = f.epi != MV_EPI_STORE;
-    const int per_tile = (glu ? 8 : 16) * batch;
+    const int lg_tile = (glu ? 3 : 4) + (batch == 2 ? 1 : 0);   // log2 of the outputs per tile
     LaneOps o;
     {
         const int bB = g >> 2, lB = g & 3;
@@ -468,8 +484,9 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
         const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
         // this thread's output of the group: its bias and residual are read
         // now, so that their latency overlaps the MMA loop
-        const int ok = tid / per_tile, orem = tid % per_tile;
-        const int orow = orem / batch, ob = orem % batch;
+        // per_tile = (8 or 16) * batch, batch 1 or 2: powers of two
+        const int ok = tid >> lg_tile, orem = tid & ((1 << lg_tile) - 1);
+        const int orow = batch == 2 ? orem >> 1 : orem, ob = batch == 2 ? (orem & 1) : 0;
         float pr = 0.0f, pb = 0.0f;
         if (!glu && ok < ng) {
             const int row = (tg0 + ok) * 16 + orow;
@@ -480,9 +497,9 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
             }
         }
         switch (ng) {
-            case 1: mv_group<TT, 1>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            case 2: mv_group<TT, 2>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
-            default: mv_group<TT, 4>(P, geo, ring, q, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 1: mv_group<TT, 1>(P, geo, ring, rp, prep_s, o, red, aborted, t_full, detail, dch); break;
+            case 2: mv_group<TT, 2>(P, geo, ring, rp, prep_s, o, red, aborted, t_full, detail, dch); break;
+            default: mv_group<TT, 4>(P, geo, ring, rp, prep_s, o, red, aborted, t_full, detail, dch); break;
         }
         dk_bar();
         if (ok < ng) {
@@ -515,15 +532,13 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
 // Producer side of one matvec phase: the same tiles and stages, in order;
 // one bulk copy per tile per stage (the tile's KC block-tiles are contiguous).
 template <int TT>
-__device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, int& q,
+__device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, RingPos& rp,
                                            unsigned long long* detail) {
     int dch = 0;
     const uint64_t pol = l2_evict_first_policy();
     constexpr int BS = pk_block_bytes(TT);
     const int lane = threadIdx.x & 31;
-    const int G = gridDim.x;
-    const int t0 = (int)((int64_t)blockIdx.x * f.tiles / G);
-    const int t1 = (int)((int64_t)(blockIdx.x + 1) * f.tiles / G);
+    const int t0 = s_tiles[f.ph][0], t1 = s_tiles[f.ph][1];
     const int nt = t1 - t0;
     if (nt <= 0) return;
     const int gs = pk_gs(P, f.ph, nt);
@@ -531,13 +546,13 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
         const int ng = ng_pow2(min(gs, t1 - tg0));
         const PGeom geo = pk_geom(P, f.ph, ng, f.KB);
         const uint32_t cbytes = (uint32_t)geo.KC * BS;
-        for (int chunk = 0; chunk < geo.nchunks; ++chunk, ++q) {
-            const int stage = q % ring.ns;
-            if (q >= ring.ns) {
+        for (int chunk = 0; chunk < geo.nchunks; ++chunk, rp.advance(ring.ns)) {
+            const int stage = rp.slot;
+            if (rp.q >= ring.ns) {   // wait for the consumers to release the slot's previous use
                 bool ok = false;
                 const uint64_t t0ns = global_ns();
                 for (uint32_t it = 0;; ++it) {
-                    if (mbar_try_wait(&ring.empty[stage], ((q / ring.ns) - 1) & 1)) { ok = true; break; }
+                    if (mbar_try_wait(&ring.empty[stage], rp.par ^ 1u)) { ok = true; break; }
                     __nanosleep(128);   // the ring is full: do not steal issue slots from the consumers
                     if ((it & 255u) == 255u && (global_ns() - t0ns > 2000000000ull || ld_volatile_int(P.abort))) break;
                 }
@@ -546,7 +561,7 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
                         atomicOr(P.err, BREW_DEVERR_TIMEOUT_EMPTY);
                         atomicExch(P.abort, 1);
                     }
-                    q = 1 << 30;   // stop producing
+                    rp.q = 1 << 30;   // stop producing
                     return;
                 }
             }
@@ -587,18 +602,43 @@ struct AttnItem {
 // This step's position of each sequence, read from P.pos once at kernel start.
 __shared__ int s_pos[DK_MAX_BATCH];
 
+// Chunk geometry of each sequence's attention for this step, computed once
+// at kernel start: [sequence][0: all positions, 1: sliding window] =
+// {start, positions per chunk, used chunks} (used = 0: no valid position).
+__shared__ int s_attg[DK_MAX_BATCH][2][3];
+// (chunk, kv head, sequence) of this CTA's first attention item (blockIdx.x)
+__shared__ int s_item0[3];
+
+__device__ __forceinline__ void attn_geometry(const DecodeParams& P, int b, int windowed, int* g) {
+    const int pos = b < P.batch ? P.pos[b] : -1;
+    g[0] = g[1] = g[2] = 0;
+    if (pos < 0 || pos >= P.seq_len) return;
+    const int nch = P.nchunk;
+    const int start = (windowed && P.window > 0) ? max(0, pos - P.window + 1) : 0;
+    const int len = pos - start + 1;
+    const int per = max(ATTN_MIN_POS, (len + nch - 1) / nch);
+    g[0] = start;
+    g[1] = per;
+    g[2] = (len + per - 1) / per;
+}
+
 __device__ __forceinline__ bool attn_item(const DecodeParams& P, int l, int item, AttnItem& it) {
     const int nch = P.nchunk;
-    const int window = arch_window(P.arch, l, P.window);   // Gemma2/Gemma3AttentionPattern.java:10-16
-    it.c = item % nch;
-    it.hk = (item / nch) % P.n_kv;
-    it.b = item / (nch * P.n_kv);
+    const bool windowed = arch_window(P.arch, l, P.window) > 0;   // Gemma2/Gemma3AttentionPattern.java:10-16
+    if (item == (int)blockIdx.x) {
+        it.c = s_item0[0];
+        it.hk = s_item0[1];
+        it.b = s_item0[2];
+    } else {
+        it.c = item % nch;
+        it.hk = (item / nch) % P.n_kv;
+        it.b = item / (nch * P.n_kv);
+    }
     it.pos = s_pos[it.b];
-    if (it.pos < 0 || it.pos >= P.seq_len) return false;
-    const int start = window > 0 ? max(0, it.pos - window + 1) : 0;
-    const int len = it.pos - start + 1;
-    const int per = max(ATTN_MIN_POS, (len + nch - 1) / nch);
-    it.used = (len + per - 1) / per;
+    const int* g = s_attg[it.b][windowed ? 1 : 0];
+    if (it.pos < 0 || it.pos >= P.seq_len || g[2] == 0) return false;
+    const int start = g[0], per = g[1];
+    it.used = g[2];
     it.p0 = start + it.c * per;
     it.n = max(0, min(it.pos + 1, it.p0 + per) - it.p0);
     return true;
@@ -610,12 +650,13 @@ __device__ __forceinline__ bool attn_item(const DecodeParams& P, int l, int item
 __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, const AttnItem& it, int r0, float* kb,
                                               float* vb) {
     const int hd = P.hd, hd4 = hd / 4, kvd = P.n_kv * hd;
+    const int lg4 = 31 - __clz(hd4);   // hd is a power of two
     const int ns = min(attn_sub(hd), it.n - r0);
     const float* kc = P.kc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     const float* vc = P.vc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     #pragma unroll 1
     for (int i = threadIdx.x; i < ns * hd4; i += DK_CT) {
-        const int r = i / hd4, ci = i % hd4;
+        const int r = i >> lg4, ci = i & (hd4 - 1);
         const int p = it.p0 + r0 + r;
         if (p == it.pos) continue;
         const int64_t off = (int64_t)p * kvd + (int64_t)it.hk * hd + 4 * ci;
@@ -953,15 +994,32 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
     }
     if (tid < 16) s_best[tid] = 0ull;
     if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
+    if (tid < 5) {
+        const int qw = P.n_heads * P.hd, kvd = P.n_kv * P.hd;
+        const int tiles = tid == PH_QKV ? (qw + 2 * kvd) / 16
+                          : tid == PH_O  ? P.dim / 16
+                          : tid == PH_GU ? P.hidden / 8
+                          : tid == PH_DOWN ? P.dim / 16
+                                           : (P.vocab + 15) / 16;
+        s_tiles[tid][0] = (int)((int64_t)blockIdx.x * tiles / gridDim.x);
+        s_tiles[tid][1] = (int)((int64_t)(blockIdx.x + 1) * tiles / gridDim.x);
+    }
+    if (tid >= 8 && tid < 8 + 2 * DK_MAX_BATCH) attn_geometry(P, (tid - 8) >> 1, tid & 1, s_attg[(tid - 8) >> 1][tid & 1]);
+    if (tid == 12) {
+        const int item = blockIdx.x, nch = P.nchunk;
+        s_item0[0] = item % nch;
+        s_item0[1] = (item / nch) % P.n_kv;
+        s_item0[2] = min(item / (nch * P.n_kv), DK_MAX_BATCH - 1);
+    }
     __syncthreads();
 
     if (warp == DK_CW) {
         // ------------------------------- producer -------------------------------
-        int q = 0;
+        RingPos rp;
         unsigned long long* dtr =
             P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots + P.trace_slots - 3 * DK_DETAIL : nullptr;
         // the consumers' phase steps, without attention (no weights)
-        for (int s = 0; s < 5 * L + 1 && q < (1 << 29); ++s) {
+        for (int s = 0; s < 5 * L + 1 && rp.q < (1 << 29); ++s) {
             const int l = s / 5, ph = s - 5 * l;
             const bool cls = s == 5 * L;
             if (ph == 1) continue;
@@ -969,12 +1027,12 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
             const DPhase f = make_phase(P, l, mph, P.x0);
             unsigned long long* d = (l == P.detail_l && mph == P.detail_ph) ? dtr : nullptr;
             if constexpr (TYPE == CTYPE) {
-                produce_phase<TYPE>(P, f, ring, q, d);
+                produce_phase<TYPE>(P, f, ring, rp, d);
             } else {
                 if (cls)
-                    produce_phase<CTYPE>(P, f, ring, q, d);
+                    produce_phase<CTYPE>(P, f, ring, rp, d);
                 else
-                    produce_phase<TYPE>(P, f, ring, q, d);
+                    produce_phase<TYPE>(P, f, ring, rp, d);
             }
         }
         return;
@@ -983,7 +1041,7 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
     // --------------------------------- consumers ---------------------------------
     const int Gc = gridDim.x;
     unsigned long long target = s_base;
-    int q = 0;
+    RingPos rp;
     bool aborted = false;
     const bool gem = arch_gemma(P.arch);
     constexpr bool lsum_l = TYPE == BREW_TYPE_Q4_0, lsum_c = CTYPE == BREW_TYPE_Q4_0;
@@ -1105,12 +1163,12 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
         mark_prep();
         const DPhase f = make_phase(P, l, mph, xcur);
         if constexpr (TYPE == CTYPE) {
-            mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+            mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
         } else {
             if (cls)
-                mv_phase<CTYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+                mv_phase<CTYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
             else
-                mv_phase<TYPE, NT>(P, f, ring, q, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+                mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
         }
         markv(tfull);
         if (cls) {
@@ -1188,6 +1246,7 @@ bool decode_supported(const brew_config& c, int batch) {
     // attention: a CTA holds the G * hd outputs of a kv head's queries in
     // four registers per thread; 16-byte copies of half rows
     if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
+    if (c.head_size & (c.head_size - 1)) return false;   // power of two (shift-based indexing)
     return true;
 }
 
@@ -1252,8 +1311,10 @@ int decode_prepare(DecodeParams* p) {
             BREW_CHECK(ng * kc[ng] * bs <= p->stage_bytes && kc[ng] < 32768, BREW_ERR_UNSUPPORTED,
                        "decode kernel: stage geometry");
             p->geo_kc[ph][ng] = (int16_t)kc[ng];
+            p->geo_nch[ph][ng] = (int16_t)(KB / kc[ng]);
         }
         p->geo_kc[ph][0] = 8;
+        p->geo_nch[ph][0] = (int16_t)(KB / 8);
         p->geo_gs[ph][0] = 1;
         for (int nt = 1; nt <= 9; ++nt) {
             int best = 1, fill = 0;

@@ -57,6 +57,7 @@ struct alignas(64) DecodeParams {
     // stage for a group of ng tiles (index ng <= 8)
     int8_t geo_gs[5][10];
     int16_t geo_kc[5][9];
+    int16_t geo_nch[5][9];              // chunks of a group: KB / geo_kc
 };
 
 // True when the model can run on the persistent decode kernel.
