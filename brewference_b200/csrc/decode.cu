@@ -592,6 +592,58 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
 //   q-norm w [hd] | k-norm w [hd] | cos [hd/2] | sin [hd/2] |
 //   scores [G][SUB] | per head: running max, running sum, round rescale, -
 // and, for the combine, the partials [heads][nchunk][hd + 4].
+// Head-wise RMSNorm (when w is given: Kernels.headWiseRmsNorm) and RoPE (when
+// rope: InterleavedRope pairs (2d, 2d+1) or NonInterleavedRope pairs
+// (d, d + hd/2), RopeCache cos / sin rows cs, sn) of one head vector in shared
+// memory by one warp: lane holds elements lane + 32 r, r < R = hd / 32.
+template <int R>
+__device__ __forceinline__ void norm_rope_warp_t(float* v, const float* w, float eps, bool rope, bool inter,
+                                                 const float* cs, const float* sn) {
+    const int lane = threadIdx.x & 31;
+    float x[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) x[r] = v[lane + 32 * r];
+    if (w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) ss += x[r] * x[r];
+        const float scale = rms_scale(warp_sum(ss), 32 * R, eps);
+#pragma unroll
+        for (int r = 0; r < R; ++r) x[r] = x[r] * scale * w[lane + 32 * r];
+    }
+    if (rope) {
+        if (inter) {   // partner element i ^ 1: the neighbouring lane, same register
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const float other = __shfl_xor_sync(0xffffffffu, x[r], 1);
+                const int i = lane + 32 * r, d = i >> 1;
+                const float c = cs[d], s = sn[d];
+                x[r] = (i & 1) == 0 ? __fsub_rn(__fmul_rn(x[r], c), __fmul_rn(other, s))
+                                    : __fadd_rn(__fmul_rn(other, s), __fmul_rn(x[r], c));
+            }
+        } else {       // partner element i + hd/2: register r + R/2 of the same lane
+#pragma unroll
+            for (int r = 0; r < R / 2; ++r) {
+                const int d = lane + 32 * r;
+                const float a = x[r], b = x[r + R / 2], c = cs[d], s = sn[d];
+                x[r] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+                x[r + R / 2] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+            }
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[lane + 32 * r] = x[r];
+    __syncwarp();
+}
+
+__device__ __noinline__ void norm_rope_warp(float* v, int hd, const float* w, float eps, bool rope, bool inter,
+                                            const float* cs, const float* sn) {
+    if (hd == 64) norm_rope_warp_t<2>(v, w, eps, rope, inter, cs, sn);
+    else if (hd == 128) norm_rope_warp_t<4>(v, w, eps, rope, inter, cs, sn);
+    else norm_rope_warp_t<8>(v, w, eps, rope, inter, cs, sn);
+}
+
 // One attention item: sequence b, kv head hk, chunk c of the positions
 // start .. pos (Gemma3's local layers: the last `window` positions), split
 // into chunks of `per` positions; `used` chunks are non-empty.
@@ -678,6 +730,8 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
     int tpp = 1;                 // lanes per (position, head) score (power of two <= 8)
     while (tpp < 8 && 2 * tpp * G * SUB <= DK_CT) tpp *= 2;
+    // (pc * gmagic) >> 16 == pc / G for the pair indices pc < G * SUB (<= 256), G <= 8
+    const int gmagic = (65536 + G - 1) / G;
     float* kb = sm;
     float* vb = kb + SUB * hd;
     float* qs = vb + SUB * hd;
@@ -733,51 +787,47 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     cp_async16(sn + 4 * i, P.rope_sin + ro + 4 * i);
                 }
             }
+            cp_async_commit();                 // group: q, k, v, norm weights, RoPE row
             attn_issue_kv(P, l, it, 0, kb, vb);
+            cp_async_commit();                 // group: the first round's cached K / V rows
             if (tid < G) {
                 st[4 * tid + 0] = -INFINITY;
                 st[4 * tid + 1] = 0.0f;
             }
-            cp_async_wait_all();
+            cp_async_wait_group<1>();          // q / k / v landed; the K / V rows may still be in flight
             dk_bar();
             if (t_wave) *t_wave = global_ns();
             stamp(1);
-            if (P.rms_q) {   // Kernels.headWiseRmsNorm (Qwen3, Gemma3)
-                #pragma unroll 1
-                for (int hh = warp; hh <= G; hh += DK_CW) {
-                    float* vecp = hh < G ? qs + hh * hd : ks;
-                    const float* w = hh < G ? wq : wk;
-                    float ss = 0.0f;
+            // one warp per vector (the G q heads, then k): head-wise RMSNorm
+            // (Kernels.headWiseRmsNorm, Qwen3 / Gemma3) and RoPE in registers,
+            // lane holding elements lane + 32 r; the k warp also appends this
+            // step's k and v to the cache (storeKeyValueInCache,
+            // AttentionEngine.java:34-38) and, when this position is in the
+            // first round, writes them into that round's K / V rows
+            const bool has_pos = pos >= p0 && pos < p0 + n;
+            #pragma unroll 1
+            for (int hh = warp; hh <= G; hh += DK_CW) {
+                float* vecp = hh < G ? qs + hh * hd : ks;
+                norm_rope_warp(vecp, hd, P.rms_q ? (hh < G ? wq : wk) : nullptr, P.eps, rope_on, inter, cs, sn);
+                if (hh == G && has_pos) {
+                    const int r = pos - p0;
+                    float* kcr = kc + (int64_t)pos * kvd + hk * hd;
+                    float* vcr = vc + (int64_t)pos * kvd + hk * hd;
                     #pragma unroll 1
-                    for (int i = lane; i < hd; i += 32) ss += vecp[i] * vecp[i];
-                    const float scale = rms_scale(warp_sum(ss), hd, P.eps);
-                    __syncwarp();
-                    #pragma unroll 1
-                    for (int i = lane; i < hd; i += 32) vecp[i] = vecp[i] * scale * w[i];
+                    for (int i = lane; i < hd; i += 32) {
+                        const float kv = ks[i], vv = vs[i];
+                        kcr[i] = kv;
+                        vcr[i] = vv;
+                        if (r < SUB) {
+                            kb[r * hd + i] = kv;
+                            vb[r * hd + i] = vv;
+                        }
+                    }
                 }
-                dk_bar();
             }
             stamp(2);
-            #pragma unroll 1
-            for (int idx = tid; rope_on && idx < (G + 1) * half; idx += DK_CT) {   // RoPE on q heads and k
-                const int hh = idx / half, d = idx % half;
-                float* vecp = hh < G ? qs + hh * hd : ks;
-                const int i0 = inter ? 2 * d : d;
-                const int i1 = inter ? 2 * d + 1 : d + half;
-                const float a = vecp[i0], bb = vecp[i1], cc = cs[d], ss = sn[d];
-                vecp[i0] = __fsub_rn(__fmul_rn(a, cc), __fmul_rn(bb, ss));
-                vecp[i1] = __fadd_rn(__fmul_rn(a, ss), __fmul_rn(bb, cc));
-            }
-            dk_bar();
+            cp_async_wait_group<0>();
             stamp(3);
-            const bool has_pos = pos >= p0 && pos < p0 + n;
-            if (has_pos) {   // storeKeyValueInCache (AttentionEngine.java:34-38)
-                #pragma unroll 1
-                for (int i = tid; i < hd; i += DK_CT) {
-                    kc[(int64_t)pos * kvd + hk * hd + i] = ks[i];
-                    vc[(int64_t)pos * kvd + hk * hd + i] = vs[i];
-                }
-            }
             float acc[DK_PVK] = {};   // outputs tid + DK_CT k of [G][hd] (G * hd <= 1024)
             #pragma unroll 1
             for (int r0 = 0; r0 < n; r0 += SUB) {
@@ -786,7 +836,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     attn_issue_kv(P, l, it, r0, kb, vb);
                     cp_async_wait_all();
                 }
-                if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
+                if (r0 > 0 && has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
                     const int r = pos - p0 - r0;
                     #pragma unroll 1
                     for (int i = tid; i < hd; i += DK_CT) {
@@ -807,7 +857,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     for (int p00 = 0; p00 < npair; p00 += ppi) {
                         const int pr = p00 + tid / tpp;
                         const int pc = pr < npair ? pr : npair - 1;
-                        const int tt = pc / G, h = pc % G;
+                        const int tt = (pc * gmagic) >> 16, h = pc - tt * G;   // pc / G, pc % G
                         const float4* q4 = reinterpret_cast<const float4*>(qs + h * hd);
                         const float4* k4 = reinterpret_cast<const float4*>(kb + tt * hd);
                         float s0 = 0.0f, s1 = 0.0f;
@@ -1246,7 +1296,8 @@ bool decode_supported(const brew_config& c, int batch) {
     // attention: a CTA holds the G * hd outputs of a kv head's queries in
     // four registers per thread; 16-byte copies of half rows
     if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
-    if (c.head_size & (c.head_size - 1)) return false;   // power of two (shift-based indexing)
+    // 64, 128 or 256: shift-based indexing, two to eight registers per lane in norm_rope_warp
+    if (c.head_size != 64 && c.head_size != 128 && c.head_size != 256) return false;
     return true;
 }
 

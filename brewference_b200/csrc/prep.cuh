@@ -150,10 +150,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // inverseRootMeanSquare (transformer/math/Kernels.java:77-88): the sum of
-// squares in fp32, meanSquare = ss / n in fp32, then 1/sqrt in double.
+// squares in fp32, meanSquare = ss / n in fp32 (IEEE division), then the
+// scale (float)(1.0 / Math.sqrt((double)(meanSquare + eps))).  The last step
+// is the correctly rounded fp32 reciprocal square root of the fp32 sum: the
+// reference's double result is within 2^-52 of the exact value before its
+// rounding to fp32, so the two round to the same float except for arguments
+// within 2^-52 of a rounding midpoint (about 4e-9 of them), where they differ
+// by one ulp.  One correctly rounded instruction sequence instead of a double
+// square root and a double division on every phase's critical path.
 __device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
-    const float meanSquare = ss / (float)n;
-    return (float)(1.0 / sqrt((double)(meanSquare + eps)));
+    const float meanSquare = __fdiv_rn(ss, (float)n);
+    return __frsqrt_rn(__fadd_rn(meanSquare, eps));
 }
 
 // Whole-CTA prep of one vector x[K] (read through L2: it may have been
