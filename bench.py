@@ -26,6 +26,11 @@ Printed JSON line (rank 0):
 N > 1: one independent model replica per GPU (decode at batch 1 does not
 shard without a per-layer exchange); value = tokens of all ranks / max time.
 
+tp (sub-record, every N including 1): the Qwen2.5-7B-shaped K-quant config
+decoding 32 sequences, every matrix row-sharded over the N ranks with NCCL
+all-gathers (strong scaling), with a bit-for-bit check of the sharded
+first-step logits against the unsharded model on one GPU (N > 1).
+
 --impl reference: times the CPU restatement of the reference path (the Java
 reference cannot run here: no JDK) on the same config and metric.
 """
@@ -384,24 +389,22 @@ def profiled_traffic(name: str):
     return None
 
 
-def run_tp(args):
-    """Tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config
-    (Q4_K attention/FFN, Q6_K down and classifier, QKV bias): every matrix
-    row-sharded over the N ranks with one NCCL all-gather per projection;
-    B concurrent sequences prefilled with seeded prompts (untimed), then
-    decode steps fed back on the device.  value = tokens of all B sequences
-    per second (the ranks cooperate on the same tokens: strong scaling)."""
+def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True):
+    """Tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config (Q4_K
+    attention/FFN, Q6_K down and classifier, QKV bias): every matrix
+    row-sharded over the `world` ranks with one NCCL all-gather per
+    projection; B concurrent sequences prefilled with seeded prompts
+    (untimed), then decode steps fed back on the device.  Returns a dict:
+    value = tokens of all B sequences per second (the ranks cooperate on the
+    same tokens: strong scaling), ms_per_step (max over ranks), and, with
+    check_parity at world > 1, whether rank 0's sharded logits of the first
+    step equal those of the same model unsharded on one GPU bit for bit."""
     import ctypes
     import torch
     from brewference_b200 import _native as N
     from brewference_b200.api import Communicator, DeviceModel, comm_unique_id
 
-    rank, world, dist = dist_init(args.gpus)
-    dev = torch.cuda.current_device() if world > 1 else 0
-    torch.cuda.set_device(dev)
-    N.init(dev)
     cfg = C.qwen25_7b()
-    B = args.batch
     box = [comm_unique_id() if rank == 0 else None]
     if dist is not None:
         dist.broadcast_object_list(box, src=0)
@@ -411,17 +414,20 @@ def run_tp(args):
     dm.set_tp(comm)
     synth_s = time.perf_counter() - t0
     rng = np.random.default_rng(SEED)
-    plen = args.prompt_len
     prompts = rng.integers(0, cfg.vocab_size, (B, plen)).astype(np.int32)
+    # first step from a reset state, logits kept for the parity check
+    lg_tp, _ = dm.forward(prompts[:, 0], np.zeros(B, np.int32), want_logits=True)
+    dm.reset()
     t0 = time.perf_counter()
     for i in range(plen):
         dm.forward(prompts[:, i], np.full(B, i, np.int32), want_logits=False)
     prefill_s = time.perf_counter() - t0
     stream = torch.cuda.Stream()
+    prev = torch.cuda.current_stream()
     torch.cuda.set_stream(stream)
     s = stream.cuda_stream
     tok = torch.from_numpy(prompts[:, -1].copy()).cuda()
-    n_pos = args.warmup + args.steps
+    n_pos = warmup + steps
     pos = torch.arange(plen, plen + n_pos, dtype=torch.int32, device="cuda").repeat_interleave(B).view(n_pos, B)
     lib = N.lib()
 
@@ -430,48 +436,78 @@ def run_tp(args):
                                            ctypes.c_void_p(pos[k].data_ptr()), B, None,
                                            ctypes.c_void_p(tok.data_ptr()), ctypes.c_void_p(s)), "forward_dev")
 
-    for k in range(args.warmup):
+    for k in range(warmup):
         step(k)
     barrier(dist)
-    clocks = ClockSampler(dev)
-    clocks.start()
     k0 = N.kernel_launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(dist)
     e0.record(stream)
-    for k in range(args.warmup, n_pos):
+    for k in range(warmup, n_pos):
         step(k)
     e1.record(stream)
     barrier(dist)
     launches = N.kernel_launches() - k0
-    clk = clocks.stop()
     ms = max_over_ranks(dist, e0.elapsed_time(e1))
-    value = B * args.steps / (ms / 1000.0)
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(prev)
+    dm.close()
+    parity = None
+    if check_parity and world > 1:
+        ok = 1.0
+        if rank == 0:   # the same seeded model unsharded on this GPU, same first step
+            ref = DeviceModel.synthesize(cfg, SEED, max_batch=B)
+            lg_1, _ = ref.forward(prompts[:, 0], np.zeros(B, np.int32), want_logits=True)
+            ref.close()
+            ok = 1.0 if np.array_equal(lg_tp, lg_1) else 0.0
+        parity = bool(max_over_ranks(dist, ok) > 0.5) if dist is not None else bool(ok)
+    comm.close()
+    value = B * steps / (ms / 1000.0)
+    return {"value": value, "unit": "tok/s", "ms_per_step": ms / steps, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "sequences": B, "prompt_tokens": plen, "gpu_launches": int(launches),
+            "collective": "NCCL all-gather per projection (q|k|v, wo, gate|up, down, logits) + argmax key reduction",
+            "parity": parity,
+            "parity_check": "rank 0: first-step logits of the sharded model == unsharded 1-GPU model, bit for bit"
+                            if world > 1 else "single GPU (no sharding)",
+            "model": cfg.name, "weight_bytes_per_step": cfg.decode_weight_bytes(),
+            "setup_s": {"synthesize": round(synth_s, 2), "prefill": round(prefill_s, 2)}}
+
+
+def run_tp(args):
+    """--tp: the tensor-parallel decode of the Qwen2.5-7B-shaped config as the
+    headline line (see tp_measure)."""
+    import torch
+    from brewference_b200 import _native as N
+
+    rank, world, dist = dist_init(args.gpus)
+    dev = torch.cuda.current_device() if world > 1 else 0
+    torch.cuda.set_device(dev)
+    N.init(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    r = tp_measure(rank, world, dist, dev, args.steps, args.warmup, args.batch, args.prompt_len)
+    clk = clocks.stop()
     peak, peak_kind = measured_peaks()
-    wbytes = cfg.decode_weight_bytes()
-    per_gpu = wbytes / world / (ms / args.steps / 1000.0) / 1e9
+    cfg = C.qwen25_7b()
+    per_gpu = cfg.decode_weight_bytes() / world / (r["ms_per_step"] / 1000.0) / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 (K-quant dequant in registers)",
         "data": "synthetic (seeded random-init N(0,0.02) weights quantized to Q4_K/Q6_K on the device, seeded prompts)",
-        "config": {"workload": f"{cfg.name} Q4_K/Q6_K decode, {B} concurrent sequences after {plen}-token prompts, "
-                               f"tensor-parallel over {world} GPU(s)",
-                   "model": cfg.name, "global_batch": B, "seq_len": cfg.seq_len,
+        "config": {"workload": f"{cfg.name} Q4_K/Q6_K decode, {args.batch} concurrent sequences after "
+                               f"{args.prompt_len}-token prompts, tensor-parallel over {world} GPU(s)",
+                   "model": cfg.name, "global_batch": args.batch, "seq_len": cfg.seq_len,
                    "parallelism": f"tp{world} (row-sharded matrices, NCCL all-gather per projection)",
                    "l2": "inputs larger than L2 (4.6 GB of weights per step)"},
-        "gpu_launches": int(launches),
+        "gpu_launches": r["gpu_launches"],
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "traffic": None, "peak_kind": peak_kind,
                      "kernel": "per-GPU weight stream of the forward (weight bytes / P per step)"},
-        "clocks": clk,
-        "setup_s": {"synthesize": round(synth_s, 2), "prefill": round(prefill_s, 2)},
+        "clocks": clk, "tp_parity": r["parity"], "setup_s": r["setup_s"],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    torch.cuda.synchronize()
-    dm.close()
-    comm.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -604,6 +640,8 @@ def run_gpu(args):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": profiled_traffic(TRAFFIC_PROFILE), "peak_kind": peak_kind,
+                     "traffic_source": f"profile: profiles/{TRAFFIC_PROFILE} (ncu dram__bytes_read.sum + "
+                                       f"dram__bytes_write.sum of one launch; the command is in the file)",
                      "kernel": "decode_kernel (persistent; one launch = one decode step, timed with the step's "
                                "1-launch token update)",
                      "bytes_per_launch": alg, "weight_bytes": wbytes, "kv_bytes": kvb,
@@ -613,6 +651,11 @@ def run_gpu(args):
         "clocks": clk,
         "setup_s": {"synthesize": round(synth_s, 2)},
     }
+    dm.close()
+    if not args.no_tp:
+        # the sharded 7B config at the same N (tensor parallelism over the
+        # ranks; strong scaling): a sub-record of the line
+        line["tp"] = tp_measure(rank, world, dist, dev, args.tp_steps, 3, args.batch, args.tp_prompt_len)
     if rank == 0 and not args.no_cpu_baseline:
         tps, thr, dt = cpu_decode_rate(cfg, args.cpu_tokens, args.prompt_len)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": thr, "kind": "port",
@@ -621,7 +664,6 @@ def run_gpu(args):
                                           f"restatement of the reference Java path), {dt:.1f}s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    dm.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -643,6 +685,9 @@ def main():
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config over --gpus ranks")
     ap.add_argument("--batch", type=int, default=32, help="concurrent sequences of the --tp workload")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel 7B sub-record")
+    ap.add_argument("--tp-steps", type=int, default=16, help="timed steps of the tensor-parallel sub-record")
+    ap.add_argument("--tp-prompt-len", type=int, default=256, help="prompt tokens of the tensor-parallel sub-record")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     args = ap.parse_args()

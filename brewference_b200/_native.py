@@ -129,6 +129,7 @@ def lib():
         "brew_gguf_tensor_info": (I, [V, I64, ctypes.c_char_p, S, ctypes.POINTER(I), ctypes.POINTER(I64),
                                       ctypes.POINTER(I64)]),
         "brew_model_load_gguf": (I, [ctypes.c_char_p, ctypes.c_int32, c_void_pp]),
+        "brew_selftest_wait_timeout": (I, [I64, c_i32p]),
         "brew_prep_bytes": (I64, [ctypes.c_int32, ctypes.c_int32]),
         "brew_prepare_input_dev": (I, [V, ctypes.c_int32, ctypes.c_int32, V, V]),
         "brew_matmul_prepared_dev": (I, [V, V, V, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, V]),

@@ -179,16 +179,39 @@ __device__ __forceinline__ uint64_t global_ns() {
 // BREW_SPIN_LIMIT polls); on timeout records `err` in the device error word
 // and returns false, so a broken pipeline ends instead of hanging the GPU.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* err_word,
-                                                  unsigned int err) {
+                                                  unsigned int err, uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t it = 0; it < BREW_SPIN_LIMIT; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         __nanosleep(64);   // leave issue slots to the warps that compute
-        if ((it & 255u) == 255u && global_ns() - t0 > 2000000000ull) break;
+        if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) break;
     }
     if (err_word) atomicOr(err_word, err);
     return false;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// Waits until the counter *ctr reaches `target` (acquire), for at most
+// limit_ns, or until *abort is set by another CTA that gave up.  Returns
+// false on timeout or abort: the grid barrier's wait, which must end instead
+// of hanging the GPU when an arrival never comes.
+__device__ __forceinline__ bool wait_counter_bounded(const unsigned long long* ctr, unsigned long long target,
+                                                     const int* abort, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+    uint32_t it = 0;
+    while (ld_acquire_u64(ctr) < target) {
+        __nanosleep(32);
+        if ((++it & 63u) == 0u && (global_ns() - t0 > limit_ns || (abort && ld_volatile_int(abort)))) return false;
+    }
+    return true;
 }
 
 // Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2.

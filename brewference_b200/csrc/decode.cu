@@ -161,13 +161,6 @@ __device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, 
     return g;
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
 // Grid barrier among the consumer warps of all CTAs.  Bounded: after ~2 s
 // (or when another CTA already gave up) it records a timeout and raises the
@@ -177,16 +170,10 @@ __device__ bool grid_sync(const DecodeParams& P, unsigned long long target, int*
     if (threadIdx.x == 0) {
         int ok = 1;
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(P.bar) : "memory");
-        const uint64_t t0 = global_ns();
-        uint32_t it = 0;
-        while (ld_acquire_u64(&P.bar[0]) < target) {
-            __nanosleep(32);
-            if ((++it & 63u) == 0u && (global_ns() - t0 > 2000000000ull || ld_volatile_int(P.abort))) {
-                atomicOr(P.err, BREW_DEVERR_TIMEOUT_FULL);
-                atomicExch(P.abort, 1);
-                ok = 0;
-                break;
-            }
+        if (!wait_counter_bounded(&P.bar[0], target, P.abort, 2000000000ull)) {
+            atomicOr(P.err, BREW_DEVERR_TIMEOUT_FULL);
+            atomicExch(P.abort, 1);
+            ok = 0;
         }
         *s_ok = ok;
     }

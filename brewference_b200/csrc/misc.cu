@@ -1,4 +1,5 @@
 // misc.cu — embedding + prep, dequantization, synthetic weights, argmax.
+#include "brew_internal.cuh"
 #include "misc.cuh"
 #include "mv_device.cuh"
 #include "prep.cuh"
@@ -314,3 +315,55 @@ int argmax_launch(const float* logits, int ld, int n, int batch, unsigned long l
 }
 
 }  // namespace brew
+
+// ---------------------------------------------------------------------------
+// Failure-detection self-test: the two bounded waits every pipeline of this
+// library uses (an mbarrier phase, the grid barrier's counter) run against
+// events that never happen and must give up after `limit_ns`, record the
+// timeout in the device error word and return, leaving the context usable.
+// ---------------------------------------------------------------------------
+namespace brew {
+namespace {
+
+__device__ unsigned long long g_selftest_counter;   // nothing ever adds to it
+
+__global__ void selftest_wait_kernel(unsigned int* err, uint64_t limit_ns, int* status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);   // one arrival completes the phase; none comes
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool a = mbar_wait_bounded(&bar, 0, err, BREW_DEVERR_TIMEOUT_FULL, limit_ns);
+        const bool b = wait_counter_bounded(&g_selftest_counter, 1ull, nullptr, limit_ns);
+        if (!b) atomicOr(err, BREW_DEVERR_TIMEOUT_EMPTY);
+        status[0] = a ? 1 : 0;
+        status[1] = b ? 1 : 0;
+    }
+}
+
+}  // namespace
+}  // namespace brew
+
+using namespace brew;
+
+extern "C" int brew_selftest_wait_timeout(int64_t limit_ns, int32_t* waits_ended) {
+    BREW_CHECK(limit_ns > 0 && limit_ns <= 1000000000LL, BREW_ERR_INVALID_ARG, "limit %lld ns (1 ns .. 1 s)",
+               (long long)limit_ns);
+    int rc = ensure_init();
+    if (rc) return rc;
+    int* st = nullptr;
+    BREW_CUDA(cudaMalloc(&st, 2 * sizeof(int)));
+    cudaStream_t s = ctx().stream;
+    selftest_wait_kernel<<<1, 32, 0, s>>>(ctx().err_word, (uint64_t)limit_ns, st);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    int h[2] = {-1, -1};
+    if (e == cudaSuccess) e = cudaMemcpy(h, st, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(st);
+    if (e != cudaSuccess) return cuda_error(e, "selftest_wait_kernel");
+    count_launch();
+    if (waits_ended) *waits_ended = (h[0] == 0 ? 1 : 0) + (h[1] == 0 ? 1 : 0);
+    return check_device_error("brew_selftest_wait_timeout");
+}

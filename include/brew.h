@@ -373,6 +373,16 @@ BREW_API int brew_model_step_kernels(brew_model m, int32_t batch, int32_t* n_ker
 BREW_API int brew_model_set_trace(brew_model m, int32_t on);
 BREW_API int brew_model_trace(brew_model m, int64_t* ns, int32_t max_n, int32_t* n);
 
+/* Failure-detection self-test (no reference counterpart): runs the library's
+ * two bounded device waits, an mbarrier phase and the grid barrier's arrival
+ * counter, against events that never happen.  Each must give up after
+ * `limit_ns` (1 ns .. 1 s), record the timeout in the device error word and
+ * return, as a decode step whose weight pipeline or grid barrier stalled
+ * does (there the limit is 2 s).  Returns BREW_ERR_TIMEOUT when the waits
+ * ended as designed; *waits_ended (optional) receives how many did (2).
+ * The context stays usable afterwards. */
+BREW_API int brew_selftest_wait_timeout(int64_t limit_ns, int32_t* waits_ended);
+
 /* Clears the sequence state (ModelSession.reset, ModelRunner.java:115-120). */
 BREW_API int brew_model_reset(brew_model m);
 
