@@ -514,6 +514,47 @@ def run_tp(args):
     return 0
 
 
+def decode_trace_table(dm, cfg, reps=3):
+    """Runs `reps` traced decode steps and summarises the last: per phase
+    (Q|K|V, attention, wo, gate|up, down, classifier) the mean and max over
+    CTAs of five stamps in microseconds after the previous phase's earliest
+    barrier exit: input wave landed, input prepared, last weight stage seen,
+    work done (barrier entry), barrier exit."""
+    L = cfg.n_layers
+    slots = 1 + 5 * (5 * L + 1) + 3 * 32
+    names = ["qkv", "attn", "wo", "gate_up", "down"]
+    stamps = ["wave", "prep", "last_weight", "work", "exit"]
+    for _ in range(reps):
+        dm.decode(1)
+        T = np.array(dm.trace(), dtype=np.int64).reshape(-1, slots).astype(np.float64)
+    acc = {n: [] for n in names}
+    prev = T[:, 0]
+    for l in range(L):
+        for p in range(5):
+            b = 1 + 5 * (5 * l + p)
+            st = T[:, b:b + 5]
+            rel = (st - prev.min()) / 1000.0
+            rel[st == 0] = np.nan
+            acc[names[p]].append(rel)
+            prev = T[:, b + 4]
+    b = 1 + 5 * (5 * L)
+    cls = (T[:, b:b + 5] - prev.min()) / 1000.0
+    out = {"step_us": float((T[:, b + 4].max() - T[:, 0].min()) / 1000.0), "layers": L,
+           "stamps": stamps, "phases_mean_over_layers": {}}
+    with np.errstate(all="ignore"):
+        import warnings
+        warnings.simplefilter("ignore")
+        for n in names:
+            a = np.stack(acc[n])
+            out["phases_mean_over_layers"][n] = {
+                "mean": [round(float(x), 2) for x in np.nanmean(np.nanmean(a, axis=1), axis=0)],
+                "max": [round(float(x), 2) for x in np.nanmean(np.nanmax(a, axis=1), axis=0)]}
+        out["phases_mean_over_layers"]["classifier"] = {
+            "mean": [round(float(x), 2) for x in np.nanmean(cls, axis=0)],
+            "max": [round(float(x), 2) for x in np.nanmax(cls, axis=0)]}
+    return out
+
+
 def run_gpu(args):
     import torch
     from brewference_b200 import _native as N
@@ -524,6 +565,9 @@ def run_gpu(args):
     torch.cuda.set_device(dev)
     N.init(dev)
     cfg = workload_cfg()
+    if args.profile_decode and (args.layers or args.vocab):
+        # a smaller model of the same shapes for detailed profiler captures
+        cfg = cfg.replace(n_layers=args.layers or cfg.n_layers, vocab_size=args.vocab or cfg.vocab_size)
     t0 = time.perf_counter()
     dm = DeviceModel.synthesize(cfg, SEED)
     synth_s = time.perf_counter() - t0
@@ -532,9 +576,24 @@ def run_gpu(args):
         # kernel of the steps after the prompt)
         rng = np.random.default_rng(SEED)
         prompt = rng.integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+        if args.batched_prefill:
+            dm.set_prefill(PREFILL_BATCHED)
         dm.prefill(prompt)
         toks = dm.decode(args.steps)
         print(json.dumps({"profile_decode": True, "prompt": args.prompt_len, "steps": args.steps, "tokens": toks[:4]}))
+        dm.close()
+        return 0
+    if args.trace_decode:
+        # per-phase timing of one decode step from the kernel's %globaltimer
+        # stamps (BREW_TRACE=1 must be set before the model is created)
+        from brewference_b200.api import PREFILL_BATCHED as _PB
+        rng = np.random.default_rng(SEED)
+        prompt = rng.integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+        dm.set_prefill(_PB)
+        dm.prefill(prompt)
+        dm.decode(4)
+        dm.set_trace(True)
+        print(json.dumps(decode_trace_table(dm, cfg)), flush=True)
         dm.close()
         return 0
     if args.kernel_only:
@@ -690,6 +749,11 @@ def main():
     ap.add_argument("--tp-prompt-len", type=int, default=256, help="prompt tokens of the tensor-parallel sub-record")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
+    ap.add_argument("--layers", type=int, default=0, help="--profile-decode: layers of the model (default: all)")
+    ap.add_argument("--vocab", type=int, default=0, help="--profile-decode: vocabulary size (default: the config's)")
+    ap.add_argument("--batched-prefill", action="store_true", help="--profile-decode: prefill the prompt batched")
+    ap.add_argument("--trace-decode", action="store_true",
+                    help="per-phase %%globaltimer table of one decode step (run with BREW_TRACE=1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
