@@ -704,6 +704,162 @@ __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, cons
     }
 }
 
+// Loads E consecutive floats (E = 2, 4 or 8: 8-, 16- or 2x16-byte aligned).
+template <int E>
+__device__ __forceinline__ void lds_vec(const float* p, float* v) {
+    if constexpr (E == 2) {
+        const float2 a = *reinterpret_cast<const float2*>(p);
+        v[0] = a.x; v[1] = a.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < E; k += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(p + k);
+            v[k] = a.x; v[k + 1] = a.y; v[k + 2] = a.z; v[k + 3] = a.w;
+        }
+    }
+}
+
+// The rounds of one attention item with the positions split over the warps:
+// warp w takes positions w, w + 8, ... of each round (K / V rows staged in
+// shared memory, kb / vb [SUB][hd]); lane holds elements lane * E .. + E - 1
+// of every row, q and the unnormalised output of each of the G <= GM heads in
+// registers, and an online softmax (running max m and sum l per head) over
+// the warp's positions, so no CTA barrier separates scores, softmax and the
+// weighted sum.  At the end the warps' (m, l, o) meet in shared memory (the
+// K staging area) and the CTA's partial for chunk c is written to pbase in
+// the layout of the cross-CTA combine: [head][chunk][m, l, -, -, o[hd]].
+template <int E, int GM, int JM>
+__device__ __forceinline__ void attn_rounds_warp(const DecodeParams& P, int l, const AttnItem& it, float* kb, float* vb,
+                                 const float* qs, const float* ks, const float* vs, float* pbase, int nch,
+                                 unsigned long long* detail) {
+    const int G = P.n_heads / P.n_kv, hd = 32 * E, SUB = attn_sub(hd);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = it.n, p0 = it.p0, pos = it.pos, c = it.c;
+    const bool has_pos = pos >= p0 && pos < p0 + n;
+    const float NEG = -INFINITY;
+    float qr[GM][E], o[GM][E], m[GM], ls[GM];
+#pragma unroll
+    for (int h = 0; h < GM; ++h) {
+        m[h] = NEG;
+        ls[h] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[h][e] = 0.0f;
+    }
+    #pragma unroll 1
+    for (int r0 = 0; r0 < n; r0 += SUB) {
+        const int ns = min(SUB, n - r0);
+        if (r0 > 0) {
+            attn_issue_kv(P, l, it, r0, kb, vb);
+            cp_async_wait_all();
+            if (has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
+                const int r = pos - p0 - r0;
+                #pragma unroll 1
+                for (int i = tid; i < hd; i += DK_CT) {
+                    kb[r * hd + i] = ks[i];
+                    vb[r * hd + i] = vs[i];
+                }
+            }
+        }
+        dk_bar();
+        if (r0 == 0) {
+            if (detail && tid == 0) detail[9] = global_ns();
+#pragma unroll
+            for (int h = 0; h < GM; ++h)
+                if (h < G) lds_vec<E>(qs + h * hd + lane * E, qr[h]);
+        }
+        // scores q.k / sqrt(hd) of this warp's positions
+        float sc[JM][GM];
+#pragma unroll
+        for (int j = 0; j < JM; ++j) {
+            const int t = warp + 8 * j;
+            float kt[E];
+            if (t < ns) lds_vec<E>(kb + t * hd + lane * E, kt);
+            else
+#pragma unroll
+                for (int e = 0; e < E; ++e) kt[e] = 0.0f;
+#pragma unroll
+            for (int h = 0; h < GM; ++h) {
+                float a = 0.0f;
+                if (h < G)
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a = fmaf(qr[h][e], kt[e], a);
+                sc[j][h] = a;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < JM; ++j)
+#pragma unroll
+            for (int h = 0; h < GM; ++h) {
+                const float v = warp_sum(sc[j][h]) * P.inv_scale;
+                sc[j][h] = (warp + 8 * j < ns) ? v : NEG;
+            }
+        // online softmax and the weighted sum of this warp's V rows
+#pragma unroll
+        for (int h = 0; h < GM; ++h) {
+            if (h >= G) continue;
+            float mx = m[h];
+#pragma unroll
+            for (int j = 0; j < JM; ++j) mx = fmaxf(mx, sc[j][h]);
+            if (mx == NEG) continue;   // no position of this warp yet
+            const float corr = expf(m[h] - mx);
+            ls[h] *= corr;
+#pragma unroll
+            for (int e = 0; e < E; ++e) o[h][e] *= corr;
+            m[h] = mx;
+#pragma unroll
+            for (int j = 0; j < JM; ++j) {
+                const int t = warp + 8 * j;
+                if (t < ns) {
+                    const float pj = expf(sc[j][h] - mx);
+                    ls[h] += pj;
+                    float vt[E];
+                    lds_vec<E>(vb + t * hd + lane * E, vt);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) o[h][e] = fmaf(pj, vt[e], o[h][e]);
+                }
+            }
+        }
+        dk_bar();   // the next round's copies overwrite kb / vb
+    }
+    // the warps' partials meet in the staging area: [warp][head][m, l, o[hd]]
+    const int wst = hd + 2;
+#pragma unroll
+    for (int h = 0; h < GM; ++h) {
+        if (h >= G) continue;
+        float* wp = kb + (warp * G + h) * wst;
+        if (lane == 0) {
+            wp[0] = m[h];
+            wp[1] = ls[h];
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) wp[2 + lane * E + e] = o[h][e];
+    }
+    dk_bar();
+    const int stride = hd + 4;
+    #pragma unroll 1
+    for (int idx = tid; idx < G * hd; idx += DK_CT) {
+        const int h = idx / hd, i = idx - h * hd;
+        float M = NEG;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, kb[(w * G + h) * wst]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float* wp = kb + (w * G + h) * wst;
+            if (wp[0] == NEG) continue;
+            const float f = expf(wp[0] - M);
+            L = fmaf(f, wp[1], L);
+            O = fmaf(f, wp[2 + i], O);
+        }
+        float* dst = pbase + ((int64_t)h * nch + c) * stride;
+        __stcg(&dst[4 + i], O);
+        if (i == 0) {
+            __stcg(&dst[0], M);
+            __stcg(&dst[1], L);
+        }
+    }
+}
+
 __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave,
                            unsigned long long* detail) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
@@ -815,123 +971,133 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             stamp(2);
             cp_async_wait_group<0>();
             stamp(3);
-            float acc[DK_PVK] = {};   // outputs tid + DK_CT k of [G][hd] (G * hd <= 1024)
-            #pragma unroll 1
-            for (int r0 = 0; r0 < n; r0 += SUB) {
-                const int ns = min(SUB, n - r0);
-                if (r0 > 0) {
-                    attn_issue_kv(P, l, it, r0, kb, vb);
-                    cp_async_wait_all();
-                }
-                if (r0 > 0 && has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
-                    const int r = pos - p0 - r0;
-                    #pragma unroll 1
-                    for (int i = tid; i < hd; i += DK_CT) {
-                        kb[r * hd + i] = ks[i];
-                        vb[r * hd + i] = vs[i];
-                    }
-                }
-                dk_bar();
-                if (r0 == 0) stamp(9);
-                // scores q.k / sqrt(hd): tpp lanes per (position, head) pair,
-                // each summing every tpp-th float4 of the row, then a shuffle
-                // sum over the pair's lanes.  Every lane runs the same number
-                // of iterations (the shuffles need the whole warp).
-                {
-                    const int npair = G * ns, ppi = DK_CT / tpp;
-                    const int j = tid & (tpp - 1);
-                    #pragma unroll 1
-                    for (int p00 = 0; p00 < npair; p00 += ppi) {
-                        const int pr = p00 + tid / tpp;
-                        const int pc = pr < npair ? pr : npair - 1;
-                        const int tt = (pc * gmagic) >> 16, h = pc - tt * G;   // pc / G, pc % G
-                        const float4* q4 = reinterpret_cast<const float4*>(qs + h * hd);
-                        const float4* k4 = reinterpret_cast<const float4*>(kb + tt * hd);
-                        float s0 = 0.0f, s1 = 0.0f;
-                        #pragma unroll 1
-                        for (int m = j; m < hd4; m += 2 * tpp) {
-                            const float4 a = q4[m], kk = k4[m];
-                            s0 = fmaf(a.x, kk.x, s0);
-                            s0 = fmaf(a.y, kk.y, s0);
-                            s0 = fmaf(a.z, kk.z, s0);
-                            s0 = fmaf(a.w, kk.w, s0);
-                            if (m + tpp < hd4) {
-                                const float4 a1 = q4[m + tpp], k1 = k4[m + tpp];
-                                s1 = fmaf(a1.x, k1.x, s1);
-                                s1 = fmaf(a1.y, k1.y, s1);
-                                s1 = fmaf(a1.z, k1.z, s1);
-                                s1 = fmaf(a1.w, k1.w, s1);
-                            }
-                        }
-                        float sv = s0 + s1;
-                        for (int o = tpp >> 1; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
-                        if (j == 0 && pr < npair) sc[h * SUB + tt] = sv * P.inv_scale;
-                    }
-                }
-                dk_bar();
-                if (r0 == 0) stamp(10);
-                // running softmax: weights of this round relative to the new maximum
+            // warp-level rounds where q and the output of the kv head's
+            // query heads fit 8 to 16 registers per lane; else the CTA-wide rounds
+            if (DK_CW == 8 && hd == 128 && G <= 2) {
+                attn_rounds_warp<4, 2, 4>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
+            } else if (DK_CW == 8 && hd == 64 && G <= 4) {
+                attn_rounds_warp<2, 4, 4>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
+            } else if (DK_CW == 8 && hd == 256 && G <= 2) {
+                attn_rounds_warp<8, 2, 2>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
+            } else {
+                float acc[DK_PVK] = {};   // outputs tid + DK_CT k of [G][hd] (G * hd <= 1024)
                 #pragma unroll 1
-                for (int h = warp; h < G; h += DK_CW) {
-                    float m = -INFINITY;
-                    #pragma unroll 1
-                    for (int tt = lane; tt < ns; tt += 32) m = fmaxf(m, sc[h * SUB + tt]);
-                    m = warp_max(m);
-                    const float mo = st[4 * h], mn = fmaxf(mo, m);
-                    float ls = 0.0f;
-                    #pragma unroll 1
-                    for (int tt = lane; tt < ns; tt += 32) {
-                        const float e = expf(sc[h * SUB + tt] - mn);
-                        sc[h * SUB + tt] = e;
-                        ls += e;
+                for (int r0 = 0; r0 < n; r0 += SUB) {
+                    const int ns = min(SUB, n - r0);
+                    if (r0 > 0) {
+                        attn_issue_kv(P, l, it, r0, kb, vb);
+                        cp_async_wait_all();
                     }
-                    ls = warp_sum(ls);
-                    __syncwarp();
-                    if (lane == 0) {
-                        const float corr = expf(mo - mn);
-                        st[4 * h + 2] = corr;
-                        st[4 * h + 0] = mn;
-                        st[4 * h + 1] = st[4 * h + 1] * corr + ls;
+                    if (r0 > 0 && has_pos && pos - p0 >= r0 && pos - p0 < r0 + ns) {
+                        const int r = pos - p0 - r0;
+                        #pragma unroll 1
+                        for (int i = tid; i < hd; i += DK_CT) {
+                            kb[r * hd + i] = ks[i];
+                            vb[r * hd + i] = vs[i];
+                        }
                     }
+                    dk_bar();
+                    if (r0 == 0) stamp(9);
+                    // scores q.k / sqrt(hd): tpp lanes per (position, head) pair,
+                    // each summing every tpp-th float4 of the row, then a shuffle
+                    // sum over the pair's lanes.  Every lane runs the same number
+                    // of iterations (the shuffles need the whole warp).
+                    {
+                        const int npair = G * ns, ppi = DK_CT / tpp;
+                        const int j = tid & (tpp - 1);
+                        #pragma unroll 1
+                        for (int p00 = 0; p00 < npair; p00 += ppi) {
+                            const int pr = p00 + tid / tpp;
+                            const int pc = pr < npair ? pr : npair - 1;
+                            const int tt = (pc * gmagic) >> 16, h = pc - tt * G;   // pc / G, pc % G
+                            const float4* q4 = reinterpret_cast<const float4*>(qs + h * hd);
+                            const float4* k4 = reinterpret_cast<const float4*>(kb + tt * hd);
+                            float s0 = 0.0f, s1 = 0.0f;
+                            #pragma unroll 1
+                            for (int m = j; m < hd4; m += 2 * tpp) {
+                                const float4 a = q4[m], kk = k4[m];
+                                s0 = fmaf(a.x, kk.x, s0);
+                                s0 = fmaf(a.y, kk.y, s0);
+                                s0 = fmaf(a.z, kk.z, s0);
+                                s0 = fmaf(a.w, kk.w, s0);
+                                if (m + tpp < hd4) {
+                                    const float4 a1 = q4[m + tpp], k1 = k4[m + tpp];
+                                    s1 = fmaf(a1.x, k1.x, s1);
+                                    s1 = fmaf(a1.y, k1.y, s1);
+                                    s1 = fmaf(a1.z, k1.z, s1);
+                                    s1 = fmaf(a1.w, k1.w, s1);
+                                }
+                            }
+                            float sv = s0 + s1;
+                            for (int o = tpp >> 1; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+                            if (j == 0 && pr < npair) sc[h * SUB + tt] = sv * P.inv_scale;
+                        }
+                    }
+                    dk_bar();
+                    if (r0 == 0) stamp(10);
+                    // running softmax: weights of this round relative to the new maximum
+                    #pragma unroll 1
+                    for (int h = warp; h < G; h += DK_CW) {
+                        float m = -INFINITY;
+                        #pragma unroll 1
+                        for (int tt = lane; tt < ns; tt += 32) m = fmaxf(m, sc[h * SUB + tt]);
+                        m = warp_max(m);
+                        const float mo = st[4 * h], mn = fmaxf(mo, m);
+                        float ls = 0.0f;
+                        #pragma unroll 1
+                        for (int tt = lane; tt < ns; tt += 32) {
+                            const float e = expf(sc[h * SUB + tt] - mn);
+                            sc[h * SUB + tt] = e;
+                            ls += e;
+                        }
+                        ls = warp_sum(ls);
+                        __syncwarp();
+                        if (lane == 0) {
+                            const float corr = expf(mo - mn);
+                            st[4 * h + 2] = corr;
+                            st[4 * h + 0] = mn;
+                            st[4 * h + 1] = st[4 * h + 1] * corr + ls;
+                        }
+                    }
+                    dk_bar();
+                    if (r0 == 0) stamp(11);
+    #pragma unroll
+                    for (int k = 0; k < DK_PVK; ++k) {
+                        const int idx = tid + DK_CT * k;
+                        if (idx < G * hd) {
+                            const int h = idx / hd, i = idx % hd;
+                            const float* sh = sc + h * SUB;
+                            const float* vcol = vb + i;
+                            float a0 = acc[k] * st[4 * h + 2], a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                            int tt = 0;
+                            #pragma unroll 1
+                            for (; tt + 4 <= ns; tt += 4) {
+                                a0 = fmaf(sh[tt], vcol[tt * hd], a0);
+                                a1 = fmaf(sh[tt + 1], vcol[(tt + 1) * hd], a1);
+                                a2 = fmaf(sh[tt + 2], vcol[(tt + 2) * hd], a2);
+                                a3 = fmaf(sh[tt + 3], vcol[(tt + 3) * hd], a3);
+                            }
+                            #pragma unroll 1
+                            for (; tt < ns; ++tt) a0 = fmaf(sh[tt], vcol[tt * hd], a0);
+                            acc[k] = (a0 + a1) + (a2 + a3);
+                        }
+                    }
+                    dk_bar();
+                    if (r0 == 0) stamp(12);
                 }
-                dk_bar();
-                if (r0 == 0) stamp(11);
-#pragma unroll
+                stamp(4);
+    #pragma unroll
                 for (int k = 0; k < DK_PVK; ++k) {
                     const int idx = tid + DK_CT * k;
                     if (idx < G * hd) {
                         const int h = idx / hd, i = idx % hd;
-                        const float* sh = sc + h * SUB;
-                        const float* vcol = vb + i;
-                        float a0 = acc[k] * st[4 * h + 2], a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                        int tt = 0;
-                        #pragma unroll 1
-                        for (; tt + 4 <= ns; tt += 4) {
-                            a0 = fmaf(sh[tt], vcol[tt * hd], a0);
-                            a1 = fmaf(sh[tt + 1], vcol[(tt + 1) * hd], a1);
-                            a2 = fmaf(sh[tt + 2], vcol[(tt + 2) * hd], a2);
-                            a3 = fmaf(sh[tt + 3], vcol[(tt + 3) * hd], a3);
-                        }
-                        #pragma unroll 1
-                        for (; tt < ns; ++tt) a0 = fmaf(sh[tt], vcol[tt * hd], a0);
-                        acc[k] = (a0 + a1) + (a2 + a3);
+                        __stcg(&pbase[((int64_t)h * nch + c) * stride + 4 + i], acc[k]);
                     }
                 }
-                dk_bar();
-                if (r0 == 0) stamp(12);
-            }
-            stamp(4);
-#pragma unroll
-            for (int k = 0; k < DK_PVK; ++k) {
-                const int idx = tid + DK_CT * k;
-                if (idx < G * hd) {
-                    const int h = idx / hd, i = idx % hd;
-                    __stcg(&pbase[((int64_t)h * nch + c) * stride + 4 + i], acc[k]);
+                if (tid < G) {
+                    __stcg(&pbase[((int64_t)tid * nch + c) * stride + 0], st[4 * tid + 0]);
+                    __stcg(&pbase[((int64_t)tid * nch + c) * stride + 1], st[4 * tid + 1]);
                 }
-            }
-            if (tid < G) {
-                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 0], st[4 * tid + 0]);
-                __stcg(&pbase[((int64_t)tid * nch + c) * stride + 1], st[4 * tid + 1]);
             }
         }
         // arrival; the last CTA of (b, hk) combines the used chunks in order.
