@@ -16,8 +16,11 @@
 //     then multiplies the staged tiles (int8 MMA, warp w taking block columns
 //     w, w + DK_CW, ... of every tile) and writes its output rows after a
 //     cross-warp sum;
-//   * phases are separated by a grid barrier among the consumer warps
-//     (acquire/release counter in global memory, bounded wait);
+//   * no grid barrier separates the phases: every vector one phase hands to
+//     the next is stored as tagged words (value | launch epoch, one 8-byte
+//     store each) in its own slot per layer, and a reader polls the words it
+//     needs until they carry this launch's epoch, so the wait for the data
+//     is the data load itself (bounded wait);
 //   * attention (QK-norm, RoPE from precomputed tables, KV append, chunked
 //     softmax.V with a last-arriver combine) runs between the QKV and wo
 //     phases on the consumer warps while the producer keeps streaming.
@@ -57,6 +60,128 @@ constexpr int DK_RED_BYTES = DK_CW * DK_GMAX * 16 * 2 * 4;   // cross-warp parti
 
 // Named barrier among the consumer warps.
 __device__ __forceinline__ void dk_bar() { asm volatile("bar.sync 1, %0;" ::"n"(DK_CT) : "memory"); }
+// The same barrier, returning the OR of v over the consumer threads: a wait
+// that gave up in one thread stops the whole CTA at the same phase boundary
+// (a thread leaving alone would strand the others at the next barrier).
+__device__ __forceinline__ bool dk_bar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(DK_CT)
+        : "memory");
+    return r != 0;
+}
+
+// ---- tagged activations ----
+// A word is (epoch << 32) | the float's bits, stored and loaded as one
+// aligned 8-byte access (single-copy atomic), so a reader that sees the
+// epoch also sees the value written with it.  Each (layer, vector) slot is
+// written once per launch, and the epoch changes every launch: a word from
+// an earlier launch never passes for this one's, and no word is overwritten
+// while another CTA may still read it.
+typedef unsigned long long u64;
+
+__shared__ uint32_t s_ep;   // this launch's epoch (never 0: the arena starts zeroed)
+
+// Slot v of layer l; word i of sequence b is at [b * tg_ls + i].
+__device__ __forceinline__ u64* tgp(const DecodeParams& P, int l, int v) {
+    return P.tg + (int64_t)l * DK_MAX_BATCH * P.tg_ls + P.tg_off[v];
+}
+__device__ __forceinline__ u64 tag_word(float v, uint32_t ep) { return ((u64)ep << 32) | __float_as_uint(v); }
+__device__ __forceinline__ bool tag_is(u64 w, uint32_t ep) { return (uint32_t)(w >> 32) == ep; }
+__device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ void st_tag(u64* p, float v, uint32_t ep) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(tag_word(v, ep)));
+}
+// four consecutive words (p 16-byte aligned)
+__device__ __forceinline__ void st_tag4(u64* p, float4 v, uint32_t ep) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(tag_word(v.x, ep)), "l"(tag_word(v.y, ep)));
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p + 2), "l"(tag_word(v.z, ep)),
+                 "l"(tag_word(v.w, ep)));
+}
+__device__ __forceinline__ u64 ld_tag(const u64* p) {
+    u64 a;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(a) : "l"(p));
+    return a;
+}
+// two consecutive words (p 16-byte aligned): each is its own atomic access
+__device__ __forceinline__ void ld_tag2(const u64* p, u64& a, u64& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p));
+}
+
+// A wait for tagged data that gave up: error word and abort flag (the other
+// CTAs' waits see the flag and end too).
+__device__ __noinline__ void tag_fail(const DecodeParams& P) {
+    atomicOr(P.err, BREW_DEVERR_TIMEOUT_FULL);
+    atomicExch(P.abort, 1);
+}
+
+// Polls the word pair at p until both words carry epoch ep.  Bounded: gives
+// up after 2 s, or as soon as the abort flag is raised; false then.
+__device__ __noinline__ bool tag_wait2(const DecodeParams& P, const u64* p, uint32_t ep, u64& a, u64& b) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        ld_tag2(p, a, b);
+        if (tag_is(a, ep) && tag_is(b, ep)) return true;
+        if ((it & 63u) == 0 && (global_ns() - t0 > 2000000000ull || ld_volatile_int(P.abort))) {
+            tag_fail(P);
+            return false;
+        }
+    }
+}
+
+// The same for one word.
+__device__ __noinline__ bool tag_wait1(const DecodeParams& P, const u64* p, uint32_t ep, u64& a) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        a = ld_tag(p);
+        if (tag_is(a, ep)) return true;
+        if ((it & 63u) == 0 && (global_ns() - t0 > 2000000000ull || ld_volatile_int(P.abort))) {
+            tag_fail(P);
+            return false;
+        }
+    }
+}
+
+// Reads this thread's word pairs i = threadIdx.x + DK_CT k (k < 32) of
+// [0, n2), pair i at addr(i) (16-byte aligned), and hands each to
+// use(i, x, y) once both words carry epoch ep.  A sweep walks the pairs
+// still pending in order, four loads in flight; when some are unwritten,
+// the first of them is polled alone and the rest are swept again after it
+// lands (the producers' stores arrive close together).  False when a wait
+// gave up.
+template <class A, class U>
+__device__ __forceinline__ bool tag_pairs(const DecodeParams& P, int n2, uint32_t ep, A addr, U use) {
+    constexpr int W = 4;
+    const int tid = threadIdx.x;
+    const int nk = tid < n2 ? min(32, (n2 - tid + DK_CT - 1) / DK_CT) : 0;   // this thread's pairs
+    uint32_t pend = nk == 32 ? 0xFFFFFFFFu : (1u << nk) - 1u;
+    for (;;) {
+        uint32_t left = 0;
+        #pragma unroll 1
+        for (int k0 = 0; k0 < nk; k0 += W) {
+            if (((pend >> k0) & ((1u << W) - 1u)) == 0u) continue;
+            u64 a[W], b[W];
+#pragma unroll
+            for (int u = 0; u < W; ++u)
+                if ((pend >> (k0 + u)) & 1u) ld_tag2(addr(tid + DK_CT * (k0 + u)), a[u], b[u]);
+#pragma unroll
+            for (int u = 0; u < W; ++u) {
+                if (!((pend >> (k0 + u)) & 1u)) continue;
+                if (tag_is(a[u], ep) && tag_is(b[u], ep)) use(tid + DK_CT * (k0 + u), tag_val(a[u]), tag_val(b[u]));
+                else left |= 1u << (k0 + u);
+            }
+        }
+        if (!left) return true;
+        const int k = __ffs(left) - 1;
+        u64 a, b;
+        if (!tag_wait2(P, addr(tid + DK_CT * k), ep, a, b)) return false;
+        use(tid + DK_CT * k, tag_val(a), tag_val(b));
+        pend = left & (left - 1u);
+        if (!pend) return true;
+    }
+}
 constexpr int DK_STAGE_BYTES = 64 * 544;           // one pipeline stage: 64 Q8_0 block-tiles
 
 // One matvec phase over fragment-packed tiles (packed.cuh): y = W x for the
@@ -65,13 +190,14 @@ struct DPhase {
     const uint8_t* w;        // this layer's packed tiles
     int KB, tiles, rows, epi, ldy, tt, ph;
     bool argmax;
-    float* y;
-    const float* resid;      // STORE: y = resid + (W x + bias)
+    float* y;                // the classifier's logits (plain floats)
+    u64* ty;                 // the other phases' outputs (tagged words, sequence stride tg_ls)
+    const u64* tresid;       // STORE: y = resid + (W x + bias), resid tagged
     const float* bias[3];    // bias of rows [r0[k], r0[k + 1]) is bias[k][row - r0[k]]
     int r0[4];
 };
 
-__device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int ph, float* xcur) {
+__device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int ph) {
     DPhase f = {};
     const int qw = P.n_heads * P.hd, kvd = P.n_kv * P.hd;
     const bool gem = arch_gemma(P.arch);
@@ -83,8 +209,8 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
             f.w = P.pk[PK_QKV] + (int64_t)l * P.pk_lb[PK_QKV];
             f.KB = P.dim / 32;
             f.rows = qw + 2 * kvd;
-            f.y = P.qkv;
-            f.ldy = f.rows;
+            f.ty = tgp(P, l, DK_TG_QKV);
+            f.ldy = P.tg_ls;
             f.bias[0] = P.q_bias ? P.q_bias + (int64_t)l * qw : nullptr;
             f.bias[1] = P.k_bias ? P.k_bias + (int64_t)l * kvd : nullptr;
             f.bias[2] = P.v_bias ? P.v_bias + (int64_t)l * kvd : nullptr;
@@ -98,9 +224,9 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
             f.w = P.pk[PK_O] + (int64_t)l * P.pk_lb[PK_O];
             f.KB = qw / 32;
             f.rows = P.dim;
-            f.y = gem ? P.xb2 : xcur;
-            f.resid = gem ? nullptr : xcur;
-            f.ldy = P.dim;
+            f.ty = tgp(P, l, gem ? DK_TG_XB2O : DK_TG_XMID);
+            f.tresid = gem ? nullptr : tgp(P, l, DK_TG_XIN);
+            f.ldy = P.tg_ls;
             f.tiles = P.dim / 16;
             break;
         case PH_GU:
@@ -108,17 +234,17 @@ __device__ __forceinline__ DPhase make_phase(const DecodeParams& P, int l, int p
             f.KB = P.dim / 32;
             f.rows = P.hidden;
             f.epi = gem ? MV_EPI_GLU_GELU : MV_EPI_GLU_SILU;
-            f.y = P.hb;
-            f.ldy = P.hidden;
+            f.ty = tgp(P, l, DK_TG_HB);
+            f.ldy = P.tg_ls;
             f.tiles = P.hidden / 8;
             break;
         case PH_DOWN:
             f.w = P.pk[PK_DOWN] + (int64_t)l * P.pk_lb[PK_DOWN];
             f.KB = P.hidden / 32;
             f.rows = P.dim;
-            f.y = gem ? P.xb2 : xcur;
-            f.resid = gem ? nullptr : xcur;
-            f.ldy = P.dim;
+            f.ty = gem ? tgp(P, l, DK_TG_XB2D) : tgp(P, l + 1, DK_TG_XIN);
+            f.tresid = gem ? nullptr : tgp(P, l, DK_TG_XMID);
+            f.ldy = P.tg_ls;
             f.tiles = P.dim / 16;
             break;
         default:  // PH_CLS
@@ -162,25 +288,6 @@ __device__ __forceinline__ PGeom pk_geom(const DecodeParams& P, int ph, int ng, 
 }
 
 
-// Grid barrier among the consumer warps of all CTAs.  Bounded: after ~2 s
-// (or when another CTA already gave up) it records a timeout and raises the
-// abort flag instead of waiting forever.
-__device__ bool grid_sync(const DecodeParams& P, unsigned long long target, int* s_ok) {
-    dk_bar();   // the CTA's writes happen before thread 0's release
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(P.bar) : "memory");
-        if (!wait_counter_bounded(&P.bar[0], target, P.abort, 2000000000ull)) {
-            atomicOr(P.err, BREW_DEVERR_TIMEOUT_FULL);
-            atomicExch(P.abort, 1);
-            ok = 0;
-        }
-        *s_ok = ok;
-    }
-    dk_bar();   // ... and the acquire happens before every thread's reads
-    return *s_ok != 0;
-}
-
 // Sum over the consumer threads.
 __device__ __forceinline__ float consumer_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -208,36 +315,31 @@ __device__ __forceinline__ void stage_async(float4* d0, const float4* s0, float4
     }
 }
 
-// This thread's sum of squares over the float4 it staged (i = tid + DK_CT k).
-__device__ __forceinline__ float sumsq4(const float4* v, int n4) {
-    float ss = 0.0f;
-    #pragma unroll 1
-    for (int i = threadIdx.x; i < n4; i += DK_CT) {
-        const float4 a = v[i];
-        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-    }
-    return ss;
-}
-
 // Builds the prep records of one phase's input vector(s) in shared memory.
 //   SRC_EMBED      v = dequant(token row) (* sqrt(dim), Gemma3); written to xout
 //   SRC_PLAIN      v = src
 //   SRC_GEMMA_ADD  v = src + rmsnorm(t, tw)   (Gemma3 post-norm residual); written to xout
-// then records of rmsnorm(v, nw) (nw != null) or of v.  The vector is staged
-// in shared memory (`vec`, K floats) and the norm weight beside it (K more
-// floats).  xout writes are split over the CTAs by block (block j by CTA
-// j % G), so each element has one writer.  `lsum`: the consumer multiplies
-// Q4_0 blocks (needs the limb sums).  `nw_staged` (SRC_PLAIN): this thread
-// already issued the copy of nw into the weight half of `vec` (stage_norm).
-__device__ void prep_phase(const DecodeParams& P, int mode, const float* src, int ld, int K, const float* nw,
-                           const float* t, const float* tw, float* xout, uint8_t* prep, float* vec, float* red,
-                           bool lsum, unsigned long long* t_wave, bool nw_staged = false) {
+// then records of rmsnorm(v, nw) (nw != null) or of v.  src, t and xout are
+// tagged slots (sequence stride tg_ls).  The vector is staged in shared
+// memory (`vec`, K floats) and the norm weight beside it (K more floats).
+// xout writes are split over the CTAs by block (block j by CTA j % G), so
+// each element has one writer.  `lsum`: the consumer multiplies Q4_0 blocks
+// (needs the limb sums).  `nw_staged` (SRC_PLAIN): this thread already
+// issued the copy of nw into the weight half of `vec` (stage_norm).  False
+// when a wait for tagged input gave up.
+__device__ bool prep_phase(const DecodeParams& P, int mode, const u64* src, int K, const float* nw, const u64* t,
+                           const float* tw, u64* xout, uint8_t* prep, float* vec, float* red, bool lsum,
+                           unsigned long long* t_wave, bool nw_staged, uint32_t ep) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int KB = K / 32, K4 = K / 4;
+    const int KB = K / 32, K4 = K / 4, K2 = K / 2;
     const int G = gridDim.x;
+    const int ls = P.tg_ls;
     float4* v4 = reinterpret_cast<float4*>(vec);
+    float2* v2 = reinterpret_cast<float2*>(vec);
     float4* w4 = v4 + K4;
+    const float2* w2 = reinterpret_cast<const float2*>(vec + K);
     const float4* nw4 = reinterpret_cast<const float4*>(nw);
+    bool ok_all = true;
     #pragma unroll 1
     for (int b = 0; b < P.batch; ++b) {
         float ss = 0.0f;
@@ -259,25 +361,40 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
             #pragma unroll 1
             for (int i = threadIdx.x; i < K; i += DK_CT) ss += vec[i] * vec[i];
         } else if (mode == SRC_GEMMA_ADD) {
-            stage_async(v4, reinterpret_cast<const float4*>(t + (int64_t)b * ld), w4,
-                        reinterpret_cast<const float4*>(tw), K4);
+            stage_async(w4, nullptr, w4, reinterpret_cast<const float4*>(tw), K4);
+            const u64* tb = t + (int64_t)b * ls;
+            float tss = 0.0f;
+            ok_all &= tag_pairs(P, K2, ep, [&](int i) { return tb + 2 * i; },
+                                [&](int i, float x, float y) {
+                                    v2[i] = make_float2(x, y);
+                                    tss += x * x + y * y;
+                                });
             cp_async_wait_all();
-            dk_bar();
-            const float tsc = rms_scale(consumer_sum(sumsq4(v4, K4), red), K, P.eps);
-            const float* sb = src + (int64_t)b * ld;
-            #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += DK_CT) vec[i] = __ldcg(&sb[i]) + vec[i] * tsc * vec[K + i];
-            dk_bar();
+            const float tsc = rms_scale(consumer_sum(tss, red), K, P.eps);
+            // each thread combines the pairs it staged itself
+            const u64* sb = src + (int64_t)b * ls;
+            ok_all &= tag_pairs(P, K2, ep, [&](int i) { return sb + 2 * i; },
+                                [&](int i, float x, float y) {
+                                    const float2 tv = v2[i], w = w2[i];
+                                    v2[i] = make_float2(x + tv.x * tsc * w.x, y + tv.y * tsc * w.y);
+                                });
+            dk_bar();   // every thread is done with tw before nw replaces it
             if (nw) stage_async(w4, nullptr, w4, nw4, K4);
             cp_async_wait_all();
             #pragma unroll 1
-            for (int i = threadIdx.x; i < K; i += DK_CT) ss += vec[i] * vec[i];
+            for (int i = threadIdx.x; i < K2; i += DK_CT) {
+                const float2 v = v2[i];
+                ss += v.x * v.x + v.y * v.y;
+            }
         } else {
-            stage_async(v4, reinterpret_cast<const float4*>(src + (int64_t)b * ld), w4,
-                        (nw && !(nw_staged && b == 0)) ? nw4 : nullptr, K4);
+            if (nw && !(nw_staged && b == 0)) stage_async(w4, nullptr, w4, nw4, K4);
+            const u64* sb = src + (int64_t)b * ls;
+            ok_all &= tag_pairs(P, K2, ep, [&](int i) { return sb + 2 * i; },
+                                [&](int i, float x, float y) {
+                                    v2[i] = make_float2(x, y);
+                                    ss += x * x + y * y;
+                                });
             cp_async_wait_all();
-            // each thread reads back only the float4 it copied itself
-            if (nw) ss = sumsq4(v4, K4);
         }
         // one barrier publishes the staged vector and the partial sums
         if (nw) {
@@ -307,8 +424,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
                 ok[u] = j < KB;
                 jj[u] = ok[u] ? j : KB - 1;
                 v[u] = v4[(32 * jj[u] + e) >> 2];
-                if (xout && ok[u] && (j % G) == (int)blockIdx.x)
-                    __stcg(reinterpret_cast<float4*>(xout + (int64_t)b * ld + 32 * j + e), v[u]);
+                if (xout && ok[u] && (j % G) == (int)blockIdx.x) st_tag4(xout + (int64_t)b * ls + 32 * j + e, v[u], ep);
                 if (nw) {
                     const float4 w = w4[(32 * jj[u] + e) >> 2];
                     v[u].x = v[u].x * scale * w.x;
@@ -322,6 +438,7 @@ __device__ void prep_phase(const DecodeParams& P, int mode, const float* src, in
         }
         dk_bar();
     }
+    return ok_all;
 }
 
 struct Ring {
@@ -440,7 +557,7 @@ __device__ __forceinline__ void mv_group(const DecodeParams& P, const PGeom& geo
 template <int TT, int NT>
 __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& ring, RingPos& rp, uint32_t prep_s,
                          float* red, unsigned long long* s_best, bool& aborted, unsigned long long* t_full,
-                         unsigned long long* detail) {
+                         unsigned long long* detail, uint32_t ep) {
     int dch = 0;
     static_assert(NT == 1, "decode batch <= 2: one n8 column tile");
     constexpr int BS = pk_block_bytes(TT);
@@ -474,13 +591,14 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
         // per_tile = (8 or 16) * batch, batch 1 or 2: powers of two
         const int ok = tid >> lg_tile, orem = tid & ((1 << lg_tile) - 1);
         const int orow = batch == 2 ? orem >> 1 : orem, ob = batch == 2 ? (orem & 1) : 0;
-        float pr = 0.0f, pb = 0.0f;
+        float pb = 0.0f;
+        u64 rw = 0;   // the residual's tagged word (checked after the MMA loop)
         if (!glu && ok < ng) {
             const int row = (tg0 + ok) * 16 + orow;
             if (row < f.rows) {
                 for (int k = 0; k < 3; ++k)
                     if (f.bias[k] && row >= f.r0[k] && row < f.r0[k + 1]) pb = __ldg(&f.bias[k][row - f.r0[k]]);
-                if (f.resid) pr = __ldcg(&f.resid[(int64_t)ob * f.ldy + row]);
+                if (f.tresid) rw = ld_tag(&f.tresid[(int64_t)ob * f.ldy + row]);
             }
         }
         switch (ng) {
@@ -503,13 +621,21 @@ __device__ void mv_phase(const DecodeParams& P, const DPhase& f, const Ring& rin
                     bool hb = false;
                     for (int k = 0; k < 3; ++k) hb |= f.bias[k] && row >= f.r0[k] && row < f.r0[k + 1];
                     if (hb) v = v + pb;
-                    if (f.resid) v = pr + v;
-                    f.y[(int64_t)ob * f.ldy + row] = v;
-                    if (f.argmax) atomicMax(&s_best[ob], argmax_key(v, row));
+                    if (f.tresid) {
+                        const u64* rp_ = &f.tresid[(int64_t)ob * f.ldy + row];
+                        if (!tag_is(rw, ep) && !tag_wait1(P, rp_, ep, rw)) aborted = true;
+                        v = tag_val(rw) + v;
+                    }
+                    if (f.argmax) {
+                        f.y[(int64_t)ob * f.ldy + row] = v;
+                        atomicMax(&s_best[ob], argmax_key(v, row));
+                    } else {
+                        st_tag(&f.ty[(int64_t)ob * f.ldy + row], v, ep);
+                    }
                 }
             } else {
                 const int i = (tg0 + ok) * 8 + orow;
-                f.y[(int64_t)ob * f.ldy + i] = act_glu(V(orow), f.epi) * V(orow + 8);
+                st_tag(&f.ty[(int64_t)ob * f.ldy + i], act_glu(V(orow), f.epi) * V(orow + 8), ep);
             }
         }
         dk_bar();
@@ -572,7 +698,7 @@ __device__ void produce_phase(const DecodeParams& P, const DPhase& f, const Ring
 // (its q heads, the new k and v, the head-norm weights, the RoPE row and the
 // K / V rows of the chunk) is fetched with asynchronous global->shared copies
 // issued together, so the item waits for one memory round trip instead of
-// one per dependent load.  Chunks longer than attn_sub(hd) positions are
+// one per dependent load.  Chunks longer than P.attn_sub positions are
 // walked in rounds with a running (online) softmax.  `sm` is the attention
 // area of shared memory (P.attn_floats floats):
 //   K rows [SUB][hd] | V rows [SUB][hd] | q [G][hd] | k [hd] | v [hd] |
@@ -690,7 +816,7 @@ __device__ __forceinline__ void attn_issue_kv(const DecodeParams& P, int l, cons
                                               float* vb) {
     const int hd = P.hd, hd4 = hd / 4, kvd = P.n_kv * hd;
     const int lg4 = 31 - __clz(hd4);   // hd is a power of two
-    const int ns = min(attn_sub(hd), it.n - r0);
+    const int ns = min(P.attn_sub, it.n - r0);
     const float* kc = P.kc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     const float* vc = P.vc + (int64_t)it.b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
     #pragma unroll 1
@@ -732,7 +858,7 @@ template <int E, int GM, int JM>
 __device__ __forceinline__ void attn_rounds_warp(const DecodeParams& P, int l, const AttnItem& it, float* kb, float* vb,
                                  const float* qs, const float* ks, const float* vs, float* pbase, int nch,
                                  unsigned long long* detail) {
-    const int G = P.n_heads / P.n_kv, hd = 32 * E, SUB = attn_sub(hd);
+    const int G = P.n_heads / P.n_kv, hd = 32 * E, SUB = P.attn_sub;   // SUB <= 8 JM
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = it.n, p0 = it.p0, pos = it.pos, c = it.c;
     const bool has_pos = pos >= p0 && pos < p0 + n;
@@ -860,16 +986,18 @@ __device__ __forceinline__ void attn_rounds_warp(const DecodeParams& P, int l, c
     }
 }
 
+
+
 __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned long long* t_wave,
-                           unsigned long long* detail) {
+                           unsigned long long* detail, uint32_t ep, bool& aborted) {
     const int G = P.n_heads / P.n_kv, hd = P.hd, half = hd / 2, hd4 = hd / 4;
-    const int kvd = P.n_kv * hd, qw = P.n_heads * hd, ldq = qw + 2 * kvd;
+    const int kvd = P.n_kv * hd, qw = P.n_heads * hd;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int table = (arch_gemma(P.arch) && !arch_global_layer(P.arch, l)) ? 1 : 0;   // local-layer base
     const bool inter = arch_interleaved(P.arch);
     const bool rope_on = arch_rope_layer(P.arch, l);
     const int nch = P.nchunk;
-    const int SUB = attn_sub(hd);
+    const int SUB = P.attn_sub;
     const int stride = hd + 4;   // partial: m, l, 2 spare, o[hd]
     int tpp = 1;                 // lanes per (position, head) score (power of two <= 8)
     while (tpp < 8 && 2 * tpp * G * SUB <= DK_CT) tpp *= 2;
@@ -899,24 +1027,29 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     #pragma unroll 1
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         AttnItem it;
-        if (!attn_item(P, l, item, it)) {
-            if (tid == 0) atomicOr(P.err, BREW_DEVERR_BAD_INDEX);
+        if (!attn_item(P, l, item, it)) {   // a position outside the context: stop the step
+            if (tid == 0) {
+                atomicOr(P.err, BREW_DEVERR_BAD_INDEX);
+                atomicExch(P.abort, 1);
+            }
+            aborted = true;
             continue;
         }
         const int c = it.c, hk = it.hk, b = it.b, pos = it.pos, used = it.used, p0 = it.p0, n = it.n;
-        float* pbase = P.attn_part + ((int64_t)b * P.n_heads + (int64_t)hk * G) * nch * stride;
+        // partials alternate between two buffers by layer parity: layer l + 2's
+        // items start only after every combine of layer l has produced its
+        // output (their inputs depend on it), so no partial is overwritten
+        // while it is read
+        float* pbase = P.attn_part + (int64_t)(l & 1) * DK_MAX_BATCH * P.n_heads * nch * stride +
+                       ((int64_t)b * P.n_heads + (int64_t)hk * G) * nch * stride;
         float* kc = P.kc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
         float* vc = P.vc + (int64_t)b * P.cache_bstride + (int64_t)l * P.seq_len * kvd;
         if (c < used) {
-            const float* qsrc = P.qkv + (int64_t)b * ldq + (int64_t)hk * G * hd;
-            const float* ksrc = P.qkv + (int64_t)b * ldq + qw + (int64_t)hk * hd;
-            const float* vsrc = ksrc + kvd;
-            #pragma unroll 1
-            for (int i = tid; i < G * hd4; i += DK_CT) cp_async16(qs + 4 * i, qsrc + 4 * i);
+            const u64* qsrc = tgp(P, l, DK_TG_QKV) + (int64_t)b * P.tg_ls + (int64_t)hk * G * hd;
+            const u64* ksrc = tgp(P, l, DK_TG_QKV) + (int64_t)b * P.tg_ls + qw + (int64_t)hk * hd;
+            const u64* vsrc = ksrc + kvd;
             #pragma unroll 1
             for (int i = tid; i < hd4; i += DK_CT) {
-                cp_async16(ks + 4 * i, ksrc + 4 * i);
-                cp_async16(vs + 4 * i, vsrc + 4 * i);
                 if (P.rms_q) {
                     cp_async16(wq + 4 * i, P.rms_q + (int64_t)l * hd + 4 * i);
                     cp_async16(wk + 4 * i, P.rms_k + (int64_t)l * hd + 4 * i);
@@ -930,14 +1063,38 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     cp_async16(sn + 4 * i, P.rope_sin + ro + 4 * i);
                 }
             }
-            cp_async_commit();                 // group: q, k, v, norm weights, RoPE row
+            cp_async_commit();                 // group: norm weights, RoPE row
             attn_issue_kv(P, l, it, 0, kb, vb);
             cp_async_commit();                 // group: the first round's cached K / V rows
             if (tid < G) {
                 st[4 * tid + 0] = -INFINITY;
                 st[4 * tid + 1] = 0.0f;
             }
-            cp_async_wait_group<1>();          // q / k / v landed; the K / V rows may still be in flight
+            // this step's q heads, k and v (tagged words, written by the Q|K|V
+            // phase): pairs [0, G hd / 2) of q, then hd / 2 of k and of v, into
+            // qs | ks | vs (contiguous)
+            {
+                const int nq2 = G * hd / 2, h2 = hd / 2, np = nq2 + 2 * h2;
+                auto pair = [&](int i) {
+                    return i < nq2 ? qsrc + 2 * i : i < nq2 + h2 ? ksrc + 2 * (i - nq2) : vsrc + 2 * (i - nq2 - h2);
+                };
+                #pragma unroll 1
+                for (int i0 = tid; i0 < np; i0 += 2 * DK_CT) {   // two pairs in flight per thread
+                    const int i1 = i0 + DK_CT;
+                    u64 a0, b0, a1 = 0, b1 = 0;
+                    ld_tag2(pair(i0), a0, b0);
+                    if (i1 < np) ld_tag2(pair(i1), a1, b1);
+                    if (!(tag_is(a0, ep) && tag_is(b0, ep)) && !tag_wait2(P, pair(i0), ep, a0, b0)) aborted = true;
+                    qs[2 * i0] = tag_val(a0);
+                    qs[2 * i0 + 1] = tag_val(b0);
+                    if (i1 < np) {
+                        if (!(tag_is(a1, ep) && tag_is(b1, ep)) && !tag_wait2(P, pair(i1), ep, a1, b1)) aborted = true;
+                        qs[2 * i1] = tag_val(a1);
+                        qs[2 * i1 + 1] = tag_val(b1);
+                    }
+                }
+            }
+            cp_async_wait_group<1>();          // weights / RoPE landed; the K / V rows may still be in flight
             dk_bar();
             if (t_wave) *t_wave = global_ns();
             stamp(1);
@@ -974,9 +1131,9 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
             // warp-level rounds where q and the output of the kv head's
             // query heads fit 8 to 16 registers per lane; else the CTA-wide rounds
             if (DK_CW == 8 && hd == 128 && G <= 2) {
-                attn_rounds_warp<4, 2, 4>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
+                attn_rounds_warp<4, 2, 6>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
             } else if (DK_CW == 8 && hd == 64 && G <= 4) {
-                attn_rounds_warp<2, 4, 4>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
+                attn_rounds_warp<2, 4, 6>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
             } else if (DK_CW == 8 && hd == 256 && G <= 2) {
                 attn_rounds_warp<8, 2, 2>(P, l, it, kb, vb, qs, ks, vs, pbase, nch, detail);
             } else {
@@ -1104,7 +1261,7 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
         // The barrier orders every thread's partial stores before thread 0's
         // release, which makes them visible before its arrival is counted.
         dk_bar();
-        int* ctr = &P.attn_ctr[b * P.n_kv + hk];
+        int* ctr = &P.attn_ctr[(l * DK_MAX_BATCH + b) * P.n_kv + hk];   // one per layer: reset by its combine
         if (tid == 0) {
             // release: the CTA's partials before the count; acquire: the
             // other CTAs' partials before the combine reads them
@@ -1151,7 +1308,8 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     float o = 0.0f;
                     #pragma unroll 1
                     for (int k = 0; k < used; ++k) o += ph[k * stride + 2] * ph[k * stride + 4 + i];
-                    P.xb[(int64_t)b * qw + (int64_t)(hk * G + h0 + hl) * hd + i] = o * ph[3];
+                    st_tag(tgp(P, l, DK_TG_XB) + (int64_t)b * P.tg_ls + (int64_t)(hk * G + h0 + hl) * hd + i, o * ph[3],
+                           ep);
                 }
                 dk_bar();
             }
@@ -1174,8 +1332,7 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
     ring.ns = NS;
     ring.stage_bytes = P.stage_bytes;
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(smem + 512);   // [16]
-    __shared__ unsigned long long s_base;
-    __shared__ int s_ok;
+    __shared__ int s_last;
     float* s_red = reinterpret_cast<float*>(smem + 640);                               // [32]
     float* red = reinterpret_cast<float*>(smem + 768);                                 // [DK_CW][DK_GMAX][16][2]
     float* vec = reinterpret_cast<float*>(smem + 768 + DK_RED_BYTES);
@@ -1193,7 +1350,9 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
             mbar_init(&ring.empty[s], DK_CW);
         }
         fence_mbar_init();
-        s_base = P.bar[1];
+        // this launch's epoch: one past the last completed launch's, never 0
+        const uint32_t e = *P.seq + 1u;
+        s_ep = e ? e : 1u;
     }
     if (tid < 16) s_best[tid] = 0ull;
     if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
@@ -1227,7 +1386,7 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
             const bool cls = s == 5 * L;
             if (ph == 1) continue;
             const int mph = cls ? PH_CLS : ph == 0 ? PH_QKV : ph == 2 ? PH_O : ph == 3 ? PH_GU : PH_DOWN;
-            const DPhase f = make_phase(P, l, mph, P.x0);
+            const DPhase f = make_phase(P, l, mph);
             unsigned long long* d = (l == P.detail_l && mph == P.detail_ph) ? dtr : nullptr;
             if constexpr (TYPE == CTYPE) {
                 produce_phase<TYPE>(P, f, ring, rp, d);
@@ -1242,42 +1401,34 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
     }
 
     // --------------------------------- consumers ---------------------------------
-    const int Gc = gridDim.x;
-    unsigned long long target = s_base;
+    const uint32_t ep = s_ep;
     RingPos rp;
     bool aborted = false;
     const bool gem = arch_gemma(P.arch);
     constexpr bool lsum_l = TYPE == BREW_TYPE_Q4_0, lsum_c = CTYPE == BREW_TYPE_Q4_0;
-    float* xcur = P.x0;
-    float* xalt = P.x1;
-    // trace: per CTA, slot 0 = start, then per phase (load wave landed, prep done, last weight stage in, work done,
-    // barrier passed)
-    int nev = 0;
-    unsigned long long* tr = P.trace ? P.trace + (size_t)blockIdx.x * P.trace_slots : nullptr;
-    auto mark = [&]() {
-        if (tr && tid == 0 && nev < P.trace_slots) tr[nev] = global_ns();
-        ++nev;
+    // trace (P.trace set): per CTA, slot 0 = start, then slots 1 + 5 s + k of
+    // step s: k = 0 load wave landed, 1 prep done, 2 last weight stage in,
+    // 3 work done, 4 phase end.  The wave / weight stamps pass through shared
+    // memory, and every address is formed from P when it is used: tracing
+    // holds no registers across the step loop.
+    __shared__ unsigned long long s_tw[2];   // [0] wave landed, [1] last weight stage in
+    auto stamp = [&](int st, int k, unsigned long long v) {
+        if (P.trace && tid == 0) P.trace[(size_t)blockIdx.x * P.trace_slots + 1 + 5 * st + k] = v;
     };
-    unsigned long long tfull = 0;
-    unsigned long long twave = 0;
-    auto markv = [&](unsigned long long v) {
-        if (tr && tid == 0 && nev < P.trace_slots) tr[nev] = v;
-        ++nev;
-        tfull = 0;
+    auto det = [&](int l, int ph) {
+        return (P.trace && l == P.detail_l && ph == P.detail_ph)
+                   ? P.trace + (size_t)blockIdx.x * P.trace_slots + P.trace_slots - 3 * DK_DETAIL
+                   : nullptr;
     };
-    auto mark_prep = [&]() {   // the prep's load wave landed, then the prep is done
-        markv(twave);
-        twave = 0;
-        mark();
-    };
-    unsigned long long* dtr = tr ? tr + P.trace_slots - 3 * DK_DETAIL : nullptr;
-    auto det = [&](int l, int ph) { return (dtr && l == P.detail_l && ph == P.detail_ph) ? dtr : nullptr; };
-    mark();
-    auto barrier = [&]() {
-        mark();
-        target += (unsigned long long)Gc;
-        if (!grid_sync(P, target, &s_ok)) aborted = true;
-        mark();
+    if (P.trace && tid == 0) {
+        P.trace[(size_t)blockIdx.x * P.trace_slots] = global_ns();
+        s_tw[0] = s_tw[1] = 0ull;
+    }
+    // the end of a phase: a wait that gave up in any consumer thread stops the CTA
+    auto phase_end = [&](int st) {
+        stamp(st, 3, global_ns());
+        aborted = dk_bar_or(aborted);
+        stamp(st, 4, global_ns());
     };
     // The next phase's RMSNorm weight is copied into shared memory, beside
     // the input vector where prep_phase reads it, while this phase
@@ -1291,7 +1442,8 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
     // One step per phase: s = 5 l + p, p = 0 Q|K|V, 1 attention, 2 wo,
     // 3 gate|up, 4 down; s = 5 L is the classifier.  Every phase function
     // has one call site (the kernel's code stays small: its instruction
-    // fetches compete with the weight stream for L2).
+    // fetches compete with the weight stream for L2).  A phase waits only for
+    // its own inputs (tagged words), never for the whole grid.
     const int nsteps = 5 * L + 1;
     for (int s = 0; s < nsteps && !aborted; ++s) {
         const int l = s / 5, ph = s - 5 * l;
@@ -1303,89 +1455,117 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
             if (P.rms_k) prefetch_l2(P.rms_k + (int64_t)l * P.hd, (uint32_t)P.hd * 4u);
         }
         if (ph == 1) {
-            attn_phase(P, l, vec, tr ? &twave : nullptr, det(l, PH_ATTN));
-            markv(twave);   // the first load wave landed
-            twave = 0;
-            markv(0);
-            markv(0);
-            barrier();
+            cp_async_wait_all();   // no staged norm weight may land in the attention area
+            attn_phase(P, l, vec, P.trace ? &s_tw[0] : nullptr, det(l, PH_ATTN), ep, aborted);
+            if (P.trace && tid == 0) {
+                stamp(s, 0, s_tw[0]);   // the first load wave landed
+                s_tw[0] = 0ull;
+            }
+            phase_end(s);
             continue;
         }
         // the phase's input vector -> prep records in shared memory
-        int mode = SRC_PLAIN, ld = P.dim, K = P.dim, mph;
-        const float* src = xcur;
-        const float *nw = nullptr, *t = nullptr, *tw = nullptr, *next_norm = nullptr;
-        float* xout = nullptr;
-        bool staged = false, swap = false;
+        //   non-Gemma: XIN(l) -> Q|K|V; XB -> wo (+ XIN) -> XMID -> gate|up ->
+        //   HB -> down (+ XMID) -> XIN(l + 1)
+        //   Gemma3:    XIN(l) = XMID(l - 1) + norm(XB2D(l - 1)) (QKV prep);
+        //   wo -> XB2O; XMID(l) = XIN(l) + norm(XB2O) (gate|up prep); down -> XB2D
+        int mode = SRC_PLAIN, K = P.dim, mph;
+        const u64 *src = nullptr, *t = nullptr;
+        const float *nw = nullptr, *tw = nullptr, *next_norm = nullptr;
+        u64* xout = nullptr;
+        bool staged = false;
         if (ph == 0) {   // RMSNorm + Q|K|V, or the final RMSNorm + classifier
             mph = cls ? PH_CLS : PH_QKV;
             nw = cls ? P.rms_final : P.rms_att + (int64_t)l * P.dim;
             if (l == 0) {
                 mode = SRC_EMBED;
-                xout = xcur;
+                xout = tgp(P, 0, DK_TG_XIN);
             } else if (gem) {   // the previous layer's post-FFN norm + residual
                 mode = SRC_GEMMA_ADD;
-                t = P.xb2;
+                src = tgp(P, l - 1, DK_TG_XMID);
+                t = tgp(P, l - 1, DK_TG_XB2D);
                 tw = P.post_ffn + (int64_t)(l - 1) * P.dim;
-                xout = cls ? nullptr : xalt;
-                swap = !cls;
+                xout = cls ? nullptr : tgp(P, l, DK_TG_XIN);
             } else {
+                src = tgp(P, l, DK_TG_XIN);
                 staged = true;
             }
         } else if (ph == 2) {   // wo (+ residual)
             mph = PH_O;
-            src = P.xb;
-            ld = K = P.n_heads * P.hd;
+            src = tgp(P, l, DK_TG_XB);
+            K = P.n_heads * P.hd;
             next_norm = P.rms_ffn + (int64_t)l * P.dim;
         } else if (ph == 3) {   // RMSNorm (FFN) + gate|up
             mph = PH_GU;
             nw = P.rms_ffn + (int64_t)l * P.dim;
             if (gem) {   // post-attention norm + residual
                 mode = SRC_GEMMA_ADD;
-                t = P.xb2;
+                src = tgp(P, l, DK_TG_XIN);
+                t = tgp(P, l, DK_TG_XB2O);
                 tw = P.post_att + (int64_t)l * P.dim;
-                xout = xalt;
-                swap = true;
+                xout = tgp(P, l, DK_TG_XMID);
             } else {
+                src = tgp(P, l, DK_TG_XMID);
                 staged = true;
             }
         } else {   // down (+ residual)
             mph = PH_DOWN;
-            src = P.hb;
-            ld = K = P.hidden;
+            src = tgp(P, l, DK_TG_HB);
+            K = P.hidden;
             next_norm = l + 1 < L ? P.rms_att + (int64_t)(l + 1) * P.dim : P.rms_final;
         }
-        prep_phase(P, mode, src, ld, K, nw, t, tw, xout, prep, vec, s_red, cls ? lsum_c : lsum_l,
-                   tr ? &twave : nullptr, staged);
-        if (swap) {
-            float* tmp = xcur;
-            xcur = xalt;
-            xalt = tmp;
-        }
+        // a CTA without tiles in this phase needs no input (unless it owns
+        // blocks of the residual the prep writes)
+        const bool need = s_tiles[mph][1] > s_tiles[mph][0] || (xout && (int)blockIdx.x < K / 32);
+        if (need && !prep_phase(P, mode, src, K, nw, t, tw, xout, prep, vec, s_red, cls ? lsum_c : lsum_l,
+                                P.trace ? &s_tw[0] : nullptr, staged, ep))
+            aborted = true;
         if (next_norm) stage_norm(next_norm);
-        mark_prep();
-        const DPhase f = make_phase(P, l, mph, xcur);
+        if (P.trace && tid == 0) {   // the prep's load wave landed, then the prep is done
+            stamp(s, 0, s_tw[0]);
+            stamp(s, 1, global_ns());
+            s_tw[0] = 0ull;
+        }
+        const DPhase f = make_phase(P, l, mph);
         if constexpr (TYPE == CTYPE) {
-            mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+            mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, P.trace ? &s_tw[1] : nullptr, det(l, mph), ep);
         } else {
             if (cls)
-                mv_phase<CTYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+                mv_phase<CTYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, P.trace ? &s_tw[1] : nullptr, det(l, mph),
+                                    ep);
             else
-                mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, tr ? &tfull : nullptr, det(l, mph));
+                mv_phase<TYPE, NT>(P, f, ring, rp, prep_s, red, s_best, aborted, P.trace ? &s_tw[1] : nullptr, det(l, mph),
+                                   ep);
         }
-        markv(tfull);
+        if (P.trace && tid == 0) {
+            stamp(s, 2, s_tw[1]);
+            s_tw[1] = 0ull;
+        }
         if (cls) {
             dk_bar();
             if (tid < P.batch) atomicMax(&P.am_key[tid], s_best[tid]);
         }
-        barrier();
+        phase_end(s);
     }
-    if (!aborted && blockIdx.x == 0) {
+    if (aborted) return;
+    // the last CTA to finish writes the argmax and opens the next epoch; the
+    // barrier orders the CTA's argmax updates before thread 0's release
+    dk_bar();
+    if (tid == 0) {
+        int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(P.done) : "memory");
+        s_last = prev == (int)gridDim.x - 1;
+    }
+    dk_bar();
+    if (s_last) {
         if (tid < P.batch) {
             const unsigned long long k = atomicExch(&P.am_key[tid], 0ull);
             P.am_out[tid] = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         }
-        if (tid == 0) P.bar[1] = target;   // arrival count at the start of the next step
+        if (tid == 0) {
+            *P.done = 0;
+            *P.seq = ep;
+        }
     }
 }
 
@@ -1451,6 +1631,8 @@ bool decode_supported(const brew_config& c, int batch) {
     if ((c.n_heads / c.n_kv_heads) * c.head_size > 1024 || c.head_size % 8) return false;
     // 64, 128 or 256: shift-based indexing, two to eight registers per lane in norm_rope_warp
     if (c.head_size != 64 && c.head_size != 128 && c.head_size != 256) return false;
+    // a prep's tagged input: at most 32 word pairs per consumer thread
+    if (std::max(std::max(c.dim, qw), c.hidden_dim) > 64 * DK_CT) return false;
     return true;
 }
 
@@ -1480,6 +1662,14 @@ int decode_prepare(DecodeParams* p) {
     const size_t attn_need = attn_fl * 4 > (size_t)p->vec_bytes ? attn_fl * 4 - p->vec_bytes : 0;
     p->prep_bytes = (int)((std::max(prep_need, attn_need) + 127) & ~size_t(127));
     p->attn_floats = (p->vec_bytes + p->prep_bytes) / 4;
+    // widen the K / V staging to what the area holds (one round per chunk
+    // of up to attn_sub_max positions)
+    {
+        const size_t fixed_fl = (size_t)G * p->hd + 5 * (size_t)p->hd + 4 * (size_t)G + 64;
+        const size_t fit = ((size_t)p->attn_floats - fixed_fl) / (2 * (size_t)p->hd + G);
+        p->attn_sub = std::max(SUB, (int)std::min<size_t>(fit, (size_t)attn_sub_max(p->hd)));
+    }
+
     p->stage_bytes = DK_STAGE_BYTES;
     const size_t fixed = 768 + (size_t)DK_RED_BYTES + 128 + p->vec_bytes + p->prep_bytes + 128;
     const size_t budget = DK_SMEM_BUDGET;

@@ -16,8 +16,30 @@ enum { PK_QKV = 0, PK_O, PK_GU, PK_DOWN, PK_OUT, PK_NFAM };
 constexpr int DK_MAX_BATCH = 2;
 constexpr int DK_DETAIL = 32;   // chunks of the detailed phase traced
 
-// K / V positions an attention item stages in shared memory per round.
+// The vectors one layer's phases hand to each other (tagged words): the
+// layer's input residual, Q|K|V, the attention output, the residual after
+// attention, the gated FFN activation, and Gemma's wo / down outputs before
+// their post-norms.  XIN of layer n_layers is the classifier's input.
+enum { DK_TG_XIN = 0, DK_TG_QKV, DK_TG_XB, DK_TG_XMID, DK_TG_HB, DK_TG_XB2O, DK_TG_XB2D, DK_TG_N };
+
+// Word offsets of the tagged vectors in a layer's sequence row; returns the
+// row length (every vector starts on a 4-word boundary).
+inline int dk_tagged_layout(int dim, int qkvw, int qw, int hidden, int* off) {
+    const int len[DK_TG_N] = {dim, qkvw, qw, dim, hidden, dim, dim};
+    int o = 0;
+    for (int v = 0; v < DK_TG_N; ++v) {
+        off[v] = o;
+        o += (len[v] + 3) & ~3;
+    }
+    return o;
+}
+
+// K / V positions an attention item stages in shared memory per round, at
+// least (decode_prepare widens it to what the attention area holds).
 __host__ __device__ inline int attn_sub(int hd) { return hd <= 128 ? 32 : 16; }
+// ... and at most: the warp-level rounds give each of the 8 consumer warps
+// this many positions / 8 of a round.
+__host__ __device__ inline int attn_sub_max(int hd) { return hd <= 128 ? 48 : 16; }
 
 struct alignas(64) DecodeParams {
     const uint8_t* pk[PK_NFAM];         // packed weights
@@ -35,19 +57,26 @@ struct alignas(64) DecodeParams {
     float *kc, *vc;
     int64_t cache_bstride;
     const float *rope_cos, *rope_sin;   // [2][seq_len][hd/2]: 0 = global/default base, 1 = Gemma3 local
-    float *x0, *x1;                     // residual stream (Gemma3 alternates between the two)
-    float *xb, *xb2, *qkv, *hb, *logits;
-    float* attn_part;                   // [batch][n_heads][nchunk][hd + 4]: m, l, -, -, o[hd]
-    int* attn_ctr;
+    // Tagged activations: [n_layers + 1][DK_MAX_BATCH][tg_ls] words, each
+    // (epoch << 32) | float bits; vector v of layer l starts at word
+    // tg_off[v] of the layer's sequence row (dk_tagged_layout)
+    unsigned long long* tg;
+    int tg_ls;
+    int tg_off[DK_TG_N];
+    float* logits;
+    float* attn_part;                   // [2 (layer parity)][DK_MAX_BATCH][n_heads][nchunk][hd + 4]: m, l, -, -, o[hd]
+    int* attn_ctr;                      // [n_layers][DK_MAX_BATCH][n_kv] arrival counters
     int nchunk, attn_floats;            // attn_floats: shared-memory floats of the attention area
+    int attn_sub;                       // K / V positions staged per round
     unsigned long long* am_key;
     int32_t* am_out;
     const int32_t *tokens, *pos;
-    unsigned long long* bar;            // [0] arrival counter, [1] its value at step start
+    unsigned int* seq;                  // epoch of the last completed launch
+    int* done;                          // CTAs done with this launch (the last one finishes the step)
     int* abort;
     unsigned int* err;
     unsigned long long* trace;          // optional [grid][trace_slots]: %globaltimer per CTA
-    int trace_slots;                    // 1 + 5 per phase (load wave landed, prep done, last weight stage in, work done, barrier passed)
+    int trace_slots;                    // 1 + 5 per phase (load wave landed, prep done, last weight stage in, work done, phase end)
     int detail_l, detail_ph;            // optional per-chunk trace of one (layer, phase): 3 x DK_DETAIL more slots
     // launch geometry
     int nstages, stage_bytes, vec_bytes, prep_bytes, rec_bytes, grid;

@@ -88,7 +88,13 @@ struct brew_model_s {
     // persistent decode kernel (batch <= DK_MAX_BATCH)
     bool use_decode = false;
     DecodeParams dp;
-    float *x1 = nullptr, *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
+    int* dk_actr = nullptr;                 // its attention arrival counters [layers][DK_MAX_BATCH][kv heads]
+    size_t dk_nactr = 0;
+    unsigned long long* dk_tg = nullptr;    // its tagged activations
+    size_t dk_tg_words = 0;
+    unsigned int* dk_seq = nullptr;         // epoch of its last completed launch
+    int* dk_done = nullptr;                 // its end-of-step arrival counter
     uint8_t* pk[PK_NFAM] = {};              // fragment-packed weight copies of the decode kernel
     // unfused forward (models with K-quant matrices)
     bool unfused = false;
@@ -114,7 +120,6 @@ struct brew_model_s {
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
     unsigned long long *tp_keys = nullptr, *tp_keys_all = nullptr;
-    unsigned long long* bar = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
     int trace_n = 0;
@@ -1125,11 +1130,11 @@ int setup_decode(brew_model_s* m) {
     const int B = std::min(m->max_batch, DK_MAX_BATCH);
     const int hd = c.head_size, half = hd / 2;
     int rc;
-    if ((rc = dalloc(m, &m->x1, (size_t)B * c.dim))) return rc;
     if ((rc = dalloc(m, &m->rope_cos, (size_t)2 * c.seq_len * half))) return rc;
     if ((rc = dalloc(m, &m->rope_sin, (size_t)2 * c.seq_len * half))) return rc;
-    if ((rc = dalloc(m, &m->bar, 2))) return rc;
     if ((rc = dalloc(m, &m->abort_flag, 1))) return rc;
+    if ((rc = dalloc(m, &m->dk_seq, 1))) return rc;
+    if ((rc = dalloc(m, &m->dk_done, 1))) return rc;
     const float base0 = arch_rope_base(c.arch, c.rope_base, false);   // global / only table
     const float base1 = arch_rope_base(c.arch, c.rope_base, true);    // Gemma local layers
     const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
@@ -1168,22 +1173,26 @@ int setup_decode(brew_model_s* m) {
     p.cache_bstride = m->cache_bstride;
     p.rope_cos = m->rope_cos;
     p.rope_sin = m->rope_sin;
-    p.x0 = m->x;
-    p.x1 = m->x1;
-    p.xb = m->xb;
-    p.xb2 = m->xb2;
-    p.qkv = m->qkv;
-    p.hb = m->hb;
+    {   // tagged activations: every layer's vectors, plus the classifier's input
+        const int qw = c.n_heads * hd, qkvw = qw + 2 * c.n_kv_heads * hd;
+        p.tg_ls = dk_tagged_layout(c.dim, qkvw, qw, c.hidden_dim, p.tg_off);
+        m->dk_tg_words = (size_t)(c.n_layers + 1) * DK_MAX_BATCH * p.tg_ls;
+        if ((rc = dalloc(m, &m->dk_tg, m->dk_tg_words))) return rc;
+        p.tg = m->dk_tg;
+    }
     p.logits = m->logits;
     p.nchunk = std::max(1, std::min(64, num_sms() / (B * c.n_kv_heads)));
-    if ((rc = dalloc(m, &m->dk_part, (size_t)B * c.n_heads * p.nchunk * (hd + 4)))) return rc;
+    if ((rc = dalloc(m, &m->dk_part, (size_t)2 * DK_MAX_BATCH * c.n_heads * p.nchunk * (hd + 4)))) return rc;
     p.attn_part = m->dk_part;
-    p.attn_ctr = m->counters + c.hidden_dim / 32 + 8;
+    m->dk_nactr = (size_t)c.n_layers * DK_MAX_BATCH * c.n_kv_heads;
+    if ((rc = dalloc(m, &m->dk_actr, m->dk_nactr))) return rc;
+    p.attn_ctr = m->dk_actr;
     p.am_key = m->am_key;
     p.am_out = m->am_out;
     p.tokens = m->tokens_d;
     p.pos = m->pos_d;
-    p.bar = m->bar;
+    p.seq = m->dk_seq;
+    p.done = m->dk_done;
     p.abort = m->abort_flag;
     p.err = ctx().err_word;
     p.trace_slots = 1 + 5 * (5 * c.n_layers + 1) + 3 * DK_DETAIL;
@@ -1221,8 +1230,9 @@ int setup_decode(brew_model_s* m) {
 // decode kernel when available, else the captured kernel graph.
 int launch_forward(brew_model_s* m, int B, bool with_classifier, cudaStream_t s);
 
-// After a device-side error the decode kernel's barrier words may be
-// inconsistent: clear them (and the abort flag) so the next step starts clean.
+// After a device-side error the decode kernel's counters may be left raised
+// and its tagged words half written with an epoch the next launch reuses:
+// clear them (and the abort flag) so the next step starts clean.
 int after_step_check(brew_model_s* m, const char* where) {
     const int rc = check_device_error(where);
     if (rc && m->kq_ctr) {   // a K-quant matvec that stopped early may leave split counters raised
@@ -1230,7 +1240,9 @@ int after_step_check(brew_model_s* m, const char* where) {
         cudaDeviceSynchronize();
     }
     if (rc && m->use_decode) {
-        cudaMemset(m->bar, 0, 2 * sizeof(unsigned long long));
+        cudaMemset(m->dk_done, 0, sizeof(int));
+        cudaMemset(m->dk_actr, 0, m->dk_nactr * sizeof(int));
+        cudaMemset(m->dk_tg, 0, m->dk_tg_words * sizeof(unsigned long long));
         cudaMemset(m->abort_flag, 0, sizeof(int));
         cudaMemset(m->am_key, 0, (size_t)m->max_batch * sizeof(unsigned long long));
         cudaMemset(m->am_ctr, 0, (size_t)m->max_batch * sizeof(int));

@@ -125,3 +125,40 @@ def test_generate_errors_and_limits(device):
     dm2 = DeviceModel.synthesize(cfg.replace(eos_token=eos), 3)
     assert dm2.generate([5, 6], 6) == full[: full.index(eos) + 1]
     dm2.close()
+
+
+@pytest.mark.parametrize("arch,dims,plen", [
+    # head 128, 8 kv heads: 18 chunks per kv head, 56 positions each at
+    # position 1000 (two rounds of staged K / V rows)
+    (C.ARCH_QWEN3, {}, 1000),
+    # head 64, 4 kv heads: 37 chunks, 49 positions each at position 1800
+    (C.ARCH_LLAMA, dict(dim=1024, hidden_dim=2048, n_heads=16, n_kv_heads=4, head_size=64), 1800),
+])
+def test_long_context_attention_rounds(device, arch, dims, plen):
+    """A prompt long enough that every attention chunk of the decode kernel
+    takes more than one round of staged positions: the next position's
+    logits and 16 greedy tokens against the oracle (prefill batched on the
+    device, token by token on the oracle)."""
+    from brewference_b200.api import PREFILL_BATCHED
+    cfg = small(arch, seq_len=2048, **dims)
+    seed = 99
+    prompt = np.random.default_rng(seed).integers(0, cfg.vocab_size, plen).astype(np.int32)
+    om = oracle.OracleModel(cfg, seed)
+    om.reset()
+    for i, t in enumerate(prompt):
+        om.forward(int(t), i)
+    pending, pos, want, ref = int(prompt[-1]), plen, [], None
+    for _ in range(16):
+        lg = om.forward(pending, pos)
+        if ref is None:
+            ref = lg.copy()
+        pending, pos = oracle.argmax(lg), pos + 1
+        want.append(pending)
+    om.close()
+    dm = DeviceModel.synthesize(cfg, seed)
+    dm.set_prefill(PREFILL_BATCHED)
+    dm.prefill(prompt)
+    lg, _ = dm.forward([int(prompt[-1])], [plen])
+    assert rel(lg[0], ref) < LOGIT_TOL, rel(lg[0], ref)
+    assert dm.generate(prompt, 16) == want
+    dm.close()
