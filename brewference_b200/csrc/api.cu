@@ -338,7 +338,12 @@ int launch_prepared(brew_tensor t, const uint8_t* w, int64_t row_bytes, const ui
     p.prep = prep;
     p.post = MV_POST_NONE;
     p.err = g_ctx.err_word;
-    return mv_launch(p, stream, false);
+    // programmatic dependent launch: the kernel streams its weight tiles
+    // before griddepcontrol.wait and reads x / writes y only after it, so
+    // back-to-back calls on one stream overlap one call's weight fetch with
+    // the previous call's tail (a preceding kernel that does not trigger
+    // early still completes first)
+    return mv_launch(p, stream, true);
 }
 
 int run_matvec_prepared(brew_tensor t, int64_t weights_offset, const uint8_t* prep, int K, int N, float* y, int batch,
