@@ -1623,8 +1623,8 @@ bool decode_supported(const brew_config& c, int batch) {
         if (t != c.type_q || (t != BREW_TYPE_Q8_0 && t != BREW_TYPE_Q4_0)) return false;
     const int tout = c.tied_embeddings ? c.type_embed : c.type_output;
     if (tout != BREW_TYPE_Q8_0 && tout != BREW_TYPE_Q4_0) return false;
-    // TMA boxes of 8 blocks over 16-byte row pitches: K multiple of 256
-    if (c.dim % 256 || qw % 256 || c.hidden_dim % 256) return false;
+    // whole 32-element blocks (a stage holds a divisor of a row's block count)
+    if (c.dim % 32 || qw % 32 || c.hidden_dim % 32) return false;
     if ((c.n_kv_heads * c.head_size) % 16) return false;
     // attention: a CTA holds the G * hd outputs of a kv head's queries in
     // four registers per thread; 16-byte copies of half rows
@@ -1684,7 +1684,6 @@ int decode_prepare(DecodeParams* p) {
     for (int ph = 0; ph < 5; ++ph) {
         const int KB = phase_kb[ph];
         const int bs = pk_block_bytes(ph == PH_CLS ? p->type_out : p->type_layer);
-        BREW_CHECK(KB % 8 == 0, BREW_ERR_UNSUPPORTED, "decode kernel: %d block columns", KB);
         int kc[9] = {0};
         for (int ng = 1; ng <= 8; ++ng) {
             const int cap = std::min(KB, p->stage_bytes / (ng * bs));
@@ -1698,6 +1697,11 @@ int decode_prepare(DecodeParams* p) {
                     found = true;
                 }
             for (int c = (cap / 8) * 8; c >= 8 && !found; c -= 8)
+                if (KB % c == 0) {
+                    kc[ng] = c;
+                    found = true;
+                }
+            for (int c = cap; c >= 1 && !found; --c)   // any divisor (rows of 36 blocks, ...)
                 if (KB % c == 0) {
                     kc[ng] = c;
                     found = true;
