@@ -26,6 +26,12 @@ Printed JSON line (rank 0):
 N > 1: one independent model replica per GPU (decode at batch 1 does not
 shard without a per-layer exchange); value = tokens of all ranks / max time.
 
+workloads (sub-records, N = 1): the other named single-GPU workloads on the
+same persistent decode kernel, each with its roofline fraction and an oracle
+CPU sample: SmolLM2-135M-shaped (32-token prompt, 128 decode tokens) and
+Gemma-3-1B-shaped (Q4_0 layers, Q8_0 embedding; 1024-token prompt, 256 decode
+tokens).
+
 tp (sub-record, every N including 1): the Qwen2.5-7B-shaped K-quant config
 decoding 32 sequences, every matrix row-sharded over the N ranks with NCCL
 all-gathers (strong scaling), with a bit-for-bit check of the sharded
@@ -207,6 +213,80 @@ def cpu_decode_rate(cfg, n_tokens: int, position: int):
     dt = time.perf_counter() - t0
     om.close()
     return n_tokens / dt, threads, dt
+
+
+def named_workloads():
+    """The other single-GPU workloads of the benchmarked configurations:
+    (model config, prompt tokens, decode tokens, oracle sample tokens)."""
+    return [(C.smollm2_135m(), 32, 128, 64), (C.gemma3_1b(), 1024, 256, 12)]
+
+
+def workload_measure(cfg, plen, n_dec, cpu_tokens, peak, peak_kind, with_cpu=True):
+    """One named workload on this GPU: a seeded prompt of `plen` tokens
+    prefilled through the batched prefill (token by token where its tiles do
+    not fit the shapes), 3 untimed decode steps, then
+    `n_dec` greedy decode steps at batch 1 with the tokens fed back on the
+    device (brew_session_decode).  CUDA events on the session's stream time
+    the prompt and the decode; value = decode tok/s.  The roofline counts the
+    packed weight bytes and the K/V rows each step reads.  The CPU baseline
+    is the oracle decoding `cpu_tokens` tokens at the same positions on all
+    host threads."""
+    import torch
+    from brewference_b200.api import PREFILL_BATCHED, DeviceModel
+
+    t0 = time.perf_counter()
+    dm = DeviceModel.synthesize(cfg, SEED)
+    synth_s = time.perf_counter() - t0
+    kernels = dm.step_kernels(1)
+    mode = "batched"
+    try:
+        dm.set_prefill(PREFILL_BATCHED)
+    except Exception:   # noqa: BLE001 - shapes the tcgen05 prefill does not tile: token by token
+        mode = "token by token"
+    prompt = np.random.default_rng(SEED).integers(0, cfg.vocab_size, plen).astype(np.int32)
+    stream = torch.cuda.Stream()
+    prev = torch.cuda.current_stream()
+    torch.cuda.set_stream(stream)
+    s = stream.cuda_stream
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    k0 = N_launches()
+    ev[0].record(stream)
+    dm.prefill(prompt, s)
+    ev[1].record(stream)
+    dm.decode(3, s, want_tokens=False)
+    ev[2].record(stream)
+    dm.decode(n_dec, s, want_tokens=False)
+    ev[3].record(stream)
+    stream.synchronize()
+    launches = N_launches() - k0
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    ms = ev[2].elapsed_time(ev[3])
+    torch.cuda.set_stream(prev)
+    dm.close()
+    positions = list(range(plen + 3, plen + 3 + n_dec))
+    wbytes = cfg.decode_weight_bytes()
+    kvb = kv_bytes_per_step(cfg, positions)
+    achieved = (wbytes + kvb) / (ms / n_dec / 1000.0) / 1e9
+    rec = {"workload": f"{cfg.name}: {plen}-token seeded prompt ({mode} prefill), then {n_dec} greedy decode "
+                       f"tokens at batch 1", "value": n_dec / (ms / 1000.0), "unit": "tok/s",
+           "ms_per_step": ms / n_dec, "steps": n_dec, "warmup": 3, "prefill_ms": prefill_ms,
+           "prefill_tok_s": plen / (prefill_ms / 1000.0), "kernels_per_step": kernels,
+           "gpu_launches": int(launches),
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "peak_kind": peak_kind, "weight_bytes": wbytes, "kv_bytes": kvb},
+           "l2": f"{wbytes / 1e6:.0f} MB of weights streamed per step vs 126 MB L2 (no flush between steps)",
+           "setup_s": {"synthesize": round(synth_s, 2)}}
+    if with_cpu:
+        tps, thr, dt = cpu_decode_rate(cfg, cpu_tokens, plen)
+        rec["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": thr, "kind": "port",
+                               "sample": f"{cpu_tokens} decode tokens at positions {plen + 1}..{plen + cpu_tokens}, "
+                                         f"oracle (C restatement of the reference Java path), {dt:.1f}s"}
+    return rec
+
+
+def N_launches():
+    from brewference_b200 import _native as N
+    return N.kernel_launches()
 
 
 def run_reference(args):
@@ -715,6 +795,11 @@ def run_gpu(args):
         # the sharded 7B config at the same N (tensor parallelism over the
         # ranks; strong scaling): a sub-record of the line
         line["tp"] = tp_measure(rank, world, dist, dev, args.tp_steps, 3, args.batch, args.tp_prompt_len)
+    if world == 1 and not args.no_workloads:
+        # the other named single-GPU workloads (one GPU only: the ranks of a
+        # multi-GPU run would wait for them at the closing barrier)
+        line["workloads"] = [workload_measure(c, pl, nd, ct, peak, peak_kind, with_cpu=not args.no_cpu_baseline)
+                             for c, pl, nd, ct in named_workloads()]
     if rank == 0 and not args.no_cpu_baseline:
         tps, thr, dt = cpu_decode_rate(cfg, args.cpu_tokens, args.prompt_len)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": thr, "kind": "port",
@@ -745,6 +830,8 @@ def main():
                     help="tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config over --gpus ranks")
     ap.add_argument("--batch", type=int, default=32, help="concurrent sequences of the --tp workload")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel 7B sub-record")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the SmolLM2-135M / Gemma-3-1B workload sub-records")
     ap.add_argument("--tp-steps", type=int, default=16, help="timed steps of the tensor-parallel sub-record")
     ap.add_argument("--tp-prompt-len", type=int, default=256, help="prompt tokens of the tensor-parallel sub-record")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")

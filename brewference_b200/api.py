@@ -333,7 +333,8 @@ class DeviceModel:
 
     def trace(self) -> list:
         """%globaltimer stamps (ns) of the last decode step, per CTA: start,
-        then per phase prep-done, work-done, barrier-passed."""
+        then per phase: input landed, prep done, last weight stage in, work
+        done, phase end."""
         buf = (ctypes.c_int64 * (1 << 18))()
         n = ctypes.c_int32()
         N.check(N.lib().brew_model_trace(self.handle, buf, 1 << 18, ctypes.byref(n)))
