@@ -1272,20 +1272,24 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
         dk_bar();
         stamp(5);
         if (s_last) {
-            const int hpw = max(1, min(G, P.attn_floats / (nch * stride)));
+            // heads per pass: as many as the area holds with their used chunks
+            const int hpw = max(1, min(G, P.attn_floats / (used * stride)));
             #pragma unroll 1
             for (int h0 = 0; h0 < G; h0 += hpw) {
                 const int nh = min(hpw, G - h0);
-                const float* src = pbase + (int64_t)h0 * nch * stride;
-                const int n4 = nh * nch * stride / 4;
+                const int n4h = used * stride / 4;   // float4 of one head's used chunks
                 #pragma unroll 1
-                for (int i = tid; i < n4; i += DK_CT) cp_async16(sm + 4 * i, src + 4 * i);
+                for (int hl = 0; hl < nh; ++hl) {
+                    const float* src = pbase + (int64_t)(h0 + hl) * nch * stride;
+                    #pragma unroll 1
+                    for (int j = tid; j < n4h; j += DK_CT) cp_async16(sm + 4 * (hl * n4h + j), src + 4 * j);
+                }
                 cp_async_wait_all();
                 dk_bar();
                 stamp(6);
                 #pragma unroll 1
                 for (int hl = warp; hl < nh; hl += DK_CW) {
-                    float* ph = sm + hl * nch * stride;
+                    float* ph = sm + hl * used * stride;
                     float M = -INFINITY;
                     #pragma unroll 1
                     for (int k = lane; k < used; k += 32) M = fmaxf(M, ph[k * stride]);
@@ -1304,10 +1308,18 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 #pragma unroll 1
                 for (int idx = tid; idx < nh * hd; idx += DK_CT) {
                     const int hl = idx / hd, i = idx % hd;
-                    const float* ph = sm + hl * nch * stride;
-                    float o = 0.0f;
+                    const float* ph = sm + hl * used * stride;
+                    // four independent partial sums over the chunks (k mod 4)
+                    float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    int k = 0;
                     #pragma unroll 1
-                    for (int k = 0; k < used; ++k) o += ph[k * stride + 2] * ph[k * stride + 4 + i];
+                    for (; k + 4 <= used; k += 4) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) o4[u] += ph[(k + u) * stride + 2] * ph[(k + u) * stride + 4 + i];
+                    }
+                    #pragma unroll 1
+                    for (; k < used; ++k) o4[0] += ph[k * stride + 2] * ph[k * stride + 4 + i];
+                    const float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
                     st_tag(tgp(P, l, DK_TG_XB) + (int64_t)b * P.tg_ls + (int64_t)(hk * G + h0 + hl) * hd + i, o * ph[3],
                            ep);
                 }
