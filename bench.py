@@ -595,43 +595,54 @@ def run_tp(args):
 
 
 def decode_trace_table(dm, cfg, reps=3):
-    """Runs `reps` traced decode steps and summarises the last: per phase
-    (Q|K|V, attention, wo, gate|up, down, classifier) the mean and max over
-    CTAs of five stamps in microseconds after the previous phase's earliest
-    barrier exit: input wave landed, input prepared, last weight stage seen,
-    work done (barrier entry), barrier exit."""
-    L = cfg.n_layers
+    """Runs `reps` traced decode steps and summarises the last along the
+    critical path.  Per phase (Q|K|V, attention, wo, gate|up, down), means
+    over the layers, in microseconds after the previous phase's last
+    producing CTA finished its work (E_prev): when the phase's input landed
+    in its first and in its last CTA, the prep time (mean over CTAs), the
+    multiply + epilogue time (mean), and the span E - E_prev, where E is the
+    phase's own last producing CTA.  The spans add up to the layer time."""
+    L, G = cfg.n_layers, None
     slots = 1 + 5 * (5 * L + 1) + 3 * 32
     names = ["qkv", "attn", "wo", "gate_up", "down"]
-    stamps = ["wave", "prep", "last_weight", "work", "exit"]
     for _ in range(reps):
         dm.decode(1)
-        T = np.array(dm.trace(), dtype=np.int64).reshape(-1, slots).astype(np.float64)
-    acc = {n: [] for n in names}
-    prev = T[:, 0]
-    for l in range(L):
-        for p in range(5):
-            b = 1 + 5 * (5 * l + p)
-            st = T[:, b:b + 5]
-            rel = (st - prev.min()) / 1000.0
-            rel[st == 0] = np.nan
-            acc[names[p]].append(rel)
-            prev = T[:, b + 4]
-    b = 1 + 5 * (5 * L)
-    cls = (T[:, b:b + 5] - prev.min()) / 1000.0
-    out = {"step_us": float((T[:, b + 4].max() - T[:, 0].min()) / 1000.0), "layers": L,
-           "stamps": stamps, "phases_mean_over_layers": {}}
+        T = np.array(dm.trace(), dtype=np.int64).reshape(-1, slots).astype(np.float64) / 1000.0
+    G = T.shape[0]
+    tiles = [(cfg.q_width + 2 * cfg.kv_dim) // 16, cfg.dim // 16, cfg.hidden_dim // 8, cfg.dim // 16]
+    owns = [np.array([(c + 1) * t // G - c * t // G > 0 for c in range(G)]) for t in tiles]
+    mph = [0, None, 1, 2, 3]
+    rows = {n: [] for n in names}
+    prev_e = None
     with np.errstate(all="ignore"):
         import warnings
         warnings.simplefilter("ignore")
+        for l in range(L):
+            for p in range(5):
+                b = 1 + 5 * (5 * l + p)
+                st = T[:, b:b + 5]
+                act = st[:, 0] > 0 if p == 1 else owns[mph[p]]
+                w = st[act]
+                e = float(np.max(w[:, 3]))
+                if prev_e is not None:
+                    land = np.where(w[:, 0] > 0, w[:, 0], np.nan) - prev_e
+                    rows[names[p]].append([np.nanmin(land), np.nanmax(land), np.nanmean(w[:, 1] - w[:, 0]),
+                                           np.nanmean(w[:, 3] - w[:, 1]), e - prev_e])
+                prev_e = e
+        b = 1 + 5 * (5 * L)
+        cls_end = float(np.max(T[:, b + 3]))
+        out = {"step_us": round(float(np.max(T[:, b + 4]) - np.min(T[:, 0])), 2), "layers": L,
+               "columns": ["input landed, first CTA", "input landed, last CTA", "prep", "multiply + epilogue",
+                           "span"],
+               "classifier_span_us": round(cls_end - prev_e, 2), "phases_mean_over_layers": {}}
+        per_layer = 0.0
         for n in names:
-            a = np.stack(acc[n])
-            out["phases_mean_over_layers"][n] = {
-                "mean": [round(float(x), 2) for x in np.nanmean(np.nanmean(a, axis=1), axis=0)],
-                "max": [round(float(x), 2) for x in np.nanmean(np.nanmax(a, axis=1), axis=0)]}
-        out["phases_mean_over_layers"]["classifier"] = {
-            "mean": [round(float(x), 2) for x in np.nanmean(cls, axis=0)],
-            "max": [round(float(x), 2) for x in np.nanmax(cls, axis=0)]}
+            a = np.nanmean(np.array(rows[n]), axis=0)
+            if n == "attn":   # no prep / multiply stamps: the attention reports its span only
+                a[2] = a[3] = np.nan
+            out["phases_mean_over_layers"][n] = [None if np.isnan(x) else round(float(x), 2) for x in a]
+            per_layer += float(a[4])
+        out["layer_us"] = round(per_layer, 2)
     return out
 
 
