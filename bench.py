@@ -469,7 +469,7 @@ def profiled_traffic(name: str):
     return None
 
 
-def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True):
+def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True, layers=0):
     """Tensor-parallel decode of the Qwen2.5-7B-shaped K-quant config (Q4_K
     attention/FFN, Q6_K down and classifier, QKV bias): every matrix
     row-sharded over the `world` ranks with one NCCL all-gather per
@@ -485,6 +485,8 @@ def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True
     from brewference_b200.api import Communicator, DeviceModel, comm_unique_id
 
     cfg = C.qwen25_7b()
+    if layers:   # a shallower model of the same shapes (profiler captures)
+        cfg = cfg.replace(n_layers=layers)
     box = [comm_unique_id() if rank == 0 else None]
     if dist is not None:
         dist.broadcast_object_list(box, src=0)
@@ -565,10 +567,12 @@ def run_tp(args):
     N.init(dev)
     clocks = ClockSampler(dev)
     clocks.start()
-    r = tp_measure(rank, world, dist, dev, args.steps, args.warmup, args.batch, args.prompt_len)
+    r = tp_measure(rank, world, dist, dev, args.steps, args.warmup, args.batch, args.prompt_len, layers=args.layers)
     clk = clocks.stop()
     peak, peak_kind = measured_peaks()
     cfg = C.qwen25_7b()
+    if args.layers:
+        cfg = cfg.replace(n_layers=args.layers)
     per_gpu = cfg.decode_weight_bytes() / world / (r["ms_per_step"] / 1000.0) / 1e9
     line = {
         "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -847,7 +851,7 @@ def main():
     ap.add_argument("--tp-prompt-len", type=int, default=256, help="prompt tokens of the tensor-parallel sub-record")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
-    ap.add_argument("--layers", type=int, default=0, help="--profile-decode: layers of the model (default: all)")
+    ap.add_argument("--layers", type=int, default=0, help="--profile-decode / --tp: layers of the model (default: all)")
     ap.add_argument("--vocab", type=int, default=0, help="--profile-decode: vocabulary size (default: the config's)")
     ap.add_argument("--batched-prefill", action="store_true", help="--profile-decode: prefill the prompt batched")
     ap.add_argument("--trace-decode", action="store_true",

@@ -22,11 +22,11 @@ __device__ __forceinline__ void kx_scale_min(const uint8_t* sb, int s, int& sc, 
     }
 }
 
-// One thread per (row, 32-element sub-block j of super-block sb).
-template <int TYPE>
+// Q6_K expanded copy: one thread per (row, 32-element sub-block j of
+// super-block sb).
 __global__ void kx_pack_kernel(const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t pitch, int64_t row_off,
-                               size_t m_off, size_t f_off) {
-    constexpr int SB = TYPE == BREW_TYPE_Q4_K ? 144 : 210;
+                               size_t f_off) {
+    constexpr int SB = 210;
     const int KB = K / 32, KSB = K / 256;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows * KB) return;
@@ -35,47 +35,24 @@ __global__ void kx_pack_kernel(const uint8_t* w, int64_t rows, int K, uint8_t* b
     const uint8_t* blk = w + row * (int64_t)KSB * SB + (int64_t)sb * SB;
     const int64_t prow = row_off + row;
     uint32_t h[8], l[8];   // 32 bytes each
-    int mv = 0;
-    float d, dmin = 0.0f;
-    if (TYPE == BREW_TYPE_Q4_K) {
-        int sc;
-        kx_scale_min(blk + 4, j, sc, mv);
-        d = kx_half(blk);
-        dmin = kx_half(blk + 2);
-        const int sh = sc >> 3, sl = sc & 7;
+    const float d = kx_half(blk + 208);
+    const int s_lo = (int8_t)blk[192 + 2 * j], s_hi = (int8_t)blk[192 + 2 * j + 1];
 #pragma unroll
-        for (int w4 = 0; w4 < 8; ++w4) {
-            uint32_t hv = 0u, lv = 0u;
+    for (int w4 = 0; w4 < 8; ++w4) {
+        uint32_t hv = 0u, lv = 0u;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int k = 4 * w4 + b;
-                const int q = (blk[16 + 32 * (j / 2) + k] >> (4 * (j & 1))) & 15;
-                hv |= (uint32_t)(q * sh) << (8 * b);
-                lv |= (uint32_t)(q * sl) << (8 * b);
-            }
-            h[w4] = hv;
-            l[w4] = lv;
+        for (int b = 0; b < 4; ++b) {
+            const int k = 4 * w4 + b;
+            const int r = 32 * j + k, hb = r / 128, rr = r % 128, grp = rr / 32, ll = rr % 32;
+            const int lq = blk[64 * hb + (grp & 1) * 32 + ll];
+            const int low = grp < 2 ? (lq & 15) : (lq >> 4);
+            const int high = (blk[128 + 32 * hb + ll] >> (2 * grp)) & 3;
+            const int v = (k < 16 ? s_lo : s_hi) * ((low | (high << 4)) - 32);   // [-4064, 4096]
+            hv |= (uint32_t)((v >> 6) & 255) << (8 * b);
+            lv |= (uint32_t)(v & 63) << (8 * b);
         }
-    } else {
-        d = kx_half(blk + 208);
-        const int s_lo = (int8_t)blk[192 + 2 * j], s_hi = (int8_t)blk[192 + 2 * j + 1];
-#pragma unroll
-        for (int w4 = 0; w4 < 8; ++w4) {
-            uint32_t hv = 0u, lv = 0u;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int k = 4 * w4 + b;
-                const int r = 32 * j + k, hb = r / 128, rr = r % 128, grp = rr / 32, ll = rr % 32;
-                const int lq = blk[64 * hb + (grp & 1) * 32 + ll];
-                const int low = grp < 2 ? (lq & 15) : (lq >> 4);
-                const int high = (blk[128 + 32 * hb + ll] >> (2 * grp)) & 3;
-                const int v = (k < 16 ? s_lo : s_hi) * ((low | (high << 4)) - 32);   // [-4064, 4096]
-                hv |= (uint32_t)((v >> 6) & 255) << (8 * b);
-                lv |= (uint32_t)(v & 63) << (8 * b);
-            }
-            h[w4] = hv;
-            l[w4] = lv;
-        }
+        h[w4] = hv;
+        l[w4] = lv;
     }
     uint8_t* hp = base;
     uint8_t* lp = base + (size_t)K * pitch;
@@ -85,10 +62,22 @@ __global__ void kx_pack_kernel(const uint8_t* w, int64_t rows, int K, uint8_t* b
         *reinterpret_cast<uint4*>(hp + o) = make_uint4(h[4 * hf], h[4 * hf + 1], h[4 * hf + 2], h[4 * hf + 3]);
         *reinterpret_cast<uint4*>(lp + o) = make_uint4(l[4 * hf], l[4 * hf + 1], l[4 * hf + 2], l[4 * hf + 3]);
     }
-    if (TYPE == BREW_TYPE_Q4_K) base[m_off + ((int64_t)sb * pitch + prow) * 16 + j] = (uint8_t)mv;
-    if (j == 0) reinterpret_cast<float2*>(base + f_off)[(int64_t)sb * pitch + prow] = make_float2(d, dmin);
+    if (j == 0) reinterpret_cast<float2*>(base + f_off)[(int64_t)sb * pitch + prow] = make_float2(d, 0.0f);
 }
 
+// Q4_K compact copy: one thread per 16-byte word of a block (9 per block):
+// block (row, sb) of the GGUF matrix -> [sb][row_off + row] of the copy.
+__global__ void kc_pack_kernel(const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t pitch, int64_t row_off) {
+    const int KSB = K / 256;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * KSB * 9) return;
+    const int64_t blk = i / 9;
+    const int wd = (int)(i % 9);
+    const int64_t row = blk / KSB;
+    const int sb = (int)(blk % KSB);
+    const uint4 v = reinterpret_cast<const uint4*>(w + blk * 144)[wd];
+    reinterpret_cast<uint4*>(base + ((int64_t)sb * pitch + row_off + row) * 144)[wd] = v;
+}
 
 // One warp per (vector t < nvp, super-block): lane i holds elements
 // 8i .. 8i + 7 (sub-block i / 4); vectors past nv are zero.
@@ -121,6 +110,60 @@ constexpr int KX_SMEM = 2 * KX_STAGE + 128;
 constexpr int KX_EPI = 16;                      // epilogue warps: 4 per tensor-memory lane quadrant
 constexpr int KX_THREADS = 64 + 32 * KX_EPI;    // loader warp, MMA warp, epilogue warps
 constexpr int KX_TMEM_COLS = 512;               // h, l, min-Xl, min-Xh accumulators at 0, 128, 256, 384
+// Q4_K (compact stream): one expanded area (h, l, min tile, zero area at the
+// offsets above), then two stages of records and two of raw block runs
+// (128 rows x 144 bytes), then the barriers.
+constexpr int KC_REC = 10 * 96 * 32;            // records of one super-block (up to 32 vectors)
+constexpr int KC_REC0 = KX_B;
+constexpr int KC_RAW = 128 * 144;
+constexpr int KC_RAW0 = KC_REC0 + 2 * KC_REC;
+constexpr int KC_BAR = KC_RAW0 + 2 * KC_RAW;
+constexpr int KC_SMEM = KC_BAR + 128;
+
+// Q4_K: expands item e (0 .. 511) of a raw run of 128 rows: row e % 128,
+// sub-blocks 2 (e / 128) and 2 (e / 128) + 1, into the h / l tiles (the
+// layout of the expanded planes: sub-block j at j 4096, K-half hk 2048
+// further, row r 16 bytes each) and, for e < 128, the row's min tile entry.
+// Element value d (8 h + l) - dmin m_j with h = q (sc >> 3), l = q (sc & 7)
+// (GGML's d sc q - dmin m), q the element's nibble.
+__device__ __forceinline__ void kc_expand(uint8_t* xa, const uint8_t* raw, int e) {
+    const int row = e & 127, pr = e >> 7;
+    const uint8_t* blk = raw + row * 144;
+    int sc[2], mn[2];
+    kx_scale_min(blk + 4, 2 * pr, sc[0], mn[0]);
+    kx_scale_min(blk + 4, 2 * pr + 1, sc[1], mn[1]);
+    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * pr);
+    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * pr);
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int sub = 0; sub < 2; ++sub) {   // sub-block 2 pr: low nibbles; 2 pr + 1: high nibbles
+        const uint32_t sh = (uint32_t)(sc[sub] >> 3), sl = (uint32_t)(sc[sub] & 7);
+#pragma unroll
+        for (int hk = 0; hk < 2; ++hk) {
+            uint32_t hv[4], lv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t qv = (sub ? (w[4 * hk + u] >> 4) : w[4 * hk + u]) & 0x0F0F0F0Fu;
+                hv[u] = qv * sh;   // bytewise: q s <= 105, no carry between the bytes
+                lv[u] = qv * sl;
+            }
+            const int so = (2 * pr + sub) * 4096 + hk * 2048 + row * 16;
+            *reinterpret_cast<uint4*>(xa + KX_AH + so) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(xa + KX_AL + so) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
+    }
+    if (pr == 0) {   // the min tile row: m_0 .. m_7, then 8 zero bytes
+        uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int scj, mj;
+            kx_scale_min(blk + 4, j, scj, mj);
+            if (j < 4) lo |= (uint32_t)mj << (8 * j);
+            else hi |= (uint32_t)mj << (8 * (j - 4));
+        }
+        *reinterpret_cast<uint4*>(xa + KX_AM + row * 16) = make_uint4(lo, hi, 0u, 0u);
+    }
+}
 
 __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned int* err, unsigned int code) {
     for (int i = 0; i < 32; ++i)
@@ -130,8 +173,14 @@ __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned
 
 // CTA = 128 rows (row0 + 128 blockIdx.x ..) x all vectors x the
 // super-blocks of split blockIdx.y.  Per super-block:
-//   warp 0      one lane bulk-copies the stage (33 copies: 32 K-half runs
-//               of h and l, the min tile, the records) into one of 2 stages;
+//   warp 0      one lane bulk-copies the stage into one of 2 stages: Q4_K
+//               the 128 rows' raw blocks (one 18 KB run) and the records;
+//               Q6_K 33 copies (32 K-half runs of h and l, the records);
+//   (Q4_K)      the epilogue warps expand the raw run into the h, l and min
+//               tiles (one (row, sub-block pair) per thread) and each
+//               thread keeps its readout row's (d, dmin); the expanded area
+//               is single: the next expansion starts after the readout,
+//               which waits for the MMAs;
 //   warp 1      one thread issues, per sub-block j, the MMAs h_j x B_j and
 //               l_j x B_j into the h and l accumulators (Q4_K: then the min
 //               tile against the two min-term tiles), all onto the preset
@@ -152,11 +201,12 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
     constexpr int CW = NC / (KX_EPI / 4), TPW = CW / 3;   // columns and vectors per epilogue warp
     constexpr int NACC = Q4 ? 4 : 2;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * KX_STAGE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (Q4 ? KC_BAR : 2 * KX_STAGE));
     uint64_t* empty = full + 2;
     uint64_t* tfull = empty + 2;
     uint64_t* tempty = tfull + 1;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 1);
+    uint64_t* xready = tempty + 1;   // Q4_K: the expanded tiles are in place
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(xready + 1);
     __shared__ int s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int KSB = K / 256, split = blockIdx.y;
@@ -172,15 +222,15 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], Q4 ? 1 + KX_EPI : 1);   // Q4_K: the MMAs' commit and every expanding warp
         }
         mbar_init(tfull, 1);
         mbar_init(tempty, KX_EPI);
+        mbar_init(xready, KX_EPI);
         fence_mbar_init();
     }
     if (Q4) {   // the min tile's second K-half: zeros, read by the tensor cores
-        for (int i = tid; i < 2 * 512; i += KX_THREADS)
-            reinterpret_cast<uint32_t*>(smem + (i / 512) * KX_STAGE + KX_Z)[i % 512] = 0u;
+        for (int i = tid; i < 512; i += KX_THREADS) reinterpret_cast<uint32_t*>(smem + KX_Z)[i] = 0u;
         fence_proxy_async();
     }
     tc_fence_before();
@@ -199,6 +249,13 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             for (int sb = sb0; sb < sb1; ++sb, ++it) {
                 const int st = it & 1;
                 if (it >= 2 && !kx_wait(&empty[st], ((it >> 1) - 1) & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
+                if (Q4) {   // the raw blocks of rows r0 .. r0 + 127 of super-block sb: one contiguous run
+                    mbar_arrive_expect_tx(&full[st], KC_RAW + bbytes);
+                    bulk_g2s_hint(smem + KC_RAW0 + st * KC_RAW, base + ((int64_t)sb * pitch + r0) * 144, KC_RAW,
+                                  &full[st], pol);
+                    bulk_g2s(smem + KC_REC0 + st * KC_REC, rec + (int64_t)sb * rec_tile, bbytes, &full[st]);
+                    continue;
+                }
                 uint8_t* s0 = smem + st * KX_STAGE;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 for (int hk = 0; hk < 16; ++hk) {   // K-half hk of the super-block: sub-block hk / 2
@@ -220,19 +277,22 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             for (int sb = sb0; sb < sb1; ++sb, ++it) {
                 const int st = it & 1;
                 if (!kx_wait(&full[st], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL)) break;
+                if (Q4 && !kx_wait(xready, it & 1, err, BREW_DEVERR_TIMEOUT_FULL)) break;
                 if (!kx_wait(tempty, it & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
                 tc_fence_after();
-                const uint32_t s0 = smem_u32(smem + st * KX_STAGE);
+                // Q4_K: the expanded tiles at 0, the stage's records apart
+                const uint32_t s0 = smem_u32(smem + (Q4 ? 0 : st * KX_STAGE));
+                const uint32_t sr = Q4 ? smem_u32(smem + KC_REC0 + st * KC_REC) : s0 + KX_B;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const uint64_t bd = umma_desc_k(s0 + KX_B + j * NC * 32, 128, 256);
+                    const uint64_t bd = umma_desc_k(sr + j * NC * 32, 128, 256);
                     umma_s8(tmem, umma_desc_k(s0 + KX_AH + j * 4096, 2048, 128), bd, idesc, 1u);
                     umma_s8(tmem + 128, umma_desc_k(s0 + KX_AL + j * 4096, 2048, 128), bd, idesc, 1u);
                 }
                 if (Q4) {
                     const uint64_t ad = umma_desc_k(s0 + KX_AM, 2048, 128);
-                    umma_s8(tmem + 256, ad, umma_desc_k(s0 + KX_B + 8 * NC * 32, 128, 256), idesc, 1u);
-                    umma_s8(tmem + 384, ad, umma_desc_k(s0 + KX_B + 9 * NC * 32, 128, 256), idesc, 1u);
+                    umma_s8(tmem + 256, ad, umma_desc_k(sr + 8 * NC * 32, 128, 256), idesc, 1u);
+                    umma_s8(tmem + 384, ad, umma_desc_k(sr + 9 * NC * 32, 128, 256), idesc, 1u);
                 }
                 umma_commit(&empty[st]);
                 umma_commit(tfull);
@@ -263,9 +323,34 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         const uint64_t k256 = f2_packf(256.0f, 256.0f), k65536 = f2_packf(65536.0f, 65536.0f);
         const float2* fpl = reinterpret_cast<const float2*>(base + f_off);
         const float* scl = reinterpret_cast<const float*>(rec + (int64_t)KSB * rec_tile);
-        float2 fr = sb0 < sb1 ? __ldg(fpl + (int64_t)sb0 * pitch + frow) : make_float2(0.0f, 0.0f);
+        float2 fr = (!Q4 && sb0 < sb1) ? __ldg(fpl + (int64_t)sb0 * pitch + frow) : make_float2(0.0f, 0.0f);
+        // the vectors' scales of a super-block, loaded one super-block ahead
+        // (their L2 round trip overlaps the previous readout)
+        float4 svn[TPW / 4];
+        auto load_scales = [&](int sbl) {
+#pragma unroll
+            for (int g = 0; g < TPW / 4; ++g)
+                svn[g] = __ldg(reinterpret_cast<const float4*>(scl + (int64_t)sbl * NVP + TPW * hh) + g);
+        };
+        if (sb0 < sb1) load_scales(sb0);
         int it = 0;
         for (int sb = sb0; sb < sb1; ++sb, ++it) {
+            if (Q4) {   // expand this super-block's raw run, keep the readout row's (d, dmin)
+                const int st = it & 1;
+                bool okx = kx_wait(&full[st], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL);
+                okx = __all_sync(0xffffffffu, okx);
+                if (!okx) break;
+                const uint8_t* raw = smem + KC_RAW0 + st * KC_RAW;
+                kc_expand(smem, raw, tid - 64);
+                const uint8_t* rb = raw + (32 * q + lane) * 144;
+                fr = make_float2(kx_half(rb), kx_half(rb + 2));
+                fence_proxy_async();   // the generic-proxy stores, before the tensor cores read them
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(xready);
+                    mbar_arrive(&empty[st]);   // the raw run is consumed
+                }
+            }
             bool ok = kx_wait(tfull, it & 1, err, BREW_DEVERR_TIMEOUT_FULL);
             ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld / st are warp-collective
             if (!ok) break;
@@ -273,14 +358,14 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             float sv[TPW];
 #pragma unroll
             for (int g = 0; g < TPW / 4; ++g) {
-                const float4 s4 = __ldg(reinterpret_cast<const float4*>(scl + (int64_t)sb * NVP + TPW * hh) + g);
-                sv[4 * g] = s4.x;
-                sv[4 * g + 1] = s4.y;
-                sv[4 * g + 2] = s4.z;
-                sv[4 * g + 3] = s4.w;
+                sv[4 * g] = svn[g].x;
+                sv[4 * g + 1] = svn[g].y;
+                sv[4 * g + 2] = svn[g].z;
+                sv[4 * g + 3] = svn[g].w;
             }
+            if (sb + 1 < sb1) load_scales(sb + 1);
             const uint64_t d2 = f2_packf(fr.x, fr.x), nm2 = f2_packf(-fr.y, -fr.y);
-            if (sb + 1 < sb1) fr = __ldg(fpl + (int64_t)(sb + 1) * pitch + frow);
+            if (!Q4 && sb + 1 < sb1) fr = __ldg(fpl + (int64_t)(sb + 1) * pitch + frow);
 #pragma unroll
             for (int e = 0; e < CW / 12; ++e) {   // 12 columns (2 vector pairs) at a time
                 const uint32_t ta = tq + 12 * e;
@@ -376,14 +461,15 @@ template <int TYPE, int NVG>
 int kx_launch_t(const uint8_t* base, int64_t N, int64_t row0, int n, int K, const uint8_t* rec, int nv, int S,
                 float* part, int* ctr, const float* bias, float* y, int ldy, unsigned int* err, cudaStream_t stream) {
     static uint64_t attr_devs = 0;   // devices whose attribute is set
+    constexpr int SMEM = TYPE == BREW_TYPE_Q4_K ? KC_SMEM : KX_SMEM;
     int dev = 0;
     BREW_CUDA(cudaGetDevice(&dev));
     if (dev < 64 && !(attr_devs >> dev & 1)) {
-        BREW_CUDA(cudaFuncSetAttribute(kx_mma_kernel<TYPE, NVG>, cudaFuncAttributeMaxDynamicSharedMemorySize, KX_SMEM));
+        BREW_CUDA(cudaFuncSetAttribute(kx_mma_kernel<TYPE, NVG>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         attr_devs |= 1ull << dev;
     }
     const dim3 grid((unsigned)((n + KX_TM - 1) / KX_TM), (unsigned)S);
-    kx_mma_kernel<TYPE, NVG><<<grid, KX_THREADS, KX_SMEM, stream>>>(base, kx_pitch(N), row0, n, K, kx_m_off(N, K),
+    kx_mma_kernel<TYPE, NVG><<<grid, KX_THREADS, SMEM, stream>>>(base, kx_pitch(N), row0, n, K, kx_m_off(N, K),
                                                                     kx_f_off(TYPE, N, K), rec, nv, S, part, ctr, bias,
                                                                     y, ldy, err);
     BREW_CUDA(cudaGetLastError());
@@ -408,14 +494,18 @@ int kx_pack_launch(int type, const uint8_t* w, int64_t rows, int K, uint8_t* bas
     BREW_CHECK((type == BREW_TYPE_Q4_K || type == BREW_TYPE_Q6_K) && K % 256 == 0 && K > 0 && rows > 0 &&
                    row_off >= 0 && row_off + rows <= N,
                BREW_ERR_INVALID_ARG, "K-quant expand: type %d rows=%lld K=%d", type, (long long)rows, K);
+    if (type == BREW_TYPE_Q4_K) {   // the compact copy: blocks reordered super-block-major
+        BREW_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0, BREW_ERR_INVALID_ARG,
+                   "K-quant copy: Q4_K rows must start 16-byte aligned");
+        const int64_t words = rows * (K / 256) * 9;
+        kc_pack_kernel<<<(unsigned)((words + 255) / 256), 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off);
+        BREW_CUDA(cudaGetLastError());
+        count_launch();
+        return BREW_OK;
+    }
     const int64_t cnt = rows * (K / 32);
     const unsigned blocks = (unsigned)((cnt + 255) / 256);
-    if (type == BREW_TYPE_Q4_K)
-        kx_pack_kernel<BREW_TYPE_Q4_K><<<blocks, 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off,
-                                                                   kx_m_off(N, K), kx_f_off(type, N, K));
-    else
-        kx_pack_kernel<BREW_TYPE_Q6_K><<<blocks, 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off,
-                                                                   kx_m_off(N, K), kx_f_off(type, N, K));
+    kx_pack_kernel<<<blocks, 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off, kx_f_off(type, N, K));
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;

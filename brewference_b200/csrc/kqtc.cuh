@@ -2,18 +2,28 @@
 // 7B config) on the 5th-generation tensor cores: tcgen05.mma kind::i8 with
 // the accumulators in tensor memory, 1..32 vectors per launch.
 //
-// Weights: an expanded copy of each matrix in which every element's
-// integer factor carries its sub-block scale, split into two int8 limbs,
-// so that a whole 256-element super-block is summed in integers by the MMA
-// and its fp32 factors are applied once:
+// Weights (Q4_K): a compact copy of each matrix (or row family of N rows),
+// the GGUF 144-byte blocks unchanged but ordered super-block-major,
+//   [K/256][P][144]  (P = N + 128 rows, the last 128 zero),
+// so the 128 rows a CTA multiplies for one super-block are one contiguous
+// 18,432-byte run: one bulk copy per stage, 0.5625 bytes per weight as in
+// the file.  The CTA expands the run in shared memory into the two int8
+// limb planes below (the epilogue warps, just before the MMA).
+// Weights (Q6_K): an expanded copy in HBM (its 210-byte blocks are only
+// 2-byte aligned, which rules out bulk copies of the rows).
+// Expanded planes: every element's integer factor carries its sub-block
+// scale, split into two int8 limbs, so that a whole 256-element
+// super-block is summed in integers by the MMA and its fp32 factors are
+// applied once:
 //   Q4_K  sc * q = 8 h + l,  h = q (sc >> 3), l = q (sc & 7)  (0..105),
 //         and the min term sum_j m_j X_j (X_j the sub-block sum of x) by
 //         one more MMA against the m_j;
 //         element value d (8 h + l) - dmin m_j  (GGML: d sc q - dmin m);
 //   Q6_K  sc * (q - 32) = 64 h + l,  h in [-64, 63], l in [0, 63];
 //         element value d (64 h + l)  (GGML: d sc (q - 32)).
-// Planes of one matrix (or row family) of N rows, pitch P = N + 128 rows
-// (the last 128 rows zero, so a 128-row box never leaves the buffer):
+// Expanded planes of one matrix (or row family) of N rows, pitch P = N + 128
+// rows (the last 128 rows zero, so a 128-row box never leaves the buffer;
+// in HBM for Q6_K, in shared memory for one super-block of Q4_K):
 //   h, l  [K/16][P][16]  int8: the 16-element K-halves of every row, row
 //                         after row, so the 128 rows of a CTA's K-half are
 //                         one contiguous 2 KB run (an MMA operand's core
@@ -50,8 +60,10 @@ inline size_t kx_m_off(int64_t N, int64_t K) { return 2 * kx_plane_bytes(N, K); 
 inline size_t kx_f_off(int type, int64_t N, int64_t K) {
     return kx_m_off(N, K) + (type == BREW_TYPE_Q4_K ? (size_t)(K / 256) * kx_pitch(N) * 16 : 0);
 }
-// Bytes of the expanded copy of an N x K matrix (or row family).
+// Bytes of the weight copy of an N x K matrix (or row family): compact
+// (Q4_K) or expanded (Q6_K).
 inline size_t kx_bytes(int type, int64_t N, int64_t K) {
+    if (type == BREW_TYPE_Q4_K) return (size_t)(K / 256) * kx_pitch(N) * 144;
     return kx_f_off(type, N, K) + (size_t)(K / 256) * kx_pitch(N) * 8;
 }
 // Bytes of the x records of nv vectors of K elements (tiles, then scales).
@@ -67,7 +79,8 @@ inline size_t kx_rec_bytes(int nv, int64_t K) {
 int kq_splits(int64_t K, int64_t n_basis);
 
 // Rows [0, rows) of GGUF matrix w (rows x K) -> rows [row_off, row_off + rows)
-// of the expanded copy `base` of a family of N rows (zeroed beforehand).
+// of the weight copy `base` (compact or expanded, kx_bytes) of a family of
+// N rows (zeroed beforehand).
 int kx_pack_launch(int type, const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t N, int64_t row_off,
                    cudaStream_t stream);
 // x [nv][ldx] (nv <= 32) -> records.
