@@ -214,6 +214,20 @@ __device__ __forceinline__ bool wait_counter_bounded(const unsigned long long* c
     return true;
 }
 
+// Waits until the int counter reaches `target` (acquire), bounded like
+// wait_counter_bounded.
+__device__ __forceinline__ bool wait_int_bounded(const int* ctr, int target, const int* abort, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+    uint32_t it = 0;
+    for (;;) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        __nanosleep(32);
+        if ((++it & 63u) == 0u && (global_ns() - t0 > limit_ns || (abort && ld_volatile_int(abort)))) return false;
+    }
+}
+
 // Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2.
 __device__ __forceinline__ void prefetch_l2(const void* src_gmem, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");

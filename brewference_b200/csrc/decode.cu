@@ -1014,16 +1014,26 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
     float* sn = cs + half;
     float* sc = sn + half;
     float* st = sc + G * SUB;
-    __shared__ int s_last;
+    __shared__ int s_all;   // every chunk of the item's (sequence, kv head) has arrived
     // detail trace (first item of the CTA): 0 start, 1 wave landed, 2 head
-    // norm, 3 RoPE, 4 rounds done, 5 arrival counted, 6 partials landed
-    // (combining CTA), 7 combine done, 8 phase end
+    // norm, 3 RoPE, 4 rounds done, 5 all chunks arrived, 6 the slice's
+    // partials staged, 7 slice combined, 8 phase end
     unsigned long long* const det0 = detail;
     auto stamp = [&](int k) {
         if (detail && tid == 0) detail[k] = global_ns();
     };
     stamp(0);
     const int items = P.batch * P.n_kv * nch;
+    // every item CTA waits for all chunks of its (sequence, kv head): one
+    // item per CTA at most (decode_prepare sizes nchunk so), else stop
+    if (items > (int)gridDim.x) {
+        if (tid == 0 && blockIdx.x == 0) {
+            atomicOr(P.err, BREW_DEVERR_BAD_INDEX);
+            atomicExch(P.abort, 1);
+        }
+        aborted = true;
+        return;
+    }
     #pragma unroll 1
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         AttnItem it;
@@ -1257,39 +1267,54 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                 }
             }
         }
-        // arrival; the last CTA of (b, hk) combines the used chunks in order.
-        // The barrier orders every thread's partial stores before thread 0's
-        // release, which makes them visible before its arrival is counted.
+        // Arrival, then every item CTA of (b, hk) combines its slice of the
+        // G hd outputs (AttentionEngine.attend's softmax over all positions,
+        // regrouped by chunk).  The counters of this launch are the set of
+        // its epoch's parity (cleared by the previous launch), so all chunks
+        // are in when the count reaches nch.  The barrier orders every
+        // thread's partial stores before thread 0's release; the acquire
+        // orders the other chunks' partials before the slice is read.
         dk_bar();
-        int* ctr = &P.attn_ctr[(l * DK_MAX_BATCH + b) * P.n_kv + hk];   // one per layer: reset by its combine
+        int* ctr = &P.attn_ctr[(((int)(ep & 1u) * P.n_layers + l) * DK_MAX_BATCH + b) * P.n_kv + hk];
         if (tid == 0) {
-            // release: the CTA's partials before the count; acquire: the
-            // other CTAs' partials before the combine reads them
             int prev;
             asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
-            s_last = (prev == nch - 1);
+            int ok = 1;
+            if (prev + 1 < nch && !wait_int_bounded(ctr, nch, P.abort, 2000000000ull)) {
+                atomicOr(P.err, BREW_DEVERR_TIMEOUT_FULL);
+                atomicExch(P.abort, 1);
+                ok = 0;
+            }
+            s_all = ok;
         }
         dk_bar();
+        if (!s_all) aborted = true;
         stamp(5);
-        if (s_last) {
-            // heads per pass: as many as the area holds with their used chunks
-            const int hpw = max(1, min(G, P.attn_floats / (used * stride)));
-            #pragma unroll 1
-            for (int h0 = 0; h0 < G; h0 += hpw) {
-                const int nh = min(hpw, G - h0);
-                const int n4h = used * stride / 4;   // float4 of one head's used chunks
+        {
+            const int tot = G * hd, S = (tot + nch - 1) / nch;   // outputs per CTA
+            const int o0 = c * S, o1 = min(tot, o0 + S);
+            if (o0 < o1 && s_all) {
+                const int lgh = 31 - __clz(hd);   // hd is a power of two
+                const int h0 = o0 >> lgh, nh = ((o1 - 1) >> lgh) - h0 + 1;   // heads of the slice
+                // stage the slice's heads: every used chunk's record [m, l, -, -, o[hd]]
+                // (contiguous per head), then the weights and 1 / L per head
+                float* srec = sm;                       // [nh][used][stride]
+                float* swt = srec + nh * used * stride; // [nh][used], then [nh] 1 / L
+                const int n4 = used * stride / 4;
                 #pragma unroll 1
-                for (int hl = 0; hl < nh; ++hl) {
-                    const float* src = pbase + (int64_t)(h0 + hl) * nch * stride;
+                for (int hh = 0; hh < nh; ++hh) {
+                    const float* src = pbase + (int64_t)(h0 + hh) * nch * stride;
                     #pragma unroll 1
-                    for (int j = tid; j < n4h; j += DK_CT) cp_async16(sm + 4 * (hl * n4h + j), src + 4 * j);
+                    for (int j = tid; j < n4; j += DK_CT) cp_async16(srec + 4 * (hh * n4 + j), src + 4 * j);
                 }
                 cp_async_wait_all();
                 dk_bar();
                 stamp(6);
+                // one warp per head of the slice: the largest running max, the
+                // chunks' weights and 1 / L
                 #pragma unroll 1
-                for (int hl = warp; hl < nh; hl += DK_CW) {
-                    float* ph = sm + hl * used * stride;
+                for (int hh = warp; hh < nh; hh += DK_CW) {
+                    const float* ph = srec + hh * used * stride;
                     float M = -INFINITY;
                     #pragma unroll 1
                     for (int k = lane; k < used; k += 32) M = fmaxf(M, ph[k * stride]);
@@ -1298,35 +1323,34 @@ __device__ void attn_phase(const DecodeParams& P, int l, float* sm, unsigned lon
                     #pragma unroll 1
                     for (int k = lane; k < used; k += 32) {
                         const float w = expf(ph[k * stride] - M);
-                        ph[k * stride + 2] = w;
+                        swt[hh * used + k] = w;
                         Ls += w * ph[k * stride + 1];
                     }
                     Ls = warp_sum(Ls);
-                    if (lane == 0) ph[3] = __frcp_rn(Ls);   // = 1.0f / Ls, correctly rounded
+                    if (lane == 0) swt[nh * used + hh] = __frcp_rn(Ls);   // = 1.0f / Ls, correctly rounded
                 }
                 dk_bar();
                 #pragma unroll 1
-                for (int idx = tid; idx < nh * hd; idx += DK_CT) {
-                    const int hl = idx / hd, i = idx % hd;
-                    const float* ph = sm + hl * used * stride;
+                for (int t = tid; t < o1 - o0; t += DK_CT) {
+                    const int oi = o0 + t, hh = (oi >> lgh) - h0, i = oi & (hd - 1);
+                    const float* ph = srec + hh * used * stride + 4 + i;
+                    const float* wt = swt + hh * used;
                     // four independent partial sums over the chunks (k mod 4)
                     float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                     int k = 0;
                     #pragma unroll 1
                     for (; k + 4 <= used; k += 4) {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) o4[u] += ph[(k + u) * stride + 2] * ph[(k + u) * stride + 4 + i];
+                        for (int u = 0; u < 4; ++u) o4[u] += wt[k + u] * ph[(k + u) * stride];
                     }
                     #pragma unroll 1
-                    for (; k < used; ++k) o4[0] += ph[k * stride + 2] * ph[k * stride + 4 + i];
+                    for (; k < used; ++k) o4[0] += wt[k] * ph[k * stride];
                     const float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
-                    st_tag(tgp(P, l, DK_TG_XB) + (int64_t)b * P.tg_ls + (int64_t)(hk * G + h0 + hl) * hd + i, o * ph[3],
-                           ep);
+                    st_tag(tgp(P, l, DK_TG_XB) + (int64_t)b * P.tg_ls + (int64_t)hk * G * hd + oi,
+                           o * swt[nh * used + hh], ep);
                 }
-                dk_bar();
+                stamp(7);
             }
-            if (tid == 0) *ctr = 0;
-            stamp(7);
         }
         dk_bar();
         detail = nullptr;   // stamps of the first item only
@@ -1363,10 +1387,17 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
         }
         fence_mbar_init();
         // this launch's epoch: one past the last completed launch's, never 0
+        // (after 2^32 - 1 comes 2: the parity keeps alternating)
         const uint32_t e = *P.seq + 1u;
-        s_ep = e ? e : 1u;
+        s_ep = e ? e : 2u;
     }
     if (tid < 16) s_best[tid] = 0ull;
+    if (blockIdx.x == 0) {   // the attention counters of the next launch's parity (the previous launch used them)
+        const uint32_t e = *P.seq + 1u, par = (e ? e : 2u) & 1u;
+        const int n = P.n_layers * DK_MAX_BATCH * P.n_kv;
+        int* nxt = P.attn_ctr + (int)(par ^ 1u) * n;
+        for (int i = tid; i < n; i += blockDim.x) nxt[i] = 0;
+    }
     if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
     if (tid < 5) {
         const int qw = P.n_heads * P.hd, kvd = P.n_kv * P.hd;
@@ -1665,9 +1696,21 @@ int decode_prepare(DecodeParams* p) {
     // attention area (vec and prep are contiguous): the item layout of
     // attn_phase, or one head's partials of all chunks for the combine
     const int SUB = attn_sub(p->hd);
+    // the combine of a CTA's slice of the G hd outputs stages the chunk
+    // records of the slice's heads (one or two) plus their weights
+    size_t comb_fl = 0;
+    {
+        const int tot = G * p->hd, S = (tot + p->nchunk - 1) / p->nchunk;
+        for (int c = 0; c < p->nchunk; ++c) {
+            const int o0 = c * S, o1 = std::min(tot, o0 + S);
+            if (o0 >= o1) break;
+            const int nh = (o1 - 1) / p->hd - o0 / p->hd + 1;
+            comb_fl = std::max(comb_fl, (size_t)nh * ((size_t)p->nchunk * (p->hd + 4) + p->nchunk) + nh);
+        }
+    }
     const size_t attn_fl = std::max((size_t)2 * SUB * p->hd + (size_t)G * p->hd + 5 * (size_t)p->hd +
                                         (size_t)G * SUB + 4 * (size_t)G + 64,
-                                    (size_t)p->nchunk * (p->hd + 4));
+                                    comb_fl);
     // staged input vector and the norm weight beside it
     p->vec_bytes = (int)(((size_t)std::max(kmax, 2 * p->dim) * 4 + 127) & ~size_t(127));
     const size_t prep_need = (size_t)(kmax / 32) * p->rec_bytes;
@@ -1741,6 +1784,9 @@ int decode_prepare(DecodeParams* p) {
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
     BREW_CHECK(coop, BREW_ERR_UNSUPPORTED, "decode kernel: cooperative launch unsupported");
     p->grid = num_sms();
+    // the attention combine waits for all chunks of a kv head: one item per CTA
+    BREW_CHECK((int64_t)p->batch * p->n_kv * p->nchunk <= p->grid, BREW_ERR_UNSUPPORTED, "decode kernel: %d attention items for %d CTAs", p->batch * p->n_kv * p->nchunk,
+               p->grid);
     return BREW_OK;
 }
 

@@ -65,7 +65,7 @@ struct alignas(64) DecodeParams {
     int tg_off[DK_TG_N];
     float* logits;
     float* attn_part;                   // [2 (layer parity)][DK_MAX_BATCH][n_heads][nchunk][hd + 4]: m, l, -, -, o[hd]
-    int* attn_ctr;                      // [n_layers][DK_MAX_BATCH][n_kv] arrival counters
+    int* attn_ctr;                      // [2 (epoch parity)][n_layers][DK_MAX_BATCH][n_kv] arrival counters
     int nchunk, attn_floats;            // attn_floats: shared-memory floats of the attention area
     int attn_sub;                       // K / V positions staged per round
     unsigned long long* am_key;

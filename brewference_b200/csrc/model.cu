@@ -89,7 +89,7 @@ struct brew_model_s {
     bool use_decode = false;
     DecodeParams dp;
     float *rope_cos = nullptr, *rope_sin = nullptr, *dk_part = nullptr;
-    int* dk_actr = nullptr;                 // its attention arrival counters [layers][DK_MAX_BATCH][kv heads]
+    int* dk_actr = nullptr;                 // its attention arrival counters [2][layers][DK_MAX_BATCH][kv heads]
     size_t dk_nactr = 0;
     unsigned long long* dk_tg = nullptr;    // its tagged activations
     size_t dk_tg_words = 0;
@@ -1184,7 +1184,7 @@ int setup_decode(brew_model_s* m) {
     p.nchunk = std::max(1, std::min(64, num_sms() / (B * c.n_kv_heads)));
     if ((rc = dalloc(m, &m->dk_part, (size_t)2 * DK_MAX_BATCH * c.n_heads * p.nchunk * (hd + 4)))) return rc;
     p.attn_part = m->dk_part;
-    m->dk_nactr = (size_t)c.n_layers * DK_MAX_BATCH * c.n_kv_heads;
+    m->dk_nactr = (size_t)2 * c.n_layers * DK_MAX_BATCH * c.n_kv_heads;
     if ((rc = dalloc(m, &m->dk_actr, m->dk_nactr))) return rc;
     p.attn_ctr = m->dk_actr;
     p.am_key = m->am_key;
