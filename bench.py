@@ -33,8 +33,9 @@ Gemma-3-1B-shaped (Q4_0 layers, Q8_0 embedding; 1024-token prompt, 256 decode
 tokens).
 
 tp (sub-record, every N including 1): the Qwen2.5-7B-shaped K-quant config
-decoding 32 sequences, every matrix row-sharded over the N ranks with NCCL
-all-gathers (strong scaling), with a bit-for-bit check of the sharded
+decoding 32 sequences, every matrix row-sharded over the N ranks, each
+projection's slices gathered by peer stores into every rank's tagged slots
+over NVLink (strong scaling), with a bit-for-bit check of the sharded
 first-step logits against the unsharded model on one GPU (N > 1).
 
 --impl reference: times the CPU restatement of the reference path (the Java
@@ -547,7 +548,10 @@ def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True
     value = B * steps / (ms / 1000.0)
     return {"value": value, "unit": "tok/s", "ms_per_step": ms / steps, "n_gpus": world, "steps": steps,
             "warmup": warmup, "sequences": B, "prompt_tokens": plen, "gpu_launches": int(launches),
-            "collective": "NCCL all-gather per projection (q|k|v, wo, gate|up, down, logits) + argmax key reduction",
+            "collective": ("peer stores of each projection's slice (q|k|v, wo, gate|up, down, logits) into every "
+                           "rank's tagged slots over NVLink (CUDA IPC), NCCL all-gather of the argmax keys"
+                           if world > 1 and not os.environ.get("BREW_TP_NCCL") else
+                           "NCCL all-gather per projection (q|k|v, wo, gate|up, down, logits) + argmax key reduction"),
             "parity": parity,
             "parity_check": "rank 0: first-step logits of the sharded model == unsharded 1-GPU model, bit for bit"
                             if world > 1 else "single GPU (no sharding)",
@@ -582,7 +586,7 @@ def run_tp(args):
         "config": {"workload": f"{cfg.name} Q4_K/Q6_K decode, {args.batch} concurrent sequences after "
                                f"{args.prompt_len}-token prompts, tensor-parallel over {world} GPU(s)",
                    "model": cfg.name, "global_batch": args.batch, "seq_len": cfg.seq_len,
-                   "parallelism": f"tp{world} (row-sharded matrices, NCCL all-gather per projection)",
+                   "parallelism": f"tp{world} (row-sharded matrices, peer-store gather per projection)",
                    "l2": "inputs larger than L2 (4.6 GB of weights per step)"},
         "gpu_launches": r["gpu_launches"],
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,

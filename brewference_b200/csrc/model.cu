@@ -119,6 +119,15 @@ struct brew_model_s {
     // tensor parallelism (brew_model_set_tp): this rank's row slices
     brew_comm comm = nullptr;
     float *tp_send = nullptr, *tp_recv = nullptr, *tp_g = nullptr, *tp_u = nullptr;
+    // ... peer-store gathers (tp.cuh): this rank's tagged arena, every
+    // rank's arena mapped here (IPC), the step counter of the tags, the
+    // gathers' abort flag; words of one layer's four gather slots
+    bool tp_p2p = false;
+    unsigned long long* tp_arena = nullptr;
+    TpPeers tp_peers = {};
+    uint32_t* tp_step = nullptr;
+    int* tp_abort = nullptr;
+    size_t tp_layer_words = 0;
     unsigned long long *tp_keys = nullptr, *tp_keys_all = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* trace = nullptr;    // phase timestamps of the last decode step
@@ -502,11 +511,27 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
     // tensor parallelism: this rank multiplies rows [R*N/P, (R+1)*N/P) of
     // every matrix and the slices are all-gathered
     const int P = m->comm ? m->comm->nranks : 1, R = m->comm ? m->comm->rank : 0;
-    auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd) {
+    // gather site k of layer l (k: 0 q|k|v, 1 wo, 2 gate|up, 3 down; the
+    // logits are site 4 L): peer stores into every rank's tagged slot, or an
+    // NCCL all-gather and an unshard kernel
+    const size_t mb = (size_t)m->max_batch;
+    auto site_off = [&](int site) -> size_t {
+        if (site == 4 * L) return (size_t)L * m->tp_layer_words;
+        const size_t o[4] = {0, mb * m->qkvw, mb * (m->qkvw + dim), mb * (m->qkvw + dim + hid)};
+        return (size_t)(site / 4) * m->tp_layer_words + o[site % 4];
+    };
+    auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd, int site) {
+        if (m->tp_p2p) {
+            const size_t off = site_off(site);
+            int r = tp_push_launch(m->tp_send, B, slice, segs, nseg, ldd, m->tp_peers, P, R, off, m->tp_step, site, s);
+            if (!r) r = tp_pull_launch(m->tp_arena + off, B, ldd, dst, m->tp_step, site, m->tp_abort, err, s);
+            return r;
+        }
         int r = tp_allgather(m->comm, m->tp_send, m->tp_recv, (size_t)B * slice, s);
         if (!r) r = tp_unshard_launch(m->tp_recv, P, B, slice, segs, nseg, dst, ldd, s);
         return r;
     };
+    if (P > 1 && m->tp_p2p && (rc = tp_step_launch(m->tp_step, s))) return rc;
     // embedding row (scaled for Gemma3); its records are not used here
     if ((rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x,
                                 m->rms_att, c.eps, m->prep_x, err, s, false)))
@@ -562,7 +587,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                  (rc = add_bias_launch(sq + qs + ks, sl, m->v_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s))))
                 return rc;
             const TpSeg segs[3] = {{qs, 0, 0}, {ks, qs, qw}, {ks, qs + ks, qw + kvd}};
-            if ((rc = gather(sl, segs, 3, m->qkv, m->qkvw))) return rc;
+            if ((rc = gather(sl, segs, 3, m->qkv, m->qkvw, 4 * l))) return rc;
         }
         {
             AttnParams a = {};
@@ -603,7 +628,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         } else {
             const TpSeg seg = {dim / P, 0, 0};
             if ((rc = mv_w(m, T_O, l, dim, qw, (int64_t)R * (dim / P), dim / P, m->xb, qw, m->tp_send, dim / P, B, s)) ||
-                (rc = gather(dim / P, &seg, 1, m->xb2, dim)))
+                (rc = gather(dim / P, &seg, 1, m->xb2, dim, 4 * l + 1)))
                 return rc;
         }
         // the attention residual, then the FFN RMSNorm
@@ -638,10 +663,10 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                        (rc = glu_launch(m->tp_send, m->tp_g, m->tp_u, hs, hs, B, gemma, s))) {
                 return rc;
             }
-            if ((rc = gather(hs, &hseg, 1, m->hb, hid)) ||
+            if ((rc = gather(hs, &hseg, 1, m->hb, hid, 4 * l + 2)) ||
                 (rc = mv_w(m, T_DOWN, l, dim, hid, (int64_t)R * (dim / P), dim / P, m->hb, hid, m->tp_send, dim / P, B,
                            s)) ||
-                (rc = gather(dim / P, &dseg, 1, m->xb2, dim)))
+                (rc = gather(dim / P, &dseg, 1, m->xb2, dim, 4 * l + 3)))
                 return rc;
         }
     }
@@ -664,7 +689,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         (rc = tp_argmax_keys_launch(m->tp_send, vs, vs, B, R * vs, m->tp_keys, s)) ||
         (rc = tp_allgather_u64(m->comm, m->tp_keys, m->tp_keys_all, (size_t)B, s)) ||
         (rc = tp_argmax_reduce_launch(m->tp_keys_all, P, B, m->am_out, s)) ||
-        (rc = gather(vs, &vseg, 1, m->logits, V)))
+        (rc = gather(vs, &vseg, 1, m->logits, V, 4 * L)))
         return rc;
     return BREW_OK;
 }
@@ -1239,6 +1264,10 @@ int after_step_check(brew_model_s* m, const char* where) {
         cudaMemset(m->kq_ctr, 0, m->kq_nctr * sizeof(int));
         cudaDeviceSynchronize();
     }
+    if (rc && m->tp_abort) {   // a peer-store gather that gave up
+        cudaMemset(m->tp_abort, 0, sizeof(int));
+        cudaDeviceSynchronize();
+    }
     if (rc && m->use_decode) {
         cudaMemset(m->dk_done, 0, sizeof(int));
         cudaMemset(m->dk_actr, 0, m->dk_nactr * sizeof(int));
@@ -1278,6 +1307,11 @@ namespace {
 void model_destroy(brew_model_s* m) {
     if (!m) return;
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    if (m->tp_p2p) {   // the other ranks' arenas mapped here
+        cudaDeviceSynchronize();
+        for (int r = 0; r < TP_MAX_RANKS; ++r)
+            if (m->tp_peers.p[r] && m->tp_peers.p[r] != m->tp_arena) cudaIpcCloseMemHandle(m->tp_peers.p[r]);
+    }
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_pin) cudaFreeHost(m->h_pin);
     if (m->prompt_d) cudaFree(m->prompt_d);
@@ -1506,6 +1540,39 @@ int brew_model_set_tp(brew_model m, brew_comm comm) {
                                     hs, c.dim, base, 2 * hs, hs, ctx().stream);
         }
         if (rc) return rc;
+    }
+    // peer-store gathers (tp.cuh): one tagged slot per gather site, every
+    // rank's arena mapped into this process through CUDA IPC, the handles
+    // exchanged over the communicator.  BREW_TP_NCCL=1 keeps the NCCL
+    // all-gathers.
+    if (P > 1 && P <= TP_MAX_RANKS && !getenv("BREW_TP_NCCL")) {
+        const int V = c.vocab_size, L = c.n_layers;
+        BREW_CHECK(4 * L + 1 <= 256, BREW_ERR_UNSUPPORTED, "peer gathers: %d layers (at most 63)", L);
+        m->tp_layer_words = (size_t)B * (m->qkvw + 2 * (size_t)c.dim + c.hidden_dim);
+        const size_t words = (size_t)L * m->tp_layer_words + (size_t)B * V;
+        if ((rc = dalloc(m, &m->tp_arena, words)) || (rc = dalloc(m, &m->tp_step, 1)) ||
+            (rc = dalloc(m, &m->tp_abort, 1)))
+            return rc;
+        cudaIpcMemHandle_t own;
+        BREW_CUDA(cudaIpcGetMemHandle(&own, m->tp_arena));
+        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+        float* hbuf = nullptr;   // [P][16] floats: the handles' bytes
+        if ((rc = dalloc(m, &hbuf, (size_t)(P + 1) * 16))) return rc;
+        BREW_CUDA(cudaMemcpy(hbuf + (size_t)P * 16, &own, 64, cudaMemcpyHostToDevice));
+        if ((rc = tp_allgather(comm, hbuf + (size_t)P * 16, hbuf, 16, ctx().stream))) return rc;
+        BREW_CUDA(cudaStreamSynchronize(ctx().stream));
+        std::vector<cudaIpcMemHandle_t> all(P);
+        BREW_CUDA(cudaMemcpy(all.data(), hbuf, (size_t)P * 64, cudaMemcpyDeviceToHost));
+        for (int r = 0; r < P; ++r) {
+            if (r == R) {
+                m->tp_peers.p[r] = m->tp_arena;
+                continue;
+            }
+            void* ptr = nullptr;
+            BREW_CUDA(cudaIpcOpenMemHandle(&ptr, all[r], cudaIpcMemLazyEnablePeerAccess));
+            m->tp_peers.p[r] = static_cast<unsigned long long*>(ptr);
+        }
+        m->tp_p2p = true;
     }
     BREW_CUDA(cudaStreamSynchronize(ctx().stream));
     m->comm = comm;

@@ -63,6 +63,55 @@ __global__ void unshard_kernel(const float* recv, int P, int B, int slice, TpSeg
     }
 }
 
+// Peer-store gather, push: one thread per pair of this rank's slice values
+// (segment lengths, offsets and ldd are even, so a pair never straddles a
+// segment and lands 16-byte aligned); the pair goes to every rank's slot.
+__global__ void tp_push_kernel(const float* send, int B, int slice, TpSeg s0, TpSeg s1, TpSeg s2, int nseg, int ldd,
+                               TpPeers peers, int P, int R, size_t site_off, const uint32_t* step, int site) {
+    const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int half = slice >> 1;
+    if (q >= (int64_t)B * half) return;
+    const int b = (int)(q / half), j = 2 * (int)(q - (int64_t)b * half);
+    const TpSeg segs[3] = {s0, s1, s2};
+    int k = 0;
+    while (k + 1 < nseg && j >= segs[k + 1].src_off) ++k;
+    const TpSeg sg = segs[k];
+    const int64_t pos = (int64_t)b * ldd + sg.dst_off + (int64_t)R * sg.n + (j - sg.src_off);
+    const uint64_t tag = (uint64_t)(*step * 256u + (uint32_t)site) << 32;
+    const float2 v = *reinterpret_cast<const float2*>(send + (int64_t)b * slice + j);
+    const uint64_t w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
+    for (int r = 0; r < P; ++r)
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(peers.p[r] + site_off + pos), "l"(w0),
+                     "l"(w1)
+                     : "memory");
+}
+
+// Peer-store gather, pull: one thread per pair of the unsharded row; polls
+// the pair in this rank's slot until both words carry the tag.  Bounded: 2 s,
+// or as soon as another pull gave up (abort), then a timeout is recorded.
+__global__ void tp_pull_kernel(const unsigned long long* slot, int B, int ldd, float* dst, const uint32_t* step,
+                               int site, int* abort, unsigned int* err) {
+    const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (int64_t)B * (ldd >> 1)) return;
+    const uint32_t tag = *step * 256u + (uint32_t)site;
+    const unsigned long long* p = slot + 2 * q;
+    unsigned long long w0, w1;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+        if ((uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag) break;
+        if ((it & 63u) == 0u && (global_ns() - t0 > 2000000000ull || ld_volatile_int(abort))) {
+            atomicOr(err, BREW_DEVERR_TIMEOUT_FULL);
+            atomicExch(abort, 1);
+            return;
+        }
+    }
+    const int64_t b = q / (ldd >> 1), i = 2 * (q - b * (ldd >> 1));
+    *reinterpret_cast<float2*>(dst + b * ldd + i) = make_float2(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1));
+}
+
+__global__ void tp_step_kernel(uint32_t* step) { *step += 1u; }
+
 __global__ void argmax_keys_kernel(const float* logits, int ld, int n, int row0, unsigned long long* keys) {
     const int b = blockIdx.x;
     const float* lr = logits + (int64_t)b * ld;
@@ -124,6 +173,43 @@ int tp_unshard_launch(const float* recv, int P, int B, int slice, const TpSeg* s
 int tp_argmax_keys_launch(const float* logits, int ld, int n, int B, int row0, unsigned long long* keys,
                           cudaStream_t stream) {
     argmax_keys_kernel<<<B, 1024, 0, stream>>>(logits, ld, n, row0, keys);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+int tp_push_launch(const float* send, int B, int slice, const TpSeg* segs, int nseg, int ldd, const TpPeers& peers,
+                   int P, int R, size_t site_off, const uint32_t* step, int site, cudaStream_t stream) {
+    BREW_CHECK(nseg >= 1 && nseg <= 3 && P >= 1 && P <= TP_MAX_RANKS && slice % 2 == 0 && ldd % 2 == 0 &&
+                   site_off % 2 == 0 && site >= 0 && site < 256,
+               BREW_ERR_INVALID_ARG, "peer gather: %d segments, %d ranks, slice %d, ldd %d", nseg, P, slice, ldd);
+    for (int k = 0; k < nseg; ++k)
+        BREW_CHECK(segs[k].n % 2 == 0 && segs[k].src_off % 2 == 0 && segs[k].dst_off % 2 == 0, BREW_ERR_INVALID_ARG,
+                   "peer gather: odd segment");
+    const TpSeg z = {0, slice, 0};
+    const int64_t pairs = (int64_t)B * (slice / 2);
+    if (pairs == 0) return BREW_OK;
+    tp_push_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, stream>>>(send, B, slice, segs[0], nseg > 1 ? segs[1] : z,
+                                                                     nseg > 2 ? segs[2] : z, nseg, ldd, peers, P, R,
+                                                                     site_off, step, site);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+int tp_pull_launch(const unsigned long long* slot, int B, int ldd, float* dst, const uint32_t* step, int site,
+                   int* abort, unsigned int* err, cudaStream_t stream) {
+    BREW_CHECK(ldd % 2 == 0 && site >= 0 && site < 256, BREW_ERR_INVALID_ARG, "peer gather: ldd %d", ldd);
+    const int64_t pairs = (int64_t)B * (ldd / 2);
+    if (pairs == 0) return BREW_OK;
+    tp_pull_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, stream>>>(slot, B, ldd, dst, step, site, abort, err);
+    BREW_CUDA(cudaGetLastError());
+    count_launch();
+    return BREW_OK;
+}
+
+int tp_step_launch(uint32_t* step, cudaStream_t stream) {
+    tp_step_kernel<<<1, 1, 0, stream>>>(step);
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;

@@ -31,6 +31,31 @@ struct TpSeg {
 // recv [P][B][slice] -> dst [B][ldd], per segment (up to 3).
 int tp_unshard_launch(const float* recv, int P, int B, int slice, const TpSeg* segs, int nseg, float* dst, int ldd,
                       cudaStream_t stream);
+
+// The peer-store gather.  Every rank holds a tagged arena with one slot per
+// gather site of a forward step ([B][ldd] words, (tag << 32) | float bits),
+// mapped into every other rank's address space (CUDA IPC).  A gather is
+// two launches: push writes this rank's slice into its place in every
+// rank's slot (system-scope 8-byte stores over NVLink), pull polls this
+// rank's own slot until every word carries the tag and writes the floats
+// unsharded.  tag = step * 256 + site, `step` a device counter advanced once
+// per forward on every rank, so no word of an earlier gather passes for this
+// one, and no slot is rewritten before every rank has read it (a rank starts
+// the next step only after the last gather of this one, which needs every
+// rank's push, and a rank pushes only after its own earlier pulls).
+constexpr int TP_MAX_RANKS = 8;
+struct TpPeers {
+    unsigned long long* p[TP_MAX_RANKS];   // every rank's arena (this rank's included)
+};
+// send [B][slice] -> the site's slot (word offset site_off) of every rank.
+int tp_push_launch(const float* send, int B, int slice, const TpSeg* segs, int nseg, int ldd, const TpPeers& peers,
+                   int P, int R, size_t site_off, const uint32_t* step, int site, cudaStream_t stream);
+// this rank's slot -> dst [B][ldd]; bounded wait (2 s, or another wait's
+// abort), then the error word records a timeout.
+int tp_pull_launch(const unsigned long long* slot, int B, int ldd, float* dst, const uint32_t* step, int site,
+                   int* abort, unsigned int* err, cudaStream_t stream);
+// step += 1 (once per forward, before its gathers)
+int tp_step_launch(uint32_t* step, cudaStream_t stream);
 // Per-row argmax keys of a logits slice whose first row is global row `row0`
 // (orderable: larger value first, then smaller index).
 int tp_argmax_keys_launch(const float* logits, int ld, int n, int B, int row0, unsigned long long* keys,
