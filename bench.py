@@ -536,14 +536,20 @@ def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True
     torch.cuda.set_stream(prev)
     dm.close()
     parity = None
+    parity_rel = None
     if check_parity and world > 1:
         ok = 1.0
         if rank == 0:   # the same seeded model unsharded on this GPU, same first step
             ref = DeviceModel.synthesize(cfg, SEED, max_batch=B)
             lg_1, _ = ref.forward(prompts[:, 0], np.zeros(B, np.int32), want_logits=True)
             ref.close()
-            ok = 1.0 if np.array_equal(lg_tp, lg_1) else 0.0
-        parity = bool(max_over_ranks(dist, ok) > 0.5) if dist is not None else bool(ok)
+            rel = float(max(np.linalg.norm(lg_tp[b].astype(np.float64) - lg_1[b]) /
+                            np.linalg.norm(lg_1[b].astype(np.float64)) for b in range(B)))
+            same = bool(np.array_equal(np.argmax(lg_tp, axis=1), np.argmax(lg_1, axis=1)))
+            ok = 1.0 if (rel <= 1e-5 and same) else 0.0
+            parity_rel = rel
+        # rank 0 decides: the minimum over ranks (the others report 1)
+        parity = bool(1.0 - max_over_ranks(dist, 1.0 - ok) > 0.5) if dist is not None else bool(ok)
     comm.close()
     value = B * steps / (ms / 1000.0)
     return {"value": value, "unit": "tok/s", "ms_per_step": ms / steps, "n_gpus": world, "steps": steps,
@@ -553,7 +559,10 @@ def tp_measure(rank, world, dist, dev, steps, warmup, B, plen, check_parity=True
                            if world > 1 and not os.environ.get("BREW_TP_NCCL") else
                            "NCCL all-gather per projection (q|k|v, wo, gate|up, down, logits) + argmax key reduction"),
             "parity": parity,
-            "parity_check": "rank 0: first-step logits of the sharded model == unsharded 1-GPU model, bit for bit"
+            "parity_rel_l2": parity_rel,
+            "parity_check": "rank 0: first-step logits of the sharded model within 1e-5 relative L2 of the unsharded "
+                            "1-GPU model, same argmax for every sequence (bit for bit with BREW_TP_EXACT=1, which "
+                            "splits K as on one GPU)"
                             if world > 1 else "single GPU (no sharding)",
             "model": cfg.name, "weight_bytes_per_step": cfg.decode_weight_bytes(),
             "setup_s": {"synthesize": round(synth_s, 2), "prefill": round(prefill_s, 2)}}

@@ -123,6 +123,10 @@ struct brew_model_s {
     // rank's arena mapped here (IPC), the step counter of the tags, the
     // gathers' abort flag; words of one layer's four gather slots
     bool tp_p2p = false;
+    // sharded K-quant matvecs split K for the rows they hold (all SMs busy),
+    // or, with BREW_TP_EXACT=1, as the whole family does on one GPU (the
+    // sharded logits then equal the one-GPU logits bit for bit)
+    bool tp_exact = false;
     unsigned long long* tp_arena = nullptr;
     TpPeers tp_peers = {};
     uint32_t* tp_step = nullptr;
@@ -464,7 +468,7 @@ KxRef kx_ref(const brew_model_s* m, int which, int l, int64_t rows, int K, int64
 // launch sums each row as the one-GPU launch does.
 int kq_run(brew_model_s* m, int type, const KxRef& r, int n, int K, const float* x, int ldx, float* y, int ldy, int B,
            cudaStream_t s, const uint8_t* rec = nullptr, const float* bias = nullptr) {
-    const int splits = kq_splits(K, r.basis);
+    const int splits = kq_splits(K, (m->comm && m->comm->nranks > 1 && !m->tp_exact) ? (int64_t)n : r.basis);
     if (rec) {
         BREW_CHECK(B <= KX_MAX_VECTORS, BREW_ERR_INVALID_ARG, "records of %d vectors", B);
         return kx_mma_launch(type, r.base, r.N, r.row0, n, K, rec, B, splits, m->kq_part, m->kq_ctr, bias, y, ldy,
@@ -1540,6 +1544,19 @@ int brew_model_set_tp(brew_model m, brew_comm comm) {
                                     hs, c.dim, base, 2 * hs, hs, ctx().stream);
         }
         if (rc) return rc;
+    }
+    // split-K scratch for the sharded launches' own splits
+    m->tp_exact = getenv("BREW_TP_EXACT") != nullptr;
+    if (P > 1 && !m->tp_exact && m->kq_part) {
+        const int hs = c.hidden_dim / P, sl = (qw + 2 * kvd) / P;
+        const int64_t shapes[5][2] = {{sl, c.dim}, {c.dim / P, qw}, {2 * hs, c.dim}, {c.dim / P, c.hidden_dim},
+                                      {c.vocab_size / P, c.dim}};
+        size_t need = 0;
+        for (const auto& sh : shapes) {
+            const int sp = kq_splits(sh[1], sh[0]);
+            if (sp > 1) need = std::max(need, (size_t)sp * KX_MAX_VECTORS * (size_t)((sh[0] + KX_TM - 1) / KX_TM * KX_TM));
+        }
+        if (need && (rc = dalloc(m, &m->kq_part, need))) return rc;
     }
     // peer-store gathers (tp.cuh): one tagged slot per gather site, every
     // rank's arena mapped into this process through CUDA IPC, the handles

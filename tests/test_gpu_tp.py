@@ -1,8 +1,11 @@
 """Tensor-parallel forward on 2 GPUs (skipped with fewer): each rank holds
-the same seeded model, shards it by rows over an NCCL communicator, and
-must (1) return the unsharded model's logits bit for bit (a row's sum does
-not depend on the split and the gathers copy), (2) match the oracle's
-logits within 1e-4 relative L2 and its greedy tokens exactly.
+the same seeded model, shards it by rows (peer-store gathers over the
+communicator), and must (1) return the unsharded model's logits: bit for
+bit for the K-quant model with BREW_TP_EXACT=1 (K split as on one GPU; the
+gathers copy), within 1e-6 relative L2 with the default per-shard K split
+(the Q8_0 model runs the persistent decode kernel unsharded, another
+summation order, and is checked against the oracle only); (2) match the
+oracle's logits within 1e-4 relative L2 and its greedy tokens exactly.
 """
 import os
 import socket
@@ -32,7 +35,9 @@ def _configs():
     kq = C.qwen25_7b().replace(dim=1024, hidden_dim=2048, n_heads=8, n_kv_heads=4, n_layers=3, vocab_size=4096,
                                seq_len=128)
     q8 = C.qwen3_1_7b().replace(n_layers=2, vocab_size=4096, seq_len=128)
-    return [("qwen2-kquant", kq, True), ("qwen3-q8_0", q8, False)]
+    # (name, config, BREW_TP_EXACT, against the unsharded model: "exact", "close" or None)
+    return [("qwen2-kquant-exact", kq, True, "exact"), ("qwen2-kquant", kq, False, "close"),
+            ("qwen3-q8_0", q8, False, None)]
 
 
 def _rank(rank, port, results):
@@ -53,9 +58,13 @@ def _rank(rank, port, results):
         dist.broadcast_object_list(box, src=0)
         comm = Communicator(box[0], WORLD, rank)
         out = {}
-        for name, cfg, exact in _configs():
+        for name, cfg, exact_env, vs_one in _configs():
             seed = 17
             dm = DeviceModel.synthesize(cfg, seed)
+            if exact_env:
+                os.environ["BREW_TP_EXACT"] = "1"
+            else:
+                os.environ.pop("BREW_TP_EXACT", None)
             dm.set_tp(comm)
             prompt = np.random.default_rng(seed).integers(0, cfg.vocab_size, 8).tolist()
             dm.reset()
@@ -73,8 +82,10 @@ def _rank(rank, port, results):
             om.close()
             for i in range(3):
                 assert _rel(lg_tp[i], lg_o[i]) < 1e-4, (name, i, _rel(lg_tp[i], lg_o[i]))
-                if exact:
+                if vs_one == "exact":
                     assert np.array_equal(lg_tp[i], lg_1[i]), (name, i)
+                elif vs_one == "close":
+                    assert _rel(lg_tp[i], lg_1[i]) < 1e-6, (name, i, _rel(lg_tp[i], lg_1[i]))
             assert toks_tp == toks_o, (name, toks_tp, toks_o)
             out[name] = "ok"
         results[rank] = out
@@ -99,5 +110,5 @@ def test_tp_two_gpus():
         for p in procs:
             p.join(timeout=600)
         got = dict(results)
-    want = {name: "ok" for name, _, _ in _configs()}
+    want = {name: "ok" for name, _, _, _ in _configs()}
     assert got == {0: want, 1: want}, got
