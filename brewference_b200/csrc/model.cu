@@ -524,17 +524,26 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
         const size_t o[4] = {0, mb * m->qkvw, mb * (m->qkvw + dim), mb * (m->qkvw + dim + hid)};
         return (size_t)(site / 4) * m->tp_layer_words + o[site % 4];
     };
-    auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd, int site) {
+    auto gather_from = [&](const float* src, int slice, const TpSeg* segs, int nseg, float* dst, int ldd, int site) {
         if (m->tp_p2p) {
             const size_t off = site_off(site);
-            int r = tp_push_launch(m->tp_send, B, slice, segs, nseg, ldd, m->tp_peers, P, R, off, m->tp_step, site, s);
+            int r = tp_push_launch(src, B, slice, segs, nseg, ldd, m->tp_peers, P, R, off, m->tp_step, site, s);
             if (!r) r = tp_pull_launch(m->tp_arena + off, B, ldd, dst, m->tp_step, site, m->tp_abort, err, s);
             return r;
         }
-        int r = tp_allgather(m->comm, m->tp_send, m->tp_recv, (size_t)B * slice, s);
+        int r = tp_allgather(m->comm, src, m->tp_recv, (size_t)B * slice, s);
         if (!r) r = tp_unshard_launch(m->tp_recv, P, B, slice, segs, nseg, dst, ldd, s);
         return r;
     };
+    auto gather = [&](int slice, const TpSeg* segs, int nseg, float* dst, int ldd, int site) {
+        return gather_from(m->tp_send, slice, segs, nseg, dst, ldd, site);
+    };
+    // attention sharded by kv head when the kv heads divide over the ranks:
+    // rank R's q|k|v rows are exactly its heads' q, k and v, so attention
+    // runs on them locally (its K/V cache holds only those heads) and the
+    // attention output is gathered instead of q|k|v
+    const bool shard_attn = P > 1 && c.n_kv_heads % P == 0;
+    const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
     if (P > 1 && m->tp_p2p && (rc = tp_step_launch(m->tp_step, s))) return rc;
     // embedding row (scaled for Gemma3); its records are not used here
     if ((rc = embed_prep_launch(c.type_embed, m->t[T_EMBED]->d, c.vocab_size, dim, m->tokens_d, B, gemma, m->x,
@@ -574,7 +583,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                 return rc;
         } else {
             // slices [q_R | k_R | v_R] per rank, gathered into q | k | v
-            const int qs = qw / P, ks = kvd / P, sl = qs + 2 * ks;
+            // (unless attention is sharded)
             float* sq = m->tp_send;
             if (m->kqp_qkv_tp) {   // this rank's q|k|v rows: one launch, the bias in its epilogue
                 const KxRef r = {m->kqp_qkv_tp + (size_t)l * kx_bytes(c.type_q, sl, dim), sl, 0, qw + 2 * kvd};
@@ -591,7 +600,7 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
                  (rc = add_bias_launch(sq + qs + ks, sl, m->v_bias + (int64_t)l * kvd + (int64_t)R * ks, ks, B, s))))
                 return rc;
             const TpSeg segs[3] = {{qs, 0, 0}, {ks, qs, qw}, {ks, qs + ks, qw + kvd}};
-            if ((rc = gather(sl, segs, 3, m->qkv, m->qkvw, 4 * l))) return rc;
+            if (!shard_attn && (rc = gather(sl, segs, 3, m->qkv, m->qkvw, 4 * l))) return rc;
         }
         {
             AttnParams a = {};
@@ -624,7 +633,21 @@ int enqueue_forward_unfused(brew_model_s* m, int B, bool with_classifier, cudaSt
             a.nchunk = m->nchunk;
             a.prep_out = nullptr;   // the matvecs of this forward make their own x records
             a.err = err;
+            if (shard_attn) {   // this rank's heads; the cache holds [layer][position][its kv heads]
+                a.n_heads = c.n_heads / P;
+                a.n_kv = c.n_kv_heads / P;
+                a.q = m->tp_send;
+                a.k = m->tp_send + qs;
+                a.v = m->tp_send + qs + ks;
+                a.ldq = a.ldkv = sl;
+                a.kcache = m->kc + (int64_t)l * c.seq_len * ks;
+                a.vcache = m->vc + (int64_t)l * c.seq_len * ks;
+                a.xb = m->tp_g;
+                a.ldxb = qs;
+            }
             if ((rc = attn_launch(a, s, false))) return rc;
+            const TpSeg xseg = {qs, 0, 0};
+            if (shard_attn && (rc = gather_from(m->tp_g, qs, &xseg, 1, m->xb, qw, 4 * l))) return rc;
         }
         if (P == 1) {
             if ((rc = mv_w(m, T_O, l, dim, qw, 0, dim, m->xb, qw, m->xb2, dim, B, s)))
@@ -1491,7 +1514,7 @@ int brew_model_set_tp(brew_model m, brew_comm comm) {
     const int B = m->max_batch;
     const int slice = std::max(std::max((qw + 2 * kvd) / P, c.dim / P), std::max(c.hidden_dim / P, c.vocab_size / P));
     if ((rc = dalloc(m, &m->tp_send, (size_t)B * slice)) || (rc = dalloc(m, &m->tp_recv, (size_t)P * B * slice)) ||
-        (rc = dalloc(m, &m->tp_g, (size_t)B * (c.hidden_dim / P))) ||
+        (rc = dalloc(m, &m->tp_g, (size_t)B * (std::max(c.hidden_dim, qw) / P))) ||   // also a sharded attention's output
         (rc = dalloc(m, &m->tp_u, (size_t)B * (c.hidden_dim / P))) || (rc = dalloc(m, &m->tp_keys, (size_t)B)) ||
         (rc = dalloc(m, &m->tp_keys_all, (size_t)P * B)))
         return rc;
