@@ -284,13 +284,19 @@ BREW_API int brew_model_free(brew_model m);
 /* ---- tensor parallelism (one process per GPU of a box) --------------------
  * Every matrix is split by rows over the ranks of a communicator: rank r of P
  * multiplies rows [r*N/P, (r+1)*N/P) of each N-row matrix and the slices are
- * all-gathered with NCCL after each projection (q|k|v, wo, gate|up, down,
- * classifier; the argmax is reduced over the ranks' (value, index) keys).
- * Attention, norms and residuals are replicated, so every rank ends a step
- * with the full activations, and each output row is the one-GPU row: the
- * sharded forward returns the one-GPU logits bit for bit.  N must be a
- * multiple of P for every matrix.  The row split is the one the reference's
- * matvec parallelises over (Linear.java:51-64, rows of `out`). */
+ * gathered after each projection (q|k|v or the attention output, wo,
+ * gate|up, down, classifier; the argmax is reduced over the ranks' (value,
+ * index) keys).  The gathers are peer stores into every rank's tagged slots
+ * through CUDA IPC over NVLink (BREW_TP_NCCL=1: NCCL all-gathers instead).
+ * Attention is sharded by kv head when the kv heads divide over the ranks
+ * (each rank's q|k|v rows are its heads), else replicated; norms and
+ * residuals are replicated, so every rank ends a step with the full
+ * activations.  The K-quant matvecs split K for each rank's own rows, so the
+ * logits match the one-GPU logits to rounding; with BREW_TP_EXACT=1 (read by
+ * brew_model_set_tp) they split K as on one GPU and every output row is the
+ * one-GPU row bit for bit.  N must be a multiple of P for every matrix.  The
+ * row split is the one the reference's matvec parallelises over
+ * (Linear.java:51-64, rows of `out`). */
 typedef struct brew_comm_s* brew_comm;
 /* Rows [r0, r1) of an N-row matrix that rank `rank` of `nranks` owns. */
 BREW_API int brew_tp_rows(int64_t rows, int32_t nranks, int32_t rank, int64_t* r0, int64_t* r1);
