@@ -802,8 +802,9 @@ def run_gpu(args):
                    "positions": [args.prompt_len + args.warmup, args.prompt_len + args.warmup + args.steps - 1],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (1.83 GB of weights per step vs 126 MB L2)"},
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
-                "call": "brew_model_forward per token, host token/position in, host argmax out"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                "call": "brew_model_forward per token, host token/position in (one 8-byte copy), host argmax out "
+                        "with the device error word (4 + 4 bytes)"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": profiled_traffic(TRAFFIC_PROFILE), "peak_kind": peak_kind,

@@ -371,8 +371,9 @@ int alloc_state(brew_model_s* m) {
     if ((rc = dalloc(m, &m->am_key, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->am_ctr, (size_t)B))) return rc;
     if ((rc = dalloc(m, &m->am_out, (size_t)B))) return rc;
-    if ((rc = dalloc(m, &m->tokens_d, (size_t)B))) return rc;
-    if ((rc = dalloc(m, &m->pos_d, (size_t)B))) return rc;
+    // tokens and positions side by side: one upload per forward call
+    if ((rc = dalloc(m, &m->tokens_d, (size_t)2 * B))) return rc;
+    m->pos_d = m->tokens_d + B;
     if ((rc = dalloc(m, &m->gen_d, (size_t)c.seq_len + 1))) return rc;
     if (uses_kquants(c) && (rc = alloc_unfused(m))) return rc;
     m->h_pin_cap = std::max(4 * B, 64);
@@ -1696,17 +1697,24 @@ int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos, 
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(api_mutex());
     cudaStream_t s = ctx().stream;
+    // pinned staging: [tokens | positions] as laid out on the device (one
+    // upload), then the argmax ids and the device error word (read back
+    // with the ids: the error path runs only when it is set)
+    const int mb = m->max_batch;
     int32_t* hp = m->h_pin;
     memcpy(hp, tokens, batch * sizeof(int32_t));
-    memcpy(hp + batch, pos, batch * sizeof(int32_t));
-    BREW_CUDA(cudaMemcpyAsync(m->tokens_d, hp, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    BREW_CUDA(cudaMemcpyAsync(m->pos_d, hp + batch, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    memcpy(hp + mb, pos, batch * sizeof(int32_t));
+    BREW_CUDA(cudaMemcpyAsync(m->tokens_d, hp, (size_t)(mb + batch) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
     if ((rc = launch_forward(m, batch, true, s))) return rc;
     if (logits)
         BREW_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
-    if (argmax) BREW_CUDA(cudaMemcpyAsync(hp + 2 * batch, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    if (argmax) BREW_CUDA(cudaMemcpyAsync(hp + 2 * mb, m->am_out, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    int32_t* herr = hp + 3 * mb;
+    *herr = 0;
+    if (ctx().err_word) BREW_CUDA(cudaMemcpyAsync(herr, ctx().err_word, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     BREW_CUDA(cudaStreamSynchronize(s));
-    if (argmax) memcpy(argmax, hp + 2 * batch, batch * sizeof(int32_t));
+    if (argmax) memcpy(argmax, hp + 2 * mb, batch * sizeof(int32_t));
+    if (*herr == 0) return BREW_OK;
     return after_step_check(m, "brew_model_forward");
 }
 
