@@ -13,7 +13,7 @@ than the 126 MB L2, so no L2 flush is needed between steps.
 Printed JSON line (rank 0):
   value      decode tok/s, device-resident, CUDA events on the launching stream
   e2e        the same metric through the C ABI call a host caller makes per
-             token (brew_model_forward: token+position H2D, argmax D2H)
+             token (brew_model_forward: token+position in, argmax id out)
   roofline   the dominant kernel, the persistent decode kernel (one launch
              per token): weight + KV bytes per step over its time, against
              the measured HBM copy peak; `traffic` is the DRAM bytes per
@@ -803,8 +803,9 @@ def run_gpu(args):
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (1.83 GB of weights per step vs 126 MB L2)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
-                "call": "brew_model_forward per token, host token/position in (one 8-byte copy), host argmax out "
-                        "with the device error word (4 + 4 bytes)"},
+                "call": "brew_model_forward per token: host token and position in (8 bytes, launch parameters of "
+                        "the decode kernel), host argmax id out with the device error word (4 + 4 bytes, written by "
+                        "the kernel into mapped pinned host memory)"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": profiled_traffic(TRAFFIC_PROFILE), "peak_kind": peak_kind,

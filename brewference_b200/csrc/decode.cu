@@ -344,7 +344,7 @@ __device__ bool prep_phase(const DecodeParams& P, int mode, const u64* src, int 
     for (int b = 0; b < P.batch; ++b) {
         float ss = 0.0f;
         if (mode == SRC_EMBED) {
-            int tok = P.tokens[b];
+            int tok = P.use_imm ? P.tok_imm : P.tokens[b];
             if (tok < 0 || tok >= P.vocab) {
                 if (threadIdx.x == 0) atomicOr(P.err, BREW_DEVERR_BAD_TOKEN);
                 tok = 0;
@@ -775,7 +775,7 @@ __shared__ int s_attg[DK_MAX_BATCH][2][3];
 __shared__ int s_item0[3];
 
 __device__ __forceinline__ void attn_geometry(const DecodeParams& P, int b, int windowed, int* g) {
-    const int pos = b < P.batch ? P.pos[b] : -1;
+    const int pos = b < P.batch ? (P.use_imm ? P.pos_imm : P.pos[b]) : -1;
     g[0] = g[1] = g[2] = 0;
     if (pos < 0 || pos >= P.seq_len) return;
     const int nch = P.nchunk;
@@ -1398,7 +1398,7 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
         int* nxt = P.attn_ctr + (int)(par ^ 1u) * n;
         for (int i = tid; i < n; i += blockDim.x) nxt[i] = 0;
     }
-    if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? P.pos[tid] : -1;
+    if (tid < DK_MAX_BATCH) s_pos[tid] = tid < P.batch ? (P.use_imm ? P.pos_imm : P.pos[tid]) : -1;
     if (tid < 5) {
         const int qw = P.n_heads * P.hd, kvd = P.n_kv * P.hd;
         const int tiles = tid == PH_QKV ? (qw + 2 * kvd) / 16
@@ -1608,6 +1608,11 @@ __global__ void __launch_bounds__(DK_CT + 32, 1) decode_kernel(const __grid_cons
         if (tid == 0) {
             *P.done = 0;
             *P.seq = ep;
+            if (P.host_out) {   // id first, then the error word: the host waits on the latter
+                P.host_out[0] = P.am_out[0];
+                __threadfence_system();
+                P.host_out[1] = (int32_t)*reinterpret_cast<volatile unsigned int*>(P.err);
+            }
         }
     }
 }

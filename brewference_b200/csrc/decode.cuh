@@ -71,6 +71,12 @@ struct alignas(64) DecodeParams {
     unsigned long long* am_key;
     int32_t* am_out;
     const int32_t *tokens, *pos;
+    // One-sequence calls from the host may pass the token and position as
+    // launch parameters instead (use_imm = 1): no upload precedes the launch.
+    int use_imm, tok_imm, pos_imm;
+    // optional mapped pinned host memory: the last CTA writes [0] the argmax
+    // id and then [1] the device error word, so a host caller needs no copy
+    int32_t* host_out;
     unsigned int* seq;                  // epoch of the last completed launch
     int* done;                          // CTAs done with this launch (the last one finishes the step)
     int* abort;

@@ -85,6 +85,8 @@ struct brew_model_s {
     int sess_generated = 0;                  // ids recorded in gen_d since prefill
     int32_t* h_pin = nullptr;                // pinned staging (tokens, pos, argmax)
     int h_pin_cap = 0;
+    int32_t* h_res = nullptr;                // mapped pinned [argmax id, device error word] of the decode kernel
+    int32_t* h_res_dev = nullptr;            // ... its device address
     // persistent decode kernel (batch <= DK_MAX_BATCH)
     bool use_decode = false;
     DecodeParams dp;
@@ -1188,6 +1190,8 @@ int setup_decode(brew_model_s* m) {
     if ((rc = dalloc(m, &m->abort_flag, 1))) return rc;
     if ((rc = dalloc(m, &m->dk_seq, 1))) return rc;
     if ((rc = dalloc(m, &m->dk_done, 1))) return rc;
+    BREW_CUDA(cudaHostAlloc(&m->h_res, 2 * sizeof(int32_t), cudaHostAllocMapped));
+    BREW_CUDA(cudaHostGetDevicePointer((void**)&m->h_res_dev, m->h_res, 0));
     const float base0 = arch_rope_base(c.arch, c.rope_base, false);   // global / only table
     const float base1 = arch_rope_base(c.arch, c.rope_base, true);    // Gemma local layers
     const float scale = c.rope_scale > 0.0f ? c.rope_scale : 1.0f;
@@ -1342,6 +1346,7 @@ void model_destroy(brew_model_s* m) {
     }
     for (void* p : m->allocs) cudaFree(p);
     if (m->h_pin) cudaFreeHost(m->h_pin);
+    if (m->h_res) cudaFreeHost(m->h_res);
     if (m->prompt_d) cudaFree(m->prompt_d);
     if (m->owns_tensors)
         for (int i = 0; i < T_COUNT; ++i)
@@ -1697,6 +1702,26 @@ int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos, 
     if (rc) return rc;
     std::lock_guard<std::mutex> lk(api_mutex());
     cudaStream_t s = ctx().stream;
+    if (m->use_decode && batch == 1 && !logits && m->h_res) {
+        // one sequence, argmax only: the token and position travel as launch
+        // parameters and the kernel's last CTA writes the id and the error
+        // word into mapped pinned memory, so the call is one launch and one
+        // synchronize (no copy either way)
+        DecodeParams dp = m->dp;
+        dp.use_imm = 1;
+        dp.tok_imm = tokens[0];
+        dp.pos_imm = pos[0];
+        dp.host_out = m->h_res_dev;
+        volatile int32_t* hr = m->h_res;
+        hr[0] = -1;
+        hr[1] = -1;   // stays -1 when the kernel stops early
+        if ((rc = decode_launch(dp, s))) return rc;
+        BREW_CUDA(cudaStreamSynchronize(s));
+        const int32_t id = hr[0], ew = hr[1];
+        if (argmax) argmax[0] = id;
+        if (ew == 0) return BREW_OK;
+        return after_step_check(m, "brew_model_forward");
+    }
     // pinned staging: [tokens | positions] as laid out on the device (one
     // upload), then the argmax ids and the device error word (read back
     // with the ids: the error path runs only when it is set)

@@ -162,3 +162,35 @@ def test_long_context_attention_rounds(device, arch, dims, plen):
     assert rel(lg[0], ref) < LOGIT_TOL, rel(lg[0], ref)
     assert dm.generate(prompt, 16) == want
     dm.close()
+
+
+@pytest.mark.parametrize("arch", [C.ARCH_QWEN3, C.ARCH_GEMMA2])
+def test_forward_argmax_only_call(device, arch):
+    """brew_model_forward without a logits buffer, one sequence: the token
+    and position go to the decode kernel as launch parameters and the id
+    comes back through mapped host memory.  Calls without and with logits
+    alternate on one model; every step's id must equal the oracle's argmax
+    (and the device argmax of the logits on the logits steps)."""
+    cfg = small(arch)
+    seed = 31 + arch
+    dm = DeviceModel.synthesize(cfg, seed)
+    om = oracle.OracleModel(cfg, seed)
+    dm.reset()
+    om.reset()
+    toks = np.random.default_rng(seed).integers(0, cfg.vocab_size, 24).tolist()
+    for i, t in enumerate(toks):
+        ref = om.forward(t, i)
+        if i % 3 == 2:
+            lg, am = dm.forward([t], [i])
+            assert rel(lg[0], ref) < LOGIT_TOL, (i, rel(lg[0], ref))
+            assert am[0] == int(np.argmax(lg[0])), i
+        else:
+            lg, am = dm.forward([t], [i], want_logits=False)
+            assert lg is None
+        assert am[0] == oracle.argmax(ref), i
+    with pytest.raises(Exception):   # rejected on the host, before any launch
+        dm.forward([cfg.vocab_size], [len(toks)], want_logits=False)
+    _, am = dm.forward([toks[0]], [len(toks)], want_logits=False)
+    assert 0 <= am[0] < cfg.vocab_size
+    dm.close()
+    om.close()
