@@ -712,8 +712,37 @@ def run_gpu(args):
                           "GBps": alg / (kms / 1000.0) / 1e9, "peak": peak, "peak_kind": peak_kind}), flush=True)
         dm.close()
         return 0
+    if args.gemm_only:
+        # the prefill GEMM alone on the gate|up-sized projection (profiling
+        # entry: activation limb split + tcgen05 GEMM per run, layers rotated)
+        T = args.gemm_tokens
+        wb, ms = time_gemm(dm.tensor(C.W_GATE), cfg.dim, cfg.hidden_dim, cfg.n_layers, T, iters=args.steps)
+        tflops = 2.0 * cfg.hidden_dim * cfg.dim * T / (ms / 1000.0) / 1e12
+        bf16_peak = measured_peaks(kind="bf16_tflops")[0]
+        print(json.dumps({"kernel": f"gemm_limbs_kernel + gemm_q8_kernel, Q8_0 {cfg.hidden_dim}x{cfg.dim}, {T} tokens",
+                          "us_per_run": ms * 1000.0, "TFLOPs_equivalent": tflops,
+                          "tensor_frac": tflops / bf16_peak if bf16_peak else None,
+                          "weight_GBps": wb / (ms / 1000.0) / 1e9}), flush=True)
+        dm.close()
+        return 0
     rng = np.random.default_rng(SEED)
     prompt = rng.integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+    if args.prefill_only:
+        # the batched prefill of the prompt, twice (profiling entry: the
+        # second prefill's launches follow the first's one-time set-up)
+        dm.set_prefill(PREFILL_BATCHED)
+        stream = torch.cuda.Stream()   # the library enqueues the prefill on it
+        ms = []
+        for _ in range(2):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dm.prefill(prompt, stream.cuda_stream)
+            e1.record(stream)
+            stream.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        print(json.dumps({"prefill_only": True, "prompt": args.prompt_len, "ms": ms}), flush=True)
+        dm.close()
+        return 0
     # a dedicated stream: the library enqueues the decode on it and the CUDA
     # events below are recorded on it
     stream = torch.cuda.Stream()
@@ -865,6 +894,10 @@ def main():
     ap.add_argument("--tp-steps", type=int, default=16, help="timed steps of the tensor-parallel sub-record")
     ap.add_argument("--tp-prompt-len", type=int, default=256, help="prompt tokens of the tensor-parallel sub-record")
     ap.add_argument("--kernel-only", action="store_true", help="time the decode matvec kernel alone")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time the prefill GEMM alone (gate|up-sized projection, --gemm-tokens tokens, --steps runs)")
+    ap.add_argument("--gemm-tokens", type=int, default=512, help="--gemm-only: token vectors per GEMM")
+    ap.add_argument("--prefill-only", action="store_true", help="batched prefill of the prompt, twice, then exit")
     ap.add_argument("--profile-decode", action="store_true", help="prompt + a few decode steps, no timing")
     ap.add_argument("--layers", type=int, default=0, help="--profile-decode / --tp: layers of the model (default: all)")
     ap.add_argument("--vocab", type=int, default=0, help="--profile-decode: vocabulary size (default: the config's)")

@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
 #pragma unroll
         for (int p = 0; p < 8; ++p) acc[p] = 0ull;
         const uint64_t negc = f2_packf(-TC_MAGIC_F, -TC_MAGIC_F);
+        const uint64_t neg257c = f2_packf(-257.0f * TC_MAGIC_F, -257.0f * TC_MAGIC_F);
         const uint64_t k256 = f2_packf(256.0f, 256.0f), k65536 = f2_packf(65536.0f, 65536.0f);
         // this column's weight scale and token scales, loaded one column ahead
         uint16_t dbits = wd[row];
@@ -223,10 +224,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_q8_kernel(const int8_t* 
                     const int p = 4 * e + pp;
                     const float4 sg = sn[p >> 1];
                     const uint64_t s2 = (p & 1) ? f2_packf(sg.z, sg.w) : f2_packf(sg.x, sg.y);
+                    // (lo + mid 2^8) + hi 2^16 from the three magic-biased
+                    // sums: hi - c is exact; mid 2^8 + lo rounds once (to a
+                    // multiple of 2^8 near 257 c: error <= 2^7), and taking
+                    // 257 c = 771 * 2^22 from it is exact
                     const uint64_t hi = f2_add(f2_pack(v[6 * pp], v[6 * pp + 1]), negc);
-                    const uint64_t mid = f2_add(f2_pack(v[6 * pp + 2], v[6 * pp + 3]), negc);
-                    const uint64_t lo = f2_add(f2_pack(v[6 * pp + 4], v[6 * pp + 5]), negc);
-                    const uint64_t val = f2_fma(hi, k65536, f2_fma(mid, k256, lo));   // (lo + mid 2^8) + hi 2^16
+                    const uint64_t ml = f2_add(f2_fma(f2_pack(v[6 * pp + 2], v[6 * pp + 3]), k256,
+                                                      f2_pack(v[6 * pp + 4], v[6 * pp + 5])),
+                                               neg257c);
+                    const uint64_t val = f2_fma(hi, k65536, ml);
                     acc[p] = f2_fma(val, f2_mul(d2, s2), acc[p]);
                 }
             }
