@@ -22,6 +22,24 @@ __device__ __forceinline__ void kx_scale_min(const uint8_t* sb, int s, int& sc, 
     }
 }
 
+// The 8 sub-block mins m_j of a Q4_K block (its 12 scale bytes at sb), one
+// byte each: m_0 .. m_3 in x, m_4 .. m_7 in y.
+__device__ __forceinline__ uint2 kx_mins(const uint8_t* sb) {
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        int sc, mj;
+        kx_scale_min(sb, j, sc, mj);
+        w[j >> 2] |= (uint32_t)mj << (8 * (j & 3));
+    }
+    return make_uint2(w[0], w[1]);
+}
+
+// Byte k of w as a float (exact: the bits of 2^23 + byte, minus 2^23).
+__device__ __forceinline__ float kx_byte_f(uint32_t w, int k) {
+    return __uint_as_float(0x4B000000u | ((w >> (8 * k)) & 255u)) - 8388608.0f;
+}
+
 // Q6_K expanded copy: one thread per (row, 32-element sub-block j of
 // super-block sb).
 __global__ void kx_pack_kernel(const uint8_t* w, int64_t rows, int K, uint8_t* base, int64_t pitch, int64_t row_off,
@@ -109,7 +127,7 @@ constexpr int KX_STAGE = KX_B + 10 * 96 * 32;   // 100352
 constexpr int KX_SMEM = 2 * KX_STAGE + 128;
 constexpr int KX_EPI = 16;                      // epilogue warps: 4 per tensor-memory lane quadrant
 constexpr int KX_THREADS = 64 + 32 * KX_EPI;    // loader warp, MMA warp, epilogue warps
-constexpr int KX_TMEM_COLS = 512;               // h, l, min-Xl, min-Xh accumulators at 0, 128, 256, 384
+constexpr int KX_TMEM_COLS = 512;               // two sets of the h, l accumulators: at 0, 128 and 256, 384
 // Q4_K (compact stream): one expanded area (h, l, min tile, zero area at the
 // offsets above), then two stages of records and two of raw block runs
 // (128 rows x 144 bytes), then the barriers.
@@ -182,15 +200,18 @@ __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned
 //               is single: the next expansion starts after the readout,
 //               which waits for the MMAs;
 //   warp 1      one thread issues, per sub-block j, the MMAs h_j x B_j and
-//               l_j x B_j into the h and l accumulators (Q4_K: then the min
-//               tile against the two min-term tiles), all onto the preset
+//               l_j x B_j into the h and l accumulators of set i % 2 (two
+//               sets, 256 tensor-memory columns apart), all onto the preset
 //               magic value, and commits to the stage's "empty" and the
-//               accumulators' "full" barriers;
-//   warps 2-17  read the four accumulators back (warp w: lanes 32 (w % 4),
-//               a quarter of the columns), reset them, release them, and add
-//               s_v (d (F h + l) - dmin (m1 + 256 m2)) to fp32 accumulators
-//               per (vector, limb).
-// The copies of the next super-block overlap the MMAs and the readout.
+//               set's "full" barriers;
+//   warps 2-17  (Q4_K) expand super-block i + 1 as soon as the MMAs of i
+//               have read the expanded area, then read set i back (warp w:
+//               lanes 32 (w % 4), a quarter of the columns), reset and
+//               release it, and add s_v d (F h + l) to fp32 accumulators per
+//               (vector, limb), and -dmin sum_j m_j X_j (the records' fp32
+//               sub-block sums) to one per vector.
+// The copies of the next super-block overlap the MMAs and the readout, and
+// the MMAs of super-block i + 1 overlap the readout of i.
 template <int TYPE, int NVG>
 __global__ void __launch_bounds__(KX_THREADS, 1)
     kx_mma_kernel(const uint8_t* base, int64_t pitch, int64_t row0, int n, int K, size_t m_off, size_t f_off,
@@ -199,13 +220,13 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
     constexpr bool Q4 = TYPE == BREW_TYPE_Q4_K;
     constexpr int NVP = 16 * NVG, NC = 3 * NVP;   // vectors and limb columns of the MMA
     constexpr int CW = NC / (KX_EPI / 4), TPW = CW / 3;   // columns and vectors per epilogue warp
-    constexpr int NACC = Q4 ? 4 : 2;
+    constexpr int NACC = 2;   // h, l
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (Q4 ? KC_BAR : 2 * KX_STAGE));
     uint64_t* empty = full + 2;
-    uint64_t* tfull = empty + 2;
-    uint64_t* tempty = tfull + 1;
-    uint64_t* xready = tempty + 1;   // Q4_K: the expanded tiles are in place
+    uint64_t* tfull = empty + 2;     // [2] per accumulator set
+    uint64_t* tempty = tfull + 2;    // [2]
+    uint64_t* xready = tempty + 2;   // Q4_K: the expanded tiles are in place
     uint32_t* tslot = reinterpret_cast<uint32_t*>(xready + 1);
     __shared__ int s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -224,8 +245,10 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], Q4 ? 1 + KX_EPI : 1);   // Q4_K: the MMAs' commit and every expanding warp
         }
-        mbar_init(tfull, 1);
-        mbar_init(tempty, KX_EPI);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], KX_EPI);
+        }
         mbar_init(xready, KX_EPI);
         fence_mbar_init();
     }
@@ -243,7 +266,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             const uint64_t pol = l2_evict_first_policy();
             const uint8_t* hp = base;
             const uint8_t* lp = base + (size_t)K * pitch;
-            const uint32_t bbytes = (Q4 ? 10 : 8) * NC * 32;
+            const uint32_t bbytes = 8 * NC * 32;   // the 8 limb tiles
             const uint32_t bytes = 16 * 4096 + (Q4 ? 2048 : 0) + bbytes;
             int it = 0;
             for (int sb = sb0; sb < sb1; ++sb, ++it) {
@@ -278,7 +301,9 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
                 const int st = it & 1;
                 if (!kx_wait(&full[st], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL)) break;
                 if (Q4 && !kx_wait(xready, it & 1, err, BREW_DEVERR_TIMEOUT_FULL)) break;
-                if (!kx_wait(tempty, it & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
+                const int b = it & 1;
+                if (!kx_wait(&tempty[b], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_EMPTY)) break;
+                const uint32_t tb = tmem + 256 * b;
                 tc_fence_after();
                 // Q4_K: the expanded tiles at 0, the stage's records apart
                 const uint32_t s0 = smem_u32(smem + (Q4 ? 0 : st * KX_STAGE));
@@ -286,16 +311,11 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const uint64_t bd = umma_desc_k(sr + j * NC * 32, 128, 256);
-                    umma_s8(tmem, umma_desc_k(s0 + KX_AH + j * 4096, 2048, 128), bd, idesc, 1u);
-                    umma_s8(tmem + 128, umma_desc_k(s0 + KX_AL + j * 4096, 2048, 128), bd, idesc, 1u);
-                }
-                if (Q4) {
-                    const uint64_t ad = umma_desc_k(s0 + KX_AM, 2048, 128);
-                    umma_s8(tmem + 256, ad, umma_desc_k(sr + 8 * NC * 32, 128, 256), idesc, 1u);
-                    umma_s8(tmem + 384, ad, umma_desc_k(sr + 9 * NC * 32, 128, 256), idesc, 1u);
+                    umma_s8(tb, umma_desc_k(s0 + KX_AH + j * 4096, 2048, 128), bd, idesc, 1u);
+                    umma_s8(tb + 128, umma_desc_k(s0 + KX_AL + j * 4096, 2048, 128), bd, idesc, 1u);
                 }
                 umma_commit(&empty[st]);
-                umma_commit(tfull);
+                umma_commit(&tfull[b]);
             }
         }
         __syncwarp();
@@ -306,16 +326,21 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         const int64_t frow = r0 + 32 * q + lane;             // row within the family (< pitch)
         const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + CW * hh;
 #pragma unroll
-        for (int a = 0; a < NACC; ++a) {   // exactly this warp's CW columns (a multiple of 4)
+        for (int b = 0; b < 2; ++b)
 #pragma unroll
-            for (int c = 0; c + 8 <= CW; c += 8) tmem_st8_const(tq + 128 * a + c, TC_MAGIC);
-            if (CW % 8) tmem_st4_const(tq + 128 * a + CW - 4, TC_MAGIC);
-        }
+            for (int a = 0; a < NACC; ++a) {   // exactly this warp's CW columns (a multiple of 4)
+#pragma unroll
+                for (int c = 0; c + 8 <= CW; c += 8) tmem_st8_const(tq + 256 * b + 128 * a + c, TC_MAGIC);
+                if (CW % 8) tmem_st4_const(tq + 256 * b + 128 * a + CW - 4, TC_MAGIC);
+            }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty);
-        uint64_t acc[TPW / 2][3];   // vector pairs x limbs (hi, mid, lo)
+        if (lane == 0) {
+            mbar_arrive(&tempty[0]);
+            mbar_arrive(&tempty[1]);
+        }
+        uint64_t acc[TPW / 2][3];   // vector pairs x limbs (hi, mid, lo; Q4_K's min term joins lo)
 #pragma unroll
         for (int p = 0; p < TPW / 2; ++p) acc[p][0] = acc[p][1] = acc[p][2] = 0ull;
         const uint64_t negc = f2_packf(-TC_MAGIC_F, -TC_MAGIC_F);
@@ -323,6 +348,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         const uint64_t k256 = f2_packf(256.0f, 256.0f), k65536 = f2_packf(65536.0f, 65536.0f);
         const float2* fpl = reinterpret_cast<const float2*>(base + f_off);
         const float* scl = reinterpret_cast<const float*>(rec + (int64_t)KSB * rec_tile);
+        const float* xsum = scl + (int64_t)KSB * NVP;   // [sb][NVP][8] fp32 sub-block sums
         float2 fr = (!Q4 && sb0 < sb1) ? __ldg(fpl + (int64_t)sb0 * pitch + frow) : make_float2(0.0f, 0.0f);
         // the vectors' scales of a super-block, loaded one super-block ahead
         // (their L2 round trip overlaps the previous readout)
@@ -332,29 +358,53 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             for (int g = 0; g < TPW / 4; ++g)
                 svn[g] = __ldg(reinterpret_cast<const float4*>(scl + (int64_t)sbl * NVP + TPW * hh) + g);
         };
-        if (sb0 < sb1) load_scales(sb0);
-        int it = 0;
-        for (int sb = sb0; sb < sb1; ++sb, ++it) {
-            if (Q4) {   // expand this super-block's raw run, keep the readout row's (d, dmin)
-                const int st = it & 1;
-                bool okx = kx_wait(&full[st], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL);
-                okx = __all_sync(0xffffffffu, okx);
-                if (!okx) break;
-                const uint8_t* raw = smem + KC_RAW0 + st * KC_RAW;
-                kc_expand(smem, raw, tid - 64);
-                const uint8_t* rb = raw + (32 * q + lane) * 144;
-                fr = make_float2(kx_half(rb), kx_half(rb + 2));
-                fence_proxy_async();   // the generic-proxy stores, before the tensor cores read them
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(xready);
-                    mbar_arrive(&empty[st]);   // the raw run is consumed
-                }
+        // this warp's vectors' sub-block sums of super-block sbl into L1
+        // (TPW x 8 fp32: 256 bytes), read by the readout one super-block on
+        auto prefetch_sums = [&](int sbl) {
+            if (lane < TPW / 4)
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(xsum + ((int64_t)sbl * NVP + TPW * hh) * 8 + 32 * lane));
+        };
+        // Q4_K: expand super-block sb0 + i of its raw run into the expanded
+        // area, and keep the readout row's (d, dmin) and mins
+        float2 frn = make_float2(0.0f, 0.0f);
+        uint2 mnn = make_uint2(0u, 0u);
+        auto expand = [&](int i) -> bool {
+            const int st = i & 1;
+            bool okx = kx_wait(&full[st], (i >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL);
+            okx = __all_sync(0xffffffffu, okx);
+            if (!okx) return false;
+            const uint8_t* raw = smem + KC_RAW0 + st * KC_RAW;
+            kc_expand(smem, raw, tid - 64);
+            const uint8_t* rb = raw + (32 * q + lane) * 144;
+            frn = make_float2(kx_half(rb), kx_half(rb + 2));
+            mnn = kx_mins(rb + 4);
+            fence_proxy_async();   // the generic-proxy stores, before the tensor cores read them
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(xready);
+                mbar_arrive(&empty[st]);   // the raw run is consumed
             }
-            bool ok = kx_wait(tfull, it & 1, err, BREW_DEVERR_TIMEOUT_FULL);
+            return true;
+        };
+        if (sb0 < sb1) {
+            load_scales(sb0);
+            if (Q4) prefetch_sums(sb0);
+        }
+        bool alive = !(Q4 && sb0 < sb1) || expand(0);
+        int it = 0;
+        for (int sb = sb0; alive && sb < sb1; ++sb, ++it) {
+            const int b = it & 1;
+            bool ok = kx_wait(&tfull[b], (it >> 1) & 1, err, BREW_DEVERR_TIMEOUT_FULL);
             ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld / st are warp-collective
             if (!ok) break;
             tc_fence_after();
+            uint2 mnb = make_uint2(0u, 0u);
+            if (Q4) {   // this super-block's factors; the MMAs are done with the expanded area: the next one
+                fr = frn;
+                mnb = mnn;
+                if (sb + 1 < sb1 && !expand(it + 1)) break;
+                if (sb + 1 < sb1) prefetch_sums(sb + 1);
+            }
             float sv[TPW];
 #pragma unroll
             for (int g = 0; g < TPW / 4; ++g) {
@@ -364,11 +414,13 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
                 sv[4 * g + 3] = svn[g].w;
             }
             if (sb + 1 < sb1) load_scales(sb + 1);
-            const uint64_t d2 = f2_packf(fr.x, fr.x), nm2 = f2_packf(-fr.y, -fr.y);
+            const uint64_t d2 = f2_packf(fr.x, fr.x);
+            const float ndm = -fr.y;
             if (!Q4 && sb + 1 < sb1) fr = __ldg(fpl + (int64_t)(sb + 1) * pitch + frow);
+            const float* xs = xsum + ((int64_t)sb * NVP + TPW * hh) * 8;
 #pragma unroll
             for (int e = 0; e < CW / 12; ++e) {   // 12 columns (2 vector pairs) at a time
-                const uint32_t ta = tq + 12 * e;
+                const uint32_t ta = tq + 256 * b + 12 * e;
                 uint32_t v[NACC][12];
 #pragma unroll
                 for (int a = 0; a < NACC; ++a) {
@@ -391,22 +443,37 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
                         const uint64_t H = f2_add(f2_pack(v[0][c], v[0][c + 1]), negc);
                         const uint64_t L = f2_add(f2_pack(v[1][c], v[1][c + 1]), negc);
                         const uint64_t val = f2_fma(H, kF, L);   // F h + l
-                        uint64_t tv;
-                        if (Q4) {
-                            const uint64_t M1 = f2_add(f2_pack(v[2 % NACC][c], v[2 % NACC][c + 1]), negc);
-                            const uint64_t M2 = f2_add(f2_pack(v[3 % NACC][c], v[3 % NACC][c + 1]), negc);
-                            tv = f2_fma(d2, val, f2_mul(nm2, f2_fma(M2, k256, M1)));
-                        } else {
-                            tv = f2_mul(d2, val);
-                        }
-                        acc[p][l] = f2_fma(s2, tv, acc[p][l]);
+                        acc[p][l] = f2_fma(s2, f2_mul(d2, val), acc[p][l]);
                     }
                 }
             }
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty);
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            if (Q4) {   // - dmin sum_j m_j X_j per vector, into the lo accumulators
+                float mn[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) mn[j] = kx_byte_f(j < 4 ? mnb.x : mnb.y, j & 3);
+#pragma unroll
+                for (int p = 0; p < TPW / 2; ++p) {
+                    float mx[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs + 8 * (2 * p + u)));
+                        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + 8 * (2 * p + u)) + 1);
+                        float t = mn[0] * x0.x;
+                        t = fmaf(mn[1], x0.y, t);
+                        t = fmaf(mn[2], x0.z, t);
+                        t = fmaf(mn[3], x0.w, t);
+                        t = fmaf(mn[4], x1.x, t);
+                        t = fmaf(mn[5], x1.y, t);
+                        t = fmaf(mn[6], x1.z, t);
+                        mx[u] = fmaf(mn[7], x1.w, t);
+                    }
+                    acc[p][2] = f2_fma(f2_packf(ndm, ndm), f2_packf(mx[0], mx[1]), acc[p][2]);
+                }
+            }
         }
         // limbs meet: (lo + mid 2^8) + hi 2^16
         const int64_t npad = (int64_t)gridDim.x * KX_TM;

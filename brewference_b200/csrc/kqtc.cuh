@@ -16,8 +16,9 @@
 // super-block is summed in integers by the MMA and its fp32 factors are
 // applied once:
 //   Q4_K  sc * q = 8 h + l,  h = q (sc >> 3), l = q (sc & 7)  (0..105),
-//         and the min term sum_j m_j X_j (X_j the sub-block sum of x) by
-//         one more MMA against the m_j;
+//         and the min term sum_j m_j X_j (X_j the sub-block sum of x) on
+//         the CUDA cores from the records' fp32 sums, so that the two
+//         tensor-memory accumulators (h, l) fit twice in the 512 columns;
 //         element value d (8 h + l) - dmin m_j  (GGML: d sc q - dmin m);
 //   Q6_K  sc * (q - 32) = 64 h + l,  h in [-64, 63], l in [0, 63];
 //         element value d (64 h + l)  (GGML: d sc (q - 32)).
@@ -37,9 +38,11 @@
 //   per super-block: 8 limb tiles (one per sub-block: NC = 48 per 16
 //   vectors columns x 32 k, K-major core-matrix layout tc_tile_off, column
 //   6 (t / 2) + 2 l + (t % 2) for vector t, limb l), then two min-term
-//   tiles with the sub-block sums X_j = 256 Xh_j + Xl_j at k = j < 8
+//   tiles with the limbs' sub-block sums X_j = 256 Xh_j + Xl_j at k = j < 8
 //   (Xl, then Xh; k >= 8 zero);
-//   scales [K/256][16 ceil(nv / 16)] fp32 (vectors past nv: zero).
+//   scales [K/256][16 ceil(nv / 16)] fp32 (vectors past nv: zero);
+//   sub-block sums [K/256][16 ceil(nv / 16)][8] fp32: the sum of the
+//   vector's 32 limb-split elements of sub-block j, scale applied.
 // Every integer sum of a super-block stays below 2^22 in magnitude, so the
 // tensor-memory cells, preset to the bits of 1.5 * 2^23, read back as
 // exact floats.
@@ -69,7 +72,7 @@ inline size_t kx_bytes(int type, int64_t N, int64_t K) {
 // Bytes of the x records of nv vectors of K elements (tiles, then scales).
 inline size_t kx_rec_tile_bytes(int nv) { return (size_t)10 * 48 * ((nv + 15) / 16) * 32; }   // per super-block
 inline size_t kx_rec_bytes(int nv, int64_t K) {
-    return (size_t)(K / 256) * (kx_rec_tile_bytes(nv) + 4 * 16 * (size_t)((nv + 15) / 16));
+    return (size_t)(K / 256) * (kx_rec_tile_bytes(nv) + 4 * 9 * 16 * (size_t)((nv + 15) / 16));
 }
 
 // Split of the super-blocks over CTAs for a matrix whose row family has
@@ -151,6 +154,11 @@ __device__ __forceinline__ void kx_emit_sb(uint8_t* rec, int K, int nvp, int t, 
             mt[tc_tile_off(c0 + 2 * l, j)] = (uint8_t)xl;
             mt[NC * 32 + tc_tile_off(c0 + 2 * l, j)] = (uint8_t)xh;
         }
+        // the fp32 sub-block sum: the limbs' sums meet exactly in an int
+        // (|.| < 2^28), then one rounding to fp32 and the scale
+        const int st = sum[0] * 65536 + sum[1] * 256 + sum[2];
+        float* xsum = reinterpret_cast<float*>(rec + (int64_t)KSB * 10 * NC * 32) + (int64_t)KSB * nvp;
+        xsum[((int64_t)sb * nvp + t) * 8 + j] = (float)st * prep_block_scale(am);
     }
     if (lane < 18) {   // k 8..31 of the min-term columns are zero
         const int tl = lane / 9, rem = lane % 9, l = rem / 3, k = 8 + 8 * (rem % 3);
