@@ -5,7 +5,8 @@ sums of the activation limbs split exactly into two int8 bytes; every
 integer sum of a 256-element super-block stays below 2^22 in magnitude (so
 tensor-memory cells preset to the bits of 1.5 * 2^23 read back exact); and,
 on blocks quantized by the oracle, the expanded form computes the same dot
-product as the oracle's dequantized rows."""
+product as the oracle's dequantized rows, also with the Q4_K min term taken
+from fp32 sub-block sums as the matvec's epilogue forms it."""
 import numpy as np
 import pytest
 
@@ -126,3 +127,38 @@ def test_expanded_superblock_dot_matches_oracle(qt):
     # tolerance: 1e-7 of sum |w x| (the fp32 factors d, dmin and the x scale
     # are the only rounded quantities)
     assert abs(total - ref) <= 1e-7 * np.abs(oracle.dequantize(qt, w, 0, K)).astype(np.float64) @ np.abs(x)
+
+
+def test_q4k_min_term_from_fp32_subblock_sums():
+    """The Q4_K min term as the matvec computes it now: the records carry,
+    per vector and sub-block, the exact integer 2^16 sum(hi) + 2^8 sum(mid)
+    + sum(lo) (an int32: |.| < 2^28) rounded once to fp32 and scaled by s;
+    the epilogue forms -dmin sum_j m_j X_j with fp32 FMAs beside the integer
+    h / l sums.  Against the oracle's dequantized row times x."""
+    rng = np.random.default_rng(29)
+    K = 2048
+    f32 = np.float32
+    for trial in range(4):
+        w = oracle.quantize(TYPE_Q4_K, (rng.standard_normal(K) * 0.02).astype(np.float32))
+        x = (rng.standard_normal(K) * (1.0 + 10.0 * trial)).astype(np.float32)
+        ref = float(oracle.dequantize(TYPE_Q4_K, w, 0, K).astype(np.float64) @ x.astype(np.float64))
+        total = 0.0
+        for sb in range(K // 256):
+            blk = np.frombuffer(bytes(w[sb * 144:(sb + 1) * 144]), dtype=np.uint8).astype(np.int64)
+            s, (hi, mid, lo) = _limbs(x[sb * 256:(sb + 1) * 256])
+            d, dmin, sc, m, q = _q4k_fields(blk)
+            scl = np.repeat(sc, 32)
+            h, l = q * (scl >> 3), q * (scl & 7)
+            main = 0.0
+            for weight, lim in zip((65536.0, 256.0, 1.0), (hi, mid, lo)):
+                main += weight * (d * (8 * int(h @ lim) + int(l @ lim)))
+            st = (65536 * hi.reshape(8, 32).sum(axis=1) + 256 * mid.reshape(8, 32).sum(axis=1)
+                  + lo.reshape(8, 32).sum(axis=1))
+            assert np.abs(st).max() < 2 ** 28
+            X = st.astype(f32) * f32(s)                      # one rounding, then the scale
+            mx = f32(0.0)
+            for j in range(8):                               # fp32 FMAs in sub-block order
+                mx = f32(np.float64(f32(m[j])) * np.float64(X[j]) + np.float64(mx))
+            total += s * main - dmin * float(mx)
+        tol = 2e-7 * float(np.abs(oracle.dequantize(TYPE_Q4_K, w, 0, K)).astype(np.float64) @ np.abs(x))
+        assert abs(total - ref) <= tol, (trial, abs(total - ref), tol)
