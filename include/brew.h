@@ -320,7 +320,10 @@ BREW_API int brew_model_tensor(brew_model m, int which, brew_tensor* out);
  * sequences (host arrays tokens[batch], pos[batch]).  Either output may be
  * NULL: logits [batch][vocab] (host fp32) and/or argmax ids [batch] computed
  * on the device with Kernels.argMax semantics (lowest index on ties,
- * transformer/math/Kernels.java:150-162). */
+ * transformer/math/Kernels.java:150-162).  One sequence without logits on
+ * the persistent decode kernel is one launch and one synchronize: the token
+ * and position are launch parameters and the kernel writes the id and the
+ * device error word into mapped pinned host memory of the model. */
 BREW_API int brew_model_forward(brew_model m, const int32_t* tokens, const int32_t* pos,
                        int32_t batch, float* logits, int32_t* argmax);
 
