@@ -119,19 +119,18 @@ __global__ void kx_prep_kernel(const float* x, int ldx, int K, int nv, int nvp, 
 }
 
 // Shared memory of one stage (one super-block): the 8 sub-blocks' h and l
-// tiles (128 rows x 32 k each: K-half 0 then K-half 1, 2 KB apart), the
-// min tile (K-half 0 = m_0..m_7, 0; K-half 1 = a zero area never copied
-// into), then the records' 8 limb tiles and 2 min-term tiles.
-constexpr int KX_AH = 0, KX_AL = 32768, KX_AM = 65536, KX_Z = 67584, KX_B = 69632;
-constexpr int KX_STAGE = KX_B + 10 * 96 * 32;   // 100352
+// tiles (128 rows x 32 k each: K-half 0 then K-half 1, 2 KB apart), then
+// the records' 8 limb tiles.
+constexpr int KX_AH = 0, KX_AL = 32768, KX_B = 65536;
+constexpr int KX_STAGE = KX_B + 8 * 96 * 32;    // 90112
 constexpr int KX_SMEM = 2 * KX_STAGE + 128;
 constexpr int KX_EPI = 16;                      // epilogue warps: 4 per tensor-memory lane quadrant
 constexpr int KX_THREADS = 64 + 32 * KX_EPI;    // loader warp, MMA warp, epilogue warps
 constexpr int KX_TMEM_COLS = 512;               // two sets of the h, l accumulators: at 0, 128 and 256, 384
-// Q4_K (compact stream): one expanded area (h, l, min tile, zero area at the
-// offsets above), then two stages of records and two of raw block runs
-// (128 rows x 144 bytes), then the barriers.
-constexpr int KC_REC = 10 * 96 * 32;            // records of one super-block (up to 32 vectors)
+// Q4_K (compact stream): one expanded area (h, l at the offsets above), then
+// two stages of records and two of raw block runs (128 rows x 144 bytes),
+// then the barriers.
+constexpr int KC_REC = 8 * 96 * 32;             // records of one super-block (up to 32 vectors)
 constexpr int KC_REC0 = KX_B;
 constexpr int KC_RAW = 128 * 144;
 constexpr int KC_RAW0 = KC_REC0 + 2 * KC_REC;
@@ -141,7 +140,7 @@ constexpr int KC_SMEM = KC_BAR + 128;
 // Q4_K: expands item e (0 .. 511) of a raw run of 128 rows: row e % 128,
 // sub-blocks 2 (e / 128) and 2 (e / 128) + 1, into the h / l tiles (the
 // layout of the expanded planes: sub-block j at j 4096, K-half hk 2048
-// further, row r 16 bytes each) and, for e < 128, the row's min tile entry.
+// further, row r 16 bytes each).
 // Element value d (8 h + l) - dmin m_j with h = q (sc >> 3), l = q (sc & 7)
 // (GGML's d sc q - dmin m), q the element's nibble.
 __device__ __forceinline__ void kc_expand(uint8_t* xa, const uint8_t* raw, int e) {
@@ -169,17 +168,6 @@ __device__ __forceinline__ void kc_expand(uint8_t* xa, const uint8_t* raw, int e
             *reinterpret_cast<uint4*>(xa + KX_AH + so) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
             *reinterpret_cast<uint4*>(xa + KX_AL + so) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
         }
-    }
-    if (pr == 0) {   // the min tile row: m_0 .. m_7, then 8 zero bytes
-        uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            int scj, mj;
-            kx_scale_min(blk + 4, j, scj, mj);
-            if (j < 4) lo |= (uint32_t)mj << (8 * j);
-            else hi |= (uint32_t)mj << (8 * (j - 4));
-        }
-        *reinterpret_cast<uint4*>(xa + KX_AM + row * 16) = make_uint4(lo, hi, 0u, 0u);
     }
 }
 
@@ -214,7 +202,7 @@ __device__ __forceinline__ bool kx_wait(uint64_t* bar, uint32_t parity, unsigned
 // the MMAs of super-block i + 1 overlap the readout of i.
 template <int TYPE, int NVG>
 __global__ void __launch_bounds__(KX_THREADS, 1)
-    kx_mma_kernel(const uint8_t* base, int64_t pitch, int64_t row0, int n, int K, size_t m_off, size_t f_off,
+    kx_mma_kernel(const uint8_t* base, int64_t pitch, int64_t row0, int n, int K, size_t f_off,
                   const uint8_t* rec, int nv, int S, float* part, int* ctr, const float* bias, float* y, int ldy,
                   unsigned int* err) {
     constexpr bool Q4 = TYPE == BREW_TYPE_Q4_K;
@@ -233,7 +221,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
     const int KSB = K / 256, split = blockIdx.y;
     const int sb0 = (int)((int64_t)split * KSB / S), sb1 = (int)((int64_t)(split + 1) * KSB / S);
     const int64_t r0 = row0 + (int64_t)blockIdx.x * KX_TM;   // the CTA's first row in the family
-    const int rec_tile = 10 * NC * 32;
+    const int rec_tile = 8 * NC * 32;
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
                      "r"(KX_TMEM_COLS)
@@ -252,10 +240,6 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
         mbar_init(xready, KX_EPI);
         fence_mbar_init();
     }
-    if (Q4) {   // the min tile's second K-half: zeros, read by the tensor cores
-        for (int i = tid; i < 512; i += KX_THREADS) reinterpret_cast<uint32_t*>(smem + KX_Z)[i] = 0u;
-        fence_proxy_async();
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -267,7 +251,7 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
             const uint8_t* hp = base;
             const uint8_t* lp = base + (size_t)K * pitch;
             const uint32_t bbytes = 8 * NC * 32;   // the 8 limb tiles
-            const uint32_t bytes = 16 * 4096 + (Q4 ? 2048 : 0) + bbytes;
+            const uint32_t bytes = 16 * 4096 + bbytes;   // Q6_K: the h and l tiles and the records
             int it = 0;
             for (int sb = sb0; sb < sb1; ++sb, ++it) {
                 const int st = it & 1;
@@ -287,7 +271,6 @@ __global__ void __launch_bounds__(KX_THREADS, 1)
                     bulk_g2s_hint(s0 + KX_AH + so, hp + o, 2048, &full[st], pol);
                     bulk_g2s_hint(s0 + KX_AL + so, lp + o, 2048, &full[st], pol);
                 }
-                if (Q4) bulk_g2s_hint(s0 + KX_AM, base + m_off + ((int64_t)sb * pitch + r0) * 16, 2048, &full[st], pol);
                 bulk_g2s(s0 + KX_B, rec + (int64_t)sb * rec_tile, bbytes, &full[st]);
             }
         }
@@ -536,8 +519,8 @@ int kx_launch_t(const uint8_t* base, int64_t N, int64_t row0, int n, int K, cons
         attr_devs |= 1ull << dev;
     }
     const dim3 grid((unsigned)((n + KX_TM - 1) / KX_TM), (unsigned)S);
-    kx_mma_kernel<TYPE, NVG><<<grid, KX_THREADS, SMEM, stream>>>(base, kx_pitch(N), row0, n, K, kx_m_off(N, K),
-                                                                    kx_f_off(TYPE, N, K), rec, nv, S, part, ctr, bias,
+    kx_mma_kernel<TYPE, NVG><<<grid, KX_THREADS, SMEM, stream>>>(base, kx_pitch(N), row0, n, K,
+                                                                    kx_f_off(N, K), rec, nv, S, part, ctr, bias,
                                                                     y, ldy, err);
     BREW_CUDA(cudaGetLastError());
     count_launch();
@@ -572,7 +555,7 @@ int kx_pack_launch(int type, const uint8_t* w, int64_t rows, int K, uint8_t* bas
     }
     const int64_t cnt = rows * (K / 32);
     const unsigned blocks = (unsigned)((cnt + 255) / 256);
-    kx_pack_kernel<<<blocks, 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off, kx_f_off(type, N, K));
+    kx_pack_kernel<<<blocks, 256, 0, stream>>>(w, rows, K, base, kx_pitch(N), row_off, kx_f_off(N, K));
     BREW_CUDA(cudaGetLastError());
     count_launch();
     return BREW_OK;

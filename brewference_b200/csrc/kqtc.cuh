@@ -24,22 +24,21 @@
 //         element value d (64 h + l)  (GGML: d sc (q - 32)).
 // Expanded planes of one matrix (or row family) of N rows, pitch P = N + 128
 // rows (the last 128 rows zero, so a 128-row box never leaves the buffer;
-// in HBM for Q6_K, in shared memory for one super-block of Q4_K):
+// in HBM for Q6_K; Q4_K's h and l tiles are built in shared memory for one
+// super-block of 128 rows at a time, and its d, dmin and m_j read from the
+// raw blocks):
 //   h, l  [K/16][P][16]  int8: the 16-element K-halves of every row, row
 //                         after row, so the 128 rows of a CTA's K-half are
 //                         one contiguous 2 KB run (an MMA operand's core
 //                         matrices: 8 rows x 16 B);
-//   m     [K/256][P][16] (Q4_K) the 8 sub-block mins m_j, then 8 zero bytes;
-//   f     [K/256][P]     float2 (d, dmin) (Q6_K: (d, 0)).
+//   f     [K/256][P]     float2 (d, 0) (Q6_K).
 //
 // Activations: per vector and super-block, 24-bit fixed point relative to
 // the super-block's max|x|, split into limbs hi / mid / lo (the prep.cuh
 // split).  Records of a launch ([K/256] super-blocks, then the scales):
 //   per super-block: 8 limb tiles (one per sub-block: NC = 48 per 16
 //   vectors columns x 32 k, K-major core-matrix layout tc_tile_off, column
-//   6 (t / 2) + 2 l + (t % 2) for vector t, limb l), then two min-term
-//   tiles with the limbs' sub-block sums X_j = 256 Xh_j + Xl_j at k = j < 8
-//   (Xl, then Xh; k >= 8 zero);
+//   6 (t / 2) + 2 l + (t % 2) for vector t, limb l);
 //   scales [K/256][16 ceil(nv / 16)] fp32 (vectors past nv: zero);
 //   sub-block sums [K/256][16 ceil(nv / 16)][8] fp32: the sum of the
 //   vector's 32 limb-split elements of sub-block j, scale applied.
@@ -59,18 +58,15 @@ constexpr int KX_MAX_VECTORS = 32;    // per launch
 
 inline int64_t kx_pitch(int64_t N) { return N + 128; }
 inline size_t kx_plane_bytes(int64_t N, int64_t K) { return (size_t)K * (size_t)kx_pitch(N); }   // h or l
-inline size_t kx_m_off(int64_t N, int64_t K) { return 2 * kx_plane_bytes(N, K); }
-inline size_t kx_f_off(int type, int64_t N, int64_t K) {
-    return kx_m_off(N, K) + (type == BREW_TYPE_Q4_K ? (size_t)(K / 256) * kx_pitch(N) * 16 : 0);
-}
+inline size_t kx_f_off(int64_t N, int64_t K) { return 2 * kx_plane_bytes(N, K); }   // Q6_K
 // Bytes of the weight copy of an N x K matrix (or row family): compact
 // (Q4_K) or expanded (Q6_K).
 inline size_t kx_bytes(int type, int64_t N, int64_t K) {
     if (type == BREW_TYPE_Q4_K) return (size_t)(K / 256) * kx_pitch(N) * 144;
-    return kx_f_off(type, N, K) + (size_t)(K / 256) * kx_pitch(N) * 8;
+    return kx_f_off(N, K) + (size_t)(K / 256) * kx_pitch(N) * 8;
 }
 // Bytes of the x records of nv vectors of K elements (tiles, then scales).
-inline size_t kx_rec_tile_bytes(int nv) { return (size_t)10 * 48 * ((nv + 15) / 16) * 32; }   // per super-block
+inline size_t kx_rec_tile_bytes(int nv) { return (size_t)8 * 48 * ((nv + 15) / 16) * 32; }   // per super-block
 inline size_t kx_rec_bytes(int nv, int64_t K) {
     return (size_t)(K / 256) * (kx_rec_tile_bytes(nv) + 4 * 9 * 16 * (size_t)((nv + 15) / 16));
 }
@@ -135,7 +131,7 @@ __device__ __forceinline__ void kx_emit_sb(uint8_t* rec, int K, int nvp, int t, 
         sum[1] += mid;
         sum[2] += lo;
     }
-    uint8_t* r = rec + (int64_t)sb * (10 * NC * 32);
+    uint8_t* r = rec + (int64_t)sb * (8 * NC * 32);
     const int j = lane >> 2, k0 = 8 * (lane & 3);
     const int c0 = 6 * (t >> 1) + (t & 1);   // limb l: column c0 + 2 l
     uint8_t* tile = r + j * NC * 32;
@@ -145,26 +141,14 @@ __device__ __forceinline__ void kx_emit_sb(uint8_t* rec, int K, int nvp, int t, 
     for (int o = 1; o < 4; o <<= 1)
 #pragma unroll
         for (int l = 0; l < 3; ++l) sum[l] += __shfl_xor_sync(0xffffffffu, sum[l], o);
-    uint8_t* mt = r + 8 * NC * 32;   // min-term tiles: Xl, then Xh
     if ((lane & 3) == 0) {
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-            const int xl = ((sum[l] + 128) & 255) - 128;
-            const int xh = (sum[l] - xl) >> 8;
-            mt[tc_tile_off(c0 + 2 * l, j)] = (uint8_t)xl;
-            mt[NC * 32 + tc_tile_off(c0 + 2 * l, j)] = (uint8_t)xh;
-        }
         // the fp32 sub-block sum: the limbs' sums meet exactly in an int
         // (|.| < 2^28), then one rounding to fp32 and the scale
         const int st = sum[0] * 65536 + sum[1] * 256 + sum[2];
-        float* xsum = reinterpret_cast<float*>(rec + (int64_t)KSB * 10 * NC * 32) + (int64_t)KSB * nvp;
+        float* xsum = reinterpret_cast<float*>(rec + (int64_t)KSB * 8 * NC * 32) + (int64_t)KSB * nvp;
         xsum[((int64_t)sb * nvp + t) * 8 + j] = (float)st * prep_block_scale(am);
     }
-    if (lane < 18) {   // k 8..31 of the min-term columns are zero
-        const int tl = lane / 9, rem = lane % 9, l = rem / 3, k = 8 + 8 * (rem % 3);
-        *reinterpret_cast<uint64_t*>(mt + tl * NC * 32 + tc_tile_off(c0 + 2 * l, k)) = 0ull;
-    }
-    if (lane == 0) reinterpret_cast<float*>(rec + (int64_t)KSB * 10 * NC * 32)[(int64_t)sb * nvp + t] = prep_block_scale(am);
+    if (lane == 0) reinterpret_cast<float*>(rec + (int64_t)KSB * 8 * NC * 32)[(int64_t)sb * nvp + t] = prep_block_scale(am);
 }
 
 #endif  // __CUDACC__

@@ -1,7 +1,6 @@
 """The integer identities the tcgen05 K-quant matvec (csrc/kqtc.cu) rests on,
 checked on the CPU: every Q4_K / Q6_K element's integer factor, with its
-sub-block scale folded in, splits exactly into two int8 limbs; the sub-block
-sums of the activation limbs split exactly into two int8 bytes; every
+sub-block scale folded in, splits exactly into two int8 limbs; every
 integer sum of a 256-element super-block stays below 2^22 in magnitude (so
 tensor-memory cells preset to the bits of 1.5 * 2^23 read back exact); and,
 on blocks quantized by the oracle, the expanded form computes the same dot
@@ -34,15 +33,6 @@ def test_q6k_scale_split_exhaustive():
     assert np.array_equal(64 * h + l, v)
     assert h.min() >= -64 and h.max() <= 64 and l.min() >= 0 and l.max() <= 63
     assert 256 * 64 * LIMB_MAX < MAGIC_RANGE and 256 * 63 * LIMB_MAX < MAGIC_RANGE
-
-
-def test_min_term_byte_split_exhaustive():
-    X = np.arange(-32 * 128, 32 * 127 + 1)   # the sum of 32 limbs of a sub-block
-    xl = ((X + 128) & 255) - 128
-    xh = (X - xl) >> 8
-    assert np.array_equal(256 * xh + xl, X)
-    assert xl.min() >= -128 and xl.max() <= 127 and xh.min() >= -16 and xh.max() <= 16
-    assert 8 * 63 * 128 < MAGIC_RANGE and 8 * 63 * 16 < MAGIC_RANGE   # mins m_j <= 63 over 8 sub-blocks
 
 
 def _half(b, o):
@@ -117,10 +107,7 @@ def test_expanded_superblock_dot_matches_oracle(qt):
         acc = 0.0
         for weight, lim in zip((65536.0, 256.0, 1.0), limbs):
             hs, ls = int(h @ lim), int(l @ lim)
-            X = lim.reshape(8, 32).sum(axis=1)
-            xl = ((X + 128) & 255) - 128
-            xh = (X - xl) >> 8
-            msum = int(m @ xl) + 256 * int(m @ xh)
+            msum = int(m @ lim.reshape(8, 32).sum(axis=1))
             assert max(abs(hs), abs(ls), abs(msum)) < MAGIC_RANGE
             acc += weight * (d * (F * hs + ls) - dmin * msum)
         total += s * acc
